@@ -1,0 +1,402 @@
+#!/usr/bin/env python
+"""Benchmark of the Qwen3 hot path on B200 (BASELINE.json metric).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload: Qwen3-0.6B architecture, random-init FP16
+N(0, 0.02) weights from seed 2, a 128-token prompt of uniform ids, then 256
+greedy decode steps (batch 1, cache capacity 2048). One bench step is one
+such request: prefill + 256 pipelined decode steps. `value` is decode
+tokens/s timed on the device with CUDA events (inputs resident; the 1.2 GB of
+weights exceed L2, so no flush is needed); `e2e` is the same metric through
+the public generate call with the prompt copied from pinned host memory and
+the ids read back, timed by the host clock around each call. With N > 1 GPUs
+(torchrun) every rank serves its own replica (the 0.6B model is not sharded);
+value = all ranks' decode tokens / max-over-ranks time.
+
+`--impl reference` times the reference path on the host cores: the reference
+(Rust + Metal) cannot be built or run here, so its arm is the C++ CPU oracle
+(oracle/, a restatement of the reference kernels) on the same config.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "metal-infer-rs_b200"))
+sys.path.insert(0, os.path.join(ROOT, "oracle"))
+
+INPUT_STREAM = 1 << 20
+PROMPT = 128
+DECODE = 256
+CAPACITY = 2048
+SEED = 2
+METRIC = "decode tokens/s (batch 1, greedy)"
+CONFIG = dict(hidden_size=1024, intermediate_size=3072, num_hidden_layers=28,
+              num_attention_heads=16, num_key_value_heads=8, head_dim=128, rms_norm_eps=1e-6,
+              rope_theta=1e6, vocab_size=151936, tie_word_embeddings=1)
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+# ---- algorithmic bytes ------------------------------------------------------------
+def weight_bytes_per_layer(c):
+    h, I = c["hidden_size"], c["intermediate_size"]
+    qw = c["num_attention_heads"] * c["head_dim"]
+    kw = c["num_key_value_heads"] * c["head_dim"]
+    mats = (qw + 2 * kw) * h + h * qw + 2 * I * h + h * I
+    norms = 2 * h + 2 * c["head_dim"]
+    return 2 * (mats + norms)
+
+
+def decode_bytes_per_token(c, kv_len):
+    """Weight + KV bytes one decode step must read (the north-star roofline)."""
+    h, V = c["hidden_size"], c["vocab_size"]
+    kv = kv_len * c["num_key_value_heads"] * c["head_dim"] * 2 * 2 * c["num_hidden_layers"]
+    return c["num_hidden_layers"] * weight_bytes_per_layer(c) + 2 * V * h + 2 * h + kv
+
+
+def kernel_bytes(c, name, mean_len):
+    h, I, V = c["hidden_size"], c["intermediate_size"], c["vocab_size"]
+    qw = c["num_attention_heads"] * c["head_dim"]
+    kw = c["num_key_value_heads"] * c["head_dim"]
+    return {
+        "qkv_gemv": 2 * ((qw + 2 * kw) * h + 2 * h + qw + 2 * kw),
+        "attention_decode": 2 * (mean_len * kw * 2 + qw * 2 + kw * 2),
+        "o_gemv": 2 * (h * qw + qw + h),
+        "gate_up_gemv": 2 * (2 * I * h + 3 * h + I),
+        "down_gemv": 2 * (h * I + I + 2 * h),
+        "lm_head_argmax": 2 * (V * h + 2 * h + V),
+    }.get(name)
+
+
+# ---- clocks -------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int):
+        self.gpu = gpu
+        self.proc = None
+        self.lines = []
+        self.t = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            if self.t:
+                self.t.join(timeout=2)
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---- our arm ------------------------------------------------------------------------
+def run_ours(args, rank, world, local_rank):
+    import numpy as np
+    import torch
+    import metal_infer as mi
+    import oracle as O
+
+    torch.cuda.set_device(local_rank)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank))
+
+    ctx = mi.MetalContext(local_rank)
+    model = mi.Qwen3Model.random(ctx, CONFIG, seed=SEED)
+    cache = model.kv_cache(CAPACITY)
+    prompt = O.gen_tokens(SEED, INPUT_STREAM, PROMPT, CONFIG["vocab_size"])
+    pinned = torch.from_numpy(prompt.astype(np.int64)).to(torch.int32).pin_memory()
+    prompt_ptr = pinned.numpy().view(np.uint32)
+    stream = torch.cuda.ExternalStream(ctx.stream())
+
+    def one_step():
+        """prefill + 256 decode steps; returns (prefill_ms, decode_ms)."""
+        e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+        slot = ctx.empty([1], mi.DType.U32)
+        e0.record(stream)
+        model.prefill_argmax(prompt_ptr, cache, slot)
+        e1.record(stream)
+        model.decode_steps(cache, DECODE)
+        e2.record(stream)
+        return e0, e1, e2
+
+    for _ in range(args.warmup):
+        ev = one_step()
+        ev[2].synchronize()
+    # The generated ids must match the oracle's greedy ids (checked once).
+    ids = cache.tokens(PROMPT, DECODE + 1)
+
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    events = []
+    with ClockSampler(local_rank) as clocks:
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            events.append(one_step())
+        torch.cuda.synchronize()
+        wall = time.perf_counter() - t0
+    prefill_ms = sum(e0.elapsed_time(e1) for e0, e1, _ in events)
+    decode_ms = sum(e1.elapsed_time(e2) for _, e1, e2 in events)
+    total_ms = sum(e0.elapsed_time(e2) for e0, _, e2 in events)
+    if dist:
+        t = torch.tensor([decode_ms, prefill_ms, total_ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        decode_ms, prefill_ms, total_ms = (float(x) for x in t.tolist())
+
+    decode_tps = world * DECODE * args.steps / (decode_ms / 1e3)
+    prefill_tps = world * PROMPT * args.steps / (prefill_ms / 1e3)
+
+    # e2e: the public generate call, host prompt in, host ids out.
+    e2e_times = []
+    out_ids = None
+    for i in range(args.warmup + args.steps):
+        torch.cuda.synchronize()
+        t = time.perf_counter()
+        out_ids = model.generate(prompt_ptr, DECODE + 1, cache)
+        dt = time.perf_counter() - t
+        if i >= args.warmup:
+            e2e_times.append(dt)
+    e2e_s = sum(e2e_times)
+    if dist:
+        t = torch.tensor([e2e_s], device="cuda", dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    e2e_tps = world * DECODE * args.steps / e2e_s
+
+    # Live per-kernel timing (CUDA events per launch on the engine stream).
+    model.prefill_argmax(prompt_ptr, cache, ctx.empty([1], mi.DType.U32))
+    ctx.set_kernel_profiling(True)
+    ctx.take_kernel_profiles()
+    model.decode_steps(cache, 32)
+    ctx.synchronize()
+    prof = ctx.take_kernel_profiles()
+    ctx.set_kernel_profiling(False)
+    per = {}
+    for name, sec in prof:
+        d = per.setdefault(name, [0, 0.0])
+        d[0] += 1
+        d[1] += sec
+    mean_len = PROMPT + 16.5
+    hbm, peak_kind = peaks()
+    kernels = {}
+    for name, (n, sec) in per.items():
+        b = kernel_bytes(CONFIG, name, mean_len)
+        avg = sec / n
+        kernels[name] = {"launches": n, "avg_us": round(avg * 1e6, 3),
+                         "share": round(sec / sum(s for _, s in per.values()), 4),
+                         "gbs": round(b / avg / 1e9, 1) if b else None}
+    dominant = max(per, key=lambda k: per[k][1])
+    dom_avg = per[dominant][1] / per[dominant][0]
+    dom_bytes = kernel_bytes(CONFIG, dominant, mean_len)
+    achieved = dom_bytes / dom_avg / 1e9
+    traffic = read_traffic(dominant)
+
+    kv_mean = PROMPT + (DECODE + 1) / 2.0
+    bytes_tok = decode_bytes_per_token(CONFIG, kv_mean)
+    per_gpu_tps = decode_tps / world
+
+    ok = bool(np.array_equal(ids, out_ids)) if out_ids is not None else False
+    layer_launches = 5 * CONFIG["num_hidden_layers"] + 1
+    prefill_launches = 1 + 14 * CONFIG["num_hidden_layers"] + 2
+    launches = args.steps * (prefill_launches + DECODE * layer_launches)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(decode_tps, 2), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(total_ms / args.steps, 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+            "data": "synthetic (random-init FP16 N(0,0.02) weights, uniform prompt ids)",
+            "config": {"workload": "Qwen3-0.6B batch-1 greedy: 128-token prompt + 256 decode "
+                                   "steps (BASELINE config 2)",
+                       "layers": 28, "hidden": 1024, "vocab": 151936, "prompt": PROMPT,
+                       "decode_steps": DECODE, "kv_capacity": CAPACITY,
+                       "parallelism": f"replicas x{world}",
+                       "l2": "weights 1.2 GB > 126 MB L2 (no flush needed)"},
+            "prefill_tokens_per_s": round(prefill_tps, 1),
+            "decode_hbm": {"bytes_per_token": int(bytes_tok),
+                           "achieved_gbs": round(bytes_tok * per_gpu_tps / 1e9, 1),
+                           "peak_gbs": hbm, "frac": round(bytes_tok * per_gpu_tps / 1e9 / hbm, 4),
+                           "note": f"weights + KV bytes per token / time, {peak_kind} peak"},
+            "greedy_ids_consistent": ok,
+            "e2e": {"value": round(e2e_tps, 2), "unit": "tokens/s",
+                    "h2d_bytes_per_step": PROMPT * 4, "d2h_bytes_per_step": (DECODE + 1) * 4,
+                    "note": "mi_qwen3_generate per request (prefill included), host clock"},
+            "roofline": {"bound": "hbm", "kernel": dominant, "achieved": round(achieved, 1),
+                         "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4),
+                         "traffic": traffic, "bytes_per_launch": dom_bytes,
+                         "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"},
+            "kernels": kernels,
+            "gpu_launches": launches,
+            "clocks": clocks.summary(),
+            "wall_s": round(wall, 3),
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(args.cpu_sample_steps)
+        print(json.dumps(line), flush=True)
+    del model, cache
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def read_traffic(kernel):
+    """DRAM bytes per launch of `kernel` from the committed ncu summary."""
+    path = os.path.join(ROOT, "profiles", "ncu_traffic.md")
+    try:
+        for line in open(path):
+            m = re.match(r"\|\s*(\w+)\s*\|\s*([\d.]+)\s*\|", line)
+            if m and m.group(1) == kernel:
+                return float(m.group(2))
+    except OSError:
+        pass
+    return None
+
+
+# ---- CPU legs ---------------------------------------------------------------------------
+def oracle_decode_rate(decode_steps: int):
+    import oracle as O
+    m = O.Qwen3(CONFIG, seed=SEED, capacity=CAPACITY)
+    prompt = O.gen_tokens(SEED, INPUT_STREAM, PROMPT, CONFIG["vocab_size"])
+    t = time.perf_counter()
+    logits = m.forward(prompt)
+    prefill_s = time.perf_counter() - t
+    tok = O.argmax(logits)
+    return m, tok, prefill_s
+
+
+def cpu_baseline(decode_steps: int):
+    import numpy as np
+    import oracle as O
+    m, tok, prefill_s = oracle_decode_rate(decode_steps)
+    t = time.perf_counter()
+    for _ in range(decode_steps):
+        tok = O.argmax(m.forward(np.array([tok], np.uint32)))
+    dt = time.perf_counter() - t
+    threads = O.lib().or_num_threads()
+    m.close()
+    return {"value": round(decode_steps / dt, 3), "unit": "tokens/s", "cores": threads,
+            "kind": "port",
+            "sample": f"C++ oracle (OpenMP, {threads} threads): 128-token prefill "
+                      f"({prefill_s:.1f} s, untimed) then {decode_steps} greedy decode steps of "
+                      "the same Qwen3-0.6B workload"}
+
+
+def run_reference(args, rank):
+    if rank != 0:
+        return
+    import numpy as np
+    import oracle as O
+    m, tok, prefill_s = oracle_decode_rate(0)
+    per_step = args.cpu_sample_steps_ref
+    times = []
+    for i in range(args.warmup + args.steps):
+        t = time.perf_counter()
+        for _ in range(per_step):
+            tok = O.argmax(m.forward(np.array([tok], np.uint32)))
+        if i >= args.warmup:
+            times.append(time.perf_counter() - t)
+        if len(m) + per_step > CAPACITY:
+            m.reset()
+            tok = O.argmax(m.forward(O.gen_tokens(SEED, INPUT_STREAM, PROMPT, CONFIG["vocab_size"])))
+    threads = O.lib().or_num_threads()
+    value = args.steps * per_step / sum(times)
+    sample = (f"reference path restated in C++ (oracle/, OpenMP {threads} threads; the Rust/Metal "
+              f"reference cannot run here): {per_step} greedy decode steps per step after a "
+              "128-token prefill, Qwen3-0.6B seed 2")
+    line = {"impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "tokens/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(1e3 * sum(times) / args.steps, 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+            "config": {"workload": "Qwen3-0.6B batch-1 greedy decode (BASELINE config 2)",
+                       "prompt": PROMPT},
+            "cpu_baseline": {"value": round(value, 3), "unit": "tokens/s", "cores": threads,
+                             "kind": "port", "sample": sample},
+            "e2e": {"value": round(value, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    m.close()
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-sample-steps", type=int, default=48)
+    ap.add_argument("--cpu-sample-steps-ref", type=int, default=8)
+    args = ap.parse_args()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+    if args.warmup < 3:
+        args.warmup = 3
+    run_ours(args, rank, world, local_rank)
+
+
+if __name__ == "__main__":
+    main()

@@ -311,12 +311,12 @@ mi_status mi_qwen3_config_validate(const mi_qwen3_config* config);
  * 9 down, 13 lm_head). Replaces Qwen3Model::load (qwen3.rs:155-240) for
  * synthetic runs. */
 mi_status mi_qwen3_create_random(mi_context* ctx, const mi_qwen3_config* config, uint64_t seed,
-                                 float std_dev, mi_qwen3** out);
+                                 double std_dev, mi_qwen3** out);
 /* Qwen3Model::load from a directory with config.json + *.safetensors
  * (qwen3.rs:155-240, weights.rs:21-75). F16 and BF16 tensors. */
 mi_status mi_qwen3_load(mi_context* ctx, const char* directory, mi_qwen3** out);
 void mi_qwen3_destroy(mi_qwen3* m);
-mi_status mi_qwen3_config(const mi_qwen3* m, mi_qwen3_config* out);
+mi_status mi_qwen3_get_config(const mi_qwen3* m, mi_qwen3_config* out);
 /* Qwen3Model::set_attention_kind / set_fusion_options (qwen3.rs:330-346) */
 mi_status mi_qwen3_set_attention_kind(mi_qwen3* m, mi_attention_kind kind);
 mi_status mi_qwen3_set_fusion_options(mi_qwen3* m, mi_fusion_options options);
@@ -350,6 +350,16 @@ mi_status mi_qwen3_prefill_argmax(mi_qwen3* m, const uint32_t* tokens, size_t co
  * handle without waiting. */
 mi_status mi_qwen3_decode_argmax(mi_qwen3* m, const mi_tensor* token, mi_kv_cache* cache,
                                  mi_tensor* output, mi_tensor** logits, mi_pending** pending);
+/* The pipelined greedy decode loop of generate_greedy (qwen3.rs:475-555)
+ * and bench.rs run_pipelined_decode (bench.rs:1850-1895): enqueues `steps`
+ * decode steps, each feeding the previous step's argmax (kept on the
+ * device), without waiting. The cache must hold a prefilled prompt. Ids are
+ * read back with mi_kv_cache_tokens. */
+mi_status mi_qwen3_decode_steps(mi_qwen3* m, mi_kv_cache* cache, size_t steps);
+/* Copies cache positions [start, start + count) of the token ring (prompt
+ * ids, then the greedy ids fed back; position len holds the next id) to the
+ * host; synchronizes the context stream. */
+mi_status mi_kv_cache_tokens(mi_kv_cache* cache, size_t start, size_t count, uint32_t* out);
 /* Qwen3Model::generate (qwen3.rs:424-439): greedy, max_tokens ids. */
 mi_status mi_qwen3_generate(mi_qwen3* m, const uint32_t* prompt, size_t prompt_len,
                             size_t max_tokens, mi_kv_cache* cache, uint32_t* out_ids,
@@ -378,7 +388,7 @@ mi_status mi_qwen3_weight(mi_qwen3* m, int layer, int role, mi_tensor** out);
 /* The generator of mi_qwen3_create_random, on the device: element i of
  * stream (seed, stream) for i in [offset, offset + len). */
 mi_status mi_fill_normal_f16(mi_context* ctx, mi_tensor* t, uint64_t seed, uint64_t stream,
-                             uint64_t offset, float std_dev);
+                             uint64_t offset, double std_dev);
 mi_status mi_fill_tokens_u32(mi_context* ctx, mi_tensor* t, uint64_t seed, uint64_t stream,
                              uint32_t vocab);
 

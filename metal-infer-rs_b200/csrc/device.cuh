@@ -1,0 +1,118 @@
+// Device-side helpers shared by the kernels.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "kernels.h"
+#include "mi_internal.h"
+
+namespace mi {
+namespace k {
+
+// ---- programmatic dependent launch ------------------------------------------
+// Blocks until the predecessor grid has completed and its writes are visible
+// (a no-op when the kernel was launched without the PDL attribute).
+__device__ __forceinline__ void pdl_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+// Lets the dependent grid start launching (its CTAs then run their
+// independent prologue while this grid finishes).
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// Prefetch `bytes` (multiple of 16, 16-byte aligned) into L2.
+__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+// Streaming 16-byte load that does not allocate in L1.
+__device__ __forceinline__ uint4 ld_stream(const uint4* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Dot product of 8 halves packed in uint4 (FP32 accumulate, sequential).
+__device__ __forceinline__ float dot8(const uint4& a, const uint4& b, float acc) {
+  const __half2* x = reinterpret_cast<const __half2*>(&a);
+  const __half2* y = reinterpret_cast<const __half2*>(&b);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float2 fx = __half22float2(x[i]);
+    float2 fy = __half22float2(y[i]);
+    acc = fmaf(fx.x, fy.x, acc);
+    acc = fmaf(fx.y, fy.y, acc);
+  }
+  return acc;
+}
+
+// rsqrt(total / width + eps) as a correctly rounded 1 / sqrt.
+__device__ __forceinline__ float rms_scale(float total, int width, float eps) {
+  return __frcp_rn(__fsqrt_rn(__fadd_rn(__fdiv_rn(total, (float)width), eps)));
+}
+
+// x * scale * g with both products rounded (no contraction), as the
+// reference's `float(x) * scale * float(w)`.
+__device__ __forceinline__ float norm_mul(float x, float scale, float g) {
+  return __fmul_rn(__fmul_rn(x, scale), g);
+}
+
+// Greedy argmax key of argmax_better (transformer.metal:1396-1411): values
+// compare by the sign-flipped bit pattern, ties go to the larger index.
+__device__ __forceinline__ uint32_t argmax_key(float v) {
+  uint32_t b = __float_as_uint(v);
+  return (b & 0x80000000u) ? ~b : (b ^ 0x80000000u);
+}
+__device__ __forceinline__ bool argmax_better(uint32_t ck, uint32_t ci, uint32_t bk,
+                                              uint32_t bi) {
+  if (ci == 0xFFFFFFFFu) return false;
+  if (bi == 0xFFFFFFFFu) return true;
+  return ck > bk || (ck == bk && ci > bi);
+}
+
+__device__ __forceinline__ uint32_t pos_of(const Pos& p) {
+  return p.dev ? (*p.dev + p.base) : p.base;
+}
+
+}  // namespace k
+
+// Host launch helper: cudaLaunchKernelEx with the PDL attribute when asked.
+template <typename... KArgs, typename... Args>
+inline void launch_kernel(const k::Launch& l, dim3 grid, dim3 block, size_t smem,
+                          void (*kernel)(KArgs...), Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = l.stream;
+  cudaLaunchAttribute attr[1];
+  if (l.pdl) {
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+  cudaError_t err = cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+  if (err != cudaSuccess)
+    fail(MI_ERR_COMMAND, "kernel launch failed: %s", cudaGetErrorString(err));
+}
+
+}  // namespace mi

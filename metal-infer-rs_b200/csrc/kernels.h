@@ -1,0 +1,165 @@
+// Kernel launch interfaces shared by the op layer (ops.cu) and the Qwen3
+// forward plans (qwen3.cu). Every launcher takes a Launch describing the
+// stream and whether the launch may overlap its predecessor through
+// programmatic dependent launch (PDL): such kernels issue their
+// predecessor-independent loads (weights) first and block on
+// griddepcontrol.wait before touching activations.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace mi {
+namespace k {
+
+struct Launch {
+  cudaStream_t stream;
+  bool pdl = false;
+  int sm_count = 148;
+};
+
+// Position of a step: kernels read `*dev + base` when dev is non-null (decode
+// graphs keep the cache length on the device), else `base`.
+struct Pos {
+  const uint32_t* dev = nullptr;
+  uint32_t base = 0;
+};
+
+// ---- decode GEMV family (M = 1) -------------------------------------------
+enum GemvIn : int {
+  kInPlain = 0,    // x as given
+  kInNorm = 1,     // half(x * rsqrt(mean(x^2) + eps) * g)       (matvec3_rms)
+  kInAddNorm = 2,  // r = x + x2; half(half(r) * scale * g)       (matvec2_add_rms)
+  kInEmbedNorm = 3, // x = table[token] (0 for 0xFFFFFFFF), then kInNorm
+  kInAddThenNorm = 4 // r = half(x + x2) (half add); half(r * scale(r) * g)  (add_f16 + rms_norm_f16)
+};
+enum GemvOut : int {
+  kOutPlain = 0,     // out[s][row] = half(dot)
+  kOutResidual = 1,  // out0[row] = res[row] + half(dot)  (half add)
+  kOutSwiglu = 2,    // out0[i] = half(silu(g) * u), g/u = half dots of rows i of w0/w1
+  kOutArgmax = 3     // out0 = logits; greedy id of the logits -> token_out
+};
+
+struct GemvProblem {
+  const __half* w[3] = {nullptr, nullptr, nullptr};
+  int n[3] = {0, 0, 0};
+  int segments = 1;
+  int k = 0;
+  // prologue
+  int in_mode = kInPlain;
+  const __half* x = nullptr;
+  const __half* x2 = nullptr;
+  const __half* norm_w = nullptr;
+  float eps = 1e-6f;
+  __half* residual_out = nullptr;     // kInAddNorm (block 0 writes)
+  const uint32_t* token = nullptr;    // kInEmbedNorm: token = token[token_pos ? *token_pos : 0]
+  const uint32_t* token_pos = nullptr;
+  const __half* table = nullptr;      // kInEmbedNorm
+  uint32_t table_rows = 0;
+  __half* embed_out = nullptr;        // kInEmbedNorm: block 0 stores the embedded row
+  // epilogue
+  int out_mode = kOutPlain;
+  __half* out[3] = {nullptr, nullptr, nullptr};
+  const __half* res = nullptr;        // kOutResidual
+  uint32_t* token_out = nullptr;      // kOutArgmax: token_out[token_pos ? *token_pos + 1 : 0]
+  float* argmax_partial = nullptr;    // kOutArgmax: [grid] values
+  uint32_t* argmax_index = nullptr;   // kOutArgmax: [grid] indices
+  uint32_t* counter = nullptr;        // kOutArgmax: zero before, zero after
+  uint32_t* step_counter = nullptr;   // kOutArgmax: optional +1 of a decode state
+};
+// True when the fast kernel accepts the problem (K % 8 == 0, 16-byte
+// aligned pointers, K <= 16384); otherwise gemv() uses the generic kernel.
+bool gemv_fast_ok(const GemvProblem& p);
+void gemv(const Launch& l, const GemvProblem& p);
+// Plain tiled reference kernel (MatmulBackend::Reference), any shape, M rows.
+void matmul_reference(const Launch& l, const __half* x, const __half* w, __half* out, int m,
+                      int n, int k);
+// Prefill GEMM (M > 1): out[m, n] = x[m, :] . w[n, :], FP32 accumulate.
+void gemm(const Launch& l, const __half* x, const __half* w, __half* out, int m, int n, int k,
+          int ldo);
+
+// ---- row / elementwise kernels ---------------------------------------------
+void add(const Launch& l, const __half* a, const __half* b, __half* out, size_t n);
+void rms_norm(const Launch& l, const __half* x, const __half* w, __half* out, int rows,
+              int width, float eps);
+void add_rms_norm(const Launch& l, const __half* left, const __half* right, const __half* w,
+                  __half* residual, __half* normalized, int rows, int width, float eps);
+void swiglu(const Launch& l, const __half* gate, const __half* up, __half* out, size_t n);
+void embedding(const Launch& l, const uint32_t* tokens, const __half* table, __half* out,
+               int count, int width, uint32_t rows);
+void rope(const Launch& l, const __half* in, __half* out, int tokens, int heads, int head_dim,
+          Pos pos, float theta);
+// round_norm: round the normalized row to FP16 before RoPE (unfused path).
+void qk_norm_rope_cache(const Launch& l, const __half* q, const __half* k, const __half* qw,
+                        const __half* kw, __half* q_out, __half* key_cache, int tokens,
+                        int q_heads, int kv_heads, int head_dim, Pos pos, float theta,
+                        float eps, bool round_norm);
+void copy_kv(const Launch& l, const __half* src, __half* cache, int tokens, int stride, Pos pos);
+// Greedy argmax; partials sized by argmax_partials(n).
+int argmax_partials(size_t n);
+void argmax(const Launch& l, const __half* logits, size_t n, float* pv, uint32_t* pi,
+            uint32_t* out);
+
+// ---- attention ----------------------------------------------------------------
+struct AttnProblem {
+  const __half* q = nullptr;  // [tokens, qh, hd]
+  const __half* k = nullptr;  // [kv_len, kvh, hd]
+  const __half* v = nullptr;
+  __half* out = nullptr;      // [tokens, qh, hd]
+  int tokens = 1, qh = 1, kvh = 1, hd = 128;
+  int kv_len = 0;             // used when kv_len_dev is null
+  const uint32_t* kv_len_dev = nullptr;  // decode graphs: *kv_len_dev + kv_len_add
+  int kv_len_add = 0;
+  int causal = 1;
+  int query_offset = 0;       // ignored for decode-from-device (offset = len - 1)
+  int round_p = 1;            // prefill: round probabilities to FP16 (FlashPrefill)
+};
+// Two-pass reference semantics (attention_reference_f16), any head_dim.
+void attention_reference(const Launch& l, const AttnProblem& p);
+// Single-query split-K decode attention for any GQA ratio; partial states in
+// `scratch` (attention_decode_scratch bytes) and per-kv-head counters that
+// must be zero on entry (they are zero again on exit).
+size_t attention_decode_scratch(int kvh, int splits, int group, int hd);
+int attention_decode_splits(int kv_len_max, int kvh, int sm_count, int block_keys);
+void attention_decode(const Launch& l, const AttnProblem& p, int splits, int block_keys,
+                      float* scratch, uint32_t* counters);
+// Fused decode front end + attention for the model: per-head RMSNorm + RoPE
+// of the query and the new key, K/V append at position len-1, split-K
+// attention over the cache.
+struct DecodeFused {
+  const __half* q_raw = nullptr;  // [qh, hd]
+  const __half* k_raw = nullptr;  // [kvh, hd]
+  const __half* v_raw = nullptr;  // [kvh, hd]
+  const __half* q_norm = nullptr;
+  const __half* k_norm = nullptr;
+  float theta = 1e6f, eps = 1e-6f;
+  bool round_norm = false;
+  __half* key_cache = nullptr;    // [cap, kvh, hd]
+  __half* value_cache = nullptr;
+  __half* out = nullptr;          // [qh, hd]
+  int qh = 16, kvh = 8, hd = 128;
+  Pos pos;                        // position of the new token (= len - 1)
+};
+void attention_decode_fused(const Launch& l, const DecodeFused& p, int splits, float* scratch,
+                            uint32_t* counters);
+// Prefill attention in 32-key blocks, any GQA ratio, head_dim <= 256: with
+// round_p the flash-prefill semantics (FP16 probabilities), without it the
+// FP32 online softmax of the tiled kernel.
+void attention_prefill(const Launch& l, const AttnProblem& p);
+
+// ---- synthetic data ------------------------------------------------------------
+void fill_normal_f16(cudaStream_t s, __half* out, size_t n, uint64_t seed, uint64_t stream,
+                     uint64_t offset, double std_dev);
+// Fills a [rows, cols] block of a larger [*, full_cols] matrix whose element
+// (r, c) is generator index (row0 + r) * full_cols + col0 + c.
+void fill_normal_f16_block(cudaStream_t s, __half* out, size_t rows, size_t cols,
+                           size_t full_cols, size_t row0, size_t col0, uint64_t seed,
+                           uint64_t stream, double std_dev);
+void fill_tokens(cudaStream_t s, uint32_t* out, size_t n, uint64_t seed, uint64_t stream,
+                 uint32_t vocab);
+void fill_f16(cudaStream_t s, __half* out, size_t n, uint16_t bits);
+
+}  // namespace k
+}  // namespace mi

@@ -1,0 +1,1017 @@
+// Qwen3 model: weights, KV cache and the forward plans
+// (crates/metal-infer-models/src/qwen3.rs).
+//
+// Prefill (T > 1) follows forward_layer's unfused prefill path
+// (qwen3.rs:647-796): rms_norm -> Q/K/V GEMMs -> qk_norm_rope_cache ->
+// copy_into_cache -> attention -> O GEMM -> add_rms_norm -> gate/up GEMMs ->
+// swiglu -> down GEMM -> add.
+//
+// Decode (T = 1) runs five fused kernels per layer:
+//   1. RMSNorm + Q/K/V GEMV            (layer 0 also gathers the embedding)
+//   2. QK-norm + RoPE + K/V append + split-K attention + merge
+//   3. O GEMV
+//   4. residual add + RMSNorm + gate/up GEMV + SwiGLU
+//   5. down GEMV + residual add
+// and one final RMSNorm + LM-head GEMV + greedy argmax. The cache keeps its
+// length and a token ring on the device (toks[pos] is the token at cache
+// position pos), so one captured CUDA graph serves every decode step: the
+// step reads toks[len], writes its argmax to toks[len + 1] and increments
+// len. Kernels after the first are launched with programmatic dependent
+// launch so each one streams its weights while its predecessor finishes.
+
+#include <cstring>
+#include <map>
+#include <memory>
+
+#include "kernels.h"
+#include "mi_internal.h"
+
+using namespace mi;
+
+namespace {
+
+enum Role {
+  kEmbedding = 0,
+  kQ = 1,
+  kK = 2,
+  kV = 3,
+  kO = 4,
+  kQNorm = 5,
+  kKNorm = 6,
+  kGate = 7,
+  kUp = 8,
+  kDown = 9,
+  kInputNorm = 10,
+  kPostNorm = 11,
+  kFinalNorm = 12,
+  kLmHead = 13,
+};
+
+struct TensorRef {
+  mi_tensor* t = nullptr;
+  TensorRef() = default;
+  explicit TensorRef(mi_tensor* x) : t(x) {}
+  TensorRef(const TensorRef&) = delete;
+  TensorRef& operator=(const TensorRef&) = delete;
+  TensorRef(TensorRef&& o) noexcept : t(o.t) { o.t = nullptr; }
+  TensorRef& operator=(TensorRef&& o) noexcept {
+    if (this != &o) {
+      reset();
+      t = o.t;
+      o.t = nullptr;
+    }
+    return *this;
+  }
+  ~TensorRef() { reset(); }
+  void reset() {
+    if (t) mi_tensor_release(t);
+    t = nullptr;
+  }
+  __half* h() const { return t->f16(); }
+};
+
+struct Layer {
+  TensorRef w[16];
+};
+
+// Decode workspace, sized once per model.
+struct Workspace {
+  TensorRef q_raw, k_raw, v_raw, attn, attn_o, residual, hidden, act, logits;
+  TensorRef argmax_pv, argmax_pi, counters, attn_scratch;
+  int attn_splits = 0;
+  size_t attn_cap = 0;
+};
+
+}  // namespace
+
+struct mi_kv_cache;
+
+struct mi_qwen3 {
+  mi_context* ctx = nullptr;
+  mi_qwen3_config cfg{};
+  TensorRef embedding, final_norm, lm_head_own;
+  const mi_tensor* lm_head = nullptr;
+  std::vector<Layer> layers;
+  mi_attention_kind attention_kind = MI_ATTENTION_TILED;
+  mi_fusion_options fusion{1, 1, 1, 1};
+  bool graphs = true;
+  Workspace ws;
+  uint64_t plan_version = 1;  // bumps invalidate captured graphs
+};
+
+struct mi_kv_cache {
+  mi_qwen3* model = nullptr;
+  size_t capacity = 0;
+  size_t filled = 0;
+  std::vector<TensorRef> key, value;
+  TensorRef toks;     // u32 [capacity + 1]
+  TensorRef dev_len;  // u32 [1]
+  cudaGraphExec_t graph = nullptr;
+  uint64_t graph_version = 0;
+  ~mi_kv_cache() {
+    if (graph) cudaGraphExecDestroy(graph);
+  }
+};
+
+namespace {
+
+void require(const void* p, const char* what) {
+  MI_REQUIRE(p != nullptr, MI_ERR_INVALID_ARGUMENT, "%s is NULL", what);
+}
+
+// Qwen3Config::validate (config.rs:23-57)
+void validate_config(const mi_qwen3_config& c) {
+  if (!c.hidden_size || !c.intermediate_size || !c.num_hidden_layers || !c.num_attention_heads ||
+      !c.num_key_value_heads || !c.head_dim || !c.vocab_size || c.head_dim % 2)
+    fail(MI_ERR_CONFIG,
+         "invalid model configuration: model dimensions must be non-zero and head_dim even");
+  if (c.num_attention_heads % c.num_key_value_heads)
+    fail(MI_ERR_CONFIG,
+         "invalid model configuration: num_attention_heads must be divisible by "
+         "num_key_value_heads");
+}
+
+k::Launch launch(mi_qwen3* m, bool pdl) {
+  k::Launch l;
+  l.stream = m->ctx->stream;
+  l.pdl = pdl;
+  l.sm_count = m->ctx->sm_count;
+  return l;
+}
+
+// Decode launches: PDL unless per-kernel profiling is on (events between
+// launches would serialise them anyway).
+k::Launch dlaunch(mi_qwen3* m, bool pdl) { return launch(m, pdl && !m->ctx->profiling); }
+
+size_t qwidth(const mi_qwen3_config& c) { return c.num_attention_heads * c.head_dim; }
+size_t kvwidth(const mi_qwen3_config& c) { return c.num_key_value_heads * c.head_dim; }
+
+bool fused_decode_supported(const mi_qwen3* m) {
+  const auto& c = m->cfg;
+  size_t g = c.num_attention_heads / c.num_key_value_heads;
+  return c.head_dim == 128 && (g == 1 || g == 2 || g == 4 || g == 8) &&
+         m->attention_kind != MI_ATTENTION_REFERENCE && c.hidden_size % 8 == 0 &&
+         c.intermediate_size % 8 == 0 && c.hidden_size <= 16384 && c.intermediate_size <= 16384;
+}
+
+void ensure_workspace(mi_qwen3* m, size_t capacity) {
+  auto& w = m->ws;
+  const auto& c = m->cfg;
+  mi_context* ctx = m->ctx;
+  if (!w.q_raw.t) {
+    w.q_raw = TensorRef(new_tensor(ctx, {qwidth(c)}, MI_F16, true));
+    w.k_raw = TensorRef(new_tensor(ctx, {kvwidth(c)}, MI_F16, true));
+    w.v_raw = TensorRef(new_tensor(ctx, {kvwidth(c)}, MI_F16, true));
+    w.attn = TensorRef(new_tensor(ctx, {qwidth(c)}, MI_F16, true));
+    w.attn_o = TensorRef(new_tensor(ctx, {c.hidden_size}, MI_F16, true));
+    w.residual = TensorRef(new_tensor(ctx, {c.hidden_size}, MI_F16, true));
+    w.hidden = TensorRef(new_tensor(ctx, {c.hidden_size}, MI_F16, true));
+    w.act = TensorRef(new_tensor(ctx, {c.intermediate_size}, MI_F16, true));
+    w.logits = TensorRef(new_tensor(ctx, {1, c.vocab_size}, MI_F16, true));
+    size_t parts = (size_t)ctx->sm_count * 4;
+    w.argmax_pv = TensorRef(new_tensor(ctx, {parts}, MI_F32, true));
+    w.argmax_pi = TensorRef(new_tensor(ctx, {parts}, MI_U32, true));
+    w.counters = TensorRef(new_tensor(ctx, {1 + c.num_key_value_heads}, MI_U32, true));
+  }
+  if (capacity > w.attn_cap) {
+    int kvh = (int)c.num_key_value_heads;
+    int splits = k::attention_decode_splits((int)capacity, kvh, ctx->sm_count, 32);
+    int group = (int)(c.num_attention_heads / c.num_key_value_heads);
+    size_t bytes = k::attention_decode_scratch(kvh, splits, group, (int)c.head_dim);
+    w.attn_scratch = TensorRef(new_tensor(ctx, {bytes / 4}, MI_F32, true));
+    w.attn_splits = splits;
+    w.attn_cap = capacity;
+    m->plan_version++;
+  }
+}
+
+// Sets the device-side cache length (stream-ordered).
+__global__ void set_u32_kernel(uint32_t* p, uint32_t v) { *p = v; }
+
+void set_dev_len(mi_kv_cache* c, size_t v) {
+  set_u32_kernel<<<1, 1, 0, c->model->ctx->stream>>>(c->dev_len.t->u32(), (uint32_t)v);
+  MI_CUDA(cudaGetLastError());
+}
+
+// ---- decode step ------------------------------------------------------------
+void encode_decode_step(mi_qwen3* m, mi_kv_cache* c) {
+  const auto& cfg = m->cfg;
+  auto& w = m->ws;
+  const int h = (int)cfg.hidden_size, I = (int)cfg.intermediate_size;
+  const int qw = (int)qwidth(cfg), kw = (int)kvwidth(cfg);
+  uint32_t* len = c->dev_len.t->u32();
+  for (size_t li = 0; li < m->layers.size(); ++li) {
+    const Layer& L = m->layers[li];
+    // 1. (embedding +) RMSNorm + QKV
+    {
+      k::GemvProblem p;
+      p.k = h;
+      p.segments = 3;
+      p.w[0] = L.w[kQ].h();
+      p.w[1] = L.w[kK].h();
+      p.w[2] = L.w[kV].h();
+      p.n[0] = qw;
+      p.n[1] = kw;
+      p.n[2] = kw;
+      p.out[0] = w.q_raw.h();
+      p.out[1] = w.k_raw.h();
+      p.out[2] = w.v_raw.h();
+      p.norm_w = L.w[kInputNorm].h();
+      p.eps = cfg.rms_norm_eps;
+      if (li == 0) {
+        p.in_mode = k::kInEmbedNorm;
+        p.token = c->toks.t->u32();
+        p.token_pos = len;
+        p.table = m->embedding.h();
+        p.table_rows = (uint32_t)cfg.vocab_size;
+        p.embed_out = w.hidden.h();
+      } else {
+        p.in_mode = k::kInNorm;
+        p.x = w.hidden.h();
+      }
+      ProfileScope ps(m->ctx, "qkv_gemv");
+      k::gemv(dlaunch(m, li != 0), p);
+    }
+    // 2. QK-norm + RoPE + KV append + attention
+    {
+      k::DecodeFused d;
+      d.q_raw = w.q_raw.h();
+      d.k_raw = w.k_raw.h();
+      d.v_raw = w.v_raw.h();
+      d.q_norm = L.w[kQNorm].h();
+      d.k_norm = L.w[kKNorm].h();
+      d.theta = cfg.rope_theta;
+      d.eps = cfg.rms_norm_eps;
+      d.round_norm = !m->fusion.qk_rope_cache;
+      d.key_cache = c->key[li].h();
+      d.value_cache = c->value[li].h();
+      d.out = w.attn.h();
+      d.qh = (int)cfg.num_attention_heads;
+      d.kvh = (int)cfg.num_key_value_heads;
+      d.hd = (int)cfg.head_dim;
+      d.pos.dev = len;
+      ProfileScope ps(m->ctx, "attention_decode");
+      k::attention_decode_fused(dlaunch(m, true), d, w.attn_splits, w.attn_scratch.t->f32(),
+                                w.counters.t->u32() + 1);
+    }
+    // 3. O projection
+    {
+      k::GemvProblem p;
+      p.k = qw;
+      p.x = w.attn.h();
+      p.w[0] = L.w[kO].h();
+      p.n[0] = h;
+      p.out[0] = w.attn_o.h();
+      ProfileScope ps(m->ctx, "o_gemv");
+      k::gemv(dlaunch(m, true), p);
+    }
+    // 4. residual + RMSNorm + gate/up + SwiGLU
+    {
+      k::GemvProblem p;
+      p.k = h;
+      p.segments = 2;
+      p.in_mode = m->fusion.add_rms_norm ? k::kInAddNorm : k::kInAddThenNorm;
+      p.x = w.hidden.h();
+      p.x2 = w.attn_o.h();
+      p.norm_w = L.w[kPostNorm].h();
+      p.eps = cfg.rms_norm_eps;
+      p.residual_out = w.residual.h();
+      p.w[0] = L.w[kGate].h();
+      p.w[1] = L.w[kUp].h();
+      p.n[0] = I;
+      p.n[1] = I;
+      p.out_mode = k::kOutSwiglu;
+      p.out[0] = w.act.h();
+      ProfileScope ps(m->ctx, "gate_up_gemv");
+      k::gemv(dlaunch(m, true), p);
+    }
+    // 5. down + residual
+    {
+      k::GemvProblem p;
+      p.k = I;
+      p.x = w.act.h();
+      p.w[0] = L.w[kDown].h();
+      p.n[0] = h;
+      p.out_mode = k::kOutResidual;
+      p.res = w.residual.h();
+      p.out[0] = w.hidden.h();
+      ProfileScope ps(m->ctx, "down_gemv");
+      k::gemv(dlaunch(m, true), p);
+    }
+  }
+  // final norm + LM head + argmax; advances the device length.
+  {
+    k::GemvProblem p;
+    p.k = h;
+    p.in_mode = k::kInNorm;
+    p.x = w.hidden.h();
+    p.norm_w = m->final_norm.h();
+    p.eps = cfg.rms_norm_eps;
+    p.w[0] = m->lm_head->f16();
+    p.n[0] = (int)cfg.vocab_size;
+    p.out_mode = k::kOutArgmax;
+    p.out[0] = w.logits.h();
+    p.token_out = c->toks.t->u32();
+    p.token_pos = len;
+    p.argmax_partial = w.argmax_pv.t->f32();
+    p.argmax_index = w.argmax_pi.t->u32();
+    p.counter = w.counters.t->u32();
+    p.step_counter = len;
+    ProfileScope ps(m->ctx, "lm_head_argmax");
+    k::gemv(dlaunch(m, true), p);
+  }
+}
+
+// Runs (or replays) one decode step at the cache's device position.
+void run_decode_step(mi_qwen3* m, mi_kv_cache* c) {
+  mi_context* ctx = m->ctx;
+  if (!m->graphs || ctx->profiling) {
+    encode_decode_step(m, c);
+    return;
+  }
+  if (!c->graph || c->graph_version != m->plan_version) {
+    if (c->graph) {
+      cudaGraphExecDestroy(c->graph);
+      c->graph = nullptr;
+    }
+    cudaGraph_t g = nullptr;
+    MI_CUDA(cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal));
+    try {
+      encode_decode_step(m, c);
+    } catch (...) {
+      cudaStreamEndCapture(ctx->stream, &g);
+      if (g) cudaGraphDestroy(g);
+      throw;
+    }
+    MI_CUDA(cudaStreamEndCapture(ctx->stream, &g));
+    cudaError_t err = cudaGraphInstantiate(&c->graph, g, 0);
+    cudaGraphDestroy(g);
+    if (err != cudaSuccess) {
+      c->graph = nullptr;
+      fail(MI_ERR_COMMAND, "graph instantiation failed: %s", cudaGetErrorString(err));
+    }
+    c->graph_version = m->plan_version;
+  }
+  MI_CUDA(cudaGraphLaunch(c->graph, ctx->stream));
+}
+
+// ---- prefill / eager forward ---------------------------------------------------
+struct Scratch {
+  std::vector<TensorRef> owned;
+  mi_context* ctx;
+  explicit Scratch(mi_context* c) : ctx(c) {}
+  __half* f16(std::vector<size_t> shape) {
+    owned.emplace_back(new_tensor(ctx, shape, MI_F16));
+    return owned.back().h();
+  }
+};
+
+mi_attention_kind prefill_kind(mi_attention_kind configured, size_t tokens) {
+  // attention_kind_for_tokens (qwen3.rs:799-822) for tokens > 1
+  switch (configured) {
+    case MI_ATTENTION_TILED:
+      return tokens >= 32 ? MI_ATTENTION_FLASH_PREFILL : MI_ATTENTION_TILED;
+    case MI_ATTENTION_DECODE_SPLIT_KV:
+    case MI_ATTENTION_FLASH_DECODE:
+      return MI_ATTENTION_TILED;
+    default:
+      return configured;
+  }
+}
+
+// One layer on hidden [T, h] at cache offset `off` (prefill semantics).
+void layer_prefill(mi_qwen3* m, mi_kv_cache* c, size_t li, __half* hidden, size_t T, size_t off,
+                   Scratch& s) {
+  const auto& cfg = m->cfg;
+  const Layer& L = m->layers[li];
+  k::Launch l = launch(m, false);
+  const int h = (int)cfg.hidden_size, I = (int)cfg.intermediate_size;
+  const int qw = (int)qwidth(cfg), kw = (int)kvwidth(cfg);
+  const int t = (int)T;
+  const float eps = cfg.rms_norm_eps;
+  __half* normalized = s.f16({T, (size_t)h});
+  __half* q = s.f16({T, (size_t)qw});
+  __half* kk = s.f16({T, (size_t)kw});
+  __half* v = s.f16({T, (size_t)kw});
+  k::rms_norm(l, hidden, L.w[kInputNorm].h(), normalized, t, h, eps);
+  k::gemm(l, normalized, L.w[kQ].h(), q, t, qw, h, qw);
+  k::gemm(l, normalized, L.w[kK].h(), kk, t, kw, h, kw);
+  k::gemm(l, normalized, L.w[kV].h(), v, t, kw, h, kw);
+  __half* query = s.f16({T, (size_t)qw});
+  k::Pos pos;
+  pos.base = (uint32_t)off;
+  k::qk_norm_rope_cache(l, q, kk, L.w[kQNorm].h(), L.w[kKNorm].h(), query, c->key[li].h(), t,
+                        (int)cfg.num_attention_heads, (int)cfg.num_key_value_heads,
+                        (int)cfg.head_dim, pos, cfg.rope_theta, eps, !m->fusion.qk_rope_cache);
+  k::copy_kv(l, v, c->value[li].h(), t, kw, pos);
+  __half* attn = s.f16({T, (size_t)qw});
+  k::AttnProblem a;
+  a.q = query;
+  a.k = c->key[li].h();
+  a.v = c->value[li].h();
+  a.out = attn;
+  a.tokens = t;
+  a.qh = (int)cfg.num_attention_heads;
+  a.kvh = (int)cfg.num_key_value_heads;
+  a.hd = (int)cfg.head_dim;
+  a.kv_len = (int)(off + T);
+  a.causal = 1;
+  a.query_offset = (int)off;
+  mi_attention_kind kind = T == 1 ? MI_ATTENTION_DECODE_SPLIT_KV
+                                  : prefill_kind(m->attention_kind, T);
+  if (m->attention_kind == MI_ATTENTION_REFERENCE) kind = MI_ATTENTION_REFERENCE;
+  if (kind == MI_ATTENTION_REFERENCE) {
+    k::attention_reference(l, a);
+  } else if (kind == MI_ATTENTION_DECODE_SPLIT_KV) {
+    auto& w = m->ws;
+    k::attention_decode(l, a, w.attn_splits, 32, w.attn_scratch.t->f32(), w.counters.t->u32() + 1);
+  } else {
+    a.round_p = kind == MI_ATTENTION_FLASH_PREFILL ? 1 : 0;
+    k::attention_prefill(l, a);
+  }
+  __half* attn_o = s.f16({T, (size_t)h});
+  k::gemm(l, attn, L.w[kO].h(), attn_o, t, h, qw, h);
+  __half* residual = s.f16({T, (size_t)h});
+  if (m->fusion.add_rms_norm) {
+    k::add_rms_norm(l, hidden, attn_o, L.w[kPostNorm].h(), residual, normalized, t, h, eps);
+  } else {
+    k::add(l, hidden, attn_o, residual, T * h);
+    k::rms_norm(l, residual, L.w[kPostNorm].h(), normalized, t, h, eps);
+  }
+  __half* gate = s.f16({T, (size_t)I});
+  __half* up = s.f16({T, (size_t)I});
+  k::gemm(l, normalized, L.w[kGate].h(), gate, t, I, h, I);
+  k::gemm(l, normalized, L.w[kUp].h(), up, t, I, h, I);
+  __half* act = s.f16({T, (size_t)I});
+  k::swiglu(l, gate, up, act, T * I);
+  __half* down = s.f16({T, (size_t)h});
+  k::gemm(l, act, L.w[kDown].h(), down, t, h, I, h);
+  k::add(l, residual, down, hidden, T * h);
+}
+
+void check_capacity(mi_kv_cache* c, size_t count) {
+  size_t requested = c->filled + count;
+  if (requested > c->capacity)
+    fail(MI_ERR_CACHE_CAPACITY, "KV cache capacity %zu exceeded by requested length %zu",
+         c->capacity, requested);
+}
+
+// Forward of T >= 1 tokens already in toks[filled .. filled + T): logits of
+// the last row into ws.logits, greedy id into toks[filled + T], length
+// advanced on host and device.
+void forward_tokens(mi_qwen3* m, mi_kv_cache* c, size_t T) {
+  const auto& cfg = m->cfg;
+  ensure_workspace(m, c->capacity);
+  size_t off = c->filled;
+  if (T == 1 && fused_decode_supported(m)) {
+    run_decode_step(m, c);
+    c->filled += 1;
+    return;
+  }
+  Scratch s(m->ctx);
+  k::Launch l = launch(m, false);
+  const int h = (int)cfg.hidden_size;
+  __half* hidden = s.f16({T, (size_t)h});
+  k::embedding(l, c->toks.t->u32() + off, m->embedding.h(), hidden, (int)T, h,
+               (uint32_t)cfg.vocab_size);
+  for (size_t li = 0; li < m->layers.size(); ++li) layer_prefill(m, c, li, hidden, T, off, s);
+  auto& w = m->ws;
+  k::GemvProblem p;
+  p.k = h;
+  p.in_mode = k::kInNorm;
+  p.x = hidden + (T - 1) * h;
+  p.norm_w = m->final_norm.h();
+  p.eps = cfg.rms_norm_eps;
+  p.w[0] = m->lm_head->f16();
+  p.n[0] = (int)cfg.vocab_size;
+  p.out_mode = k::kOutArgmax;
+  p.out[0] = w.logits.h();
+  p.token_out = c->toks.t->u32() + off + T;
+  p.argmax_partial = w.argmax_pv.t->f32();
+  p.argmax_index = w.argmax_pi.t->u32();
+  p.counter = w.counters.t->u32();
+  k::gemv(l, p);
+  c->filled = off + T;
+  set_dev_len(c, c->filled);
+}
+
+void upload_tokens(mi_kv_cache* c, const uint32_t* tokens, size_t count, size_t at) {
+  MI_CUDA(cudaMemcpyAsync(c->toks.t->u32() + at, tokens, count * 4, cudaMemcpyHostToDevice,
+                          c->model->ctx->stream));
+}
+
+mi_tensor* copy_logits(mi_qwen3* m) {
+  mi_tensor* out = new_tensor(m->ctx, {1, m->cfg.vocab_size}, MI_F16);
+  MI_CUDA(cudaMemcpyAsync(out->base(), m->ws.logits.t->base(), out->bytes(),
+                          cudaMemcpyDeviceToDevice, m->ctx->stream));
+  return out;
+}
+
+struct Timer {
+  cudaEvent_t a = nullptr, b = nullptr;
+  std::chrono::steady_clock::time_point w;
+  cudaStream_t s;
+  explicit Timer(cudaStream_t st) : s(st) {
+    cudaEventCreate(&a);
+    cudaEventCreate(&b);
+    cudaEventRecord(a, s);
+    w = std::chrono::steady_clock::now();
+  }
+  void finish(mi_dispatch_stats* st) {
+    cudaEventRecord(b, s);
+    cudaError_t err = cudaEventSynchronize(b);
+    float ms = 0;
+    cudaEventElapsedTime(&ms, a, b);
+    if (err != cudaSuccess) fail(MI_ERR_COMMAND, "command failed: %s", cudaGetErrorString(err));
+    if (st) {
+      st->gpu_time = ms * 1e-3;
+      st->wall_time =
+          std::chrono::duration<double>(std::chrono::steady_clock::now() - w).count();
+    }
+  }
+  ~Timer() {
+    cudaEventDestroy(a);
+    cudaEventDestroy(b);
+  }
+};
+
+void check_cache(mi_qwen3* m, mi_kv_cache* c) {
+  require(m, "model");
+  require(c, "cache");
+  if (c->model != m)
+    fail(MI_ERR_CONFIG, "invalid model configuration: KV cache layer count differs from model");
+}
+
+}  // namespace
+
+extern "C" {
+
+mi_status mi_qwen3_config_validate(const mi_qwen3_config* config) {
+  return guard([&] {
+    require(config, "config");
+    validate_config(*config);
+  });
+}
+
+mi_status mi_qwen3_create_random(mi_context* ctx, const mi_qwen3_config* config, uint64_t seed,
+                                 double std_dev, mi_qwen3** out) {
+  return guard([&] {
+    require(ctx, "ctx");
+    require(config, "config");
+    require(out, "out");
+    validate_config(*config);
+    auto m = std::make_unique<mi_qwen3>();
+    m->ctx = ctx;
+    m->cfg = *config;
+    const auto& c = m->cfg;
+    size_t h = c.hidden_size, hd = c.head_dim, qw = qwidth(c), kw = kvwidth(c),
+           I = c.intermediate_size, V = c.vocab_size;
+    cudaStream_t st = ctx->stream;
+    auto matrix = [&](int layer, int role, size_t rows, size_t cols) {
+      TensorRef t(new_tensor(ctx, {rows, cols}, MI_F16));
+      k::fill_normal_f16(st, t.h(), rows * cols, seed, (uint64_t)((layer + 1) * 16 + role), 0,
+                         std_dev);
+      return t;
+    };
+    auto ones = [&](size_t n) {
+      TensorRef t(new_tensor(ctx, {n}, MI_F16));
+      k::fill_f16(st, t.h(), n, 0x3c00);
+      return t;
+    };
+    m->embedding = matrix(-1, kEmbedding, V, h);
+    m->final_norm = ones(h);
+    if (c.tie_word_embeddings) {
+      m->lm_head = m->embedding.t;
+    } else {
+      m->lm_head_own = matrix(-1, kLmHead, V, h);
+      m->lm_head = m->lm_head_own.t;
+    }
+    m->layers.resize(c.num_hidden_layers);
+    for (size_t l = 0; l < c.num_hidden_layers; ++l) {
+      Layer& L = m->layers[l];
+      int li = (int)l;
+      L.w[kQ] = matrix(li, kQ, qw, h);
+      L.w[kK] = matrix(li, kK, kw, h);
+      L.w[kV] = matrix(li, kV, kw, h);
+      L.w[kO] = matrix(li, kO, h, qw);
+      L.w[kQNorm] = ones(hd);
+      L.w[kKNorm] = ones(hd);
+      L.w[kGate] = matrix(li, kGate, I, h);
+      L.w[kUp] = matrix(li, kUp, I, h);
+      L.w[kDown] = matrix(li, kDown, h, I);
+      L.w[kInputNorm] = ones(h);
+      L.w[kPostNorm] = ones(h);
+    }
+    sync_context(ctx);
+    *out = m.release();
+  });
+}
+
+void mi_qwen3_destroy(mi_qwen3* m) {
+  if (!m) return;
+  cudaStreamSynchronize(m->ctx->stream);
+  delete m;
+}
+
+mi_status mi_qwen3_get_config(const mi_qwen3* m, mi_qwen3_config* out) {
+  return guard([&] {
+    require(m, "model");
+    require(out, "out");
+    *out = m->cfg;
+  });
+}
+
+mi_status mi_qwen3_set_attention_kind(mi_qwen3* m, mi_attention_kind kind) {
+  return guard([&] {
+    require(m, "model");
+    MI_REQUIRE(kind >= MI_ATTENTION_REFERENCE && kind <= MI_ATTENTION_FLASH_DECODE,
+               MI_ERR_INVALID_ARGUMENT, "unknown attention kind %d", (int)kind);
+    m->attention_kind = kind;
+    m->plan_version++;
+  });
+}
+
+mi_status mi_qwen3_set_fusion_options(mi_qwen3* m, mi_fusion_options options) {
+  return guard([&] {
+    require(m, "model");
+    m->fusion = options;
+    m->plan_version++;
+  });
+}
+
+mi_fusion_options mi_qwen3_fusion_options(const mi_qwen3* m) {
+  return m ? m->fusion : mi_fusion_options{1, 1, 1, 1};
+}
+
+mi_status mi_qwen3_set_decode_graphs(mi_qwen3* m, int enabled) {
+  return guard([&] {
+    require(m, "model");
+    m->graphs = enabled != 0;
+  });
+}
+
+mi_status mi_kv_cache_create(mi_qwen3* m, size_t capacity, mi_kv_cache** out) {
+  return guard([&] {
+    require(m, "model");
+    require(out, "out");
+    if (capacity == 0)
+      fail(MI_ERR_CONFIG, "invalid model configuration: KV cache capacity must be non-zero");
+    MI_REQUIRE(capacity < 0x7FFFFFFF, MI_ERR_CONFIG, "KV cache capacity too large");
+    auto c = std::make_unique<mi_kv_cache>();
+    c->model = m;
+    c->capacity = capacity;
+    size_t kvh = m->cfg.num_key_value_heads, hd = m->cfg.head_dim;
+    for (size_t l = 0; l < m->cfg.num_hidden_layers; ++l) {
+      c->key.emplace_back(new_tensor(m->ctx, {capacity, kvh, hd}, MI_F16, true));
+      c->value.emplace_back(new_tensor(m->ctx, {capacity, kvh, hd}, MI_F16, true));
+    }
+    c->toks = TensorRef(new_tensor(m->ctx, {capacity + 1}, MI_U32, true));
+    c->dev_len = TensorRef(new_tensor(m->ctx, {1}, MI_U32, true));
+    ensure_workspace(m, capacity);
+    sync_context(m->ctx);
+    *out = c.release();
+  });
+}
+
+void mi_kv_cache_destroy(mi_kv_cache* c) {
+  if (!c) return;
+  cudaStreamSynchronize(c->model->ctx->stream);
+  delete c;
+}
+
+size_t mi_kv_cache_len(const mi_kv_cache* c) { return c ? c->filled : 0; }
+size_t mi_kv_cache_capacity(const mi_kv_cache* c) { return c ? c->capacity : 0; }
+
+void mi_kv_cache_reset(mi_kv_cache* c) {
+  if (!c) return;
+  c->filled = 0;
+  try {
+    set_dev_len(c, 0);
+  } catch (...) {
+  }
+}
+
+mi_status mi_kv_cache_layer(mi_kv_cache* c, size_t layer, mi_tensor** key, mi_tensor** value) {
+  return guard([&] {
+    require(c, "cache");
+    MI_REQUIRE(layer < c->key.size(), MI_ERR_INVALID_ARGUMENT, "layer %zu out of range", layer);
+    if (key) *key = view(c->key[layer].t, c->key[layer].t->shape, 0);
+    if (value) *value = view(c->value[layer].t, c->value[layer].t->shape, 0);
+  });
+}
+
+// prefill_with_stats (qwen3.rs:356-373)
+mi_status mi_qwen3_prefill(mi_qwen3* m, const uint32_t* tokens, size_t count, mi_kv_cache* cache,
+                           mi_tensor** logits, mi_dispatch_stats* stats) {
+  return guard([&] {
+    check_cache(m, cache);
+    if (count == 0) fail(MI_ERR_CONFIG, "invalid model configuration: prefill requires at least one token");
+    require(tokens, "tokens");
+    cache->filled = 0;
+    check_capacity(cache, count);
+    Timer t(m->ctx->stream);
+    upload_tokens(cache, tokens, count, 0);
+    try {
+      forward_tokens(m, cache, count);
+      t.finish(stats);
+    } catch (...) {
+      cache->filled = 0;
+      throw;
+    }
+    if (logits) *logits = copy_logits(m);
+  });
+}
+
+// decode_with_stats (qwen3.rs:375-386)
+mi_status mi_qwen3_decode(mi_qwen3* m, uint32_t token, mi_kv_cache* cache, mi_tensor** logits,
+                          mi_dispatch_stats* stats) {
+  return guard([&] {
+    check_cache(m, cache);
+    check_capacity(cache, 1);
+    size_t previous = cache->filled;
+    Timer t(m->ctx->stream);
+    uint32_t tok = token;
+    upload_tokens(cache, &tok, 1, previous);
+    try {
+      forward_tokens(m, cache, 1);
+      t.finish(stats);
+    } catch (...) {
+      cache->filled = previous;
+      set_dev_len(cache, previous);
+      throw;
+    }
+    if (logits) *logits = copy_logits(m);
+  });
+}
+
+// prefill_argmax (qwen3.rs:388-410)
+mi_status mi_qwen3_prefill_argmax(mi_qwen3* m, const uint32_t* tokens, size_t count,
+                                  mi_kv_cache* cache, mi_tensor* output, mi_tensor** logits,
+                                  mi_dispatch_stats* stats) {
+  return guard([&] {
+    check_cache(m, cache);
+    if (count == 0) fail(MI_ERR_CONFIG, "invalid model configuration: prefill requires at least one token");
+    require(tokens, "tokens");
+    require(output, "output");
+    if (output->dtype != MI_U32 || output->len() != 1)
+      fail(MI_ERR_CONFIG, "invalid model configuration: argmax output must be one u32");
+    cache->filled = 0;
+    check_capacity(cache, count);
+    Timer t(m->ctx->stream);
+    upload_tokens(cache, tokens, count, 0);
+    try {
+      forward_tokens(m, cache, count);
+      MI_CUDA(cudaMemcpyAsync(output->base(), cache->toks.t->u32() + count, 4,
+                              cudaMemcpyDeviceToDevice, m->ctx->stream));
+      t.finish(stats);
+    } catch (...) {
+      cache->filled = 0;
+      throw;
+    }
+    if (logits) *logits = copy_logits(m);
+  });
+}
+
+// decode_argmax (qwen3.rs:412-422)
+mi_status mi_qwen3_decode_argmax(mi_qwen3* m, const mi_tensor* token, mi_kv_cache* cache,
+                                 mi_tensor* output, mi_tensor** logits, mi_pending** pending) {
+  return guard([&] {
+    check_cache(m, cache);
+    require(token, "token");
+    require(output, "output");
+    require(pending, "pending");
+    if (token->shape != std::vector<size_t>{1} || token->dtype != MI_U32)
+      fail(MI_ERR_CONFIG, "invalid model configuration: decode token must be one u32");
+    if (output->dtype != MI_U32 || output->len() != 1)
+      fail(MI_ERR_CONFIG, "invalid model configuration: argmax output must be one u32");
+    check_capacity(cache, 1);
+    mi_batch* b = nullptr;
+    mi_status s = mi_context_begin_batch(m->ctx, &b);
+    if (s != MI_OK) fail(s, "%s", mi_last_error_message());
+    size_t previous = cache->filled;
+    try {
+      MI_CUDA(cudaMemcpyAsync(cache->toks.t->u32() + previous, token->base(), 4,
+                              cudaMemcpyDeviceToDevice, m->ctx->stream));
+      forward_tokens(m, cache, 1);
+      MI_CUDA(cudaMemcpyAsync(output->base(), cache->toks.t->u32() + previous + 1, 4,
+                              cudaMemcpyDeviceToDevice, m->ctx->stream));
+      if (logits) *logits = copy_logits(m);
+    } catch (...) {
+      mi_batch_abandon(b);
+      cache->filled = previous;
+      throw;
+    }
+    s = mi_batch_commit(b, pending);
+    if (s != MI_OK) fail(s, "%s", mi_last_error_message());
+  });
+}
+
+}  // extern "C"
+
+namespace {
+
+// generate_greedy (qwen3.rs:475-555): prefill, then decode steps enqueued
+// back to back on the device. Without stop tokens or a callback all steps are
+// launched before the single readback; otherwise steps are checked in chunks
+// and the cache length is rolled back past a stop.
+size_t generate_greedy(mi_qwen3* m, mi_kv_cache* c, const uint32_t* prompt, size_t prompt_len,
+                       size_t max_tokens, const uint32_t* stops, size_t nstops,
+                       mi_token_callback cb, void* user, uint32_t* out_ids, size_t capacity) {
+  if (max_tokens == 0) return 0;
+  if (prompt_len == 0)
+    fail(MI_ERR_CONFIG, "invalid model configuration: prefill requires at least one token");
+  c->filled = 0;
+  check_capacity(c, prompt_len);
+  // Decode steps needed: max_tokens - 1 (the first id comes from prefill).
+  size_t steps = max_tokens - 1;
+  if (prompt_len + steps > c->capacity)
+    fail(MI_ERR_CACHE_CAPACITY, "KV cache capacity %zu exceeded by requested length %zu",
+         c->capacity, prompt_len + steps);
+  upload_tokens(c, prompt, prompt_len, 0);
+  forward_tokens(m, c, prompt_len);
+  std::vector<uint32_t> ids(max_tokens);
+  size_t produced = 0;
+  size_t stop_index = max_tokens;  // index of the token that ended generation
+  const bool checks = nstops > 0 || cb != nullptr;
+  const size_t chunk = checks ? 16 : max_tokens;
+  size_t launched = 0;  // decode steps enqueued
+  size_t have = 0;      // ids copied to host
+  size_t seen = 0;      // ids examined
+  while (stop_index == max_tokens && seen < max_tokens) {
+    size_t n_new = std::min(chunk, steps - launched);
+    for (size_t i = 0; i < n_new; ++i) forward_tokens(m, c, 1);
+    launched += n_new;
+    size_t avail = 1 + launched;  // ids at toks[prompt_len .. prompt_len + avail)
+    MI_CUDA(cudaMemcpyAsync(ids.data() + have, c->toks.t->u32() + prompt_len + have,
+                            (avail - have) * 4, cudaMemcpyDeviceToHost, m->ctx->stream));
+    MI_CUDA(cudaStreamSynchronize(m->ctx->stream));
+    have = avail;
+    for (; seen < have && stop_index == max_tokens; ++seen) {
+      uint32_t tok = ids[seen];
+      if (tok == 0xFFFFFFFFu)
+        fail(MI_ERR_CONFIG, "invalid model configuration: logits contain no finite value");
+      bool is_stop = false;
+      for (size_t s = 0; s < nstops; ++s) is_stop |= stops[s] == tok;
+      if (is_stop) {
+        stop_index = seen;
+        break;
+      }
+      if (produced < capacity) out_ids[produced] = tok;
+      ++produced;
+      if (cb && !cb(tok, user)) stop_index = seen;
+    }
+  }
+  if (stop_index < max_tokens) {
+    // As generate_greedy's rollback: the cache keeps the prompt and the
+    // tokens fed back before the one that ended generation.
+    size_t keep = prompt_len + stop_index;
+    if (keep < c->filled) {
+      c->filled = keep;
+      set_dev_len(c, keep);
+    }
+  }
+  return produced;
+}
+
+}  // namespace
+
+extern "C" {
+
+mi_status mi_qwen3_decode_steps(mi_qwen3* m, mi_kv_cache* cache, size_t steps) {
+  return guard([&] {
+    check_cache(m, cache);
+    if (cache->filled == 0)
+      fail(MI_ERR_CONFIG, "invalid model configuration: decode needs a prefilled cache");
+    check_capacity(cache, steps);
+    for (size_t i = 0; i < steps; ++i) forward_tokens(m, cache, 1);
+  });
+}
+
+mi_status mi_kv_cache_tokens(mi_kv_cache* cache, size_t start, size_t count, uint32_t* out) {
+  return guard([&] {
+    require(cache, "cache");
+    if (count) require(out, "out");
+    MI_REQUIRE(start <= cache->capacity + 1 && count <= cache->capacity + 1 - start,
+               MI_ERR_SHAPE, "token range %zu..%zu is outside the cache", start, start + count);
+    mi_context* ctx = cache->model->ctx;
+    MI_CUDA(cudaMemcpyAsync(out, cache->toks.t->u32() + start, count * 4, cudaMemcpyDeviceToHost,
+                            ctx->stream));
+    MI_CUDA(cudaStreamSynchronize(ctx->stream));
+  });
+}
+
+// generate (qwen3.rs:424-439)
+mi_status mi_qwen3_generate(mi_qwen3* m, const uint32_t* prompt, size_t prompt_len,
+                            size_t max_tokens, mi_kv_cache* cache, uint32_t* out_ids,
+                            size_t* out_count) {
+  return guard([&] {
+    check_cache(m, cache);
+    require(out_count, "out_count");
+    if (max_tokens) require(out_ids, "out_ids");
+    require(prompt, "prompt");
+    *out_count = generate_greedy(m, cache, prompt, prompt_len, max_tokens, nullptr, 0, nullptr,
+                                 nullptr, out_ids, max_tokens);
+  });
+}
+
+// generate_with (qwen3.rs:441-473)
+mi_status mi_qwen3_generate_with(mi_qwen3* m, const uint32_t* prompt, size_t prompt_len,
+                                 const mi_generation_options* options, mi_kv_cache* cache,
+                                 mi_token_callback on_token, void* user, uint32_t* out_ids,
+                                 size_t capacity, size_t* out_count) {
+  return guard([&] {
+    check_cache(m, cache);
+    require(options, "options");
+    require(out_count, "out_count");
+    require(prompt, "prompt");
+    if (!std::isfinite(options->temperature) || options->temperature < 0.f)
+      fail(MI_ERR_CONFIG, "invalid model configuration: temperature must be finite and non-negative");
+    if (!(options->top_p > 0.f && options->top_p <= 1.f))
+      fail(MI_ERR_CONFIG, "invalid model configuration: top_p must be in (0, 1]");
+    if (options->temperature != 0.f)
+      fail(MI_ERR_UNSUPPORTED, "unsupported model: sampling with temperature > 0 is not on the device path");
+    *out_count = generate_greedy(m, cache, prompt, prompt_len, options->max_tokens,
+                                 options->stop_token_ids, options->stop_token_count, on_token,
+                                 user, out_ids, capacity);
+  });
+}
+
+// run_first_block (qwen3.rs:557-583)
+mi_status mi_qwen3_run_first_block(mi_qwen3* m, const uint32_t* tokens, size_t count,
+                                   mi_tensor** out) {
+  return guard([&] {
+    require(m, "model");
+    require(out, "out");
+    if (count == 0) fail(MI_ERR_CONFIG, "invalid model configuration: block benchmark requires tokens");
+    require(tokens, "tokens");
+    mi_kv_cache* c = nullptr;
+    mi_status s = mi_kv_cache_create(m, count, &c);
+    if (s != MI_OK) fail(s, "%s", mi_last_error_message());
+    std::unique_ptr<mi_kv_cache> guard_cache(c);
+    upload_tokens(c, tokens, count, 0);
+    const int h = (int)m->cfg.hidden_size;
+    TensorRef hidden(new_tensor(m->ctx, {count, (size_t)h}, MI_F16));
+    k::embedding(launch(m, false), c->toks.t->u32(), m->embedding.h(), hidden.h(), (int)count, h,
+                 (uint32_t)m->cfg.vocab_size);
+    Scratch sc(m->ctx);
+    layer_prefill(m, c, 0, hidden.h(), count, 0, sc);
+    sync_context(m->ctx);
+    *out = hidden.t;
+    hidden.t = nullptr;
+  });
+}
+
+// Every layer on given hidden states (no embedding, no head).
+mi_status mi_qwen3_forward_hidden(mi_qwen3* m, const mi_tensor* hidden, mi_kv_cache* cache,
+                                  mi_tensor** out) {
+  return guard([&] {
+    check_cache(m, cache);
+    require(hidden, "hidden");
+    require(out, "out");
+    if (hidden->dtype != MI_F16 || hidden->shape.size() != 2 ||
+        hidden->shape[1] != m->cfg.hidden_size || hidden->shape[0] == 0)
+      fail(MI_ERR_SHAPE, "invalid tensor shape: hidden must be [tokens, hidden_size] f16");
+    size_t T = hidden->shape[0];
+    check_capacity(cache, T);
+    ensure_workspace(m, cache->capacity);
+    TensorRef x(new_tensor(m->ctx, hidden->shape, MI_F16));
+    MI_CUDA(cudaMemcpyAsync(x.h(), hidden->base(), hidden->bytes(), cudaMemcpyDeviceToDevice,
+                            m->ctx->stream));
+    Scratch sc(m->ctx);
+    size_t off = cache->filled;
+    for (size_t li = 0; li < m->layers.size(); ++li) layer_prefill(m, cache, li, x.h(), T, off, sc);
+    cache->filled = off + T;
+    set_dev_len(cache, cache->filled);
+    sync_context(m->ctx);
+    *out = x.t;
+    x.t = nullptr;
+  });
+}
+
+mi_status mi_qwen3_weight(mi_qwen3* m, int layer, int role, mi_tensor** out) {
+  return guard([&] {
+    require(m, "model");
+    require(out, "out");
+    const mi_tensor* t = nullptr;
+    if (layer < 0) {
+      if (role == kEmbedding) t = m->embedding.t;
+      else if (role == kFinalNorm) t = m->final_norm.t;
+      else if (role == kLmHead) t = m->lm_head;
+    } else if ((size_t)layer < m->layers.size() && role > 0 && role < 16) {
+      t = m->layers[layer].w[role].t;
+    }
+    if (!t) fail(MI_ERR_MISSING_TENSOR, "missing model tensor (layer %d, role %d)", layer, role);
+    *out = view(t, t->shape, 0);
+  });
+}
+
+mi_status mi_qwen3_load(mi_context* ctx, const char* directory, mi_qwen3** out) {
+  return guard([&] {
+    require(ctx, "ctx");
+    require(directory, "directory");
+    require(out, "out");
+    fail(MI_ERR_UNSUPPORTED, "unsupported model: safetensors loading is not built yet");
+  });
+}
+
+}  // extern "C"

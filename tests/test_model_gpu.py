@@ -1,0 +1,224 @@
+"""GPU parity of the Qwen3 forward (prefill + greedy decode) against the oracle.
+
+Bars: identical greedy token ids over the decode
+horizon; logits within 1e-2 relative (max |gpu - oracle| / max |oracle|);
+hidden states per op within 2e-3 relative.
+"""
+import json
+import os
+
+import numpy as np
+import pytest
+
+import metal_infer as mi
+import oracle as O
+from conftest import INPUT_STREAM
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
+LOGIT_REL = 1e-2
+HIDDEN_REL = 2e-3
+
+
+def rel_err(actual_bits, expected_bits):
+    a = O.f32(np.asarray(actual_bits).ravel())
+    e = O.f32(np.asarray(expected_bits).ravel())
+    return float(np.max(np.abs(a - e)) / max(float(np.max(np.abs(e))), 1e-6))
+
+
+def small_cfg(layers=2, vocab=4096, **kw):
+    cfg = dict(mi.QWEN3_0_6B)
+    cfg.update(num_hidden_layers=layers, vocab_size=vocab, **kw)
+    return cfg
+
+
+@pytest.fixture(scope="module")
+def small(ctx):
+    cfg = small_cfg()
+    model = mi.Qwen3Model.random(ctx, cfg, seed=5)
+    ref = O.Qwen3(cfg, seed=5, capacity=256)
+    return cfg, model, ref
+
+
+def test_weights_match_oracle_bit_exact(small):
+    cfg, model, ref = small
+    for layer, role in ((-1, "embedding"), (0, "q"), (1, "down"), (1, "k_norm")):
+        w = model.weight(layer, role)
+        np.testing.assert_array_equal(w.f16_bits().ravel(),
+                                      ref.weight(layer, role, w.shape()).ravel())
+
+
+@pytest.mark.parametrize("prompt_len", [1, 7, 31, 32, 45])
+def test_prefill_logits_and_cache_match_oracle(small, prompt_len):
+    cfg, model, ref = small
+    prompt = O.gen_tokens(5, INPUT_STREAM, prompt_len, cfg["vocab_size"])
+    cache = model.kv_cache(256)
+    logits = model.prefill(prompt, cache).f16_bits()
+    ref.reset()
+    ref_logits = ref.forward(prompt)
+    assert rel_err(logits, ref_logits) <= LOGIT_REL
+    assert len(cache) == prompt_len
+    k0, v0 = cache.layer(1)
+    kk = k0.f16_bits().reshape(256, -1)[:prompt_len]
+    assert rel_err(kk, ref.cache(1, False, prompt_len)) <= HIDDEN_REL
+    vv = v0.f16_bits().reshape(256, -1)[:prompt_len]
+    assert rel_err(vv, ref.cache(1, True, prompt_len)) <= HIDDEN_REL
+
+
+@pytest.mark.parametrize("graphs", [True, False])
+def test_decode_logits_match_oracle(small, graphs):
+    cfg, model, ref = small
+    model.set_decode_graphs(graphs)
+    try:
+        prompt = O.gen_tokens(5, INPUT_STREAM + 1, 40, cfg["vocab_size"])
+        cache = model.kv_cache(256)
+        model.prefill(prompt, cache)
+        ref.reset()
+        ref.forward(prompt)
+        for step in range(12):
+            tok = int((step * 7919 + 13) % cfg["vocab_size"])
+            logits = model.decode(tok, cache).f16_bits()
+            ref_logits = ref.forward(np.array([tok], np.uint32))
+            assert rel_err(logits, ref_logits) <= LOGIT_REL, step
+            assert mi_argmax(logits) == O.argmax(ref_logits), step
+        assert len(cache) == 52
+    finally:
+        model.set_decode_graphs(True)
+
+
+def mi_argmax(bits):
+    return O.argmax(np.asarray(bits).ravel())
+
+
+def test_greedy_tokens_match_oracle_small(small):
+    cfg, model, ref = small
+    prompt = O.gen_tokens(5, INPUT_STREAM + 2, 33, cfg["vocab_size"])
+    cache = model.kv_cache(256)
+    ids = model.generate(prompt, 64, cache)
+    ref_ids = ref.generate_greedy(prompt, 64)
+    np.testing.assert_array_equal(ids, ref_ids)
+    assert len(cache) == 33 + 63
+
+
+def test_graph_and_eager_decode_are_bit_identical(small):
+    cfg, model, _ = small
+    prompt = O.gen_tokens(5, INPUT_STREAM + 3, 20, cfg["vocab_size"])
+    outs = []
+    for graphs in (True, False):
+        model.set_decode_graphs(graphs)
+        cache = model.kv_cache(128)
+        model.prefill(prompt, cache)
+        outs.append(np.stack([model.decode(int(t), cache).f16_bits().ravel()
+                              for t in (5, 77, 901, 4000)]))
+    model.set_decode_graphs(True)
+    np.testing.assert_array_equal(outs[0], outs[1])
+
+
+def test_pipelined_decode_argmax_matches_generate(ctx, small):
+    cfg, model, _ = small
+    prompt = O.gen_tokens(5, INPUT_STREAM + 4, 24, cfg["vocab_size"])
+    cache = model.kv_cache(128)
+    want = model.generate(prompt, 10, cache)
+    slots = ctx.tensor_u32(np.full(11, 0xFFFFFFFF, np.uint32), [11])
+    model.prefill_argmax(prompt, cache, slots.slice_1d(0, 1))
+    pending = None
+    for step in range(9):
+        _, pending = model.decode_argmax(slots.slice_1d(step, 1), cache, slots.slice_1d(step + 1, 1))
+    pending.wait()
+    np.testing.assert_array_equal(slots.to_u32_vec()[:10], want)
+
+
+def test_generate_with_stop_tokens_rolls_back_cache(small):
+    cfg, model, _ = small
+    prompt = O.gen_tokens(5, INPUT_STREAM + 5, 16, cfg["vocab_size"])
+    cache = model.kv_cache(128)
+    full = model.generate(prompt, 12, cache)
+    stop = int(full[5])
+    first = int(np.nonzero(full == stop)[0][0])
+    got = model.generate_with(prompt, {"max_tokens": 12, "stop_token_ids": [stop]}, cache)
+    np.testing.assert_array_equal(got, full[:first])
+    assert len(cache) == 16 + first
+    seen = []
+    got = model.generate_with(prompt, {"max_tokens": 12}, cache,
+                              on_token=lambda t: seen.append(t) or len(seen) < 3)
+    np.testing.assert_array_equal(got, full[:3])
+    assert len(cache) == 16 + 2
+    with pytest.raises(mi.ModelError) as e:
+        model.generate_with(prompt, {"max_tokens": 4, "temperature": 0.7}, cache)
+    assert e.value.status == mi.ERR_UNSUPPORTED
+
+
+def test_cache_capacity_error(small):
+    cfg, model, _ = small
+    cache = model.kv_cache(8)
+    with pytest.raises(mi.ModelError) as e:
+        model.prefill(np.arange(9), cache)
+    assert e.value.status == mi.ERR_CACHE_CAPACITY
+    model.prefill(np.arange(8), cache)
+    with pytest.raises(mi.ModelError) as e:
+        model.decode(3, cache)
+    assert e.value.status == mi.ERR_CACHE_CAPACITY
+    assert len(cache) == 8
+
+
+def test_unfused_options_match_oracle(ctx):
+    cfg = small_cfg(layers=2)
+    model = mi.Qwen3Model.random(ctx, cfg, seed=6)
+    model.set_fusion_options(mi.FusionOptions.none())
+    ref = O.Qwen3(cfg, seed=6, capacity=128)
+    ref.set_fusion(qk_rope_cache=False, add_rms_norm=False)
+    prompt = O.gen_tokens(6, INPUT_STREAM, 35, cfg["vocab_size"])
+    cache = model.kv_cache(128)
+    assert rel_err(model.prefill(prompt, cache).f16_bits(), ref.forward(prompt)) <= LOGIT_REL
+    for tok in (3, 99, 1234):
+        got = model.decode(tok, cache).f16_bits()
+        assert rel_err(got, ref.forward(np.array([tok], np.uint32))) <= LOGIT_REL
+
+
+@pytest.mark.parametrize("heads", [(32, 8), (64, 8), (16, 16)])
+def test_gqa_ratios_decode(ctx, heads):
+    qh, kvh = heads
+    cfg = small_cfg(layers=1, hidden_size=512, intermediate_size=1024, num_attention_heads=qh,
+                    num_key_value_heads=kvh, tie_word_embeddings=0)
+    model = mi.Qwen3Model.random(ctx, cfg, seed=7)
+    ref = O.Qwen3(cfg, seed=7, capacity=128)
+    prompt = O.gen_tokens(7, INPUT_STREAM, 40, cfg["vocab_size"])
+    ids = model.generate(prompt, 16, model.kv_cache(128))
+    np.testing.assert_array_equal(ids, ref.generate_greedy(prompt, 16))
+
+
+def test_config0_one_block_matches_oracle(ctx):
+    with open(os.path.join(GOLDEN, "block0.json")) as f:
+        meta = json.load(f)
+    golden = np.load(os.path.join(GOLDEN, "block0_hidden.npy"))
+    cfg = meta["config"]
+    model = mi.Qwen3Model.random(ctx, cfg, seed=0)
+    cache = model.kv_cache(2048)
+    h = cfg["hidden_size"]
+    outs = []
+    x = ctx.tensor_f16_bits(O.gen_normal_f16(0, INPUT_STREAM, 64 * h, 1.0), [64, h])
+    outs.append(model.forward_hidden(x, cache).f16_bits())
+    for step in range(16):
+        x = ctx.tensor_f16_bits(O.gen_normal_f16(0, INPUT_STREAM + 1 + step, h, 1.0), [1, h])
+        outs.append(model.forward_hidden(x, cache).f16_bits())
+    got = np.concatenate([o.reshape(-1, h) for o in outs])
+    assert got.shape == golden.shape
+    assert rel_err(got, golden) <= HIDDEN_REL
+    assert len(cache) == 80
+
+
+def test_config2_greedy_tokens_identical_to_golden(ctx):
+    """Full Qwen3-0.6B (seed 2): 128-token prompt, 256 decode steps."""
+    with open(os.path.join(GOLDEN, "qwen3_0_6b_greedy.json")) as f:
+        g = json.load(f)
+    cfg = g["config"]
+    model = mi.Qwen3Model.random(ctx, cfg, seed=g["seed"])
+    prompt = O.gen_tokens(g["seed"], g["prompt_stream"], g["prompt_len"], cfg["vocab_size"])
+    cache = model.kv_cache(2048)
+    logits = model.prefill(prompt, cache).f16_bits().ravel()
+    np.testing.assert_allclose(O.f32(logits[:16]), O.f32(np.array(g["prefill_logits_head"], np.uint16)),
+                               atol=LOGIT_REL * float(np.max(np.abs(O.f32(logits)))))
+    ids = model.generate(prompt, g["max_tokens"], cache)
+    np.testing.assert_array_equal(ids, np.array(g["ids"], np.uint32))
+    assert len(cache) == 128 + 256

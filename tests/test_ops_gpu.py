@@ -1,0 +1,432 @@
+"""GPU parity of every op against the CPU oracle, through the C ABI.
+
+Ports the cases of crates/metal-infer-core/tests/gpu.rs (absolute tolerance
+0.02 there) and adds seeded checks at the op-sweep shapes
+at the stricter per-op bar: max |gpu - oracle| / max |oracle| <= 2e-3.
+Integer and copy work (argmax, embedding, cache append, generator) is
+bit-exact.
+"""
+import numpy as np
+import pytest
+
+import metal_infer as mi
+import oracle as O
+from conftest import INPUT_STREAM
+
+pytestmark = pytest.mark.gpu
+
+REF_TOL = 0.02   # gpu.rs:6
+OP_REL = 2e-3    # per-op bar
+
+
+def f16(values):
+    return O.f16_bits(values)
+
+
+def assert_close(actual_bits, expected_bits, rel=OP_REL, abs_tol=REF_TOL):
+    a = O.f32(np.asarray(actual_bits).ravel())
+    e = O.f32(np.asarray(expected_bits).ravel())
+    assert a.shape == e.shape
+    err = np.abs(a - e)
+    scale = max(float(np.max(np.abs(e))), 1e-6)
+    assert np.all(np.isfinite(a)), "non-finite output"
+    assert float(err.max()) <= abs_tol, f"max abs err {err.max()}"
+    assert float(err.max()) / scale <= rel, f"rel err {err.max() / scale}"
+
+
+def T(ctx, bits, shape):
+    return ctx.tensor_f16_bits(np.asarray(bits, np.uint16).ravel(), shape)
+
+
+def rand16(seed, stream, shape, std=1.0):
+    return O.gen_normal_f16(seed, stream, int(np.prod(shape)), std).reshape(shape)
+
+
+# ---- known answers (gpu.rs) ---------------------------------------------------------
+
+@pytest.mark.parametrize("backend", [mi.MatmulBackend.AUTO, mi.MatmulBackend.REFERENCE])
+def test_matmul_and_matvec_known_answers(ctx, backend):
+    ctx.set_matmul_backend(backend)
+    try:
+        out = ctx.matmul(ctx.tensor_f16([1, 2, 3, 4], [2, 2]), ctx.tensor_f16([5, 6, 7, 8], [2, 2]))
+        np.testing.assert_array_equal(out.to_f32_vec(), [17, 23, 39, 53])
+        out = ctx.matmul(ctx.tensor_f16([1, 2, 3], [1, 3]),
+                         ctx.tensor_f16([4, 5, 6, 7, 8, 9], [2, 3]))
+        np.testing.assert_array_equal(out.to_f32_vec(), [32, 50])
+    finally:
+        ctx.set_matmul_backend(mi.MatmulBackend.AUTO)
+
+
+def test_mps_backend_is_rejected(ctx):
+    with pytest.raises(mi.ModelError) as e:
+        ctx.set_matmul_backend(mi.MatmulBackend.MPS)
+    assert e.value.status == mi.ERR_UNSUPPORTED
+
+
+@pytest.mark.parametrize("size", [1, 2, 31, 32, 33, 2048, 2049, 151936])
+def test_argmax_matches_cpu(ctx, size):
+    bits = ((np.arange(size, dtype=np.uint64) * 1103 + 17) & 0xFFFF).astype(np.uint16)
+    bits[0] = 0x7C00
+    if size > 1:
+        bits[1] = 0x7E00
+        bits[size // 2] = 0x7BFF
+        bits[-1] = 0x7BFF
+    else:
+        bits[0] = 0
+    logits = ctx.tensor_f16_bits(bits, [size])
+    out = ctx.tensor_u32([0], [1])
+    b = ctx.begin_batch()
+    b.argmax(logits, out)
+    b.finish()
+    assert int(out.to_u32_vec()[0]) == O.argmax(bits)
+
+
+def test_argmax_signed_zero_and_no_finite(ctx):
+    for bits, want in (([0x8000, 0], 1), ([0x7C00, 0x7E00], 0xFFFFFFFF)):
+        out = ctx.tensor_u32([0], [1])
+        b = ctx.begin_batch()
+        b.argmax(ctx.tensor_f16_bits(bits, [2]), out)
+        b.finish()
+        assert int(out.to_u32_vec()[0]) == want
+
+
+def test_speculative_embedding_handles_missing_argmax(ctx):
+    logits = ctx.tensor_f16_bits([0x7C00, 0x7E00], [2])
+    token = ctx.tensor_u32([0], [1])
+    table = ctx.tensor_f16([1.0, 2.0], [1, 2])
+    first = ctx.begin_batch()
+    first.argmax(logits, token)
+    first = first.commit()
+    second = ctx.begin_batch()
+    embedded = second.embedding(token, table)
+    second = second.commit()
+    first.wait()
+    second.wait()
+    assert int(token.to_u32_vec()[0]) == 0xFFFFFFFF
+    np.testing.assert_array_equal(embedded.to_f32_vec(), [0, 0])
+
+
+def test_vectorized_matvec_matches_oracle(ctx):
+    xv = f16(np.arange(128) / 128.0 - 0.5).reshape(1, 128)
+    wv = f16((np.arange(257 * 128) % 31) / 31.0 - 0.5).reshape(257, 128)
+    out = ctx.matmul(T(ctx, xv, [1, 128]), T(ctx, wv, [257, 128])).f16_bits()
+    assert_close(out, O.matmul(xv, wv))
+
+
+@pytest.mark.parametrize("n,k", [(1024, 1024), (1024, 3072), (65537, 256)])
+def test_tuned_matvec_matches_reference_across_qwen_shapes(ctx, n, k):
+    xv = f16((np.arange(k) % 17) / 34.0 - 0.25).reshape(1, k)
+    wv = f16((np.arange(n * k) % 29) / 58.0 - 0.25).reshape(n, k)
+    x, w = T(ctx, xv, [1, k]), T(ctx, wv, [n, k])
+    ctx.set_matmul_backend(mi.MatmulBackend.REFERENCE)
+    ref = ctx.matmul(x, w).f16_bits()
+    ctx.set_matmul_backend(mi.MatmulBackend.AUTO)
+    auto = ctx.matmul(x, w).f16_bits()
+    expected = O.matmul(xv, wv)
+    assert_close(ref, expected)
+    assert_close(auto, expected)
+
+
+def test_rms_norm_matches_oracle(ctx):
+    xv = f16((np.arange(3 * 65) % 23) / 11.0 - 1.0).reshape(3, 65)
+    wv = f16(0.5 + np.arange(65) / 130.0)
+    out = ctx.rms_norm(T(ctx, xv, [3, 65]), T(ctx, wv, [65]), 1e-6).f16_bits()
+    assert_close(out, O.rms_norm(xv, wv, 1e-6))
+
+
+@pytest.mark.parametrize("k", [1024, 128, 127])
+def test_fused_projections_match_individual_matvecs(ctx, k):
+    xv = f16((np.arange(k) % 17) / 17.0 - 0.5).reshape(1, k)
+    ws = [f16((np.arange(r * k) % m) / m - 0.5).reshape(r, k) for r, m in ((35, 19), (17, 23), (6, 29))]
+    x = T(ctx, xv, [1, k])
+    wt = [T(ctx, w, list(w.shape)) for w in ws]
+    b = ctx.begin_batch()
+    o3 = b.matmul3(x, *wt)
+    o2 = b.matmul2(x, wt[0], wt[1])
+    b.finish()
+    for o, w in zip(o3, ws):
+        assert_close(o.f16_bits(), O.matmul(xv, w))
+    for o, w in zip(o2, ws[:2]):
+        assert_close(o.f16_bits(), O.matmul(xv, w))
+
+
+def test_fused_add_rms_norm_matches_oracle(ctx):
+    left = f16([1.0, -2.0, 3.0, 0.5, 0.25, -0.75]).reshape(2, 3)
+    right = f16([0.5, 1.0, -1.0, 1.5, -0.25, 0.5]).reshape(2, 3)
+    w = f16([0.5, 1.0, 1.5])
+    b = ctx.begin_batch()
+    r, n = b.add_rms_norm(T(ctx, left, [2, 3]), T(ctx, right, [2, 3]), T(ctx, w, [3]), 1e-6)
+    b.finish()
+    er, en = O.add_rms_norm(left, right, w, 1e-6)
+    np.testing.assert_array_equal(r.f16_bits().ravel(), er.ravel())
+    assert_close(n.f16_bits(), en)
+
+
+@pytest.mark.parametrize("k", [256, 1024])
+def test_fused_decode_norm_projections_match_oracle(ctx, k):
+    iv = f16((np.arange(k) % 29) / 29.0 - 0.5).reshape(1, k)
+    rv = f16((np.arange(k) % 19) / 38.0 - 0.25).reshape(1, k)
+    nv = f16(0.5 + (np.arange(k) % 17) / 34.0)
+    ws = [f16((np.arange(r * k) % m) / m - 0.5).reshape(r, k) for r, m in ((40, 31), (24, 37), (16, 41))]
+    wt = [T(ctx, w, list(w.shape)) for w in ws]
+    x, right, norm = T(ctx, iv, [1, k]), T(ctx, rv, [1, k]), T(ctx, nv, [k])
+    b = ctx.begin_batch()
+    q, kk, v = b.rms_norm_matmul3(x, norm, *wt, 1e-6)
+    res, gate, up = b.add_rms_norm_matmul2(x, right, norm, wt[0], wt[1], 1e-6)
+    b.finish()
+    for o, e in zip((q, kk, v), O.rms_norm_matmul3(iv, nv, *ws, 1e-6)):
+        assert_close(o.f16_bits(), e)
+    er, eg, eu = O.add_rms_norm_matmul2(iv, rv, nv, ws[0], ws[1], 1e-6)
+    np.testing.assert_array_equal(res.f16_bits().ravel(), er.ravel())
+    assert_close(gate.f16_bits(), eg)
+    assert_close(up.f16_bits(), eu)
+
+
+def test_fused_rms_norm_matmul3_rejects_bad_width(ctx):
+    x = ctx.tensor_f16(np.zeros(100), [1, 100])
+    w = ctx.tensor_f16(np.zeros(200), [2, 100])
+    b = ctx.begin_batch()
+    with pytest.raises(mi.CoreError) as e:
+        b.rms_norm_matmul3(x, ctx.tensor_f16(np.ones(100), [100]), w, w, w, 1e-6)
+    assert e.value.status == mi.ERR_SHAPE
+    b.finish()
+
+
+def test_fused_qk_transform_matches_oracle(ctx):
+    qv = f16(np.arange(32) / 16.0 - 1.0).reshape(2, 2, 8)
+    kv = f16(np.arange(16) / 12.0 - 0.5).reshape(2, 1, 8)
+    nw = f16(0.75 + np.arange(8) / 16.0)
+    cache = ctx.tensor_f16(np.zeros(32), [4, 1, 8])
+    b = ctx.begin_batch()
+    out = b.qk_norm_rope_cache(T(ctx, qv, [2, 2, 8]), T(ctx, kv, [2, 1, 8]), T(ctx, nw, [8]),
+                               T(ctx, nw, [8]), cache, mi.QkNormRopeCacheConfig(1, 1e4, 1e-6))
+    b.finish()
+    ocache = np.zeros((4, 1, 8), np.uint16)
+    eq = O.qk_norm_rope_cache(qv, kv, nw, nw, ocache, 1, 1e4, 1e-6)
+    assert_close(out.f16_bits(), eq)
+    assert_close(cache.f16_bits(), ocache)
+    rot = ctx.rope(T(ctx, qv, [2, 2, 8]), 3, 1e4).f16_bits()
+    assert_close(rot, O.rope(qv, 3, 1e4))
+
+
+def test_batched_dependent_kernels_match_eager_execution(ctx):
+    left = ctx.tensor_f16([1, 2, 3, 4], [2, 2])
+    right = ctx.tensor_f16([0.5, 1.0, 1.5, 2.0], [2, 2])
+    eager = ctx.add(ctx.add(left, right), right)
+    b = ctx.begin_batch()
+    mid = b.add(left, right)
+    out = b.add(mid, right)
+    del mid
+    out = b.add(out, right)
+    b.finish()
+    np.testing.assert_array_equal(out.to_f32_vec(), ctx.add(eager, right).to_f32_vec())
+
+
+def test_invalid_batch_can_be_abandoned(ctx):
+    b = ctx.begin_batch()
+    with pytest.raises(mi.CoreError) as e:
+        b.matmul(ctx.tensor_f16([1, 2], [1, 2]), ctx.tensor_f16([1, 2, 3], [1, 3]))
+    assert e.value.status == mi.ERR_SHAPE
+    del b
+
+
+def test_dtype_errors(ctx):
+    with pytest.raises(mi.CoreError) as e:
+        ctx.add(ctx.tensor_u32([1, 2], [2]), ctx.tensor_u32([1, 2], [2]))
+    assert e.value.status == mi.ERR_DTYPE
+    with pytest.raises(mi.CoreError) as e:
+        ctx.tensor_f16([1, 2, 3], [2, 2])
+    assert e.value.status == mi.ERR_DATA_LENGTH
+
+
+def test_tensor_views(ctx):
+    t = ctx.tensor_f16(np.arange(12), [3, 4])
+    np.testing.assert_array_equal(t.row(1).to_f32_vec(), [4, 5, 6, 7])
+    np.testing.assert_array_equal(t.prefix(2).to_f32_vec(), np.arange(8))
+    np.testing.assert_array_equal(t.reshape([12]).slice_1d(3, 4).to_f32_vec(), [3, 4, 5, 6])
+    with pytest.raises(mi.CoreError):
+        t.row(3)
+    with pytest.raises(mi.CoreError):
+        t.reshape([5])
+    with pytest.raises(mi.CoreError):
+        t.prefix(0)
+
+
+def test_swiglu_and_add_match_oracle(ctx):
+    g = rand16(1, INPUT_STREAM + 50, (3072,))
+    u = rand16(1, INPUT_STREAM + 51, (3072,))
+    out = ctx.swiglu(T(ctx, g, [3072]), T(ctx, u, [3072])).f16_bits()
+    assert_close(out, O.swiglu(g, u))
+    s = ctx.add(T(ctx, g, [3072]), T(ctx, u, [3072])).f16_bits()
+    np.testing.assert_array_equal(s.ravel(), O.add(g, u))
+
+
+def test_embedding_and_copy_into_cache_are_bit_exact(ctx):
+    table = rand16(1, INPUT_STREAM + 60, (500, 64), 0.02)
+    toks = np.array([3, 0xFFFFFFFF, 499, 17], np.uint32)
+    out = ctx.embedding(ctx.tensor_u32(toks, [4]), T(ctx, table, [500, 64])).f16_bits()
+    np.testing.assert_array_equal(out, O.embedding(toks, table))
+    src = rand16(1, INPUT_STREAM + 61, (3, 2, 8))
+    cache = ctx.tensor_f16(np.zeros(10 * 16), [10, 2, 8])
+    ctx.copy_into_cache(T(ctx, src, [3, 2, 8]), cache, 5)
+    ocache = np.zeros((10, 2, 8), np.uint16)
+    O.copy_into_cache(src, ocache, 5)
+    np.testing.assert_array_equal(cache.f16_bits(), ocache)
+    with pytest.raises(mi.CoreError):
+        ctx.copy_into_cache(T(ctx, src, [3, 2, 8]), cache, 8)
+
+
+def test_generator_matches_oracle_bit_exact(ctx):
+    t = ctx.empty([1 << 20], mi.DType.F16)
+    ctx.fill_normal_f16(t, 3, 1 * 16 + 1, 0.02)
+    np.testing.assert_array_equal(t.f16_bits(), O.gen_normal_f16(3, 17, 1 << 20, 0.02))
+    tok = ctx.empty([4096], mi.DType.U32)
+    ctx.fill_tokens_u32(tok, 2, INPUT_STREAM, 151936)
+    np.testing.assert_array_equal(tok.to_u32_vec(), O.gen_tokens(2, INPUT_STREAM, 4096, 151936))
+
+
+# ---- attention ------------------------------------------------------------------------
+
+def _cfg(qh, kvh, hd, offset, causal=True):
+    return mi.AttentionConfig(qh, kvh, hd, int(causal), offset)
+
+
+def test_tiled_attention_matches_reference(ctx):
+    q = f16((np.arange(2 * 2 * 128) % 41) / 41.0 - 0.5)
+    k = f16((np.arange(2 * 128) % 37) / 37.0 - 0.25)
+    v = f16((np.arange(2 * 128) % 29) / 29.0)
+    cfg = _cfg(2, 1, 128, 0)
+    args = (T(ctx, q, [2, 2, 128]), T(ctx, k, [2, 1, 128]), T(ctx, v, [2, 1, 128]), cfg)
+    expected = O.attention(q, k, v, 2, 1, 128, True, 0)
+    for kind in (mi.AttentionKind.REFERENCE, mi.AttentionKind.TILED):
+        assert_close(ctx.attention(*args, kind).f16_bits(), expected)
+    q = f16((np.arange(2 * 128) % 43) / 43.0 - 0.5)
+    k = f16((np.arange(17 * 128) % 37) / 37.0 - 0.25)
+    v = f16((np.arange(17 * 128) % 29) / 29.0)
+    cfg = _cfg(2, 1, 128, 16)
+    args = (T(ctx, q, [1, 2, 128]), T(ctx, k, [17, 1, 128]), T(ctx, v, [17, 1, 128]), cfg)
+    expected = O.attention(q, k, v, 2, 1, 128, True, 16)
+    for kind in (mi.AttentionKind.REFERENCE, mi.AttentionKind.TILED,
+                 mi.AttentionKind.DECODE_SPLIT_KV, mi.AttentionKind.FLASH_DECODE):
+        assert_close(ctx.attention(*args, kind).f16_bits(), expected)
+
+
+@pytest.mark.parametrize("head_dim", [1, 2, 4, 8, 16, 32, 64, 128, 256])
+def test_flash_prefill_matches_oracle_at_tile_edges(ctx, head_dim):
+    for tokens, length in [(1, 1), (31, 31), (32, 32), (33, 33), (63, 63), (64, 64), (65, 65),
+                           (33, 65)]:
+        qh, kvh = 4, 2
+        q = f16((np.arange(tokens * qh * head_dim) % 43) / 43.0 - 0.5)
+        k = f16((np.arange(length * kvh * head_dim) % 37) / 37.0 - 0.25)
+        v = f16((np.arange(length * kvh * head_dim) % 29) / 29.0 - 0.5)
+        cfg = _cfg(qh, kvh, head_dim, length - tokens)
+        out = ctx.attention(T(ctx, q, [tokens, qh, head_dim]), T(ctx, k, [length, kvh, head_dim]),
+                            T(ctx, v, [length, kvh, head_dim]), cfg,
+                            mi.AttentionKind.FLASH_PREFILL).f16_bits()
+        exp = O.attention(q, k, v, qh, kvh, head_dim, True, length - tokens, O.FLASH_PREFILL)
+        assert_close(out, exp)
+
+
+@pytest.mark.parametrize("length", [1, 63, 64, 65, 256, 640, 8192])
+def test_flash_decode_matches_reference_across_block_boundaries(ctx, length):
+    q = f16(np.where(np.arange(2 * 128) % 3 == 0, 2.0, -2.0))
+    k = f16(np.where(np.arange(length * 128) % 7 < 3, 2.0, -2.0))
+    v = f16((np.arange(length * 128) % 37) / 37.0 - 0.5)
+    cfg = _cfg(2, 1, 128, length - 1)
+    tq, tk, tv = T(ctx, q, [1, 2, 128]), T(ctx, k, [length, 1, 128]), T(ctx, v, [length, 1, 128])
+    expected = O.attention(q, k, v, 2, 1, 128, True, length - 1)
+    for block in (32, 64, 128, 256):
+        for threads in (128, 256):
+            out = ctx.attention_flash_decode_with_configuration(tq, tk, tv, cfg, block, threads)
+            assert_close(out.f16_bits(), expected)
+
+
+def test_flash_decode_multiple_gqa_groups_and_causal_limit(ctx):
+    q = f16((np.arange(16 * 128) % 41) / 41.0 - 0.5)
+    k = f16((np.arange(65 * 8 * 128) % 37) / 37.0 - 0.5)
+    v = f16((np.arange(65 * 8 * 128) % 29) / 29.0)
+    tq, tk, tv = T(ctx, q, [1, 16, 128]), T(ctx, k, [65, 8, 128]), T(ctx, v, [65, 8, 128])
+    for offset in (62, 64):
+        cfg = _cfg(16, 8, 128, offset)
+        expected = O.attention(q, k, v, 16, 8, 128, True, offset)
+        for threads in (128, 256):
+            out = ctx.attention_flash_decode_with_configuration(tq, tk, tv, cfg, 64, threads)
+            assert_close(out.f16_bits(), expected)
+
+
+def test_flash_decode_rejects_other_gqa_ratios(ctx):
+    q = ctx.tensor_f16(np.zeros(4 * 128), [1, 4, 128])
+    k = ctx.tensor_f16(np.zeros(8 * 128), [8, 1, 128])
+    with pytest.raises(mi.CoreError) as e:
+        ctx.attention(q, k, k, _cfg(4, 1, 128, 7), mi.AttentionKind.FLASH_DECODE)
+    assert e.value.status == mi.ERR_SHAPE
+
+
+# ---- op sweep at BASELINE config 1 shapes (seed 1) -----------------------------------
+
+GEMV_SHAPES = {"q": (2048, 1024), "k": (1024, 1024), "o": (1024, 2048), "gate": (3072, 1024),
+               "down": (1024, 3072), "lm_head": (151936, 1024)}
+
+
+@pytest.mark.parametrize("name", list(GEMV_SHAPES))
+def test_config1_gemv_sweep(ctx, name):
+    n, k = GEMV_SHAPES[name]
+    x = rand16(1, INPUT_STREAM + 1, (1, k))
+    w = rand16(1, INPUT_STREAM + 2 + list(GEMV_SHAPES).index(name), (n, k), 0.02)
+    out = ctx.matmul(T(ctx, x, [1, k]), T(ctx, w, [n, k])).f16_bits()
+    assert_close(out, O.matmul(x, w))
+
+
+def test_config1_gate_up_pair(ctx):
+    x = rand16(1, INPUT_STREAM + 1, (1, 1024))
+    g = rand16(1, INPUT_STREAM + 20, (3072, 1024), 0.02)
+    u = rand16(1, INPUT_STREAM + 21, (3072, 1024), 0.02)
+    b = ctx.begin_batch()
+    og, ou = b.matmul2(T(ctx, x, [1, 1024]), T(ctx, g, [3072, 1024]), T(ctx, u, [3072, 1024]))
+    b.finish()
+    assert_close(og.f16_bits(), O.matmul(x, g))
+    assert_close(ou.f16_bits(), O.matmul(x, u))
+
+
+@pytest.mark.parametrize("length", [512, 2048, 8192])
+@pytest.mark.parametrize("kind", [mi.AttentionKind.DECODE_SPLIT_KV, mi.AttentionKind.FLASH_DECODE])
+def test_config1_attention_sweep(ctx, length, kind):
+    q = rand16(1, INPUT_STREAM + 30, (1, 16, 128))
+    k = rand16(1, INPUT_STREAM + 31, (length, 8, 128))
+    v = rand16(1, INPUT_STREAM + 32, (length, 8, 128))
+    cfg = _cfg(16, 8, 128, length - 1)
+    out = ctx.attention(T(ctx, q, [1, 16, 128]), T(ctx, k, [length, 8, 128]),
+                        T(ctx, v, [length, 8, 128]), cfg, kind).f16_bits()
+    assert_close(out, O.attention(q, k, v, 16, 8, 128, True, length - 1))
+
+
+def test_config1_rms_norm_rope_rows(ctx):
+    x = rand16(1, INPUT_STREAM + 40, (1, 1024))
+    w = f16(np.ones(1024))
+    assert_close(ctx.rms_norm(T(ctx, x, [1, 1024]), T(ctx, w, [1024]), 1e-6).f16_bits(),
+                 O.rms_norm(x, w, 1e-6))
+    q = rand16(1, INPUT_STREAM + 41, (1, 16, 128))
+    kk = rand16(1, INPUT_STREAM + 42, (1, 8, 128))
+    nw = f16(np.ones(128))
+    cache = ctx.tensor_f16(np.zeros(2048 * 8 * 128), [2048, 8, 128])
+    b = ctx.begin_batch()
+    out = b.qk_norm_rope_cache(T(ctx, q, [1, 16, 128]), T(ctx, kk, [1, 8, 128]), T(ctx, nw, [128]),
+                               T(ctx, nw, [128]), cache, mi.QkNormRopeCacheConfig(1500, 1e6, 1e-6))
+    b.finish()
+    ocache = np.zeros((2048, 8, 128), np.uint16)
+    eq = O.qk_norm_rope_cache(q, kk, nw, nw, ocache, 1500, 1e6, 1e-6)
+    assert_close(out.f16_bits(), eq)
+    assert_close(cache.f16_bits()[1500], ocache[1500])
+
+
+def test_kernel_profiler_records_only_enabled_dispatches(ctx):
+    x = ctx.tensor_f16([1, 2, 3], [1, 3])
+    w = ctx.tensor_f16([4, 5, 6, 7, 8, 9], [2, 3])
+    ctx.take_kernel_profiles()
+    ctx.set_kernel_profiling(True)
+    np.testing.assert_array_equal(ctx.matmul(x, w).to_f32_vec(), [32, 50])
+    profiles = ctx.take_kernel_profiles()
+    assert len(profiles) == 1 and profiles[0][0] == "gemv" and profiles[0][1] > 0
+    ctx.set_kernel_profiling(False)
+    ctx.matmul(x, w)
+    assert ctx.take_kernel_profiles() == []
