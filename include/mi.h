@@ -132,6 +132,12 @@ mi_status mi_context_take_kernel_profiles(mi_context* ctx, mi_kernel_profile* ou
                                           size_t capacity, size_t* count);
 /* Blocks until all work of the context's stream is done. */
 mi_status mi_context_synchronize(mi_context* ctx);
+/* Synchronizes, then reports (and clears) the code of a bounded device wait
+ * that expired since the last call: 0 = none; otherwise MI_ERR_TIMEOUT is
+ * returned and *code names the wait (tensor-core GEMM pipeline: 1 producer,
+ * 2 MMA issuer, 3 epilogue, 4 drain). No reference counterpart: Metal
+ * command-buffer errors (context.rs:1058-1063) have no device-side waits. */
+mi_status mi_context_kernel_status(mi_context* ctx, uint32_t* code);
 /* The context's CUDA stream (cudaStream_t) for interop. */
 void* mi_context_stream(mi_context* ctx);
 

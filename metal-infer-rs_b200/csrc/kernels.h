@@ -79,6 +79,9 @@ void matmul_reference(const Launch& l, const __half* x, const __half* w, __half*
 // Prefill GEMM (M > 1): out[m, n] = x[m, :] . w[n, :], FP32 accumulate.
 void gemm(const Launch& l, const __half* x, const __half* w, __half* out, int m, int n, int k,
           int ldo);
+// Expired-wait code of the tensor-core GEMM (0 = none); optionally cleared.
+unsigned gemm_tc_status(bool reset);
+bool gemm_tc_available();
 
 // ---- row / elementwise kernels ---------------------------------------------
 void add(const Launch& l, const __half* a, const __half* b, __half* out, size_t n);

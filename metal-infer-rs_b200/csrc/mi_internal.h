@@ -99,6 +99,10 @@ struct mi_tensor {
 };
 
 struct mi_context {
+  // Released by mi_context_destroy and by every buffer, batch and model that
+  // refers to the context; torn down when the count reaches zero, so handles
+  // may be destroyed in any order.
+  std::atomic<int> refs{1};
   int device = 0;
   cudaStream_t stream = nullptr;
   std::string name;
@@ -137,6 +141,8 @@ namespace mi {
 mi_tensor* new_tensor(mi_context* ctx, const std::vector<size_t>& shape, mi_dtype dtype,
                       bool zero = false);
 mi_tensor* view(const mi_tensor* t, const std::vector<size_t>& shape, size_t extra_offset);
+void context_retain(mi_context* ctx);
+void context_release(mi_context* ctx);
 void* context_scratch(mi_context* ctx, size_t bytes);
 void sync_context(mi_context* ctx);
 

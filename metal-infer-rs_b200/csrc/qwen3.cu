@@ -87,6 +87,8 @@ struct Workspace {
 struct mi_kv_cache;
 
 struct mi_qwen3 {
+  // Released by mi_qwen3_destroy and by each KV cache of the model.
+  std::atomic<int> refs{1};
   mi_context* ctx = nullptr;
   mi_qwen3_config cfg{};
   TensorRef embedding, final_norm, lm_head_own;
@@ -117,6 +119,15 @@ namespace {
 
 void require(const void* p, const char* what) {
   MI_REQUIRE(p != nullptr, MI_ERR_INVALID_ARGUMENT, "%s is NULL", what);
+}
+
+void model_release(mi_qwen3* m) {
+  if (!m || m->refs.fetch_sub(1) != 1) return;
+  mi_context* ctx = m->ctx;
+  cudaSetDevice(ctx->device);
+  cudaStreamSynchronize(ctx->stream);
+  delete m;
+  context_release(ctx);
 }
 
 // Qwen3Config::validate (config.rs:23-57)
@@ -563,6 +574,13 @@ mi_status mi_qwen3_create_random(mi_context* ctx, const mi_qwen3_config* config,
     auto m = std::make_unique<mi_qwen3>();
     m->ctx = ctx;
     m->cfg = *config;
+    context_retain(ctx);
+    struct CtxGuard {
+      mi_qwen3* m;
+      ~CtxGuard() {
+        if (m) context_release(m->ctx);
+      }
+    } ctx_guard{m.get()};
     const auto& c = m->cfg;
     size_t h = c.hidden_size, hd = c.head_dim, qw = qwidth(c), kw = kvwidth(c),
            I = c.intermediate_size, V = c.vocab_size;
@@ -603,15 +621,12 @@ mi_status mi_qwen3_create_random(mi_context* ctx, const mi_qwen3_config* config,
       L.w[kPostNorm] = ones(h);
     }
     sync_context(ctx);
+    ctx_guard.m = nullptr;
     *out = m.release();
   });
 }
 
-void mi_qwen3_destroy(mi_qwen3* m) {
-  if (!m) return;
-  cudaStreamSynchronize(m->ctx->stream);
-  delete m;
-}
+void mi_qwen3_destroy(mi_qwen3* m) { model_release(m); }
 
 mi_status mi_qwen3_get_config(const mi_qwen3* m, mi_qwen3_config* out) {
   return guard([&] {
@@ -659,6 +674,7 @@ mi_status mi_kv_cache_create(mi_qwen3* m, size_t capacity, mi_kv_cache** out) {
     MI_REQUIRE(capacity < 0x7FFFFFFF, MI_ERR_CONFIG, "KV cache capacity too large");
     auto c = std::make_unique<mi_kv_cache>();
     c->model = m;
+    m->refs.fetch_add(1);
     c->capacity = capacity;
     size_t kvh = m->cfg.num_key_value_heads, hd = m->cfg.head_dim;
     for (size_t l = 0; l < m->cfg.num_hidden_layers; ++l) {
@@ -675,8 +691,11 @@ mi_status mi_kv_cache_create(mi_qwen3* m, size_t capacity, mi_kv_cache** out) {
 
 void mi_kv_cache_destroy(mi_kv_cache* c) {
   if (!c) return;
-  cudaStreamSynchronize(c->model->ctx->stream);
+  mi_qwen3* m = c->model;
+  cudaSetDevice(m->ctx->device);
+  cudaStreamSynchronize(m->ctx->stream);
   delete c;
+  model_release(m);
 }
 
 size_t mi_kv_cache_len(const mi_kv_cache* c) { return c ? c->filled : 0; }
@@ -947,7 +966,7 @@ mi_status mi_qwen3_run_first_block(mi_qwen3* m, const uint32_t* tokens, size_t c
     mi_kv_cache* c = nullptr;
     mi_status s = mi_kv_cache_create(m, count, &c);
     if (s != MI_OK) fail(s, "%s", mi_last_error_message());
-    std::unique_ptr<mi_kv_cache> guard_cache(c);
+    std::unique_ptr<mi_kv_cache, void (*)(mi_kv_cache*)> guard_cache(c, mi_kv_cache_destroy);
     upload_tokens(c, tokens, count, 0);
     const int h = (int)m->cfg.hidden_size;
     TensorRef hidden(new_tensor(m->ctx, {count, (size_t)h}, MI_F16));

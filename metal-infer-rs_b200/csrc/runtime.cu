@@ -9,6 +9,7 @@
 #include <cstring>
 #include <mutex>
 
+#include "kernels.h"
 #include "mi_internal.h"
 
 namespace mi {
@@ -40,11 +41,30 @@ void fail(mi_status status, const char* fmt, ...) {
 void buffer_release(Buffer* b) {
   if (!b) return;
   if (b->refs.fetch_sub(1) != 1) return;
+  mi_context* ctx = b->ctx;
   if (b->owned && b->ptr) {
-    cudaFreeAsync(b->ptr, b->ctx->stream);
-    b->ctx->allocated -= b->bytes;
+    cudaSetDevice(ctx->device);
+    cudaFreeAsync(b->ptr, ctx->stream);
+    ctx->allocated -= b->bytes;
   }
   delete b;
+  context_release(ctx);
+}
+
+void context_retain(mi_context* ctx) { ctx->refs.fetch_add(1); }
+
+void context_release(mi_context* ctx) {
+  if (!ctx || ctx->refs.fetch_sub(1) != 1) return;
+  cudaSetDevice(ctx->device);
+  cudaStreamSynchronize(ctx->stream);
+  for (auto& p : ctx->pending_profiles) {
+    cudaEventDestroy(p.start);
+    cudaEventDestroy(p.stop);
+  }
+  if (ctx->scratch) cudaFreeAsync(ctx->scratch, ctx->stream);
+  cudaStreamSynchronize(ctx->stream);
+  cudaStreamDestroy(ctx->stream);
+  delete ctx;
 }
 
 mi_tensor* new_tensor(mi_context* ctx, const std::vector<size_t>& shape, mi_dtype dtype,
@@ -67,6 +87,7 @@ mi_tensor* new_tensor(mi_context* ctx, const std::vector<size_t>& shape, mi_dtyp
   }
   b->bytes = alloc;
   ctx->allocated += alloc;
+  context_retain(ctx);
   if (zero) {
     err = cudaMemsetAsync(b->ptr, 0, alloc, ctx->stream);
     if (err != cudaSuccess) {
@@ -224,10 +245,7 @@ void mi_context_destroy(mi_context* ctx) {
   cudaSetDevice(ctx->device);
   cudaStreamSynchronize(ctx->stream);
   resolve_profiles(ctx);
-  if (ctx->scratch) cudaFreeAsync(ctx->scratch, ctx->stream);
-  cudaStreamSynchronize(ctx->stream);
-  cudaStreamDestroy(ctx->stream);
-  delete ctx;
+  context_release(ctx);
 }
 
 mi_status mi_context_device_name(const mi_context* ctx, char* buf, size_t len) {
@@ -285,6 +303,20 @@ mi_status mi_context_synchronize(mi_context* ctx) {
 }
 
 void* mi_context_stream(mi_context* ctx) { return ctx ? (void*)ctx->stream : nullptr; }
+
+mi_status mi_context_kernel_status(mi_context* ctx, uint32_t* code) {
+  mi_status st = guard([&] {
+    require_ctx(ctx, "ctx");
+    require_ctx(code, "code");
+    sync_context(ctx);
+    *code = k::gemm_tc_status(true);
+  });
+  if (st == MI_OK && *code != 0) {
+    set_error("a bounded device wait expired (code %u)", *code);
+    return MI_ERR_TIMEOUT;
+  }
+  return st;
+}
 
 // ---- tensors -----------------------------------------------------------------
 
@@ -382,6 +414,7 @@ mi_status mi_context_tensor_from_device(mi_context* ctx, void* device_ptr, const
     b->ctx = ctx;
     b->ptr = device_ptr;
     b->owned = false;
+    context_retain(ctx);
     auto* t = new mi_tensor();
     t->buf = b;
     t->shape = shape_of(shape, rank);
@@ -541,8 +574,13 @@ mi_status mi_context_begin_batch(mi_context* ctx, mi_batch** out) {
     require_ctx(out, "out");
     auto* b = new mi_batch();
     b->ctx = ctx;
-    MI_CUDA(cudaEventCreate(&b->start));
-    MI_CUDA(cudaEventRecord(b->start, ctx->stream));
+    context_retain(ctx);
+    cudaError_t err = cudaEventCreate(&b->start);
+    if (err == cudaSuccess) err = cudaEventRecord(b->start, ctx->stream);
+    if (err != cudaSuccess) {
+      mi_batch_abandon(b);
+      fail(MI_ERR_COMMAND, "batch creation failed: %s", cudaGetErrorString(err));
+    }
     b->wall_start = std::chrono::steady_clock::now();
     *out = b;
   });
@@ -562,6 +600,7 @@ mi_status mi_batch_commit(mi_batch* b, mi_pending** out) {
     if (err == cudaSuccess) err = cudaEventRecord(p->stop, p->ctx->stream);
     if (err != cudaSuccess) {
       cudaEventDestroy(p->start);
+      context_release(p->ctx);
       delete p;
       fail(MI_ERR_COMMAND, "commit failed: %s", cudaGetErrorString(err));
     }
@@ -578,6 +617,7 @@ mi_status mi_pending_wait(mi_pending* p, mi_dispatch_stats* stats) {
     auto wall = std::chrono::steady_clock::now() - p->wall_start;
     cudaEventDestroy(p->start);
     cudaEventDestroy(p->stop);
+    context_release(p->ctx);
     delete p;
     if (err != cudaSuccess) fail(MI_ERR_COMMAND, "command failed: %s", cudaGetErrorString(err));
     if (stats) {
@@ -601,7 +641,9 @@ mi_status mi_batch_finish(mi_batch* b, mi_dispatch_stats* stats) {
 void mi_batch_abandon(mi_batch* b) {
   if (!b) return;
   if (b->start) cudaEventDestroy(b->start);
+  mi_context* ctx = b->ctx;
   delete b;
+  context_release(ctx);
 }
 
 }  // extern "C"

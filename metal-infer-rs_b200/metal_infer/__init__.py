@@ -143,6 +143,7 @@ EXPORTS = [
     "mi_context_device_name", "mi_context_allocated_bytes", "mi_context_set_matmul_backend",
     "mi_context_matmul_backend", "mi_context_set_kernel_profiling",
     "mi_context_take_kernel_profiles", "mi_context_synchronize", "mi_context_stream",
+    "mi_context_kernel_status",
     "mi_context_empty", "mi_context_tensor_f16", "mi_context_tensor_f16_bits",
     "mi_context_tensor_f16_bytes", "mi_context_tensor_bf16_as_f16_bytes",
     "mi_context_tensor_u32", "mi_context_tensor_from_device", "mi_tensor_clone",
@@ -356,6 +357,13 @@ class MetalContext:
 
     def stream(self) -> int:
         return int(lib().mi_context_stream(self._h) or 0)
+
+    def kernel_status(self) -> int:
+        """Synchronizes; raises CoreError(ERR_TIMEOUT) if a bounded device
+        wait expired since the last call."""
+        code = ctypes.c_uint32(0)
+        _check(lib().mi_context_kernel_status(self._h, ctypes.byref(code)))
+        return code.value
 
     # tensors (context.rs:740-872)
     def _new(self, fn, *args) -> Tensor:

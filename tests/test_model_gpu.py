@@ -91,13 +91,36 @@ def mi_argmax(bits):
     return O.argmax(np.asarray(bits).ravel())
 
 
+def divergence_report(model, ref, prompt, ids, ref_ids, capacity):
+    """Where two greedy sequences part, with both sides' logits at that step
+    (teacher-forced with the common prefix)."""
+    n = min(len(ids), len(ref_ids))
+    d = next((i for i in range(n) if ids[i] != ref_ids[i]), None)
+    if d is None:
+        return f"lengths differ: {len(ids)} vs {len(ref_ids)}"
+    cache = model.kv_cache(capacity)
+    g = model.prefill(prompt, cache).f16_bits().ravel()
+    ref.reset()
+    r = ref.forward(prompt)
+    for i in range(d):
+        g = model.decode(int(ref_ids[i]), cache).f16_bits().ravel()
+        r = ref.forward(np.array([ref_ids[i]], np.uint32))
+    rf, gf = O.f32(r), O.f32(g)
+    top = np.argsort(-rf, kind="stable")[:3]
+    return (f"first divergence at step {d}: gpu {int(ids[d])} oracle {int(ref_ids[d])}; "
+            f"oracle top3 {[(int(t), float(rf[t])) for t in top]}; gpu at those "
+            f"{[float(gf[t]) for t in top]}; teacher-forced gpu argmax {mi_argmax(g)}; "
+            f"logits rel err {rel_err(g, r):.2e}")
+
+
 def test_greedy_tokens_match_oracle_small(small):
     cfg, model, ref = small
     prompt = O.gen_tokens(5, INPUT_STREAM + 2, 33, cfg["vocab_size"])
     cache = model.kv_cache(256)
     ids = model.generate(prompt, 64, cache)
     ref_ids = ref.generate_greedy(prompt, 64)
-    np.testing.assert_array_equal(ids, ref_ids)
+    if not np.array_equal(ids, ref_ids):
+        pytest.fail(divergence_report(model, ref, prompt, ids, ref_ids, 256))
     assert len(cache) == 33 + 63
 
 
@@ -220,5 +243,8 @@ def test_config2_greedy_tokens_identical_to_golden(ctx):
     np.testing.assert_allclose(O.f32(logits[:16]), O.f32(np.array(g["prefill_logits_head"], np.uint16)),
                                atol=LOGIT_REL * float(np.max(np.abs(O.f32(logits)))))
     ids = model.generate(prompt, g["max_tokens"], cache)
-    np.testing.assert_array_equal(ids, np.array(g["ids"], np.uint32))
+    want = np.array(g["ids"], np.uint32)
+    if not np.array_equal(ids, want):
+        ref = O.Qwen3(cfg, seed=g["seed"], capacity=2048)
+        pytest.fail(divergence_report(model, ref, prompt, ids, want, 2048))
     assert len(cache) == 128 + 256

@@ -285,6 +285,30 @@ def test_generator_matches_oracle_bit_exact(ctx):
     np.testing.assert_array_equal(tok.to_u32_vec(), O.gen_tokens(2, INPUT_STREAM, 4096, 151936))
 
 
+# ---- prefill GEMM (tcgen05 tensor cores) ---------------------------------------------
+
+@pytest.mark.parametrize("m,n,k", [(128, 1024, 1024), (64, 3072, 1024), (200, 300, 520),
+                                   (33, 1000, 72), (2048, 4096, 4096), (128, 1024, 3072),
+                                   (512, 6144, 1024)])
+def test_prefill_gemm_matches_oracle(ctx, m, n, k):
+    x = rand16(4, INPUT_STREAM + 70, (m, k))
+    w = rand16(4, INPUT_STREAM + 71, (n, k), 0.02)
+    out = ctx.matmul(T(ctx, x, [m, k]), T(ctx, w, [n, k])).f16_bits()
+    assert ctx.kernel_status() == 0
+    assert_close(out, O.matmul(x, w))
+
+
+def test_prefill_gemm_reference_backend_agrees(ctx):
+    x = rand16(4, INPUT_STREAM + 72, (96, 256))
+    w = rand16(4, INPUT_STREAM + 73, (160, 256), 0.02)
+    tx, tw = T(ctx, x, [96, 256]), T(ctx, w, [160, 256])
+    fast = ctx.matmul(tx, tw).f16_bits()
+    ctx.set_matmul_backend(mi.MatmulBackend.REFERENCE)
+    ref = ctx.matmul(tx, tw).f16_bits()
+    ctx.set_matmul_backend(mi.MatmulBackend.AUTO)
+    assert_close(fast, ref)
+
+
 # ---- attention ------------------------------------------------------------------------
 
 def _cfg(qh, kvh, hd, offset, causal=True):
