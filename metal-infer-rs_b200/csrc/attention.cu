@@ -2,24 +2,35 @@
 // FP16 cache (qwen3.rs:68-117):
 //   attention_reference  two-pass FP32 softmax, one thread per output element
 //                        (attention_reference_f16, transformer.metal:1579-1612)
-//   attention_decode     single query, split-K over key blocks for any GQA
-//                        ratio; each CTA keeps FP32 online-softmax states for
-//                        the whole query group of one KV head and the last CTA
-//                        of the head merges them by log-sum-exp
-//                        (attention_flash_decode_*, transformer.metal:1911-2316)
+//   attention_decode     one query, flash decode (transformer.metal:2127-2316)
+//                        for any GQA ratio: blocks of B keys, 8 interleaved
+//                        online-softmax streams per block (one per half-warp;
+//                        a lane owns 8 of the 128 dims), stream then block
+//                        log-sum-exp merges in index order; the last CTA of a
+//                        KV head merges the blocks
 //   attention_decode_fused  the same with the per-head QK RMSNorm + RoPE and
 //                        the K/V append of the new token folded in
-//                        (qk_norm_rope_cache_f16 + copy_kv_f16)
-//   attention_prefill    flash-prefill semantics: 32-key blocks, FP32 scores
-//                        and row sums, probabilities rounded to FP16 before
-//                        they weight V (transformer.metal:1669-1822)
+//                        (qk_norm_rope_cache_f16 + copy_kv_f16); the cached
+//                        K/V rows are staged by cp.async before the kernel
+//                        waits on its predecessor
+//   attention_prefill    32-key blocks per query with the block sums of a
+//                        32-lane butterfly; flash prefill rounds the
+//                        probabilities to FP16 (transformer.metal:1614-1822)
+// All reductions follow numerics.cuh.
 
 #include "device.cuh"
+#include "pipeline.cuh"
 
 namespace mi {
 namespace k {
 
 namespace {
+
+constexpr int HD = 128;
+constexpr int kDecodeThreads = 128;  // 4 warps = 8 half-warp streams
+constexpr int kStreams = 8;
+constexpr int kTile = 64;            // keys staged per shared-memory tile
+constexpr int kRowBytes = HD * 2;
 
 __device__ __forceinline__ int kv_len_of(const AttnProblem& p) {
   return p.kv_len_dev ? (int)(*p.kv_len_dev) + p.kv_len_add : p.kv_len;
@@ -35,8 +46,7 @@ __global__ void attention_reference_kernel(AttnProblem p) {
   int L = kv_len_of(p);
   int kvh = h / (p.qh / p.kvh);
   int available = p.causal ? min(L, p.query_offset + qi + 1) : L;
-  float scale = rsqrtf((float)p.hd);
-  scale = __frcp_rn(__fsqrt_rn((float)p.hd));
+  float scale = __frcp_rn(__fsqrt_rn((float)p.hd));
   const __half* q = p.q + ((size_t)qi * p.qh + h) * p.hd;
   float maximum = -INFINITY;
   for (int j = 0; j < available; ++j) {
@@ -50,359 +60,452 @@ __global__ void attention_reference_kernel(AttnProblem p) {
     const __half* kr = p.k + ((size_t)j * p.kvh + kvh) * p.hd;
     float s = 0.f;
     for (int x = 0; x < p.hd; ++x) s = fmaf(__half2float(q[x]), __half2float(kr[x]), s);
-    float prob = expf(s * scale - maximum);
+    float prob = mi_exp(s * scale - maximum);
     den += prob;
     num = fmaf(prob, __half2float(p.v[((size_t)j * p.kvh + kvh) * p.hd + d]), num);
   }
   p.out[((size_t)qi * p.qh + h) * p.hd + d] = __float2half_rn(num / den);
 }
 
-// ---- split-K decode --------------------------------------------------------------
-// CTA (s, g) handles keys [s*chunk, min(L, (s+1)*chunk)) of KV head g for the
-// G query heads of its group. Warps stride over keys; each lane owns HD/32
-// consecutive dims. Partial state per (split, head): [max, sum, acc[HD]].
-constexpr int kDecodeWarps = 4;
-constexpr int kMinKeysPerSplit = 32;
-
-template <int HD, int G>
-struct DecodeState {
-  float m[G], l[G], acc[G][HD / 32];
+// ---- flash decode ----------------------------------------------------------------
+struct DecodeArgs {
+  const __half* q;        // [qh, 128]: final queries, or raw ones when fused
+  const __half* k_cache;  // [*, kvh, 128]
+  const __half* v_cache;
+  int qh, kvh;
+  int length;             // keys when length_dev is null
+  const uint32_t* length_dev;  // fused: position of the new token (keys = *dev + 1)
+  int block;              // keys per block (multiple of kTile)
+  __half* out;            // [qh, 128]
+  float* scratch;         // [kvh, gridDim.x, G, 130]
+  uint32_t* counters;     // [kvh], zero on entry and exit
+  // fused front end
+  int fused;
+  const __half* k_raw;
+  const __half* v_raw;
+  const __half* q_norm;
+  const __half* k_norm;
+  __half* k_cache_w;
+  __half* v_cache_w;
+  float theta, eps;
+  int round_norm;
 };
 
-template <int HD, int G>
-__device__ __forceinline__ void decode_keys(const float (&q)[G][HD / 32], const __half* K,
-                                            const __half* V, int kvh_stride, int begin, int end,
-                                            float scale, DecodeState<HD, G>& st) {
-  constexpr int E = HD / 32;
-  const int lane = threadIdx.x & 31;
-  const int warp = threadIdx.x >> 5;
-  for (int j = begin + warp; j < end; j += kDecodeWarps) {
-    const __half* kr = K + (size_t)j * kvh_stride + lane * E;
-    const __half* vr = V + (size_t)j * kvh_stride + lane * E;
-    float kf[E], vf[E];
-    if (E == 4) {
-      uint2 kk = *reinterpret_cast<const uint2*>(kr);
-      uint2 vv = *reinterpret_cast<const uint2*>(vr);
-      const __half2* hk = reinterpret_cast<const __half2*>(&kk);
-      const __half2* hv = reinterpret_cast<const __half2*>(&vv);
-      float2 a = __half22float2(hk[0]), b = __half22float2(hk[1]);
-      kf[0] = a.x; kf[1] = a.y; kf[2] = b.x; kf[3] = b.y;
-      a = __half22float2(hv[0]); b = __half22float2(hv[1]);
-      vf[0] = a.x; vf[1] = a.y; vf[2] = b.x; vf[3] = b.y;
-    } else {
+// Per-head RMSNorm + RoPE of one 128-dim head held by a half-warp (lane li
+// owns dims 8 li .. 8 li + 7; the rotation partner of dim d is d +- 64, lane
+// li ^ 8). Returns the FP16-rounded rotated values as floats.
+__device__ __forceinline__ void norm_rope_half(const uint4& raw, const __half* w, uint32_t pos,
+                                               float theta, float eps, bool round_norm,
+                                               float (&out)[8]) {
+  const int li = threadIdx.x & 15;
+  float total = canon_butterfly(chunk_sq(raw, 0.f), 16);
+  float scale = rms_scale(total, HD, eps);
+  const __half2* hr = reinterpret_cast<const __half2*>(&raw);
+  uint4 wr = reinterpret_cast<const uint4*>(w)[li];
+  const __half2* hw = reinterpret_cast<const __half2*>(&wr);
+  float nx[8];
 #pragma unroll
-      for (int e = 0; e < E; ++e) {
-        kf[e] = __half2float(kr[e]);
-        vf[e] = __half2float(vr[e]);
-      }
-    }
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-      float part = 0.f;
-#pragma unroll
-      for (int e = 0; e < E; ++e) part = fmaf(q[g][e], kf[e], part);
-      float s = warp_sum(part) * scale;
-      float nm = fmaxf(st.m[g], s);
-      float prev = expf(st.m[g] - nm);
-      float cur = expf(s - nm);
-#pragma unroll
-      for (int e = 0; e < E; ++e) st.acc[g][e] = fmaf(st.acc[g][e], prev, cur * vf[e]);
-      st.l[g] = fmaf(st.l[g], prev, cur);
-      st.m[g] = nm;
-    }
+  for (int i = 0; i < 4; ++i) {
+    float2 f = __half22float2(hr[i]);
+    float2 g = __half22float2(hw[i]);
+    nx[2 * i] = norm_mul(f.x, scale, g.x);
+    nx[2 * i + 1] = norm_mul(f.y, scale, g.y);
   }
-}
-
-// Combines the warps' states in shared memory and writes the CTA partial;
-// the last CTA of the KV head merges all partials into the output.
-template <int HD, int G>
-__device__ void decode_finish(DecodeState<HD, G>& st, float* scratch, uint32_t* counters,
-                              int splits_eff, int split, int g_kv, __half* out) {
-  constexpr int E = HD / 32;
-  constexpr int stride = HD + 2;
-  __shared__ float sm_m[kDecodeWarps][G], sm_l[kDecodeWarps][G];
-  __shared__ float sm_acc[kDecodeWarps][G][HD];
-  __shared__ bool last;
-  const int lane = threadIdx.x & 31;
-  const int warp = threadIdx.x >> 5;
+  if (round_norm)
 #pragma unroll
-  for (int g = 0; g < G; ++g) {
-    if (lane == 0) {
-      sm_m[warp][g] = st.m[g];
-      sm_l[warp][g] = st.l[g];
-    }
+    for (int e = 0; e < 8; ++e) nx[e] = __half2float(__float2half_rn(nx[e]));
+  const bool first = li < 8;
 #pragma unroll
-    for (int e = 0; e < E; ++e) sm_acc[warp][g][lane * E + e] = st.acc[g][e];
-  }
-  __syncthreads();
-  float* part = scratch + ((size_t)g_kv * gridDim.x + split) * G * stride;
-  for (int idx = threadIdx.x; idx < G * HD; idx += blockDim.x) {
-    int g = idx / HD, d = idx - g * HD;
-    float M = -INFINITY;
-#pragma unroll
-    for (int w = 0; w < kDecodeWarps; ++w) M = fmaxf(M, sm_m[w][g]);
-    float num = 0.f, den = 0.f;
-#pragma unroll
-    for (int w = 0; w < kDecodeWarps; ++w) {
-      float f = sm_m[w][g] == -INFINITY ? 0.f : expf(sm_m[w][g] - M);
-      num = fmaf(sm_acc[w][g][d], f, num);
-      den = fmaf(sm_l[w][g], f, den);
-    }
-    part[g * stride + 2 + d] = num;
-    if (d == 0) {
-      part[g * stride] = M;
-      part[g * stride + 1] = den;
-    }
-  }
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    uint32_t done = atomicAdd(counters + g_kv, 1u);
-    last = done == (uint32_t)splits_eff - 1;
-  }
-  __syncthreads();
-  if (!last) return;
-  __threadfence();
-  const float* base = scratch + (size_t)g_kv * gridDim.x * G * stride;
-  for (int idx = threadIdx.x; idx < G * HD; idx += blockDim.x) {
-    int g = idx / HD, d = idx - g * HD;
-    float M = -INFINITY;
-    for (int s = 0; s < splits_eff; ++s) M = fmaxf(M, __ldcg(base + (size_t)(s * G + g) * stride));
-    float num = 0.f, den = 0.f;
-    for (int s = 0; s < splits_eff; ++s) {
-      const float* ps = base + (size_t)(s * G + g) * stride;
-      float m = __ldcg(ps);
-      float f = m == -INFINITY ? 0.f : expf(m - M);
-      den = fmaf(__ldcg(ps + 1), f, den);
-      num = fmaf(__ldcg(ps + 2 + d), f, num);
-    }
-    out[(size_t)(g_kv * G + g) * HD + d] = __float2half_rn(num / den);
-  }
-  if (threadIdx.x == 0) counters[g_kv] = 0u;
-}
-
-template <int HD, int G>
-__global__ void __launch_bounds__(kDecodeWarps * 32)
-    attention_decode_kernel(AttnProblem p, float* scratch, uint32_t* counters, int block_keys) {
-  constexpr int E = HD / 32;
-  const int lane = threadIdx.x & 31;
-  const int g_kv = blockIdx.y;
-  const int split = blockIdx.x;
-  pdl_wait();
-  const int L = kv_len_of(p);
-  const int available = p.causal && p.query_offset < L ? p.query_offset + 1 : L;
-  int splits_eff = min((int)gridDim.x, (available + block_keys - 1) / block_keys);
-  if (splits_eff < 1) splits_eff = 1;
-  if (split >= splits_eff) return;
-  const int chunk = (available + splits_eff - 1) / splits_eff;
-  const int begin = split * chunk;
-  const int end = min(available, begin + chunk);
-  float q[G][E];
-#pragma unroll
-  for (int g = 0; g < G; ++g)
-#pragma unroll
-    for (int e = 0; e < E; ++e)
-      q[g][e] = __half2float(p.q[(size_t)(g_kv * G + g) * HD + lane * E + e]);
-  DecodeState<HD, G> st;
-#pragma unroll
-  for (int g = 0; g < G; ++g) {
-    st.m[g] = -INFINITY;
-    st.l[g] = 0.f;
-#pragma unroll
-    for (int e = 0; e < E; ++e) st.acc[g][e] = 0.f;
-  }
-  const float scale = __frcp_rn(__fsqrt_rn((float)HD));
-  decode_keys<HD, G>(q, p.k + (size_t)g_kv * HD, p.v + (size_t)g_kv * HD, p.kvh * HD, begin, end,
-                     scale, st);
-  decode_finish<HD, G>(st, scratch, counters, splits_eff, split, g_kv, p.out);
-}
-
-// Per-head RMSNorm + RoPE of one head held as E = HD/32 consecutive dims per
-// lane (lane l owns dims [l*E, l*E + E)); the rotation partner of dim d is
-// d +- HD/2, which lives in lane l ^ 16.
-template <int HD>
-__device__ __forceinline__ void norm_rope_lane(float (&x)[HD / 32], const __half* w,
-                                               uint32_t pos, float theta, float eps,
-                                               bool round_norm, float (&out)[HD / 32]) {
-  constexpr int E = HD / 32;
-  const int lane = threadIdx.x & 31;
-  float ss = 0.f;
-#pragma unroll
-  for (int e = 0; e < E; ++e) ss = fmaf(x[e], x[e], ss);
-  float scale = rms_scale(warp_sum(ss), HD, eps);
-  float nx[E];
-#pragma unroll
-  for (int e = 0; e < E; ++e) {
-    nx[e] = norm_mul(x[e], scale, __half2float(w[lane * E + e]));
-    if (round_norm) nx[e] = __half2float(__float2half_rn(nx[e]));
-  }
-  const bool first = lane < 16;
-#pragma unroll
-  for (int e = 0; e < E; ++e) {
-    float partner = __shfl_xor_sync(0xffffffffu, nx[e], 16);
-    int d = lane * E + e;
+  for (int e = 0; e < 8; ++e) {
+    float partner = __shfl_xor_sync(0xffffffffu, nx[e], 8);
+    int d = 8 * li + e;
     int pair = first ? d : d - HD / 2;
-    float exponent = __fdiv_rn(-(float)(pair * 2), (float)HD);
-    float frequency = powf(theta, exponent);
-    float angle = __fmul_rn((float)pos, frequency);
-    float sn, cs;
-    sincosf(angle, &sn, &cs);
-    float r = first ? __fsub_rn(__fmul_rn(nx[e], cs), __fmul_rn(partner, sn))
-                    : __fadd_rn(__fmul_rn(partner, sn), __fmul_rn(nx[e], cs));
+    float c, s;
+    rope_cs(pos, pair, HD, theta, &c, &s);
+    float r = first ? __fsub_rn(__fmul_rn(nx[e], c), __fmul_rn(partner, s))
+                    : __fadd_rn(__fmul_rn(partner, s), __fmul_rn(nx[e], c));
     out[e] = __half2float(__float2half_rn(r));
   }
 }
 
-template <int HD, int G>
-__global__ void __launch_bounds__(kDecodeWarps * 32)
-    attention_decode_fused_kernel(DecodeFused p, float* scratch, uint32_t* counters) {
-  constexpr int E = HD / 32;
-  const int lane = threadIdx.x & 31;
-  const int warp = threadIdx.x >> 5;
-  const int g_kv = blockIdx.y;
-  const int split = blockIdx.x;
-  pdl_trigger();
-  pdl_wait();
-  const uint32_t pos = pos_of(p.pos);
-  const int L = (int)pos + 1;
-  int splits_eff = min((int)gridDim.x, (L + kMinKeysPerSplit - 1) / kMinKeysPerSplit);
-  if (splits_eff < 1) splits_eff = 1;
-  if (split >= splits_eff) return;
-  const int chunk = (L + splits_eff - 1) / splits_eff;
-  const int begin = split * chunk;
-  const int end = min(L, begin + chunk);
-  const int kv_stride = p.kvh * HD;
+template <int G>
+struct DecodeSmem {
+  __half k[2][kTile][HD];
+  __half v[2][kTile][HD];
+  __half new_k[HD];
+  __half new_v[HD];
+  float q[G][HD];
+  float m[kStreams][G];
+  float l[kStreams][G];
+  float acc[kStreams][G][HD];
+  bool last;
+};
 
-  // Query heads of this group: RMSNorm + RoPE, rounded to FP16.
-  float q[G][E];
-#pragma unroll
-  for (int g = 0; g < G; ++g) {
-    float raw[E];
-#pragma unroll
-    for (int e = 0; e < E; ++e)
-      raw[e] = __half2float(p.q_raw[(size_t)(g_kv * G + g) * HD + lane * E + e]);
-    norm_rope_lane<HD>(raw, p.q_norm, pos, p.theta, p.eps, p.round_norm, q[g]);
+// Stages keys [j0, j1) of head g into buffer `buf` (cp.async, 16 bytes per
+// copy), skipping `skip`.
+__device__ __forceinline__ void stage_tile(const DecodeArgs& a, int g, int j0, int j1, int skip,
+                                           __half (*kt)[HD], __half (*vt)[HD]) {
+  const int per_row = kRowBytes / 16;
+  const int total = (j1 - j0) * per_row;
+  const size_t stride = (size_t)a.kvh * HD;
+  for (int i = threadIdx.x; i < total; i += kDecodeThreads) {
+    int r = i / per_row, c = i - r * per_row;
+    int j = j0 + r;
+    if (j == skip) continue;
+    const __half* ks = a.k_cache + (size_t)j * stride + (size_t)g * HD + 8 * c;
+    const __half* vs = a.v_cache + (size_t)j * stride + (size_t)g * HD + 8 * c;
+    pipe::cp_async16(&kt[r][8 * c], ks);
+    pipe::cp_async16(&vt[r][8 * c], vs);
   }
-  // The CTA that owns the new position appends the rotated key and the value.
-  if (warp == 0 && (int)(pos) >= begin && (int)pos < end) {
-    float raw[E], kr[E];
-#pragma unroll
-    for (int e = 0; e < E; ++e) raw[e] = __half2float(p.k_raw[(size_t)g_kv * HD + lane * E + e]);
-    norm_rope_lane<HD>(raw, p.k_norm, pos, p.theta, p.eps, p.round_norm, kr);
-    __half* kd = p.key_cache + (size_t)pos * kv_stride + (size_t)g_kv * HD + lane * E;
-    __half* vd = p.value_cache + (size_t)pos * kv_stride + (size_t)g_kv * HD + lane * E;
-#pragma unroll
-    for (int e = 0; e < E; ++e) {
-      kd[e] = __float2half_rn(kr[e]);
-      vd[e] = p.v_raw[(size_t)g_kv * HD + lane * E + e];
-    }
-  }
-  __syncthreads();
-  DecodeState<HD, G> st;
-#pragma unroll
-  for (int g = 0; g < G; ++g) {
-    st.m[g] = -INFINITY;
-    st.l[g] = 0.f;
-#pragma unroll
-    for (int e = 0; e < E; ++e) st.acc[g][e] = 0.f;
-  }
-  const float scale = __frcp_rn(__fsqrt_rn((float)HD));
-  decode_keys<HD, G>(q, p.key_cache + (size_t)g_kv * HD, p.value_cache + (size_t)g_kv * HD,
-                     kv_stride, begin, end, scale, st);
-  decode_finish<HD, G>(st, scratch, counters, splits_eff, split, g_kv, p.out);
+  pipe::cp_async_commit();
 }
 
-// ---- prefill (flash-prefill semantics) ----------------------------------------
-// One warp per (query, head). Keys in blocks of 32 from 0: lane j scores key
-// (block + j); the block max updates the running max; weights exp(s - max)
-// sum unrounded into the row sum and are rounded to FP16 before weighting V.
-constexpr int kPrefillWarps = 4;
-
-__global__ void __launch_bounds__(kPrefillWarps * 32) attention_prefill_kernel(AttnProblem p) {
-  __shared__ float qs[kPrefillWarps][256];
+template <int G>
+__global__ void __launch_bounds__(kDecodeThreads) attention_decode_kernel(DecodeArgs a) {
+  extern __shared__ __align__(16) uint8_t raw_smem[];
+  DecodeSmem<G>& sm = *reinterpret_cast<DecodeSmem<G>*>(raw_smem);
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
-  const int row = blockIdx.x * kPrefillWarps + warp;  // qi * qh + h
+  const int li = lane & 15;
+  const int hw = warp * 2 + (lane >> 4);  // stream index
+  const int g_kv = blockIdx.y;
+  const int b = blockIdx.x;
+
+  // Keys and this block's range are fixed before the predecessor finishes:
+  // the cache length only changes between decode steps.
+  const int pos = a.fused ? (int)*a.length_dev : -1;
+  const int L = a.fused ? pos + 1 : a.length;
+  const int nb = (L + a.block - 1) / a.block;
+  const int begin = b * a.block;
+  const int end = min(L, begin + a.block);
+  const int ntiles = b < nb ? (end - begin + kTile - 1) / kTile : 0;
+  if (ntiles > 0) stage_tile(a, g_kv, begin, min(end, begin + kTile), pos, sm.k[0], sm.v[0]);
+  pdl_trigger();
+  pdl_wait();
+  if (b >= nb) return;
+
+  // Queries of this group (and, fused, the new key / value).
+  if (hw < G) {
+    const __half* qsrc = a.q + (size_t)(g_kv * G + hw) * HD;
+    uint4 raw = reinterpret_cast<const uint4*>(qsrc)[li];
+    float qv[8];
+    if (a.fused) {
+      norm_rope_half(raw, a.q_norm, (uint32_t)pos, a.theta, a.eps, a.round_norm != 0, qv);
+    } else {
+      const __half2* hr = reinterpret_cast<const __half2*>(&raw);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float2 f = __half22float2(hr[i]);
+        qv[2 * i] = f.x;
+        qv[2 * i + 1] = f.y;
+      }
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) sm.q[hw][8 * li + e] = qv[e];
+  }
+  if (a.fused && pos >= begin && pos < end && warp == 3 && lane >= 16) {
+    uint4 raw = reinterpret_cast<const uint4*>(a.k_raw + (size_t)g_kv * HD)[li];
+    float kv[8];
+    norm_rope_half(raw, a.k_norm, (uint32_t)pos, a.theta, a.eps, a.round_norm != 0, kv);
+    uint4 kk;
+    __half2* hk = reinterpret_cast<__half2*>(&kk);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) hk[i] = __floats2half2_rn(kv[2 * i], kv[2 * i + 1]);
+    uint4 vv = reinterpret_cast<const uint4*>(a.v_raw + (size_t)g_kv * HD)[li];
+    const size_t row = (size_t)pos * a.kvh * HD + (size_t)g_kv * HD;
+    reinterpret_cast<uint4*>(a.k_cache_w + row)[li] = kk;
+    reinterpret_cast<uint4*>(a.v_cache_w + row)[li] = vv;
+    reinterpret_cast<uint4*>(sm.new_k)[li] = kk;
+    reinterpret_cast<uint4*>(sm.new_v)[li] = vv;
+  }
+
+  float qreg[G][8];
+  float m[G], l[G], acc[G][8];
+  __syncthreads();
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      qreg[g][e] = sm.q[g][8 * li + e];
+      acc[g][e] = 0.f;
+    }
+    m[g] = -INFINITY;
+    l[g] = 0.f;
+  }
+  const float scale = __frcp_rn(__fsqrt_rn((float)HD));
+
+  for (int t = 0; t < ntiles; ++t) {
+    const int buf = t & 1;
+    const int j0 = begin + t * kTile;
+    const int j1 = min(end, j0 + kTile);
+    if (t + 1 < ntiles)
+      stage_tile(a, g_kv, j1, min(end, j1 + kTile), pos, sm.k[buf ^ 1], sm.v[buf ^ 1]);
+    if (t + 1 < ntiles)
+      asm volatile("cp.async.wait_group 1;" ::: "memory");
+    else
+      pipe::cp_async_wait_all();
+    __syncthreads();
+    // Stream hw takes block-relative keys hw, hw + 8, ... (tiles are
+    // multiples of 8 keys, so the order is the block's).
+    for (int r = hw; r < j1 - j0; r += kStreams) {
+      const int j = j0 + r;
+      uint4 kk, vv;
+      if (j == pos) {
+        kk = reinterpret_cast<const uint4*>(sm.new_k)[li];
+        vv = reinterpret_cast<const uint4*>(sm.new_v)[li];
+      } else {
+        kk = reinterpret_cast<const uint4*>(sm.k[buf][r])[li];
+        vv = reinterpret_cast<const uint4*>(sm.v[buf][r])[li];
+      }
+      float kf[8], vf[8];
+      const __half2* hk = reinterpret_cast<const __half2*>(&kk);
+      const __half2* hv = reinterpret_cast<const __half2*>(&vv);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float2 fk = __half22float2(hk[i]);
+        float2 fv = __half22float2(hv[i]);
+        kf[2 * i] = fk.x;
+        kf[2 * i + 1] = fk.y;
+        vf[2 * i] = fv.x;
+        vf[2 * i + 1] = fv.y;
+      }
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        float d = 0.f;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) d = __fmaf_rn(qreg[g][e], kf[e], d);
+        float s = __fmul_rn(canon_butterfly(d, 16), scale);
+        float nm = fmaxf(m[g], s);
+        float pa = mi_exp(__fsub_rn(m[g], nm));
+        float pc = mi_exp(__fsub_rn(s, nm));
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[g][e] = __fmaf_rn(acc[g][e], pa, __fmul_rn(pc, vf[e]));
+        l[g] = __fmaf_rn(l[g], pa, pc);
+        m[g] = nm;
+      }
+    }
+    __syncthreads();
+  }
+
+  // Stream merge (index order) -> block partial.
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    if (li == 0) {
+      sm.m[hw][g] = m[g];
+      sm.l[hw][g] = l[g];
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) sm.acc[hw][g][8 * li + e] = acc[g][e];
+  }
+  __syncthreads();
+  const int stride = HD + 2;
+  float* part = a.scratch + ((size_t)g_kv * gridDim.x + b) * G * stride;
+  for (int idx = threadIdx.x; idx < G * HD; idx += kDecodeThreads) {
+    int g = idx / HD, d = idx - g * HD;
+    float M = -INFINITY;
+#pragma unroll
+    for (int s = 0; s < kStreams; ++s) M = fmaxf(M, sm.m[s][g]);
+    float num = 0.f, den = 0.f;
+#pragma unroll
+    for (int s = 0; s < kStreams; ++s) {
+      float f = sm.m[s][g] == -INFINITY ? 0.f : mi_exp(__fsub_rn(sm.m[s][g], M));
+      num = __fmaf_rn(sm.acc[s][g][d], f, num);
+      den = __fmaf_rn(sm.l[s][g], f, den);
+    }
+    if (nb == 1) {
+      a.out[(size_t)(g_kv * G + g) * HD + d] = __float2half_rn(__fdiv_rn(num, den));
+    } else {
+      part[g * stride + 2 + d] = num;
+      if (d == 0) {
+        part[g * stride] = M;
+        part[g * stride + 1] = den;
+      }
+    }
+  }
+  if (nb == 1) return;
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) sm.last = atomicAdd(a.counters + g_kv, 1u) == (uint32_t)nb - 1;
+  __syncthreads();
+  if (!sm.last) return;
+  __threadfence();
+  const float* base = a.scratch + (size_t)g_kv * gridDim.x * G * stride;
+  for (int idx = threadIdx.x; idx < G * HD; idx += kDecodeThreads) {
+    int g = idx / HD, d = idx - g * HD;
+    float M = -INFINITY;
+    for (int s = 0; s < nb; ++s) M = fmaxf(M, __ldcg(base + (size_t)(s * G + g) * stride));
+    float num = 0.f, den = 0.f;
+    for (int s = 0; s < nb; ++s) {
+      const float* ps = base + (size_t)(s * G + g) * stride;
+      float mm = __ldcg(ps);
+      float f = mm == -INFINITY ? 0.f : mi_exp(__fsub_rn(mm, M));
+      den = __fmaf_rn(__ldcg(ps + 1), f, den);
+      num = __fmaf_rn(__ldcg(ps + 2 + d), f, num);
+    }
+    a.out[(size_t)(g_kv * G + g) * HD + d] = __float2half_rn(__fdiv_rn(num, den));
+  }
+  if (threadIdx.x == 0) a.counters[g_kv] = 0u;
+}
+
+template <int G>
+void launch_decode_g(const Launch& l, const DecodeArgs& a, int blocks) {
+  auto kernel = attention_decode_kernel<G>;
+  size_t smem = sizeof(DecodeSmem<G>);
+  static bool configured = false;
+  if (!configured) {
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    configured = true;
+  }
+  launch_kernel(l, dim3(blocks, a.kvh), dim3(kDecodeThreads), smem, kernel, a);
+}
+
+void launch_decode(const Launch& l, const DecodeArgs& a, int blocks) {
+  switch (a.qh / a.kvh) {
+    case 1: launch_decode_g<1>(l, a, blocks); break;
+    case 2: launch_decode_g<2>(l, a, blocks); break;
+    case 4: launch_decode_g<4>(l, a, blocks); break;
+    case 8: launch_decode_g<8>(l, a, blocks); break;
+    default: fail(MI_ERR_SHAPE, "decode attention supports GQA ratios 1, 2, 4 and 8");
+  }
+}
+
+// ---- prefill ------------------------------------------------------------------------
+// One warp per query row; the 4 warps of a CTA take 4 consecutive queries of
+// one head and share 32-key K/V tiles in shared memory (rows padded by 16
+// bytes). Lane j scores key j with the canonical DOT computed in-thread.
+constexpr int kPrefillWarps = 4;
+
+template <int D>
+__global__ void __launch_bounds__(kPrefillWarps * 32) attention_prefill_kernel(AttnProblem p) {
+  constexpr int kPad = D * 2 + 16;  // bytes per staged row
+  __shared__ __align__(16) uint8_t ks[32 * kPad];
+  __shared__ __align__(16) uint8_t vs[32 * kPad];
+  __shared__ float qs[kPrefillWarps][D];
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int h = blockIdx.y;
+  const int kvh = h / (p.qh / p.kvh);
+  const int q0 = blockIdx.x * kPrefillWarps;
+  const int qi = q0 + warp;
+  pdl_wait();
+  const int L = kv_len_of(p);
+  const int last_q = min(p.tokens, q0 + kPrefillWarps) - 1;
+  const int limit = p.causal ? min(L, p.query_offset + last_q + 1) : L;
+  const bool active = qi < p.tokens;
+  const int available = active ? (p.causal ? min(L, p.query_offset + qi + 1) : L) : 0;
+  if (active)
+    for (int d = lane; d < D; d += 32) qs[warp][d] = __half2float(p.q[((size_t)qi * p.qh + h) * D + d]);
+  const size_t stride = (size_t)p.kvh * D;
+  const float scale = __frcp_rn(__fsqrt_rn((float)D));
+  constexpr int E = (D + 31) / 32;
+  float acc[E];
+#pragma unroll
+  for (int i = 0; i < E; ++i) acc[i] = 0.f;
+  float row_max = -INFINITY, row_sum = 0.f;
+  for (int base = 0; base < limit; base += 32) {
+    const int count = min(32, limit - base);
+    __syncthreads();
+    for (int i = threadIdx.x; i < count * (D / 8); i += kPrefillWarps * 32) {
+      int r = i / (D / 8), c = i - r * (D / 8);
+      const size_t src = (size_t)(base + r) * stride + (size_t)kvh * D + 8 * c;
+      *reinterpret_cast<uint4*>(ks + r * kPad + 16 * c) = *reinterpret_cast<const uint4*>(p.k + src);
+      *reinterpret_cast<uint4*>(vs + r * kPad + 16 * c) = *reinterpret_cast<const uint4*>(p.v + src);
+    }
+    __syncthreads();
+    if (base >= available) continue;
+    const int valid_n = min(32, available - base);
+    const bool valid = lane < valid_n;
+    float s = -INFINITY;
+    if (valid)
+      s = __fmul_rn(canon_dot_thread<D>(qs[warp], reinterpret_cast<const uint4*>(ks + lane * kPad)),
+                    scale);
+    float block_max = warp_max(s);
+    float next_max = fmaxf(row_max, block_max);
+    float alpha = isinf(row_max) ? 0.f : mi_exp(__fsub_rn(row_max, next_max));
+    float w = valid ? mi_exp(__fsub_rn(s, next_max)) : 0.f;
+    float block_sum = canon_butterfly(w, 32);
+    float prob = p.round_p ? __half2float(__float2half_rn(w)) : w;
+    row_sum = __fmaf_rn(row_sum, alpha, block_sum);
+    row_max = next_max;
+#pragma unroll
+    for (int i = 0; i < E; ++i) acc[i] = __fmul_rn(acc[i], alpha);
+    for (int c = 0; c < valid_n; ++c) {
+      float pc = __shfl_sync(0xffffffffu, prob, c);
+      const __half* vr = reinterpret_cast<const __half*>(vs + c * kPad);
+#pragma unroll
+      for (int i = 0; i < E; ++i) {
+        int d = lane + i * 32;
+        if (d < D) acc[i] = __fmaf_rn(pc, __half2float(vr[d]), acc[i]);
+      }
+    }
+  }
+  if (!active) return;
+#pragma unroll
+  for (int i = 0; i < E; ++i) {
+    int d = lane + i * 32;
+    if (d < D) p.out[((size_t)qi * p.qh + h) * D + d] = __float2half_rn(__fdiv_rn(acc[i], row_sum));
+  }
+}
+
+// Any head_dim <= 256 (test shapes): direct global reads, same arithmetic.
+__global__ void attention_prefill_scalar_kernel(AttnProblem p) {
+  const int lane = threadIdx.x & 31;
+  const int row = blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
   pdl_wait();
   if (row >= p.tokens * p.qh) return;
-  const int qi = row / p.qh;
-  const int h = row - qi * p.qh;
+  const int qi = row / p.qh, h = row - (row / p.qh) * p.qh;
   const int kvh = h / (p.qh / p.kvh);
   const int L = kv_len_of(p);
   const int available = p.causal ? min(L, p.query_offset + qi + 1) : L;
   const int hd = p.hd;
-  const int kv_stride = p.kvh * hd;
-  for (int d = lane; d < hd; d += 32) qs[warp][d] = __half2float(p.q[(size_t)row * hd + d]);
-  __syncwarp();
+  const size_t stride = (size_t)p.kvh * hd;
   const float scale = __frcp_rn(__fsqrt_rn((float)hd));
+  const __half* q = p.q + (size_t)row * hd;
+  const int lanes = canon_lanes(hd);
+  const int chunks = (hd + 7) / 8;
   float acc[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) acc[i] = 0.f;
   float row_max = -INFINITY, row_sum = 0.f;
-  const bool vec = (hd % 8) == 0;
   for (int base = 0; base < available; base += 32) {
-    const int key = base + lane;
-    const bool valid = key < available;
+    const int valid_n = min(32, available - base);
+    const bool valid = lane < valid_n;
     float s = -INFINITY;
     if (valid) {
-      const __half* kr = p.k + (size_t)key * kv_stride + (size_t)kvh * hd;
-      float dot = 0.f;
-      if (vec) {
-        for (int c = 0; c < hd; c += 8) {
-          uint4 kk = *reinterpret_cast<const uint4*>(kr + c);
-          const __half2* hk = reinterpret_cast<const __half2*>(&kk);
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            float2 f = __half22float2(hk[i]);
-            dot = fmaf(qs[warp][c + 2 * i], f.x, dot);
-            dot = fmaf(qs[warp][c + 2 * i + 1], f.y, dot);
-          }
-        }
-      } else {
-        for (int c = 0; c < hd; ++c) dot = fmaf(qs[warp][c], __half2float(kr[c]), dot);
-      }
-      s = dot * scale;
+      const __half* kr = p.k + (size_t)(base + lane) * stride + (size_t)kvh * hd;
+      float v[32];
+      for (int c = 0; c < 32; ++c) v[c] = 0.f;
+      for (int c = 0; c < chunks; ++c)
+        for (int i = 8 * c; i < min(hd, 8 * c + 8); ++i)
+          v[c % lanes] = __fmaf_rn(__half2float(q[i]), __half2float(kr[i]), v[c % lanes]);
+      for (int step = lanes / 2; step >= 1; step /= 2)
+        for (int t = 0; t < step; ++t) v[t] = __fadd_rn(v[t], v[t + step]);
+      s = __fmul_rn(v[0], scale);
     }
     float block_max = warp_max(s);
     float next_max = fmaxf(row_max, block_max);
-    float alpha = isinf(row_max) ? 0.f : expf(row_max - next_max);
-    float w = valid ? expf(s - next_max) : 0.f;
-    float block_sum = warp_sum(w);
+    float alpha = isinf(row_max) ? 0.f : mi_exp(__fsub_rn(row_max, next_max));
+    float w = valid ? mi_exp(__fsub_rn(s, next_max)) : 0.f;
+    float block_sum = canon_butterfly(w, 32);
     float prob = p.round_p ? __half2float(__float2half_rn(w)) : w;
-    row_sum = fmaf(row_sum, alpha, block_sum);
+    row_sum = __fmaf_rn(row_sum, alpha, block_sum);
     row_max = next_max;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) acc[i] *= alpha;
-    const int count = min(32, available - base);
-    for (int c = 0; c < count; ++c) {
+    for (int i = 0; i < 8; ++i) acc[i] = __fmul_rn(acc[i], alpha);
+    for (int c = 0; c < valid_n; ++c) {
       float pc = __shfl_sync(0xffffffffu, prob, c);
-      const __half* vr = p.v + (size_t)(base + c) * kv_stride + (size_t)kvh * hd;
+      const __half* vr = p.v + (size_t)(base + c) * stride + (size_t)kvh * hd;
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         int d = lane + i * 32;
-        if (d < hd) acc[i] = fmaf(pc, __half2float(vr[d]), acc[i]);
+        if (d < hd) acc[i] = __fmaf_rn(pc, __half2float(vr[d]), acc[i]);
       }
     }
   }
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     int d = lane + i * 32;
-    if (d < hd) p.out[(size_t)row * hd + d] = __float2half_rn(acc[i] / row_sum);
-  }
-}
-
-template <int HD>
-bool launch_decode_hd(const Launch& l, const AttnProblem& p, int splits, int block_keys,
-                      float* scratch, uint32_t* counters) {
-  int G = p.qh / p.kvh;
-  dim3 grid(splits, p.kvh);
-  dim3 block(kDecodeWarps * 32);
-  switch (G) {
-    case 1: launch_kernel(l, grid, block, 0, attention_decode_kernel<HD, 1>, p, scratch, counters, block_keys); return true;
-    case 2: launch_kernel(l, grid, block, 0, attention_decode_kernel<HD, 2>, p, scratch, counters, block_keys); return true;
-    case 4: launch_kernel(l, grid, block, 0, attention_decode_kernel<HD, 4>, p, scratch, counters, block_keys); return true;
-    case 8: launch_kernel(l, grid, block, 0, attention_decode_kernel<HD, 8>, p, scratch, counters, block_keys); return true;
-    default: return false;
+    if (d < hd) p.out[(size_t)row * hd + d] = __float2half_rn(__fdiv_rn(acc[i], row_sum));
   }
 }
 
@@ -413,48 +516,89 @@ void attention_reference(const Launch& l, const AttnProblem& p) {
   launch_kernel(l, grid, dim3(128), 0, attention_reference_kernel, p);
 }
 
-size_t attention_decode_scratch(int kvh, int splits, int group, int hd) {
-  return (size_t)kvh * splits * group * (hd + 2) * sizeof(float);
+int decode_block_for(int capacity) {
+  if (capacity <= 8192) return 64;
+  int b = 64;
+  while ((long long)b * 128 < capacity) b <<= 1;
+  return b;
+}
+
+size_t attention_decode_scratch(int kvh, int blocks, int group, int hd) {
+  return (size_t)kvh * blocks * group * (hd + 2) * sizeof(float);
 }
 
 int attention_decode_splits(int kv_len_max, int kvh, int sm_count, int block_keys) {
-  int by_len = (kv_len_max + block_keys - 1) / block_keys;
-  int by_sm = (2 * sm_count + kvh - 1) / kvh;
-  int s = by_len < by_sm ? by_len : by_sm;
-  return s < 1 ? 1 : s;
+  (void)kvh;
+  (void)sm_count;
+  int b = (kv_len_max + block_keys - 1) / block_keys;
+  return b < 1 ? 1 : b;
 }
 
 void attention_decode(const Launch& l, const AttnProblem& p, int splits, int block_keys,
                       float* scratch, uint32_t* counters) {
-  bool ok = false;
-  if (p.hd == 128) ok = launch_decode_hd<128>(l, p, splits, block_keys, scratch, counters);
-  else if (p.hd == 64) ok = launch_decode_hd<64>(l, p, splits, block_keys, scratch, counters);
-  else if (p.hd == 256) ok = launch_decode_hd<256>(l, p, splits, block_keys, scratch, counters);
-  if (!ok) attention_reference(l, p);
+  if (p.hd != 128 || (p.qh / p.kvh) > 8 || ((p.qh / p.kvh) & ((p.qh / p.kvh) - 1)) ||
+      block_keys % 8 || (block_keys > kTile && block_keys % kTile)) {
+    attention_reference(l, p);
+    return;
+  }
+  DecodeArgs a = {};
+  a.q = p.q;
+  a.k_cache = p.k;
+  a.v_cache = p.v;
+  a.qh = p.qh;
+  a.kvh = p.kvh;
+  const int L = p.kv_len;
+  a.length = p.causal && p.query_offset < L ? p.query_offset + 1 : L;
+  a.block = block_keys;
+  a.out = p.out;
+  a.scratch = scratch;
+  a.counters = counters;
+  launch_decode(l, a, splits);
 }
 
 void attention_decode_fused(const Launch& l, const DecodeFused& p, int splits, float* scratch,
-                            uint32_t* counters) {
+                            uint32_t* counters, int block_keys) {
   MI_REQUIRE(p.hd == 128, MI_ERR_SHAPE, "fused decode attention needs head_dim 128");
-  int G = p.qh / p.kvh;
-  dim3 grid(splits, p.kvh);
-  dim3 block(kDecodeWarps * 32);
-  switch (G) {
-    case 1: launch_kernel(l, grid, block, 0, attention_decode_fused_kernel<128, 1>, p, scratch, counters); break;
-    case 2: launch_kernel(l, grid, block, 0, attention_decode_fused_kernel<128, 2>, p, scratch, counters); break;
-    case 4: launch_kernel(l, grid, block, 0, attention_decode_fused_kernel<128, 4>, p, scratch, counters); break;
-    case 8: launch_kernel(l, grid, block, 0, attention_decode_fused_kernel<128, 8>, p, scratch, counters); break;
-    default: fail(MI_ERR_SHAPE, "fused decode attention supports GQA ratios 1, 2, 4 and 8");
-  }
+  DecodeArgs a = {};
+  a.q = p.q_raw;
+  a.k_cache = p.key_cache;
+  a.v_cache = p.value_cache;
+  a.k_cache_w = p.key_cache;
+  a.v_cache_w = p.value_cache;
+  a.qh = p.qh;
+  a.kvh = p.kvh;
+  a.length_dev = p.pos.dev;
+  a.block = block_keys;
+  a.out = p.out;
+  a.scratch = scratch;
+  a.counters = counters;
+  a.fused = 1;
+  a.k_raw = p.k_raw;
+  a.v_raw = p.v_raw;
+  a.q_norm = p.q_norm;
+  a.k_norm = p.k_norm;
+  a.theta = p.theta;
+  a.eps = p.eps;
+  a.round_norm = p.round_norm ? 1 : 0;
+  launch_decode(l, a, splits);
 }
 
 void attention_prefill(const Launch& l, const AttnProblem& p) {
   MI_REQUIRE(p.hd <= 256, MI_ERR_SHAPE, "prefill attention needs head_dim <= 256");
+  if (p.tokens * p.qh <= 0) return;
+  dim3 grid((p.tokens + kPrefillWarps - 1) / kPrefillWarps, p.qh);
+  dim3 block(kPrefillWarps * 32);
+  switch (p.hd) {
+    case 64: launch_kernel(l, grid, block, 0, attention_prefill_kernel<64>, p); return;
+    case 128: launch_kernel(l, grid, block, 0, attention_prefill_kernel<128>, p); return;
+    case 256: launch_kernel(l, grid, block, 0, attention_prefill_kernel<256>, p); return;
+    default: break;
+  }
   int rows = p.tokens * p.qh;
-  if (rows <= 0) return;
-  launch_kernel(l, dim3((rows + kPrefillWarps - 1) / kPrefillWarps), dim3(kPrefillWarps * 32), 0,
-                attention_prefill_kernel, p);
+  launch_kernel(l, dim3((rows + 3) / 4), dim3(128), 0, attention_prefill_scalar_kernel, p);
 }
+
+unsigned attention_status(bool reset) { return pipe::read_status(reset); }
 
 }  // namespace k
 }  // namespace mi

@@ -8,6 +8,7 @@
 
 #include "kernels.h"
 #include "mi_internal.h"
+#include "numerics.cuh"
 
 namespace mi {
 namespace k {
@@ -48,31 +49,6 @@ __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
   return v;
-}
-
-// Dot product of 8 halves packed in uint4 (FP32 accumulate, sequential).
-__device__ __forceinline__ float dot8(const uint4& a, const uint4& b, float acc) {
-  const __half2* x = reinterpret_cast<const __half2*>(&a);
-  const __half2* y = reinterpret_cast<const __half2*>(&b);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    float2 fx = __half22float2(x[i]);
-    float2 fy = __half22float2(y[i]);
-    acc = fmaf(fx.x, fy.x, acc);
-    acc = fmaf(fx.y, fy.y, acc);
-  }
-  return acc;
-}
-
-// rsqrt(total / width + eps) as a correctly rounded 1 / sqrt.
-__device__ __forceinline__ float rms_scale(float total, int width, float eps) {
-  return __frcp_rn(__fsqrt_rn(__fadd_rn(__fdiv_rn(total, (float)width), eps)));
-}
-
-// x * scale * g with both products rounded (no contraction), as the
-// reference's `float(x) * scale * float(w)`.
-__device__ __forceinline__ float norm_mul(float x, float scale, float g) {
-  return __fmul_rn(__fmul_rn(x, scale), g);
 }
 
 // Greedy argmax key of argmax_better (transformer.metal:1396-1411): values

@@ -1,6 +1,7 @@
 // Row and elementwise kernels: residual add, RMSNorm, fused add+RMSNorm,
 // SwiGLU, embedding gather, RoPE, fused per-head QK-norm + RoPE + K-cache
-// append, V-cache append and the standalone greedy argmax.
+// append, V-cache append and the standalone greedy argmax. Row reductions use
+// the canonical order of numerics.cuh (one warp per row).
 
 #include "device.cuh"
 
@@ -9,8 +10,31 @@ namespace k {
 
 namespace {
 
+// Canonical sum of squares of `width` FP16 values (one warp).
+__device__ __forceinline__ float row_sumsq(const __half* row, int width) {
+  const int lane = threadIdx.x & 31;
+  const int lanes = canon_lanes(width);
+  const int chunks = (width + 7) / 8;
+  float acc = 0.f;
+  if (lane < lanes) {
+    const bool vec = (width % 8 == 0) && ((reinterpret_cast<uintptr_t>(row) & 15) == 0);
+    for (int c = lane; c < chunks; c += lanes) {
+      if (vec) {
+        acc = chunk_sq(reinterpret_cast<const uint4*>(row)[c], acc);
+      } else {
+        for (int i = 8 * c; i < min(width, 8 * c + 8); ++i) {
+          float v = __half2float(row[i]);
+          acc = __fmaf_rn(v, v, acc);
+        }
+      }
+    }
+  }
+  return canon_butterfly(acc, lanes);
+}
+
 // add_f16 (transformer.metal:61-68): a correctly rounded half addition.
 __global__ void add_kernel(const __half* a, const __half* b, __half* out, size_t n) {
+  pdl_wait();
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
        i += (size_t)gridDim.x * blockDim.x)
     out[i] = __hadd(a[i], b[i]);
@@ -24,20 +48,14 @@ __global__ void rms_norm_kernel(const __half* x, const __half* w, __half* out, i
   pdl_wait();
   if (row >= rows) return;
   const __half* xr = x + (size_t)row * width;
-  float ss = 0.f;
-  for (int i = lane; i < width; i += 32) {
-    float v = __half2float(xr[i]);
-    ss = fmaf(v, v, ss);
-  }
-  float scale = rms_scale(warp_sum(ss), width, eps);
+  float scale = rms_scale(row_sumsq(xr, width), width, eps);
   for (int i = lane; i < width; i += 32)
     out[(size_t)row * width + i] =
         __float2half_rn(norm_mul(__half2float(xr[i]), scale, __half2float(w[i])));
 }
 
 // add_rms_norm_f16 (transformer.metal:1342-1369): residual = half(l + r);
-// the sum of squares uses the unrounded sums, the normalized row the rounded
-// residual.
+// squares of the unrounded sums; normalized from the rounded residual.
 __global__ void add_rms_norm_kernel(const __half* l, const __half* r, const __half* w,
                                     __half* residual, __half* normalized, int rows, int width,
                                     float eps) {
@@ -46,13 +64,18 @@ __global__ void add_rms_norm_kernel(const __half* l, const __half* r, const __ha
   pdl_wait();
   if (row >= rows) return;
   size_t base = (size_t)row * width;
-  float ss = 0.f;
-  for (int i = lane; i < width; i += 32) {
-    float v = __fadd_rn(__half2float(l[base + i]), __half2float(r[base + i]));
-    residual[base + i] = __float2half_rn(v);
-    ss = fmaf(v, v, ss);
-  }
-  float scale = rms_scale(warp_sum(ss), width, eps);
+  const int lanes = canon_lanes(width);
+  const int chunks = (width + 7) / 8;
+  float acc = 0.f;
+  if (lane < lanes)
+    for (int c = lane; c < chunks; c += lanes)
+      for (int i = 8 * c; i < min(width, 8 * c + 8); ++i) {
+        float v = __fadd_rn(__half2float(l[base + i]), __half2float(r[base + i]));
+        residual[base + i] = __float2half_rn(v);
+        acc = __fmaf_rn(v, v, acc);
+      }
+  float scale = rms_scale(canon_butterfly(acc, lanes), width, eps);
+  __syncwarp();
   for (int i = lane; i < width; i += 32) {
     float v = __half2float(__float2half_rn(
         __fadd_rn(__half2float(l[base + i]), __half2float(r[base + i]))));
@@ -64,11 +87,8 @@ __global__ void add_rms_norm_kernel(const __half* l, const __half* r, const __ha
 __global__ void swiglu_kernel(const __half* gate, const __half* up, __half* out, size_t n) {
   pdl_wait();
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
-       i += (size_t)gridDim.x * blockDim.x) {
-    float g = __half2float(gate[i]);
-    float v = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), __half2float(up[i]));
-    out[i] = __float2half_rn(v);
-  }
+       i += (size_t)gridDim.x * blockDim.x)
+    out[i] = __float2half_rn(silu_mul(__half2float(gate[i]), __half2float(up[i])));
 }
 
 // embedding_f16 (transformer.metal:1382-1394); out-of-range ids (including
@@ -84,14 +104,11 @@ __global__ void embedding_kernel(const uint32_t* tokens, const __half* table, __
     out[(size_t)t * width + i] = zero ? __half(0.f) : table[(size_t)tok * width + i];
 }
 
-// Rotate-half RoPE of one pair: freq = theta^(-2i/d), angle = pos * freq.
+// Rotate-half RoPE of one pair with the engine's RoPE terms.
 __device__ __forceinline__ void rope_pair(float x, float y, int pair, int head_dim, uint32_t pos,
                                           float theta, __half* ox, __half* oy) {
-  float exponent = __fdiv_rn(-(float)(pair * 2), (float)head_dim);
-  float frequency = powf(theta, exponent);
-  float angle = __fmul_rn((float)pos, frequency);
-  float s, c;
-  sincosf(angle, &s, &c);
+  float c, s;
+  rope_cs(pos, pair, head_dim, theta, &c, &s);
   *ox = __float2half_rn(__fsub_rn(__fmul_rn(x, c), __fmul_rn(y, s)));
   *oy = __float2half_rn(__fadd_rn(__fmul_rn(x, s), __fmul_rn(y, c)));
 }
@@ -132,12 +149,7 @@ __global__ void qk_norm_rope_cache_kernel(const __half* q, const __half* k, cons
   int head = row - token * heads;
   const __half* in = (is_q ? q : k) + (size_t)row * head_dim;
   const __half* w = is_q ? qw : kw;
-  float ss = 0.f;
-  for (int i = lane; i < head_dim; i += 32) {
-    float v = __half2float(in[i]);
-    ss = fmaf(v, v, ss);
-  }
-  float scale = rms_scale(warp_sum(ss), head_dim, eps);
+  float scale = rms_scale(row_sumsq(in, head_dim), head_dim, eps);
   uint32_t p = pos_of(pos) + token;
   __half* dst = is_q ? q_out + (size_t)row * head_dim
                      : key_cache + ((size_t)p * kv_heads + head) * head_dim;

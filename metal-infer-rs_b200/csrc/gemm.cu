@@ -2,8 +2,12 @@
 // accumulation and one FP16 rounding (matmul_simd_db_f16,
 // transformer.metal:174-272).
 //
-// This file holds the CUDA-core tiled kernel used for ragged shapes; aligned
-// shapes go to the tcgen05 tensor-core kernel (gemm_tc.cu) when it is built.
+//   gemm_canon  CUDA-core kernel with the canonical reduction of numerics.cuh
+//               (each output is DOT(x[m], w[n]) exactly as the decode GEMV
+//               computes it); used for prompts up to kCanonRows rows, where
+//               the weight stream, not the arithmetic, bounds the time
+//   gemm_tc     tcgen05 tensor-core kernel (gemm_tc.cu) for longer prompts
+//   gemm_simt   tiled fallback for ragged K or unaligned operands
 
 #include "device.cuh"
 
@@ -11,6 +15,60 @@ namespace mi {
 namespace k {
 
 namespace {
+
+constexpr int kCanonRows = 512;
+
+// Warp tile: 8 rows of x by 8 rows of w; CTA: 2 x 4 warp tiles (16 x 32).
+// Lane l reduces chunks l, l + 32, ... of every pair, then the canonical
+// butterfly completes each of the 64 dots.
+__global__ void __launch_bounds__(256) gemm_canon_kernel(const __half* x, const __half* w,
+                                                         __half* out, int m, int n, int k,
+                                                         int ldo) {
+  pdl_wait();
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int m0 = blockIdx.y * 16 + (warp & 1) * 8;
+  const int n0 = blockIdx.x * 32 + (warp >> 1) * 8;
+  const int kc = k >> 3;
+  const int lanes = canon_lanes(k);
+  float acc[8][8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+  const uint4 zero = make_uint4(0, 0, 0, 0);
+  for (int c = lane; c < kc; c += 32) {
+    uint4 xv[8], wv[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      xv[i] = m0 + i < m ? __ldg(reinterpret_cast<const uint4*>(x + (size_t)(m0 + i) * k) + c)
+                         : zero;
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      wv[j] = n0 + j < n ? __ldg(reinterpret_cast<const uint4*>(w + (size_t)(n0 + j) * k) + c)
+                         : zero;
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[i][j] = chunk_dot(xv[i], wv[j], acc[i][j]);
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[i][j] = canon_butterfly(acc[i][j], lanes);
+  // Lane l writes outputs (l / 8, l % 8) and (l / 8 + 4, l % 8).
+#pragma unroll
+  for (int half = 0; half < 2; ++half) {
+    int i = lane / 8 + 4 * half, j = lane % 8;
+    float v = 0.f;
+#pragma unroll
+    for (int ii = 0; ii < 8; ++ii)
+#pragma unroll
+      for (int jj = 0; jj < 8; ++jj)
+        if (ii == i && jj == j) v = acc[ii][jj];
+    if (m0 + i < m && n0 + j < n) out[(size_t)(m0 + i) * ldo + n0 + j] = __float2half_rn(v);
+  }
+}
 
 constexpr int BM = 64, BN = 64, BK = 16;
 
@@ -61,15 +119,22 @@ __global__ void __launch_bounds__(256) gemm_simt_kernel(const __half* x, const _
   }
 }
 
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
 }  // namespace
 
-bool gemm_tc_available();
 bool gemm_tc(const Launch& l, const __half* x, const __half* w, __half* out, int m, int n, int k,
              int ldo);
 
 void gemm(const Launch& l, const __half* x, const __half* w, __half* out, int m, int n, int k,
           int ldo) {
   if (m <= 0 || n <= 0) return;
+  const bool vec = k % 8 == 0 && aligned16(x) && aligned16(w);
+  if (vec && m <= kCanonRows) {
+    dim3 grid((n + 31) / 32, (m + 15) / 16);
+    launch_kernel(l, grid, dim3(256), 0, gemm_canon_kernel, x, w, out, m, n, k, ldo);
+    return;
+  }
   if (gemm_tc(l, x, w, out, m, n, k, ldo)) return;
   dim3 grid((n + BN - 1) / BN, (m + BM - 1) / BM);
   launch_kernel(l, grid, dim3(256), 0, gemm_simt_kernel, x, w, out, m, n, k, ldo);

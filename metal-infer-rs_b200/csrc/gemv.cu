@@ -1,18 +1,24 @@
-// Decode GEMV family (M = 1): y = x . W^T with FP16 weights streamed by
-// 16-byte loads, FP32 accumulation and warp-shuffle reductions, fused with the
-// prologues and epilogues of the decode step:
+// Decode GEMV family (M = 1): y = x . W^T over FP16 weights with the
+// canonical FP32 reduction (numerics.cuh), fused with the prologues and
+// epilogues of the decode step:
 //   kInNorm      matvec3_rms_impl      (transformer.metal:937-1009)
 //   kInAddNorm   matvec2_add_rms_impl  (transformer.metal:1091-1160)
 //   kOutResidual matmul + add_f16      (transformer.metal:274-347, 61-68)
 //   kOutSwiglu   matvec2 + swiglu_f16  (transformer.metal:484-542, 1371-1380)
 //   kOutArgmax   matvec_vocab + argmax (transformer.metal:473-482, 1396-1512)
 //
-// Each warp owns whole rows (no split-K): lane l reads 16-byte chunks
-// l, l+32, ... of a row, so a warp-wide load covers 512 contiguous bytes.
-// Before waiting on its predecessor (PDL) every warp prefetches its rows into
-// L2, so the weight stream overlaps the previous kernel's tail.
+// Weight staging: each CTA owns a contiguous block of output rows. Thread 0
+// streams the block's weights into a one- or two-stage shared-memory ring
+// with 1-D bulk copies (TMA engine) that complete on mbarriers. The first
+// stages are issued before griddepcontrol.wait, so under programmatic
+// dependent launch the weight stream of this kernel overlaps the previous
+// kernel; only the activation read and the reductions remain on the
+// dependency chain. A warp then reduces a row from shared memory: lane l
+// takes chunks l, l + 32, ... (16 bytes each) and the lanes meet in the
+// canonical butterfly.
 
 #include "device.cuh"
+#include "pipeline.cuh"
 
 namespace mi {
 namespace k {
@@ -21,31 +27,57 @@ namespace {
 
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
+constexpr int kSmemBudget = 112 * 1024;  // two GEMV CTAs fit on one SM
 
-struct RowRef {
-  const __half* ptr;
-  int seg;
-  int row;
+struct Plan {
+  int rpc;      // items per CTA
+  int rps;      // items per stage
+  int stages;   // ring depth (1 or 2)
+  int x_bytes;  // shared bytes of the input row
+  int stage_bytes;
 };
 
-__device__ __forceinline__ RowRef locate(const GemvProblem& p, int item) {
-  int r = item;
-  int s = 0;
-  if (r >= p.n[0]) {
-    r -= p.n[0];
-    s = 1;
-    if (r >= p.n[1]) {
-      r -= p.n[1];
-      s = 2;
-    }
-  }
-  return {p.w[s] + (size_t)r * p.k, s, r};
+__device__ __forceinline__ int items_of(const GemvProblem& p, int out_mode) {
+  return out_mode == kOutSwiglu ? p.n[0] : p.n[0] + p.n[1] + p.n[2];
 }
 
-// Builds the GEMV input in shared memory (k halves as k/8 uint4 chunks).
+// Issues the bulk copies of `chunk` of this CTA's items into its stage.
+template <int OUT>
+__device__ void issue_stage(const GemvProblem& p, const Plan& plan, uint8_t* stages,
+                            uint64_t* full, int first, int last, int chunk) {
+  const int s = chunk % plan.stages;
+  const int i0 = first + chunk * plan.rps;
+  const int cnt = min(plan.rps, last - i0);
+  const uint32_t row_bytes = (uint32_t)p.k * 2u;
+  uint8_t* dst = stages + (size_t)s * plan.stage_bytes;
+  if (OUT == kOutSwiglu) {
+    pipe::mbar_expect_tx(&full[s], 2u * cnt * row_bytes);
+    pipe::bulk_g2s(dst, p.w[0] + (size_t)i0 * p.k, cnt * row_bytes, &full[s]);
+    pipe::bulk_g2s(dst + (size_t)cnt * row_bytes, p.w[1] + (size_t)i0 * p.k, cnt * row_bytes,
+                   &full[s]);
+    return;
+  }
+  pipe::mbar_expect_tx(&full[s], (uint32_t)cnt * row_bytes);
+  int seg_start = 0;
+  int done = 0;
+  for (int seg = 0; seg < 3 && done < cnt; ++seg) {
+    int seg_end = seg_start + p.n[seg];
+    int a = max(i0 + done, seg_start), b = min(i0 + cnt, seg_end);
+    if (a < b) {
+      pipe::bulk_g2s(dst + (size_t)done * row_bytes, p.w[seg] + (size_t)(a - seg_start) * p.k,
+                     (uint32_t)(b - a) * row_bytes, &full[s]);
+      done += b - a;
+    }
+    seg_start = seg_end;
+  }
+}
+
+// Builds the GEMV input in shared memory (k halves as k/8 uint4 chunks) with
+// the canonical sum of squares (one warp) for the normalizing prologues.
 template <int IN>
-__device__ void build_input(const GemvProblem& p, uint4* xs, float* red) {
+__device__ void build_input(const GemvProblem& p, uint4* xs, float* s_scale) {
   const int tid = threadIdx.x;
+  const int lane = tid & 31;
   const int kc = p.k >> 3;
   const uint4* src = reinterpret_cast<const uint4*>(p.x);
   if (IN == kInEmbedNorm) {
@@ -53,10 +85,9 @@ __device__ void build_input(const GemvProblem& p, uint4* xs, float* red) {
     bool zero = tok == 0xFFFFFFFFu || tok >= p.table_rows;
     src = zero ? nullptr : reinterpret_cast<const uint4*>(p.table + (size_t)tok * p.k);
   }
-  float ss = 0.f;
   for (int c = tid; c < kc; c += kThreads) {
     uint4 v;
-    if (IN == kInAddNorm) {
+    if (IN == kInAddNorm || IN == kInAddThenNorm) {
       uint4 a = src[c];
       uint4 b = reinterpret_cast<const uint4*>(p.x2)[c];
       const __half2* ha = reinterpret_cast<const __half2*>(&a);
@@ -64,60 +95,50 @@ __device__ void build_input(const GemvProblem& p, uint4* xs, float* red) {
       __half2* hv = reinterpret_cast<__half2*>(&v);
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        float2 fa = __half22float2(ha[i]);
-        float2 fb = __half22float2(hb[i]);
-        float s0 = __fadd_rn(fa.x, fb.x), s1 = __fadd_rn(fa.y, fb.y);
-        ss = fmaf(s0, s0, ss);
-        ss = fmaf(s1, s1, ss);
-        hv[i] = __floats2half2_rn(s0, s1);
-      }
-      if (blockIdx.x == 0 && p.residual_out)
-        reinterpret_cast<uint4*>(p.residual_out)[c] = v;
-    } else if (IN == kInAddThenNorm) {
-      uint4 a = src[c];
-      uint4 b = reinterpret_cast<const uint4*>(p.x2)[c];
-      const __half2* ha = reinterpret_cast<const __half2*>(&a);
-      const __half2* hb = reinterpret_cast<const __half2*>(&b);
-      __half2* hv = reinterpret_cast<__half2*>(&v);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        hv[i] = __hadd2(ha[i], hb[i]);
-        float2 f = __half22float2(hv[i]);
-        ss = fmaf(f.x, f.x, ss);
-        ss = fmaf(f.y, f.y, ss);
-      }
-      if (blockIdx.x == 0 && p.residual_out)
-        reinterpret_cast<uint4*>(p.residual_out)[c] = v;
-    } else {
-      if (IN == kInEmbedNorm && src == nullptr)
-        v = make_uint4(0, 0, 0, 0);
-      else
-        v = src[c];
-      if (IN == kInEmbedNorm && blockIdx.x == 0 && p.embed_out)
-        reinterpret_cast<uint4*>(p.embed_out)[c] = v;
-      if (IN != kInPlain) {
-        const __half2* hv = reinterpret_cast<const __half2*>(&v);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          float2 f = __half22float2(hv[i]);
-          ss = fmaf(f.x, f.x, ss);
-          ss = fmaf(f.y, f.y, ss);
+        if (IN == kInAddNorm) {
+          float2 fa = __half22float2(ha[i]);
+          float2 fb = __half22float2(hb[i]);
+          hv[i] = __floats2half2_rn(__fadd_rn(fa.x, fb.x), __fadd_rn(fa.y, fb.y));
+        } else {
+          hv[i] = __hadd2(ha[i], hb[i]);
         }
       }
+      if (blockIdx.x == 0 && p.residual_out) reinterpret_cast<uint4*>(p.residual_out)[c] = v;
+    } else {
+      v = (IN == kInEmbedNorm && src == nullptr) ? make_uint4(0, 0, 0, 0) : src[c];
+      if (IN == kInEmbedNorm && blockIdx.x == 0 && p.embed_out)
+        reinterpret_cast<uint4*>(p.embed_out)[c] = v;
     }
     xs[c] = v;
   }
-  if (IN == kInPlain) {
-    __syncthreads();
-    return;
-  }
-  ss = warp_sum(ss);
-  if ((tid & 31) == 0) red[tid >> 5] = ss;
   __syncthreads();
-  float total = 0.f;
+  if (IN == kInPlain) return;
+  if (tid < 32) {
+    float acc = 0.f;
+    for (int c = lane; c < kc; c += 32) {
+      if (IN == kInAddNorm) {
+        // squares of the unrounded sums (matvec2_add_rms_impl)
+        uint4 a = src[c];
+        uint4 b = reinterpret_cast<const uint4*>(p.x2)[c];
+        const __half2* ha = reinterpret_cast<const __half2*>(&a);
+        const __half2* hb = reinterpret_cast<const __half2*>(&b);
 #pragma unroll
-  for (int w = 0; w < kWarps; ++w) total += red[w];
-  float scale = rms_scale(total, p.k, p.eps);
+        for (int i = 0; i < 4; ++i) {
+          float2 fa = __half22float2(ha[i]);
+          float2 fb = __half22float2(hb[i]);
+          float s0 = __fadd_rn(fa.x, fb.x), s1 = __fadd_rn(fa.y, fb.y);
+          acc = __fmaf_rn(s0, s0, acc);
+          acc = __fmaf_rn(s1, s1, acc);
+        }
+      } else {
+        acc = chunk_sq(xs[c], acc);
+      }
+    }
+    float total = canon_butterfly(acc, canon_lanes(p.k));
+    if (lane == 0) *s_scale = rms_scale(total, p.k, p.eps);
+  }
+  __syncthreads();
+  const float scale = *s_scale;
   const uint4* g4 = reinterpret_cast<const uint4*>(p.norm_w);
   for (int c = tid; c < kc; c += kThreads) {
     uint4 v = xs[c];
@@ -137,121 +158,95 @@ __device__ void build_input(const GemvProblem& p, uint4* xs, float* red) {
   __syncthreads();
 }
 
-__device__ __forceinline__ float silu_mul(float g, float u) {
-  // half((g / (1 + exp(-g))) * u) of swiglu_f16, without contraction.
-  return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+__device__ __forceinline__ void argmax_take(float v, uint32_t idx, uint32_t& bk, uint32_t& bi) {
+  if (isfinite(v) && argmax_better(argmax_key(v), idx, bk, bi)) {
+    bk = argmax_key(v);
+    bi = idx;
+  }
 }
 
 template <int IN, int OUT>
-__global__ void __launch_bounds__(kThreads) gemv_fast_kernel(GemvProblem p) {
-  extern __shared__ uint4 xs[];
-  __shared__ float red[kWarps];
+__global__ void __launch_bounds__(kThreads) gemv_staged_kernel(GemvProblem p, Plan plan) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ uint64_t full[2];
+  __shared__ float s_scale;
   __shared__ uint32_t best_key_s[kWarps];
   __shared__ uint32_t best_idx_s[kWarps];
   __shared__ bool is_last;
-  const int lane = threadIdx.x & 31;
-  const int warp = threadIdx.x >> 5;
-  const int warps_total = gridDim.x * kWarps;
-  const int gw = blockIdx.x * kWarps + warp;
+  uint4* xs = reinterpret_cast<uint4*>(smem);
+  uint8_t* stages = smem + plan.x_bytes;
+
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int warp = tid >> 5;
   const int kc = p.k >> 3;
-  const int items = (OUT == kOutSwiglu) ? p.n[0] : p.n[0] + p.n[1] + p.n[2];
+  const int lanes = canon_lanes(p.k);
+  const int items = items_of(p, OUT);
+  const int first = blockIdx.x * plan.rpc;
+  const int last = min(items, first + plan.rpc);
+  const int nchunks = first < last ? (last - first + plan.rps - 1) / plan.rps : 0;
   const uint32_t row_bytes = (uint32_t)p.k * 2u;
 
-  // Independent of the predecessor: warm L2 with this warp's first rows.
-  {
-    int item = gw + lane * warps_total;
-    if (item < items) {
-      if (OUT == kOutSwiglu) {
-        prefetch_l2(p.w[0] + (size_t)item * p.k, row_bytes);
-        prefetch_l2(p.w[1] + (size_t)item * p.k, row_bytes);
-      } else {
-        prefetch_l2(locate(p, item).ptr, row_bytes);
-      }
-    }
+  // Predecessor-independent: start the weight stream.
+  if (tid == 0) {
+    for (int s = 0; s < plan.stages; ++s) pipe::mbar_init(&full[s], 1);
+    pipe::fence_mbar_init();
+    for (int c = 0; c < plan.stages && c < nchunks; ++c)
+      issue_stage<OUT>(p, plan, stages, full, first, last, c);
   }
   pdl_trigger();
   pdl_wait();
-  build_input<IN>(p, xs, red);
+  build_input<IN>(p, xs, &s_scale);
 
   uint32_t best_key = 0, best_idx = 0xFFFFFFFFu;
-  for (int item = gw; item < items; item += 2 * warps_total) {
-    const int item_b = item + warps_total;
-    const bool has_b = item_b < items;
-    const uint4 *r0, *r1, *r2 = nullptr, *r3 = nullptr;
-    RowRef ra{}, rb{};
-    if (OUT == kOutSwiglu) {
-      r0 = reinterpret_cast<const uint4*>(p.w[0] + (size_t)item * p.k);
-      r1 = reinterpret_cast<const uint4*>(p.w[1] + (size_t)item * p.k);
-      if (has_b) {
-        r2 = reinterpret_cast<const uint4*>(p.w[0] + (size_t)item_b * p.k);
-        r3 = reinterpret_cast<const uint4*>(p.w[1] + (size_t)item_b * p.k);
-      }
-    } else {
-      ra = locate(p, item);
-      r0 = reinterpret_cast<const uint4*>(ra.ptr);
-      r1 = nullptr;
-      if (has_b) {
-        rb = locate(p, item_b);
-        r2 = reinterpret_cast<const uint4*>(rb.ptr);
-      }
-    }
-    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
-#pragma unroll 4
-    for (int c = lane; c < kc; c += 32) {
-      uint4 xv = xs[c];
-      uint4 w0 = ld_stream(r0 + c);
-      uint4 w1, w2, w3;
-      if (OUT == kOutSwiglu) w1 = ld_stream(r1 + c);
-      if (has_b) {
-        w2 = ld_stream(r2 + c);
-        if (OUT == kOutSwiglu) w3 = ld_stream(r3 + c);
-      }
-      a0 = dot8(xv, w0, a0);
-      if (OUT == kOutSwiglu) a1 = dot8(xv, w1, a1);
-      if (has_b) {
-        a2 = dot8(xv, w2, a2);
-        if (OUT == kOutSwiglu) a3 = dot8(xv, w3, a3);
-      }
-    }
-    a0 = warp_sum(a0);
-    if (OUT == kOutSwiglu) a1 = warp_sum(a1);
-    if (has_b) {
-      a2 = warp_sum(a2);
-      if (OUT == kOutSwiglu) a3 = warp_sum(a3);
-    }
-    if (lane == 0) {
+  for (int chunk = 0; chunk < nchunks; ++chunk) {
+    const int s = chunk % plan.stages;
+    pipe::mbar_wait(&full[s], (uint32_t)((chunk / plan.stages) & 1), 0x100u | IN);
+    const int i0 = first + chunk * plan.rps;
+    const int cnt = min(plan.rps, last - i0);
+    const uint8_t* st = stages + (size_t)s * plan.stage_bytes;
+    for (int r = warp; r < cnt; r += kWarps) {
+      const uint4* w0 = reinterpret_cast<const uint4*>(st + (size_t)r * row_bytes);
+      float a0 = 0.f, a1 = 0.f;
       if (OUT == kOutSwiglu) {
-        float g = __half2float(__float2half_rn(a0));
-        float u = __half2float(__float2half_rn(a1));
-        p.out[0][item] = __float2half_rn(silu_mul(g, u));
-        if (has_b) {
-          g = __half2float(__float2half_rn(a2));
-          u = __half2float(__float2half_rn(a3));
-          p.out[0][item_b] = __float2half_rn(silu_mul(g, u));
+        const uint4* w1 = reinterpret_cast<const uint4*>(st + (size_t)(cnt + r) * row_bytes);
+        for (int c = lane; c < kc; c += 32) {
+          uint4 xv = xs[c];
+          a0 = chunk_dot(xv, w0[c], a0);
+          a1 = chunk_dot(xv, w1[c], a1);
         }
-      } else if (OUT == kOutResidual) {
-        p.out[0][item] = __hadd(p.res[item], __float2half_rn(a0));
-        if (has_b) p.out[0][item_b] = __hadd(p.res[item_b], __float2half_rn(a2));
+        a1 = canon_butterfly(a1, lanes);
       } else {
-        __half h0 = __float2half_rn(a0);
-        p.out[ra.seg][ra.row] = h0;
-        if (has_b) p.out[rb.seg][rb.row] = __float2half_rn(a2);
-        if (OUT == kOutArgmax) {
-          float v0 = __half2float(h0);
-          if (isfinite(v0) && argmax_better(argmax_key(v0), item, best_key, best_idx)) {
-            best_key = argmax_key(v0);
-            best_idx = item;
-          }
-          if (has_b) {
-            float v1 = __half2float(__float2half_rn(a2));
-            if (isfinite(v1) && argmax_better(argmax_key(v1), item_b, best_key, best_idx)) {
-              best_key = argmax_key(v1);
-              best_idx = item_b;
+        for (int c = lane; c < kc; c += 32) a0 = chunk_dot(xs[c], w0[c], a0);
+      }
+      a0 = canon_butterfly(a0, lanes);
+      if (lane == 0) {
+        const int item = i0 + r;
+        if (OUT == kOutSwiglu) {
+          float g = __half2float(__float2half_rn(a0));
+          float u = __half2float(__float2half_rn(a1));
+          p.out[0][item] = __float2half_rn(silu_mul(g, u));
+        } else if (OUT == kOutResidual) {
+          p.out[0][item] = __hadd(p.res[item], __float2half_rn(a0));
+        } else {
+          int seg = 0, row = item;
+          if (row >= p.n[0]) {
+            row -= p.n[0];
+            seg = 1;
+            if (row >= p.n[1]) {
+              row -= p.n[1];
+              seg = 2;
             }
           }
+          __half h0 = __float2half_rn(a0);
+          p.out[seg][row] = h0;
+          if (OUT == kOutArgmax) argmax_take(__half2float(h0), (uint32_t)item, best_key, best_idx);
         }
       }
     }
+    __syncthreads();
+    if (tid == 0 && chunk + plan.stages < nchunks)
+      issue_stage<OUT>(p, plan, stages, full, first, last, chunk + plan.stages);
   }
 
   if (OUT == kOutArgmax) {
@@ -260,7 +255,7 @@ __global__ void __launch_bounds__(kThreads) gemv_fast_kernel(GemvProblem p) {
       best_idx_s[warp] = best_idx;
     }
     __syncthreads();
-    if (threadIdx.x == 0) {
+    if (tid == 0) {
       uint32_t bk = 0, bi = 0xFFFFFFFFu;
       for (int w = 0; w < kWarps; ++w)
         if (argmax_better(best_key_s[w], best_idx_s[w], bk, bi)) {
@@ -277,7 +272,7 @@ __global__ void __launch_bounds__(kThreads) gemv_fast_kernel(GemvProblem p) {
     if (is_last) {
       __threadfence();
       uint32_t bk = 0, bi = 0xFFFFFFFFu;
-      for (int b = threadIdx.x; b < (int)gridDim.x; b += kThreads) {
+      for (int b = tid; b < (int)gridDim.x; b += kThreads) {
         uint32_t ck = __float_as_uint(__ldcg(p.argmax_partial + b));
         uint32_t ci = __ldcg(p.argmax_index + b);
         if (argmax_better(ck, ci, bk, bi)) {
@@ -299,7 +294,7 @@ __global__ void __launch_bounds__(kThreads) gemv_fast_kernel(GemvProblem p) {
         best_idx_s[warp] = bi;
       }
       __syncthreads();
-      if (threadIdx.x == 0) {
+      if (tid == 0) {
         for (int w = 0; w < kWarps; ++w)
           if (argmax_better(best_key_s[w], best_idx_s[w], bk, bi)) {
             bk = best_key_s[w];
@@ -315,16 +310,21 @@ __global__ void __launch_bounds__(kThreads) gemv_fast_kernel(GemvProblem p) {
 }
 
 // Generic GEMV for any K and alignment (plain input and output only): one
-// warp per row, scalar loads.
+// warp per row with the canonical chunk order, scalar loads.
 __global__ void gemv_generic_kernel(const __half* x, const __half* w, __half* out, int n, int k) {
   int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   int lane = threadIdx.x & 31;
   pdl_wait();
   if (warp >= n) return;
   const __half* row = w + (size_t)warp * k;
+  const int lanes = canon_lanes(k);
+  const int chunks = (k + 7) / 8;
   float acc = 0.f;
-  for (int i = lane; i < k; i += 32) acc = fmaf(__half2float(x[i]), __half2float(row[i]), acc);
-  acc = warp_sum(acc);
+  if (lane < lanes)
+    for (int c = lane; c < chunks; c += lanes)
+      for (int i = 8 * c; i < min(k, 8 * c + 8); ++i)
+        acc = __fmaf_rn(__half2float(x[i]), __half2float(row[i]), acc);
+  acc = canon_butterfly(acc, lanes);
   if (lane == 0) out[warp] = __float2half_rn(acc);
 }
 
@@ -353,24 +353,39 @@ __global__ void matmul_reference_kernel(const __half* x, const __half* w, __half
   if (row < m && col < n) out[(size_t)row * n + col] = __float2half_rn(sum);
 }
 
-template <int IN, int OUT>
-void launch_fast(const Launch& l, const GemvProblem& p) {
-  int items = (OUT == kOutSwiglu) ? p.n[0] : p.n[0] + p.n[1] + p.n[2];
-  int want = (items + kWarps - 1) / kWarps;
-  int cap = l.sm_count * 8;
-  if (OUT == kOutArgmax) cap = l.sm_count * 4;  // bounded partial array
-  int grid = want < cap ? want : cap;
-  if (grid < 1) grid = 1;
-  size_t smem = (size_t)p.k * 2;
-  auto kernel = gemv_fast_kernel<IN, OUT>;
-  if (smem > 48 * 1024) {
-    static bool done = false;
-    if (!done) {
-      cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
-      done = true;
-    }
+Plan make_plan(const GemvProblem& p, int items, int grid, bool pair) {
+  Plan pl;
+  pl.rpc = (items + grid - 1) / grid;
+  pl.x_bytes = ((p.k * 2) + 127) / 128 * 128;
+  int item_bytes = p.k * 2 * (pair ? 2 : 1);
+  int budget = kSmemBudget - pl.x_bytes;
+  if (pl.rpc * item_bytes <= budget) {
+    pl.stages = 1;
+    pl.rps = pl.rpc;
+  } else {
+    pl.stages = 2;
+    pl.rps = budget / 2 / item_bytes;
+    if (pl.rps < 1) pl.rps = 1;
   }
-  launch_kernel(l, dim3(grid), dim3(kThreads), smem, kernel, p);
+  pl.stage_bytes = (pl.rps * item_bytes + 127) / 128 * 128;
+  return pl;
+}
+
+template <int IN, int OUT>
+void launch_staged(const Launch& l, const GemvProblem& p) {
+  int items = (OUT == kOutSwiglu) ? p.n[0] : p.n[0] + p.n[1] + p.n[2];
+  if (items <= 0) return;
+  int grid = items < l.sm_count ? items : l.sm_count;
+  Plan plan = make_plan(p, items, grid, OUT == kOutSwiglu);
+  grid = (items + plan.rpc - 1) / plan.rpc;
+  size_t smem = (size_t)plan.x_bytes + (size_t)plan.stages * plan.stage_bytes;
+  auto kernel = gemv_staged_kernel<IN, OUT>;
+  static bool configured = false;
+  if (!configured) {
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBudget + 1024);
+    configured = true;
+  }
+  launch_kernel(l, dim3(grid), dim3(kThreads), smem, kernel, p, plan);
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
@@ -387,7 +402,7 @@ bool gemv_fast_ok(const GemvProblem& p) {
   return true;
 }
 
-int argmax_grid_cap(int sm_count) { return sm_count * 4; }
+unsigned gemv_status(bool reset) { return pipe::read_status(reset); }
 
 void gemv(const Launch& l, const GemvProblem& p) {
   if (!gemv_fast_ok(p)) {
@@ -401,10 +416,10 @@ void gemv(const Launch& l, const GemvProblem& p) {
     }
     return;
   }
-#define MI_GEMV_CASE(IN, OUT)                      \
-  if (p.in_mode == IN && p.out_mode == OUT) {      \
-    launch_fast<IN, OUT>(l, p);                    \
-    return;                                        \
+#define MI_GEMV_CASE(IN, OUT)                 \
+  if (p.in_mode == IN && p.out_mode == OUT) { \
+    launch_staged<IN, OUT>(l, p);             \
+    return;                                   \
   }
   MI_GEMV_CASE(kInPlain, kOutPlain)
   MI_GEMV_CASE(kInNorm, kOutPlain)

@@ -146,7 +146,13 @@ struct DecodeFused {
   Pos pos;                        // position of the new token (= len - 1)
 };
 void attention_decode_fused(const Launch& l, const DecodeFused& p, int splits, float* scratch,
-                            uint32_t* counters);
+                            uint32_t* counters, int block_keys);
+// Keys per flash-decode block for a cache of `capacity` positions (64 up to
+// 8192 positions, then doubled until at most 128 blocks).
+int decode_block_for(int capacity);
+// Expired-wait codes of the staged kernels (0 = none), optionally cleared.
+unsigned gemv_status(bool reset);
+unsigned attention_status(bool reset);
 // Prefill attention in 32-key blocks, any GQA ratio, head_dim <= 256: with
 // round_p the flash-prefill semantics (FP16 probabilities), without it the
 // FP32 online softmax of the tiled kernel.

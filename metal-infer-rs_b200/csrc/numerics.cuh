@@ -1,0 +1,142 @@
+// The engine's arithmetic contract, shared by every kernel on the decode path
+// and by the small-prompt prefill path (the CPU oracle states the same
+// contract independently, which makes those paths bit-exact):
+//
+//  * DOT(x, y, n): chunks of 8 consecutive elements; chunk c belongs to lane
+//    c mod L, L = min(32, next_pow2(ceil(n / 8))); a lane accumulates its
+//    chunks in increasing order with 8 sequential fused multiply-adds per
+//    chunk; the L lane sums meet in a butterfly (xor L/2, ..., 1). Sums of
+//    squares are DOT(x, x). This is one fixed instance of the reference's
+//    lane-strided loops + simd_sum.
+//  * exp: Cody-Waite reduction n = rint(x log2 e), r = x - n ln2 (two-part
+//    constant), e^r by the degree-7 Taylor polynomial (Horner, fused
+//    multiply-adds), scaled by 2^n.
+//  * rsqrt(v) = 1 / sqrt(v), both correctly rounded.
+//  * RoPE: frequency = float(pow(theta, -2i / d)); cos / sin of the FP32
+//    angle pos * frequency in double precision, rounded once to FP32.
+#pragma once
+
+#include <cuda_fp16.h>
+
+#include <cstdint>
+
+namespace mi {
+namespace k {
+
+__device__ __forceinline__ float mi_exp(float x) {
+  if (x != x) return x;
+  if (x > 89.0f) return __int_as_float(0x7f800000);
+  if (x < -104.0f) return 0.0f;
+  const float kLog2e = 0x1.715476p+0f;
+  const float kLn2Hi = 0x1.62e4p-1f;
+  const float kLn2Lo = 0x1.7f7d1cp-20f;
+  float n = rintf(__fmul_rn(x, kLog2e));
+  float r = __fmaf_rn(n, -kLn2Hi, x);
+  r = __fmaf_rn(n, -kLn2Lo, r);
+  float p = 0x1.a01a02p-13f;
+  p = __fmaf_rn(p, r, 0x1.6c16c2p-10f);
+  p = __fmaf_rn(p, r, 0x1.111112p-7f);
+  p = __fmaf_rn(p, r, 0x1.555556p-5f);
+  p = __fmaf_rn(p, r, 0x1.555556p-3f);
+  p = __fmaf_rn(p, r, 0.5f);
+  p = __fmaf_rn(p, r, 1.0f);
+  p = __fmaf_rn(p, r, 1.0f);
+  int ni = (int)n;
+  if (ni < -126)
+    return __fmul_rn(__fmul_rn(p, __int_as_float((ni + 64 + 127) << 23)),
+                     __int_as_float((-64 + 127) << 23));
+  if (ni > 127) return __fmul_rn(__fmul_rn(p, __int_as_float((127 + 127) << 23)), 2.0f);
+  return __fmul_rn(p, __int_as_float((ni + 127) << 23));
+}
+
+// Lanes of the canonical reduction for n elements.
+__host__ __device__ __forceinline__ int canon_lanes(int n) {
+  int chunks = (n + 7) / 8;
+  int l = 1;
+  while (l < chunks && l < 32) l <<= 1;
+  return l;
+}
+
+// Butterfly over `lanes` lanes of a warp (lanes a power of two <= 32); every
+// lane of each group ends with the group's sum.
+__device__ __forceinline__ float canon_butterfly(float v, int lanes) {
+  for (int o = lanes >> 1; o >= 1; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// 8 sequential fused multiply-adds of one chunk (FP16 x FP16).
+__device__ __forceinline__ float chunk_dot(const uint4& a, const uint4& b, float acc) {
+  const __half2* x = reinterpret_cast<const __half2*>(&a);
+  const __half2* y = reinterpret_cast<const __half2*>(&b);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float2 fx = __half22float2(x[i]);
+    float2 fy = __half22float2(y[i]);
+    acc = __fmaf_rn(fx.x, fy.x, acc);
+    acc = __fmaf_rn(fx.y, fy.y, acc);
+  }
+  return acc;
+}
+
+// Sum of squares of one FP16 chunk.
+__device__ __forceinline__ float chunk_sq(const uint4& a, float acc) { return chunk_dot(a, a, acc); }
+
+// Single-thread canonical DOT of FP32 q (8 consecutive per chunk) with an
+// FP16 row, n % 8 == 0, n <= 256: one partial per chunk, then the butterfly
+// tree in registers.
+template <int N>
+__device__ __forceinline__ float canon_dot_thread(const float* q, const uint4* row) {
+  constexpr int kChunks = N / 8;
+  constexpr int kLanes = kChunks <= 1 ? 1 : kChunks <= 2 ? 2 : kChunks <= 4 ? 4 : kChunks <= 8 ? 8 : kChunks <= 16 ? 16 : 32;
+  float v[kLanes];
+#pragma unroll
+  for (int c = 0; c < kLanes; ++c) v[c] = 0.f;
+#pragma unroll
+  for (int c = 0; c < kChunks; ++c) {
+    uint4 w = row[c];
+    const __half2* hw = reinterpret_cast<const __half2*>(&w);
+    float acc = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float2 f = __half22float2(hw[i]);
+      acc = __fmaf_rn(q[8 * c + 2 * i], f.x, acc);
+      acc = __fmaf_rn(q[8 * c + 2 * i + 1], f.y, acc);
+    }
+    v[c] = acc;
+  }
+#pragma unroll
+  for (int step = kLanes / 2; step >= 1; step >>= 1)
+#pragma unroll
+    for (int l = 0; l < step; ++l) v[l] = __fadd_rn(v[l], v[l + step]);
+  return v[0];
+}
+
+// RoPE terms of (position, pair).
+__device__ __forceinline__ void rope_cs(uint32_t pos, int pair, int head_dim, float theta,
+                                        float* c, float* s) {
+  float exponent = __fdiv_rn(-(float)(pair * 2), (float)head_dim);
+  float frequency = (float)pow((double)theta, (double)exponent);
+  float angle = __fmul_rn((float)pos, frequency);
+  double sd, cd;
+  sincos((double)angle, &sd, &cd);
+  *c = (float)cd;
+  *s = (float)sd;
+}
+
+// x * scale * g with both products rounded.
+__device__ __forceinline__ float norm_mul(float x, float scale, float g) {
+  return __fmul_rn(__fmul_rn(x, scale), g);
+}
+
+// rsqrt(total / width + eps), correctly rounded 1 / sqrt.
+__device__ __forceinline__ float rms_scale(float total, int width, float eps) {
+  return __frcp_rn(__fsqrt_rn(__fadd_rn(__fdiv_rn(total, (float)width), eps)));
+}
+
+// SwiGLU of swiglu_f16: (g / (1 + exp(-g))) * u.
+__device__ __forceinline__ float silu_mul(float g, float u) {
+  return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, mi_exp(-g))), u);
+}
+
+}  // namespace k
+}  // namespace mi

@@ -527,10 +527,13 @@ mi_tensor* attention_impl(mi_batch* b, const mi_tensor* query, const mi_tensor* 
         size_t available = config.causal ? std::min(kv_len, config.query_offset + 1) : kv_len;
         if (available == 0)
           fail(MI_ERR_SHAPE, "invalid tensor shape: flash decode requires at least one available key");
-      } else {
-        block_keys = 32;
       }
       size_t available = config.causal ? std::min(kv_len, config.query_offset + 1) : kv_len;
+      if (kind == MI_ATTENTION_DECODE_SPLIT_KV) {
+        // attention_decode_f16 (transformer.metal:1824-1909): one block over
+        // all keys, interleaved streams merged at the end.
+        block_keys = std::max<size_t>(64, (available + 63) / 64 * 64);
+      }
       int splits = (int)std::max<size_t>(1, std::min<size_t>((available + block_keys - 1) / block_keys,
                                                               4096));
       int group = (int)(qh / kh);

@@ -78,7 +78,8 @@ struct Layer {
 struct Workspace {
   TensorRef q_raw, k_raw, v_raw, attn, attn_o, residual, hidden, act, logits;
   TensorRef argmax_pv, argmax_pi, counters, attn_scratch;
-  int attn_splits = 0;
+  int attn_splits = 0;  // flash-decode blocks for the largest cache seen
+  int attn_block = 64;  // keys per flash-decode block
   size_t attn_cap = 0;
 };
 
@@ -186,11 +187,13 @@ void ensure_workspace(mi_qwen3* m, size_t capacity) {
   }
   if (capacity > w.attn_cap) {
     int kvh = (int)c.num_key_value_heads;
-    int splits = k::attention_decode_splits((int)capacity, kvh, ctx->sm_count, 32);
+    int block = k::decode_block_for((int)capacity);
+    int splits = ((int)capacity + block - 1) / block;
     int group = (int)(c.num_attention_heads / c.num_key_value_heads);
     size_t bytes = k::attention_decode_scratch(kvh, splits, group, (int)c.head_dim);
     w.attn_scratch = TensorRef(new_tensor(ctx, {bytes / 4}, MI_F32, true));
     w.attn_splits = splits;
+    w.attn_block = block;
     w.attn_cap = capacity;
     m->plan_version++;
   }
@@ -263,7 +266,7 @@ void encode_decode_step(mi_qwen3* m, mi_kv_cache* c) {
       d.pos.dev = len;
       ProfileScope ps(m->ctx, "attention_decode");
       k::attention_decode_fused(dlaunch(m, true), d, w.attn_splits, w.attn_scratch.t->f32(),
-                                w.counters.t->u32() + 1);
+                                w.counters.t->u32() + 1, k::decode_block_for((int)c->capacity));
     }
     // 3. O projection
     {
@@ -435,7 +438,9 @@ void layer_prefill(mi_qwen3* m, mi_kv_cache* c, size_t li, __half* hidden, size_
     k::attention_reference(l, a);
   } else if (kind == MI_ATTENTION_DECODE_SPLIT_KV) {
     auto& w = m->ws;
-    k::attention_decode(l, a, w.attn_splits, 32, w.attn_scratch.t->f32(), w.counters.t->u32() + 1);
+    int block = k::decode_block_for((int)c->capacity);
+    k::attention_decode(l, a, ((int)(off + T) + block - 1) / block, block,
+                        w.attn_scratch.t->f32(), w.counters.t->u32() + 1);
   } else {
     a.round_p = kind == MI_ATTENTION_FLASH_PREFILL ? 1 : 0;
     k::attention_prefill(l, a);
@@ -458,6 +463,13 @@ void layer_prefill(mi_qwen3* m, mi_kv_cache* c, size_t li, __half* hidden, size_
   __half* down = s.f16({T, (size_t)h});
   k::gemm(l, act, L.w[kDown].h(), down, t, h, I, h);
   k::add(l, residual, down, hidden, T * h);
+}
+
+void check_capacity_from(mi_kv_cache* c, size_t from, size_t count) {
+  size_t requested = from + count;
+  if (requested > c->capacity)
+    fail(MI_ERR_CACHE_CAPACITY, "KV cache capacity %zu exceeded by requested length %zu",
+         c->capacity, requested);
 }
 
 void check_capacity(mi_kv_cache* c, size_t count) {
@@ -726,7 +738,8 @@ mi_status mi_qwen3_prefill(mi_qwen3* m, const uint32_t* tokens, size_t count, mi
     check_cache(m, cache);
     if (count == 0) fail(MI_ERR_CONFIG, "invalid model configuration: prefill requires at least one token");
     require(tokens, "tokens");
-    cache->filled = 0;
+    cache->filled = 0;  // KvCache::reset, then the capacity check (qwen3.rs:366, 617-624)
+    set_dev_len(cache, 0);
     check_capacity(cache, count);
     Timer t(m->ctx->stream);
     upload_tokens(cache, tokens, count, 0);
@@ -774,7 +787,8 @@ mi_status mi_qwen3_prefill_argmax(mi_qwen3* m, const uint32_t* tokens, size_t co
     require(output, "output");
     if (output->dtype != MI_U32 || output->len() != 1)
       fail(MI_ERR_CONFIG, "invalid model configuration: argmax output must be one u32");
-    cache->filled = 0;
+    cache->filled = 0;  // KvCache::reset, then the capacity check (qwen3.rs:366, 617-624)
+    set_dev_len(cache, 0);
     check_capacity(cache, count);
     Timer t(m->ctx->stream);
     upload_tokens(cache, tokens, count, 0);
@@ -840,6 +854,7 @@ size_t generate_greedy(mi_qwen3* m, mi_kv_cache* c, const uint32_t* prompt, size
   if (prompt_len == 0)
     fail(MI_ERR_CONFIG, "invalid model configuration: prefill requires at least one token");
   c->filled = 0;
+  set_dev_len(c, 0);
   check_capacity(c, prompt_len);
   // Decode steps needed: max_tokens - 1 (the first id comes from prefill).
   size_t steps = max_tokens - 1;

@@ -310,6 +310,8 @@ mi_status mi_context_kernel_status(mi_context* ctx, uint32_t* code) {
     require_ctx(code, "code");
     sync_context(ctx);
     *code = k::gemm_tc_status(true);
+    if (unsigned g = k::gemv_status(true)) *code = *code ? *code : g;
+    if (unsigned a = k::attention_status(true)) *code = *code ? *code : a;
   });
   if (st == MI_OK && *code != 0) {
     set_error("a bounded device wait expired (code %u)", *code);

@@ -89,14 +89,32 @@ void or_copy_into_cache(const uint16_t* src, size_t tokens, size_t stride,
                         size_t offset, uint16_t* cache);
 
 /* Attention semantics. OR_ATTN_REFERENCE is the two-pass FP32 softmax of
- * attention_reference_f16 (transformer.metal:1579-1612), which is also the
- * semantics of every decode and tiled variant. OR_ATTN_FLASH_PREFILL rounds
- * the probabilities to FP16 per 32-key block (transformer.metal:1669-1822). */
-enum { OR_ATTN_REFERENCE = 0, OR_ATTN_FLASH_PREFILL = 1 };
+ * attention_reference_f16 (transformer.metal:1579-1612). OR_ATTN_TILED and
+ * OR_ATTN_FLASH_PREFILL process keys in 32-key blocks with an online softmax
+ * (transformer.metal:1614-1822); flash prefill rounds the probabilities to
+ * FP16 before they weight V. */
+enum { OR_ATTN_REFERENCE = 0, OR_ATTN_FLASH_PREFILL = 1, OR_ATTN_TILED = 2 };
 void or_attention(const uint16_t* q, const uint16_t* k, const uint16_t* v,
                   size_t tokens, size_t q_heads, size_t kv_heads,
                   size_t head_dim, size_t kv_length, int causal,
                   size_t query_offset, int semantics, uint16_t* out);
+/* One-query flash decode (transformer.metal:2127-2316) over `length` keys:
+ * blocks of `block` keys, `streams` interleaved online-softmax streams per
+ * block, log-sum-exp merges in index order. */
+void or_attention_decode(const uint16_t* q, const uint16_t* k, const uint16_t* v,
+                         size_t q_heads, size_t kv_heads, size_t head_dim,
+                         size_t length, size_t block, size_t streams,
+                         uint16_t* out);
+/* Decode block size used for a cache of `capacity` positions, and the
+ * stream count for a head dimension. */
+size_t or_decode_block(size_t capacity);
+size_t or_decode_streams(size_t head_dim);
+
+/* ---- numerics primitives (for direct checks) ---------------------------- */
+void or_exp(const float* in, float* out, size_t n);
+float or_dot(const float* x, const float* y, size_t n);
+void or_rope_cs(size_t position, size_t pair, size_t head_dim, float theta,
+                float* c, float* s);
 
 /* ---- Qwen3 model (qwen3.rs:602-796) ----------------------------------- */
 typedef struct or_qwen3_config {

@@ -51,6 +51,9 @@ def lib():
         L = ctypes.CDLL(LIB_PATH)
         L.or_argmax.restype = ctypes.c_uint32
         L.or_num_threads.restype = ctypes.c_int
+        L.or_dot.restype = ctypes.c_float
+        L.or_decode_block.restype = _sz
+        L.or_decode_streams.restype = _sz
         L.or_qwen3_create_random.restype = ctypes.c_void_p
         L.or_qwen3_create_random.argtypes = [ctypes.POINTER(Qwen3Config), ctypes.c_uint64,
                                              ctypes.c_double, _sz]
@@ -231,6 +234,49 @@ def copy_into_cache(src, cache, offset):
 
 REFERENCE = 0
 FLASH_PREFILL = 1
+TILED = 2
+
+
+def attention_decode(q, k, v, q_heads, kv_heads, head_dim, block=64, streams=None):
+    """One-query flash decode over all keys of k/v (see oracle.h)."""
+    q = np.ascontiguousarray(q, np.uint16)
+    k = np.ascontiguousarray(k, np.uint16)
+    v = np.ascontiguousarray(v, np.uint16)
+    length = k.size // (kv_heads * head_dim)
+    if streams is None:
+        streams = decode_streams(head_dim)
+    out = np.empty((1, q_heads, head_dim), np.uint16)
+    lib().or_attention_decode(_p16(q), _p16(k), _p16(v), _sz(q_heads), _sz(kv_heads),
+                              _sz(head_dim), _sz(length), _sz(block), _sz(streams), _p16(out))
+    return out
+
+
+def decode_block(capacity: int) -> int:
+    return int(lib().or_decode_block(_sz(capacity)))
+
+
+def decode_streams(head_dim: int) -> int:
+    return int(lib().or_decode_streams(_sz(head_dim)))
+
+
+def exp(values) -> np.ndarray:
+    a = np.ascontiguousarray(np.asarray(values, np.float32).ravel())
+    out = np.empty_like(a)
+    lib().or_exp(a.ctypes.data_as(_f32p), out.ctypes.data_as(_f32p), _sz(a.size))
+    return out
+
+
+def dot(x, y) -> float:
+    x = np.ascontiguousarray(np.asarray(x, np.float32).ravel())
+    y = np.ascontiguousarray(np.asarray(y, np.float32).ravel())
+    return float(lib().or_dot(x.ctypes.data_as(_f32p), y.ctypes.data_as(_f32p), _sz(x.size)))
+
+
+def rope_cs(position: int, pair: int, head_dim: int, theta: float):
+    c, s = ctypes.c_float(), ctypes.c_float()
+    lib().or_rope_cs(_sz(position), _sz(pair), _sz(head_dim), ctypes.c_float(theta),
+                     ctypes.byref(c), ctypes.byref(s))
+    return c.value, s.value
 
 
 def attention(q, k, v, q_heads, kv_heads, head_dim, causal=True, query_offset=0,

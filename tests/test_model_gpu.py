@@ -1,8 +1,10 @@
 """GPU parity of the Qwen3 forward (prefill + greedy decode) against the oracle.
 
 Bars: identical greedy token ids over the decode
-horizon; logits within 1e-2 relative (max |gpu - oracle| / max |oracle|);
-hidden states per op within 2e-3 relative.
+horizon; logits within 1e-2 relative and hidden states per op within 2e-3.
+The decode path and prompts up to 512 tokens run the engine's canonical
+arithmetic, which the oracle restates, so logits, caches and hidden states
+are compared bit for bit (a stronger bar than the tolerances).
 """
 import json
 import os
@@ -25,6 +27,14 @@ def rel_err(actual_bits, expected_bits):
     a = O.f32(np.asarray(actual_bits).ravel())
     e = O.f32(np.asarray(expected_bits).ravel())
     return float(np.max(np.abs(a - e)) / max(float(np.max(np.abs(e))), 1e-6))
+
+
+def exact(actual_bits, expected_bits):
+    a = np.asarray(actual_bits, np.uint16).ravel()
+    e = np.asarray(expected_bits, np.uint16).ravel()
+    bad = np.nonzero(a != e)[0]
+    assert a.shape == e.shape and bad.size == 0, (
+        f"{bad.size} values differ (rel err {rel_err(a, e):.2e}); first at {bad[:1]}")
 
 
 def small_cfg(layers=2, vocab=4096, **kw):
@@ -57,13 +67,11 @@ def test_prefill_logits_and_cache_match_oracle(small, prompt_len):
     logits = model.prefill(prompt, cache).f16_bits()
     ref.reset()
     ref_logits = ref.forward(prompt)
-    assert rel_err(logits, ref_logits) <= LOGIT_REL
+    exact(logits, ref_logits)
     assert len(cache) == prompt_len
     k0, v0 = cache.layer(1)
-    kk = k0.f16_bits().reshape(256, -1)[:prompt_len]
-    assert rel_err(kk, ref.cache(1, False, prompt_len)) <= HIDDEN_REL
-    vv = v0.f16_bits().reshape(256, -1)[:prompt_len]
-    assert rel_err(vv, ref.cache(1, True, prompt_len)) <= HIDDEN_REL
+    exact(k0.f16_bits().reshape(256, -1)[:prompt_len], ref.cache(1, False, prompt_len))
+    exact(v0.f16_bits().reshape(256, -1)[:prompt_len], ref.cache(1, True, prompt_len))
 
 
 @pytest.mark.parametrize("graphs", [True, False])
@@ -80,8 +88,7 @@ def test_decode_logits_match_oracle(small, graphs):
             tok = int((step * 7919 + 13) % cfg["vocab_size"])
             logits = model.decode(tok, cache).f16_bits()
             ref_logits = ref.forward(np.array([tok], np.uint32))
-            assert rel_err(logits, ref_logits) <= LOGIT_REL, step
-            assert mi_argmax(logits) == O.argmax(ref_logits), step
+            exact(logits, ref_logits)
         assert len(cache) == 52
     finally:
         model.set_decode_graphs(True)
@@ -193,10 +200,9 @@ def test_unfused_options_match_oracle(ctx):
     ref.set_fusion(qk_rope_cache=False, add_rms_norm=False)
     prompt = O.gen_tokens(6, INPUT_STREAM, 35, cfg["vocab_size"])
     cache = model.kv_cache(128)
-    assert rel_err(model.prefill(prompt, cache).f16_bits(), ref.forward(prompt)) <= LOGIT_REL
+    exact(model.prefill(prompt, cache).f16_bits(), ref.forward(prompt))
     for tok in (3, 99, 1234):
-        got = model.decode(tok, cache).f16_bits()
-        assert rel_err(got, ref.forward(np.array([tok], np.uint32))) <= LOGIT_REL
+        exact(model.decode(tok, cache).f16_bits(), ref.forward(np.array([tok], np.uint32)))
 
 
 @pytest.mark.parametrize("heads", [(32, 8), (64, 8), (16, 16)])
@@ -227,7 +233,7 @@ def test_config0_one_block_matches_oracle(ctx):
         outs.append(model.forward_hidden(x, cache).f16_bits())
     got = np.concatenate([o.reshape(-1, h) for o in outs])
     assert got.shape == golden.shape
-    assert rel_err(got, golden) <= HIDDEN_REL
+    exact(got, golden)
     assert len(cache) == 80
 
 
@@ -240,8 +246,7 @@ def test_config2_greedy_tokens_identical_to_golden(ctx):
     prompt = O.gen_tokens(g["seed"], g["prompt_stream"], g["prompt_len"], cfg["vocab_size"])
     cache = model.kv_cache(2048)
     logits = model.prefill(prompt, cache).f16_bits().ravel()
-    np.testing.assert_allclose(O.f32(logits[:16]), O.f32(np.array(g["prefill_logits_head"], np.uint16)),
-                               atol=LOGIT_REL * float(np.max(np.abs(O.f32(logits)))))
+    exact(logits[:16], np.array(g["prefill_logits_head"], np.uint16))
     ids = model.generate(prompt, g["max_tokens"], cache)
     want = np.array(g["ids"], np.uint32)
     if not np.array_equal(ids, want):

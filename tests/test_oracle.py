@@ -189,6 +189,52 @@ def test_half_add_is_correctly_rounded():
     np.testing.assert_array_equal(O.add(a, b), expected)
 
 
+def test_exp_accuracy_and_special_values():
+    rng = np.random.default_rng(1)
+    x = np.concatenate([rng.uniform(-104, 88.5, 200000), rng.uniform(-1, 1, 100000),
+                        -np.abs(rng.standard_normal(100000)) * 10]).astype(np.float32)
+    got = O.exp(x).astype(np.float64)
+    want = np.exp(x.astype(np.float64))
+    ok = want > np.finfo(np.float32).tiny  # normal results
+    ulp = np.spacing(want[ok].astype(np.float32)).astype(np.float64)
+    assert np.max(np.abs(got[ok] - want[ok]) / ulp) <= 2.0
+    special = O.exp(np.array([0.0, -np.inf, np.inf, 100.0, -200.0, np.nan], np.float32))
+    assert special[0] == 1.0 and special[1] == 0.0 and np.isinf(special[2])
+    assert np.isinf(special[3]) and special[4] == 0.0 and np.isnan(special[5])
+
+
+def test_canonical_dot_order_and_fast_path():
+    rng = np.random.default_rng(2)
+    for k in (8, 65, 128, 256, 1024, 3072):
+        x = f16(rng.standard_normal(k))
+        w = f16(rng.standard_normal(k) * 0.02)
+        xf, wf = O.f32(x), O.f32(w)
+        # the matmul's vector path equals the scalar canonical DOT bit for bit
+        got = O.matmul(x.reshape(1, k), w.reshape(1, k))[0, 0]
+        assert got == f16([O.dot(xf, wf)])[0]
+        assert abs(O.dot(xf, wf) - float(np.dot(xf.astype(np.float64), wf))) < 1e-4
+
+
+def test_rope_terms_are_double_precision_trig():
+    for pos, pair in ((0, 0), (1, 5), (777, 31), (33000, 63), (2047, 17)):
+        c, s = O.rope_cs(pos, pair, 128, 1e6)
+        freq = np.float32(1e6 ** np.float64(np.float32(-(2 * pair)) / np.float32(128)))
+        ang = np.float32(np.float32(pos) * freq)
+        assert c == np.float32(np.cos(np.float64(ang))) and s == np.float32(np.sin(np.float64(ang)))
+
+
+@pytest.mark.parametrize("length", [1, 63, 64, 65, 300, 2048])
+def test_flash_decode_semantics_match_reference(length):
+    rng = np.random.default_rng(length)
+    q = f16(rng.standard_normal(16 * 128))
+    k = f16(rng.standard_normal(length * 8 * 128))
+    v = f16(rng.standard_normal(length * 8 * 128))
+    ref = O.attention(q, k, v, 16, 8, 128, True, length - 1)
+    for block in (32, 64, 256):
+        got = O.attention_decode(q, k, v, 16, 8, 128, block=block)
+        close(got, O.f32(ref), tol=4e-3)
+
+
 def test_f16_conversion_round_to_nearest_even():
     vals = np.array([1.0 + 2.0 ** -11, 1.0 + 3 * 2.0 ** -11, 65519.0, 65520.0, 2.0 ** -25,
                      3 * 2.0 ** -26, -0.0], np.float32)
