@@ -536,8 +536,12 @@ int attention_decode_splits(int kv_len_max, int kvh, int sm_count, int block_key
 
 void attention_decode(const Launch& l, const AttnProblem& p, int splits, int block_keys,
                       float* scratch, uint32_t* counters) {
-  if (p.hd != 128 || (p.qh / p.kvh) > 8 || ((p.qh / p.kvh) & ((p.qh / p.kvh) - 1)) ||
-      block_keys % 8 || (block_keys > kTile && block_keys % kTile)) {
+  const bool aligned =
+      ((reinterpret_cast<uintptr_t>(p.q) | reinterpret_cast<uintptr_t>(p.k) |
+        reinterpret_cast<uintptr_t>(p.v)) & 15) == 0;
+  if (!aligned || p.hd != 128 || (p.qh / p.kvh) > 8 ||
+      ((p.qh / p.kvh) & ((p.qh / p.kvh) - 1)) || block_keys % 8 ||
+      (block_keys > kTile && block_keys % kTile)) {
     attention_reference(l, p);
     return;
   }
@@ -588,7 +592,9 @@ void attention_prefill(const Launch& l, const AttnProblem& p) {
   if (p.tokens * p.qh <= 0) return;
   dim3 grid((p.tokens + kPrefillWarps - 1) / kPrefillWarps, p.qh);
   dim3 block(kPrefillWarps * 32);
-  switch (p.hd) {
+  const bool aligned =
+      ((reinterpret_cast<uintptr_t>(p.k) | reinterpret_cast<uintptr_t>(p.v)) & 15) == 0;
+  switch (aligned ? p.hd : 0) {
     case 64: launch_kernel(l, grid, block, 0, attention_prefill_kernel<64>, p); return;
     case 128: launch_kernel(l, grid, block, 0, attention_prefill_kernel<128>, p); return;
     case 256: launch_kernel(l, grid, block, 0, attention_prefill_kernel<256>, p); return;

@@ -465,13 +465,6 @@ void layer_prefill(mi_qwen3* m, mi_kv_cache* c, size_t li, __half* hidden, size_
   k::add(l, residual, down, hidden, T * h);
 }
 
-void check_capacity_from(mi_kv_cache* c, size_t from, size_t count) {
-  size_t requested = from + count;
-  if (requested > c->capacity)
-    fail(MI_ERR_CACHE_CAPACITY, "KV cache capacity %zu exceeded by requested length %zu",
-         c->capacity, requested);
-}
-
 void check_capacity(mi_kv_cache* c, size_t count) {
   size_t requested = c->filled + count;
   if (requested > c->capacity)
