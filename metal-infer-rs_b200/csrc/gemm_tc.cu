@@ -31,7 +31,7 @@ __device__ unsigned int mi_tc_status = 0;
 constexpr int BM = 128;
 constexpr int BK = 64;  // halves per stage = one 128-byte swizzle row
 constexpr int kThreads = 192;
-constexpr uint32_t kWaitLimit = 1u << 26;
+constexpr uint64_t kWaitNs = 200ull * 1000 * 1000;  // give up after 200 ms
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -60,11 +60,22 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Bounded wait; returns false (and records `code`) when the limit expires.
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Bounded on time (a single try_wait may suspend for a while).
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned code) {
-  for (uint32_t i = 0; i < kWaitLimit; ++i)
-    if (mbar_try_wait(bar, parity)) return true;
-  atomicCAS(&mi_tc_status, 0u, code);
-  return false;
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t start = global_ns();
+  while (!mbar_try_wait(bar, parity))
+    if (global_ns() - start > kWaitNs) {
+      atomicCAS(&mi_tc_status, 0u, code);
+      return false;
+    }
+  return true;
 }
 
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar,

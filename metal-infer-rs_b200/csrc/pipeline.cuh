@@ -15,7 +15,16 @@ namespace pipe {
 
 static __device__ unsigned g_wait_status = 0;
 
-constexpr uint32_t kWaitLimit = 1u << 26;
+// A wait gives up after kWaitNs nanoseconds of the global timer (one
+// try_wait may itself suspend for a while, so the bound is on time, not on
+// the number of polls).
+constexpr uint64_t kWaitNs = 200ull * 1000 * 1000;
+
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -48,10 +57,14 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned code) {
-  for (uint32_t i = 0; i < kWaitLimit; ++i)
-    if (mbar_try_wait(bar, parity)) return true;
-  atomicCAS(&g_wait_status, 0u, code);
-  return false;
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t start = global_ns();
+  while (!mbar_try_wait(bar, parity))
+    if (global_ns() - start > kWaitNs) {
+      atomicCAS(&g_wait_status, 0u, code);
+      return false;
+    }
+  return true;
 }
 
 // 1-D bulk copy global -> shared completing on `bar` (no multicast).
