@@ -93,12 +93,13 @@ struct DecodeArgs {
 
 // Per-head RMSNorm + RoPE of one 128-dim head held by a half-warp (lane li
 // owns dims 8 li .. 8 li + 7; the rotation partner of dim d is d +- 64, lane
-// li ^ 8). Returns the FP16-rounded rotated values as floats.
+// li ^ 8). Returns the FP16-rounded rotated values as floats. `mask` names
+// the lanes of the warp executing the call (one or both half-warps).
 __device__ __forceinline__ void norm_rope_half(const uint4& raw, const __half* w, uint32_t pos,
                                                float theta, float eps, bool round_norm,
-                                               float (&out)[8]) {
+                                               unsigned mask, float (&out)[8]) {
   const int li = threadIdx.x & 15;
-  float total = canon_butterfly(chunk_sq(raw, 0.f), 16);
+  float total = canon_butterfly_mask(chunk_sq(raw, 0.f), 16, mask);
   float scale = rms_scale(total, HD, eps);
   const __half2* hr = reinterpret_cast<const __half2*>(&raw);
   uint4 wr = reinterpret_cast<const uint4*>(w)[li];
@@ -117,7 +118,7 @@ __device__ __forceinline__ void norm_rope_half(const uint4& raw, const __half* w
   const bool first = li < 8;
 #pragma unroll
   for (int e = 0; e < 8; ++e) {
-    float partner = __shfl_xor_sync(0xffffffffu, nx[e], 8);
+    float partner = __shfl_xor_sync(mask, nx[e], 8);
     int d = 8 * li + e;
     int pair = first ? d : d - HD / 2;
     float c, s;
@@ -186,11 +187,13 @@ __global__ void __launch_bounds__(kDecodeThreads) attention_decode_kernel(Decode
 
   // Queries of this group (and, fused, the new key / value).
   if (hw < G) {
+    // Both half-warps of this warp take a head unless G is odd here.
+    const unsigned mask = (warp * 2 + 1 < G) ? 0xffffffffu : 0x0000ffffu;
     const __half* qsrc = a.q + (size_t)(g_kv * G + hw) * HD;
     uint4 raw = reinterpret_cast<const uint4*>(qsrc)[li];
     float qv[8];
     if (a.fused) {
-      norm_rope_half(raw, a.q_norm, (uint32_t)pos, a.theta, a.eps, a.round_norm != 0, qv);
+      norm_rope_half(raw, a.q_norm, (uint32_t)pos, a.theta, a.eps, a.round_norm != 0, mask, qv);
     } else {
       const __half2* hr = reinterpret_cast<const __half2*>(&raw);
 #pragma unroll
@@ -206,7 +209,8 @@ __global__ void __launch_bounds__(kDecodeThreads) attention_decode_kernel(Decode
   if (a.fused && pos >= begin && pos < end && warp == 3 && lane >= 16) {
     uint4 raw = reinterpret_cast<const uint4*>(a.k_raw + (size_t)g_kv * HD)[li];
     float kv[8];
-    norm_rope_half(raw, a.k_norm, (uint32_t)pos, a.theta, a.eps, a.round_norm != 0, kv);
+    norm_rope_half(raw, a.k_norm, (uint32_t)pos, a.theta, a.eps, a.round_norm != 0, 0xffff0000u,
+                   kv);
     uint4 kk;
     __half2* hk = reinterpret_cast<__half2*>(&kk);
 #pragma unroll
@@ -246,14 +250,19 @@ __global__ void __launch_bounds__(kDecodeThreads) attention_decode_kernel(Decode
       pipe::cp_async_wait_all();
     __syncthreads();
     // Stream hw takes block-relative keys hw, hw + 8, ... (tiles are
-    // multiples of 8 keys, so the order is the block's).
-    for (int r = hw; r < j1 - j0; r += kStreams) {
+    // multiples of 8 keys, so the order is the block's). Both half-warps of
+    // a warp run the same trip count (the shuffles span the whole warp); a
+    // half-warp past the end computes on zeros and keeps its state.
+    const int count = j1 - j0;
+    for (int base = warp * 2; base < count; base += kStreams) {
+      const int r = base + (lane >> 4);
+      const bool valid = r < count;
       const int j = j0 + r;
-      uint4 kk, vv;
-      if (j == pos) {
+      uint4 kk = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
+      if (valid && j == pos) {
         kk = reinterpret_cast<const uint4*>(sm.new_k)[li];
         vv = reinterpret_cast<const uint4*>(sm.new_v)[li];
-      } else {
+      } else if (valid) {
         kk = reinterpret_cast<const uint4*>(sm.k[buf][r])[li];
         vv = reinterpret_cast<const uint4*>(sm.v[buf][r])[li];
       }
@@ -275,6 +284,7 @@ __global__ void __launch_bounds__(kDecodeThreads) attention_decode_kernel(Decode
 #pragma unroll
         for (int e = 0; e < 8; ++e) d = __fmaf_rn(qreg[g][e], kf[e], d);
         float s = __fmul_rn(canon_butterfly(d, 16), scale);
+        if (!valid) continue;
         float nm = fmaxf(m[g], s);
         float pa = mi_exp(__fsub_rn(m[g], nm));
         float pc = mi_exp(__fsub_rn(s, nm));

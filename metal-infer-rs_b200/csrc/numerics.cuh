@@ -64,6 +64,13 @@ __device__ __forceinline__ float canon_butterfly(float v, int lanes) {
   return v;
 }
 
+// The same over a subset of a warp: `mask` names exactly the lanes that
+// execute the call (every xor partner must be in it).
+__device__ __forceinline__ float canon_butterfly_mask(float v, int lanes, unsigned mask) {
+  for (int o = lanes >> 1; o >= 1; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(mask, v, o));
+  return v;
+}
+
 // 8 sequential fused multiply-adds of one chunk (FP16 x FP16).
 __device__ __forceinline__ float chunk_dot(const uint4& a, const uint4& b, float acc) {
   const __half2* x = reinterpret_cast<const __half2*>(&a);
