@@ -29,7 +29,7 @@ __device__ __forceinline__ float row_sumsq(const __half* row, int width) {
       }
     }
   }
-  return canon_butterfly(acc, lanes);
+  return canon_reduce(acc, lanes);
 }
 
 // add_f16 (transformer.metal:61-68): a correctly rounded half addition.
@@ -74,7 +74,7 @@ __global__ void add_rms_norm_kernel(const __half* l, const __half* r, const __ha
         residual[base + i] = __float2half_rn(v);
         acc = __fmaf_rn(v, v, acc);
       }
-  float scale = rms_scale(canon_butterfly(acc, lanes), width, eps);
+  float scale = rms_scale(canon_reduce(acc, lanes), width, eps);
   __syncwarp();
   for (int i = lane; i < width; i += 32) {
     float v = __half2float(__float2half_rn(

@@ -55,7 +55,7 @@ __global__ void __launch_bounds__(256) gemm_canon_kernel(const __half* x, const 
 #pragma unroll
   for (int i = 0; i < 8; ++i)
 #pragma unroll
-    for (int j = 0; j < 8; ++j) acc[i][j] = canon_butterfly(acc[i][j], lanes);
+    for (int j = 0; j < 8; ++j) acc[i][j] = canon_reduce(acc[i][j], lanes);
   // Lane l writes outputs (l / 8, l % 8) and (l / 8 + 4, l % 8).
 #pragma unroll
   for (int half = 0; half < 2; ++half) {

@@ -134,7 +134,7 @@ __device__ void build_input(const GemvProblem& p, uint4* xs, float* s_scale) {
         acc = chunk_sq(xs[c], acc);
       }
     }
-    float total = canon_butterfly(acc, canon_lanes(p.k));
+    float total = canon_reduce(acc, canon_lanes(p.k));
     if (lane == 0) *s_scale = rms_scale(total, p.k, p.eps);
   }
   __syncthreads();
@@ -215,11 +215,11 @@ __global__ void __launch_bounds__(kThreads) gemv_staged_kernel(GemvProblem p, Pl
           a0 = chunk_dot(xv, w0[c], a0);
           a1 = chunk_dot(xv, w1[c], a1);
         }
-        a1 = canon_butterfly(a1, lanes);
+        a1 = canon_reduce(a1, lanes);
       } else {
         for (int c = lane; c < kc; c += 32) a0 = chunk_dot(xs[c], w0[c], a0);
       }
-      a0 = canon_butterfly(a0, lanes);
+      a0 = canon_reduce(a0, lanes);
       if (lane == 0) {
         const int item = i0 + r;
         if (OUT == kOutSwiglu) {
@@ -324,7 +324,7 @@ __global__ void gemv_generic_kernel(const __half* x, const __half* w, __half* ou
     for (int c = lane; c < chunks; c += lanes)
       for (int i = 8 * c; i < min(k, 8 * c + 8); ++i)
         acc = __fmaf_rn(__half2float(x[i]), __half2float(row[i]), acc);
-  acc = canon_butterfly(acc, lanes);
+  acc = canon_reduce(acc, lanes);
   if (lane == 0) out[warp] = __float2half_rn(acc);
 }
 

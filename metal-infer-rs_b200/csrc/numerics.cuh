@@ -64,6 +64,13 @@ __device__ __forceinline__ float canon_butterfly(float v, int lanes) {
   return v;
 }
 
+// One canonical reduction per warp, returned to every lane (lanes outside
+// the first group of `lanes` hold other sums after the butterfly alone).
+__device__ __forceinline__ float canon_reduce(float v, int lanes) {
+  v = canon_butterfly(v, lanes);
+  return lanes < 32 ? __shfl_sync(0xffffffffu, v, 0) : v;
+}
+
 // The same over a subset of a warp: `mask` names exactly the lanes that
 // execute the call (every xor partner must be in it).
 __device__ __forceinline__ float canon_butterfly_mask(float v, int lanes, unsigned mask) {
