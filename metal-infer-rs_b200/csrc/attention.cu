@@ -89,6 +89,7 @@ struct DecodeArgs {
   __half* v_cache_w;
   float theta, eps;
   int round_norm;
+  const float2* rope;     // RoPE table (null: evaluate the terms)
 };
 
 // Per-head RMSNorm + RoPE of one 128-dim head held by a half-warp (lane li
@@ -97,7 +98,8 @@ struct DecodeArgs {
 // the lanes of the warp executing the call (one or both half-warps).
 __device__ __forceinline__ void norm_rope_half(const uint4& raw, const __half* w, uint32_t pos,
                                                float theta, float eps, bool round_norm,
-                                               unsigned mask, float (&out)[8]) {
+                                               unsigned mask, const float2* rope,
+                                               float (&out)[8]) {
   const int li = threadIdx.x & 15;
   float total = canon_butterfly_mask(chunk_sq(raw, 0.f), 16, mask);
   float scale = rms_scale(total, HD, eps);
@@ -122,7 +124,13 @@ __device__ __forceinline__ void norm_rope_half(const uint4& raw, const __half* w
     int d = 8 * li + e;
     int pair = first ? d : d - HD / 2;
     float c, s;
-    rope_cs(pos, pair, HD, theta, &c, &s);
+    if (rope) {
+      float2 cs = rope[(size_t)pos * (HD / 2) + pair];
+      c = cs.x;
+      s = cs.y;
+    } else {
+      rope_cs(pos, pair, HD, theta, &c, &s);
+    }
     float r = first ? __fsub_rn(__fmul_rn(nx[e], c), __fmul_rn(partner, s))
                     : __fadd_rn(__fmul_rn(partner, s), __fmul_rn(nx[e], c));
     out[e] = __half2float(__float2half_rn(r));
@@ -193,7 +201,8 @@ __global__ void __launch_bounds__(kDecodeThreads) attention_decode_kernel(Decode
     uint4 raw = reinterpret_cast<const uint4*>(qsrc)[li];
     float qv[8];
     if (a.fused) {
-      norm_rope_half(raw, a.q_norm, (uint32_t)pos, a.theta, a.eps, a.round_norm != 0, mask, qv);
+      norm_rope_half(raw, a.q_norm, (uint32_t)pos, a.theta, a.eps, a.round_norm != 0, mask,
+                     a.rope, qv);
     } else {
       const __half2* hr = reinterpret_cast<const __half2*>(&raw);
 #pragma unroll
@@ -210,7 +219,7 @@ __global__ void __launch_bounds__(kDecodeThreads) attention_decode_kernel(Decode
     uint4 raw = reinterpret_cast<const uint4*>(a.k_raw + (size_t)g_kv * HD)[li];
     float kv[8];
     norm_rope_half(raw, a.k_norm, (uint32_t)pos, a.theta, a.eps, a.round_norm != 0, 0xffff0000u,
-                   kv);
+                   a.rope, kv);
     uint4 kk;
     __half2* hk = reinterpret_cast<__half2*>(&kk);
 #pragma unroll
@@ -594,6 +603,7 @@ void attention_decode_fused(const Launch& l, const DecodeFused& p, int splits, f
   a.theta = p.theta;
   a.eps = p.eps;
   a.round_norm = p.round_norm ? 1 : 0;
+  a.rope = p.rope;
   launch_decode(l, a, splits);
 }
 

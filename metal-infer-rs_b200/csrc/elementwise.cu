@@ -104,11 +104,19 @@ __global__ void embedding_kernel(const uint32_t* tokens, const __half* table, __
     out[(size_t)t * width + i] = zero ? __half(0.f) : table[(size_t)tok * width + i];
 }
 
-// Rotate-half RoPE of one pair with the engine's RoPE terms.
+// Rotate-half RoPE of one pair with the engine's RoPE terms (from the table
+// when one is given).
 __device__ __forceinline__ void rope_pair(float x, float y, int pair, int head_dim, uint32_t pos,
-                                          float theta, __half* ox, __half* oy) {
+                                          float theta, __half* ox, __half* oy,
+                                          const float2* table = nullptr) {
   float c, s;
-  rope_cs(pos, pair, head_dim, theta, &c, &s);
+  if (table) {
+    float2 cs = table[(size_t)pos * (head_dim / 2) + pair];
+    c = cs.x;
+    s = cs.y;
+  } else {
+    rope_cs(pos, pair, head_dim, theta, &c, &s);
+  }
   *ox = __float2half_rn(__fsub_rn(__fmul_rn(x, c), __fmul_rn(y, s)));
   *oy = __float2half_rn(__fadd_rn(__fmul_rn(x, s), __fmul_rn(y, c)));
 }
@@ -136,7 +144,8 @@ __global__ void rope_kernel(const __half* in, __half* out, int tokens, int heads
 __global__ void qk_norm_rope_cache_kernel(const __half* q, const __half* k, const __half* qw,
                                           const __half* kw, __half* q_out, __half* key_cache,
                                           int tokens, int q_heads, int kv_heads, int head_dim,
-                                          Pos pos, float theta, float eps, int round_norm) {
+                                          Pos pos, float theta, float eps, int round_norm,
+                                          const float2* table) {
   int group = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   int lane = threadIdx.x & 31;
   pdl_wait();
@@ -161,7 +170,18 @@ __global__ void qk_norm_rope_cache_kernel(const __half* q, const __half* k, cons
       x = __half2float(__float2half_rn(x));
       y = __half2float(__float2half_rn(y));
     }
-    rope_pair(x, y, pair, head_dim, p, theta, dst + pair, dst + pair + half_dim);
+    rope_pair(x, y, pair, head_dim, p, theta, dst + pair, dst + pair + half_dim, table);
+  }
+}
+
+__global__ void rope_table_kernel(float2* out, int positions, int head_dim, float theta) {
+  const int pairs = head_dim / 2;
+  const size_t n = (size_t)positions * pairs;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
+       i += (size_t)gridDim.x * blockDim.x) {
+    float c, s;
+    rope_cs((uint32_t)(i / pairs), (int)(i % pairs), head_dim, theta, &c, &s);
+    out[i] = make_float2(c, s);
   }
 }
 
@@ -306,12 +326,20 @@ void rope(const Launch& l, const __half* in, __half* out, int tokens, int heads,
 void qk_norm_rope_cache(const Launch& l, const __half* q, const __half* k, const __half* qw,
                         const __half* kw, __half* q_out, __half* key_cache, int tokens,
                         int q_heads, int kv_heads, int head_dim, Pos pos, float theta,
-                        float eps, bool round_norm) {
+                        float eps, bool round_norm, const float2* rope) {
   int rows = tokens * (q_heads + kv_heads);
   if (rows <= 0) return;
   launch_kernel(l, dim3((rows + 7) / 8), dim3(256), 0, qk_norm_rope_cache_kernel, q, k, qw, kw,
                 q_out, key_cache, tokens, q_heads, kv_heads, head_dim, pos, theta, eps,
-                (int)round_norm);
+                (int)round_norm, rope);
+}
+
+void rope_table(cudaStream_t s, float2* out, int positions, int head_dim, float theta) {
+  size_t n = (size_t)positions * (head_dim / 2);
+  if (!n) return;
+  int grid = (int)std::min<size_t>((n + 255) / 256, 4096);
+  rope_table_kernel<<<grid, 256, 0, s>>>(out, positions, head_dim, theta);
+  MI_CUDA(cudaGetLastError());
 }
 
 void copy_kv(const Launch& l, const __half* src, __half* cache, int tokens, int stride,

@@ -28,11 +28,12 @@ namespace {
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
 constexpr int kSmemBudget = 112 * 1024;  // two GEMV CTAs fit on one SM
+constexpr int kMaxStages = 6;
 
 struct Plan {
   int rpc;      // items per CTA
   int rps;      // items per stage
-  int stages;   // ring depth (1 or 2)
+  int stages;   // ring depth (1 .. kMaxStages)
   int x_bytes;  // shared bytes of the input row
   int stage_bytes;
 };
@@ -168,7 +169,7 @@ __device__ __forceinline__ void argmax_take(float v, uint32_t idx, uint32_t& bk,
 template <int IN, int OUT>
 __global__ void __launch_bounds__(kThreads) gemv_staged_kernel(GemvProblem p, Plan plan) {
   extern __shared__ __align__(128) uint8_t smem[];
-  __shared__ uint64_t full[2];
+  __shared__ uint64_t full[kMaxStages];
   __shared__ float s_scale;
   __shared__ uint32_t best_key_s[kWarps];
   __shared__ uint32_t best_idx_s[kWarps];
@@ -360,12 +361,16 @@ Plan make_plan(const GemvProblem& p, int items, int grid, bool pair) {
   int item_bytes = p.k * 2 * (pair ? 2 : 1);
   int budget = kSmemBudget - pl.x_bytes;
   if (pl.rpc * item_bytes <= budget) {
-    pl.stages = 1;
+    pl.stages = 1;  // the whole block is prefetched before the dependency wait
     pl.rps = pl.rpc;
   } else {
-    pl.stages = 2;
-    pl.rps = budget / 2 / item_bytes;
+    // Streaming: a ring of kMaxStages stages keeps most of the budget in
+    // flight while one stage is consumed.
+    pl.rps = budget / kMaxStages / item_bytes;
     if (pl.rps < 1) pl.rps = 1;
+    pl.stages = kMaxStages;
+    if (pl.rps * pl.stages * item_bytes > budget) pl.stages = budget / (pl.rps * item_bytes);
+    if (pl.stages < 1) pl.stages = 1;
   }
   pl.stage_bytes = (pl.rps * item_bytes + 127) / 128 * 128;
   return pl;

@@ -95,10 +95,11 @@ void embedding(const Launch& l, const uint32_t* tokens, const __half* table, __h
 void rope(const Launch& l, const __half* in, __half* out, int tokens, int heads, int head_dim,
           Pos pos, float theta);
 // round_norm: round the normalized row to FP16 before RoPE (unfused path).
+// `rope` (optional) is a rope_table of the same theta and head_dim.
 void qk_norm_rope_cache(const Launch& l, const __half* q, const __half* k, const __half* qw,
                         const __half* kw, __half* q_out, __half* key_cache, int tokens,
                         int q_heads, int kv_heads, int head_dim, Pos pos, float theta,
-                        float eps, bool round_norm);
+                        float eps, bool round_norm, const float2* rope = nullptr);
 void copy_kv(const Launch& l, const __half* src, __half* cache, int tokens, int stride, Pos pos);
 // Greedy argmax; partials sized by argmax_partials(n).
 int argmax_partials(size_t n);
@@ -144,7 +145,11 @@ struct DecodeFused {
   __half* out = nullptr;          // [qh, hd]
   int qh = 16, kvh = 8, hd = 128;
   Pos pos;                        // position of the new token (= len - 1)
+  const float2* rope = nullptr;   // RoPE table [cap, hd / 2] of (cos, sin), or null
 };
+// RoPE table of (cos, sin) for positions [0, positions) and pairs [0, hd/2),
+// entry p * (hd / 2) + i; the values are those of rope_cs (numerics.cuh).
+void rope_table(cudaStream_t s, float2* out, int positions, int head_dim, float theta);
 void attention_decode_fused(const Launch& l, const DecodeFused& p, int splits, float* scratch,
                             uint32_t* counters, int block_keys);
 // Keys per flash-decode block for a cache of `capacity` positions (64 up to

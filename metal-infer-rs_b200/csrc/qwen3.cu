@@ -109,6 +109,8 @@ struct mi_kv_cache {
   std::vector<TensorRef> key, value;
   TensorRef toks;     // u32 [capacity + 1]
   TensorRef dev_len;  // u32 [1]
+  TensorRef rope;     // f32 [capacity, head_dim / 2, 2]: (cos, sin) per position and pair
+  const float2* rope_table() const { return reinterpret_cast<const float2*>(rope.t->f32()); }
   cudaGraphExec_t graph = nullptr;
   uint64_t graph_version = 0;
   ~mi_kv_cache() {
@@ -264,6 +266,7 @@ void encode_decode_step(mi_qwen3* m, mi_kv_cache* c) {
       d.kvh = (int)cfg.num_key_value_heads;
       d.hd = (int)cfg.head_dim;
       d.pos.dev = len;
+      d.rope = c->rope_table();
       ProfileScope ps(m->ctx, "attention_decode");
       k::attention_decode_fused(dlaunch(m, true), d, w.attn_splits, w.attn_scratch.t->f32(),
                                 w.counters.t->u32() + 1, k::decode_block_for((int)c->capacity));
@@ -416,7 +419,8 @@ void layer_prefill(mi_qwen3* m, mi_kv_cache* c, size_t li, __half* hidden, size_
   pos.base = (uint32_t)off;
   k::qk_norm_rope_cache(l, q, kk, L.w[kQNorm].h(), L.w[kKNorm].h(), query, c->key[li].h(), t,
                         (int)cfg.num_attention_heads, (int)cfg.num_key_value_heads,
-                        (int)cfg.head_dim, pos, cfg.rope_theta, eps, !m->fusion.qk_rope_cache);
+                        (int)cfg.head_dim, pos, cfg.rope_theta, eps, !m->fusion.qk_rope_cache,
+                        c->rope_table());
   k::copy_kv(l, v, c->value[li].h(), t, kw, pos);
   __half* attn = s.f16({T, (size_t)qw});
   k::AttnProblem a;
@@ -688,6 +692,9 @@ mi_status mi_kv_cache_create(mi_qwen3* m, size_t capacity, mi_kv_cache** out) {
     }
     c->toks = TensorRef(new_tensor(m->ctx, {capacity + 1}, MI_U32, true));
     c->dev_len = TensorRef(new_tensor(m->ctx, {1}, MI_U32, true));
+    c->rope = TensorRef(new_tensor(m->ctx, {capacity, hd / 2, 2}, MI_F32));
+    k::rope_table(m->ctx->stream, reinterpret_cast<float2*>(c->rope.t->f32()), (int)capacity,
+                  (int)hd, m->cfg.rope_theta);
     ensure_workspace(m, capacity);
     sync_context(m->ctx);
     *out = c.release();
