@@ -154,8 +154,19 @@ k::Launch launch(mi_qwen3* m, bool pdl) {
 }
 
 // Decode launches: PDL unless per-kernel profiling is on (events between
-// launches would serialise them anyway).
-k::Launch dlaunch(mi_qwen3* m, bool pdl) { return launch(m, pdl && !m->ctx->profiling); }
+// launches would serialise them anyway) or MI_DECODE_PDL=0.
+bool pdl_enabled() {
+  static int on = -1;
+  if (on < 0) {
+    const char* e = getenv("MI_DECODE_PDL");
+    on = (e && *e == '0') ? 0 : 1;
+  }
+  return on == 1;
+}
+
+k::Launch dlaunch(mi_qwen3* m, bool pdl) {
+  return launch(m, pdl && !m->ctx->profiling && pdl_enabled());
+}
 
 size_t qwidth(const mi_qwen3_config& c) { return c.num_attention_heads * c.head_dim; }
 size_t kvwidth(const mi_qwen3_config& c) { return c.num_key_value_heads * c.head_dim; }
