@@ -269,6 +269,26 @@ mi_status mi_batch_attention_flash_decode_with_configuration(
 mi_status mi_batch_copy_into_cache(mi_batch* b, const mi_tensor* source, mi_tensor* cache,
                                    size_t offset);
 
+/* One-query flash decode that allocates nothing. No counterpart in the
+ * reference: it serves callers that cannot allocate device memory at the
+ * call — hosts that reserve the whole GPU for their own memory pool, and
+ * latency-critical loops where cudaMalloc/cudaFree would synchronize the
+ * device. Same result as mi_batch_attention_flash_decode_with_configuration
+ * on [1, query_heads, 128] queries and [length, kv_heads, 128] FP16 keys and
+ * values (all keys visible); the caller passes every input and the output as
+ * 16-byte aligned device pointers and the cudaStream_t to run on.
+ * Scratch: a fixed device array inside the library (1 MiB of FP32 block
+ * partials plus 64 merge counters), held by every GPU that loads the library
+ * until exit. Limits: head_dim 128, GQA ratio 1/2/4/8, block_keys 32/64/
+ * 128/256, kv_heads <= 64, kv_heads * ceil(length / block_keys) * ratio *
+ * 130 * 4 <= 1 MiB; larger sizes return MI_ERR_SHAPE. The first call on a
+ * device looks up the array's device address (make it before any stream
+ * capture). Calls share the array: calls that overlap on the GPU race. */
+mi_status mi_attention_flash_decode_noalloc(const void* query, const void* key,
+                                            const void* value, void* out, size_t query_heads,
+                                            size_t kv_heads, size_t head_dim, size_t length,
+                                            size_t block_keys, void* stream);
+
 /* ---- Qwen3 model (crates/metal-infer-models/src/qwen3.rs) ----------------- */
 
 /* Qwen3Config (crates/metal-infer-models/src/config.rs:5-21) */

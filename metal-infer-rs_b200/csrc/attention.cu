@@ -18,6 +18,8 @@
 //                        probabilities to FP16 (transformer.metal:1614-1822)
 // All reductions follow numerics.cuh.
 
+#include <mutex>
+
 #include "device.cuh"
 #include "pipeline.cuh"
 
@@ -626,5 +628,101 @@ void attention_prefill(const Launch& l, const AttnProblem& p) {
 
 unsigned attention_status(bool reset) { return pipe::read_status(reset); }
 
+// ---- flash decode without allocation ------------------------------------------------
+// Some callers cannot allocate device memory at the point of the call: hosts
+// that reserve the whole device for their own memory pool up front (a
+// cudaMalloc there fails or fragments the pool), and latency-critical loops
+// where cudaMalloc / cudaFree would stall because they synchronize the
+// device. For them, mi_attention_flash_decode_noalloc runs the flash-decode
+// kernel with its scratch (per-block softmax partials and per-KV-head merge
+// counters) in this file-scope device array instead of allocated memory.
+// Every GPU that loads the library holds the array until the process exits.
+namespace {
+
+constexpr size_t kNoAllocPartialBytes = size_t(1) << 20;  // FP32 block partials
+constexpr size_t kNoAllocMaxKvHeads = 64;                  // one u32 counter each
+constexpr size_t kNoAllocBytes = kNoAllocPartialBytes + kNoAllocMaxKvHeads * sizeof(uint32_t);
+constexpr int kNoAllocMaxDevices = 64;
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocBytes];
+
+std::mutex g_noalloc_mutex;
+void* g_noalloc_ptr[kNoAllocMaxDevices] = {};
+
+// Device address of the scratch array on the current device, looked up once
+// per device (the array's host-side name is not a device address).
+void* noalloc_scratch(int device) {
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (!g_noalloc_ptr[device]) {
+    void* ptr = nullptr;
+    cudaError_t err = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (err != cudaSuccess || !ptr)
+      fail(MI_ERR_RESOURCE, "cannot resolve the decode scratch array: %s",
+           cudaGetErrorString(err));
+    g_noalloc_ptr[device] = ptr;
+  }
+  return g_noalloc_ptr[device];
+}
+
+}  // namespace
+
 }  // namespace k
 }  // namespace mi
+
+extern "C" mi_status mi_attention_flash_decode_noalloc(const void* query, const void* key,
+                                                       const void* value, void* out,
+                                                       size_t query_heads, size_t kv_heads,
+                                                       size_t head_dim, size_t length,
+                                                       size_t block_keys, void* stream) {
+  using namespace mi;
+  using namespace mi::k;
+  return guard([&] {
+    MI_REQUIRE(query && key && value && out, MI_ERR_INVALID_ARGUMENT,
+               "query, key, value and out must be device pointers");
+    MI_REQUIRE(((reinterpret_cast<uintptr_t>(query) | reinterpret_cast<uintptr_t>(key) |
+                 reinterpret_cast<uintptr_t>(value) | reinterpret_cast<uintptr_t>(out)) & 15) == 0,
+               MI_ERR_INVALID_ARGUMENT, "query, key, value and out must be 16-byte aligned");
+    MI_REQUIRE(head_dim == 128, MI_ERR_SHAPE, "flash decode without allocation needs head_dim 128");
+    MI_REQUIRE(kv_heads > 0 && query_heads % kv_heads == 0, MI_ERR_SHAPE,
+               "query_heads must be divisible by kv_heads");
+    const size_t group = query_heads / kv_heads;
+    MI_REQUIRE(group == 1 || group == 2 || group == 4 || group == 8, MI_ERR_SHAPE,
+               "GQA ratio must be 1, 2, 4 or 8");
+    MI_REQUIRE(block_keys == 32 || block_keys == 64 || block_keys == 128 || block_keys == 256,
+               MI_ERR_SHAPE, "flash decode block size must be 32, 64, 128, or 256");
+    MI_REQUIRE(length > 0 && length < 0x7FFFFFFF, MI_ERR_SHAPE, "length must be positive");
+    MI_REQUIRE(kv_heads <= kNoAllocMaxKvHeads, MI_ERR_SHAPE,
+               "kv_heads %zu exceeds the scratch limit of %zu", kv_heads, kNoAllocMaxKvHeads);
+    const size_t blocks = (length + block_keys - 1) / block_keys;
+    const size_t partial_bytes = attention_decode_scratch((int)kv_heads, (int)blocks, (int)group,
+                                                          (int)head_dim);
+    MI_REQUIRE(partial_bytes <= kNoAllocPartialBytes, MI_ERR_SHAPE,
+               "kv_heads x blocks x group x 130 x 4 = %zu bytes exceeds the %zu-byte scratch "
+               "(lengthen block_keys or split the call)",
+               partial_bytes, kNoAllocPartialBytes);
+    int device = 0;
+    MI_CUDA(cudaGetDevice(&device));
+    MI_REQUIRE(device >= 0 && device < kNoAllocMaxDevices, MI_ERR_NO_DEVICE, "device %d", device);
+    uint8_t* scratch = static_cast<uint8_t*>(noalloc_scratch(device));
+    uint32_t* counters = reinterpret_cast<uint32_t*>(scratch + kNoAllocPartialBytes);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    // The merge counters must start at zero (the kernel leaves them at zero,
+    // but an interrupted earlier call may not have).
+    MI_CUDA(cudaMemsetAsync(counters, 0, kv_heads * sizeof(uint32_t), s));
+    Launch l;
+    l.stream = s;
+    l.pdl = false;
+    DecodeArgs a = {};
+    a.q = static_cast<const __half*>(query);
+    a.k_cache = static_cast<const __half*>(key);
+    a.v_cache = static_cast<const __half*>(value);
+    a.qh = (int)query_heads;
+    a.kvh = (int)kv_heads;
+    a.length = (int)length;
+    a.block = (int)block_keys;
+    a.out = static_cast<__half*>(out);
+    a.scratch = reinterpret_cast<float*>(scratch);
+    a.counters = counters;
+    launch_decode(l, a, (int)blocks);
+  });
+}

@@ -157,6 +157,7 @@ EXPORTS = [
     "mi_batch_add_rms_norm", "mi_batch_swiglu", "mi_batch_embedding", "mi_batch_argmax",
     "mi_batch_rope", "mi_batch_qk_norm_rope_cache", "mi_batch_attention",
     "mi_batch_attention_flash_decode_with_configuration", "mi_batch_copy_into_cache",
+    "mi_attention_flash_decode_noalloc",
     "mi_qwen3_config_validate", "mi_qwen3_create_random", "mi_qwen3_load", "mi_qwen3_destroy",
     "mi_qwen3_get_config", "mi_qwen3_set_attention_kind", "mi_qwen3_set_fusion_options",
     "mi_qwen3_fusion_options", "mi_qwen3_set_decode_graphs", "mi_kv_cache_create",
