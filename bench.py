@@ -38,6 +38,7 @@ INPUT_STREAM = 1 << 20
 PROMPT = 128
 DECODE = 256
 CAPACITY = 2048
+PROFILE_STEPS = 32  # decode steps of the per-kernel timing pass
 SEED = 2
 METRIC = "decode tokens/s (batch 1, greedy)"
 CONFIG = dict(hidden_size=1024, intermediate_size=3072, num_hidden_layers=28,
@@ -71,7 +72,11 @@ def decode_bytes_per_token(c, kv_len):
     return c["num_hidden_layers"] * weight_bytes_per_layer(c) + 2 * V * h + 2 * h + kv
 
 
-def kernel_bytes(c, name, mean_len):
+def kernel_bytes(c, name, mean_len, steps=1):
+    """Algorithmic bytes of one launch of `name` (`steps` decode steps for the
+    persistent decode kernel, which runs a whole call in one launch)."""
+    if name == "decode_loop":
+        return int(steps * decode_bytes_per_token(c, mean_len))
     h, I, V = c["hidden_size"], c["intermediate_size"], c["vocab_size"]
     qw = c["num_attention_heads"] * c["head_dim"]
     kw = c["num_key_value_heads"] * c["head_dim"]
@@ -226,7 +231,7 @@ def run_ours(args, rank, world, local_rank):
     model.prefill_argmax(prompt_ptr, cache, ctx.empty([1], mi.DType.U32))
     ctx.set_kernel_profiling(True)
     ctx.take_kernel_profiles()
-    model.decode_steps(cache, 32)
+    model.decode_steps(cache, PROFILE_STEPS)
     ctx.synchronize()
     prof = ctx.take_kernel_profiles()
     ctx.set_kernel_profiling(False)
@@ -235,18 +240,18 @@ def run_ours(args, rank, world, local_rank):
         d = per.setdefault(name, [0, 0.0])
         d[0] += 1
         d[1] += sec
-    mean_len = PROMPT + 16.5
+    mean_len = PROMPT + (PROFILE_STEPS + 1) / 2.0
     hbm, peak_kind = peaks()
     kernels = {}
     for name, (n, sec) in per.items():
-        b = kernel_bytes(CONFIG, name, mean_len)
+        b = kernel_bytes(CONFIG, name, mean_len, PROFILE_STEPS)
         avg = sec / n
         kernels[name] = {"launches": n, "avg_us": round(avg * 1e6, 3),
                          "share": round(sec / sum(s for _, s in per.values()), 4),
                          "gbs": round(b / avg / 1e9, 1) if b else None}
     dominant = max(per, key=lambda k: per[k][1])
     dom_avg = per[dominant][1] / per[dominant][0]
-    dom_bytes = kernel_bytes(CONFIG, dominant, mean_len)
+    dom_bytes = kernel_bytes(CONFIG, dominant, mean_len, PROFILE_STEPS)
     achieved = dom_bytes / dom_avg / 1e9
     traffic = read_traffic(dominant)
 
@@ -255,9 +260,11 @@ def run_ours(args, rank, world, local_rank):
     per_gpu_tps = decode_tps / world
 
     ok = bool(np.array_equal(ids, out_ids)) if out_ids is not None else False
+    persistent = model.decode_persistent()
     layer_launches = 5 * CONFIG["num_hidden_layers"] + 1
     prefill_launches = 1 + 14 * CONFIG["num_hidden_layers"] + 2
-    launches = args.steps * (prefill_launches + DECODE * layer_launches)
+    decode_launches = 1 if persistent else DECODE * layer_launches
+    launches = args.steps * (prefill_launches + decode_launches)
 
     if rank == 0:
         line = {
@@ -285,6 +292,7 @@ def run_ours(args, rank, world, local_rank):
                          "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4),
                          "traffic": traffic, "bytes_per_launch": dom_bytes,
                          "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"},
+            "decode_path": "persistent kernel" if persistent else "kernel chain (CUDA graph)",
             "kernels": kernels,
             "gpu_launches": launches,
             "clocks": clocks.summary(),
@@ -386,7 +394,11 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-sample-steps", type=int, default=48)
     ap.add_argument("--cpu-sample-steps-ref", type=int, default=8)
+    ap.add_argument("--decode-steps", type=int, default=DECODE,
+                    help="decode steps per request (smaller only for profiler launch lists)")
     args = ap.parse_args()
+    if args.decode_steps != DECODE:
+        globals()["DECODE"] = args.decode_steps
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))

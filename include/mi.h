@@ -349,6 +349,14 @@ mi_status mi_qwen3_set_fusion_options(mi_qwen3* m, mi_fusion_options options);
 mi_fusion_options mi_qwen3_fusion_options(const mi_qwen3* m);
 /* Decode steps run as one CUDA graph (default on); 0 launches eagerly. */
 mi_status mi_qwen3_set_decode_graphs(mi_qwen3* m, int enabled);
+/* No counterpart in the reference (its decode encodes one command buffer per
+ * step). Greedy decode steps run in one persistent cooperative kernel per
+ * call (default on, also off with the environment variable
+ * MI_DECODE_LOOP=0); 0 selects the per-kernel chain above. Both give the
+ * same ids and logits. mi_qwen3_decode_persistent reports whether the
+ * persistent kernel is in use for this model on this device. */
+mi_status mi_qwen3_set_decode_persistent(mi_qwen3* m, int enabled);
+mi_status mi_qwen3_decode_persistent(mi_qwen3* m, int* active);
 
 /* KvCache::new / len / capacity / reset (qwen3.rs:75-117) */
 mi_status mi_kv_cache_create(mi_qwen3* m, size_t capacity, mi_kv_cache** out);

@@ -94,51 +94,6 @@ struct DecodeArgs {
   const float2* rope;     // RoPE table (null: evaluate the terms)
 };
 
-// Per-head RMSNorm + RoPE of one 128-dim head held by a half-warp (lane li
-// owns dims 8 li .. 8 li + 7; the rotation partner of dim d is d +- 64, lane
-// li ^ 8). Returns the FP16-rounded rotated values as floats. `mask` names
-// the lanes of the warp executing the call (one or both half-warps).
-__device__ __forceinline__ void norm_rope_half(const uint4& raw, const __half* w, uint32_t pos,
-                                               float theta, float eps, bool round_norm,
-                                               unsigned mask, const float2* rope,
-                                               float (&out)[8]) {
-  const int li = threadIdx.x & 15;
-  float total = canon_butterfly_mask(chunk_sq(raw, 0.f), 16, mask);
-  float scale = rms_scale(total, HD, eps);
-  const __half2* hr = reinterpret_cast<const __half2*>(&raw);
-  uint4 wr = reinterpret_cast<const uint4*>(w)[li];
-  const __half2* hw = reinterpret_cast<const __half2*>(&wr);
-  float nx[8];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    float2 f = __half22float2(hr[i]);
-    float2 g = __half22float2(hw[i]);
-    nx[2 * i] = norm_mul(f.x, scale, g.x);
-    nx[2 * i + 1] = norm_mul(f.y, scale, g.y);
-  }
-  if (round_norm)
-#pragma unroll
-    for (int e = 0; e < 8; ++e) nx[e] = __half2float(__float2half_rn(nx[e]));
-  const bool first = li < 8;
-#pragma unroll
-  for (int e = 0; e < 8; ++e) {
-    float partner = __shfl_xor_sync(mask, nx[e], 8);
-    int d = 8 * li + e;
-    int pair = first ? d : d - HD / 2;
-    float c, s;
-    if (rope) {
-      float2 cs = rope[(size_t)pos * (HD / 2) + pair];
-      c = cs.x;
-      s = cs.y;
-    } else {
-      rope_cs(pos, pair, HD, theta, &c, &s);
-    }
-    float r = first ? __fsub_rn(__fmul_rn(nx[e], c), __fmul_rn(partner, s))
-                    : __fadd_rn(__fmul_rn(partner, s), __fmul_rn(nx[e], c));
-    out[e] = __half2float(__float2half_rn(r));
-  }
-}
-
 template <int G>
 struct DecodeSmem {
   __half k[2][kTile][HD];

@@ -163,6 +163,66 @@ unsigned attention_status(bool reset);
 // FP32 online softmax of the tiled kernel.
 void attention_prefill(const Launch& l, const AttnProblem& p);
 
+// ---- persistent decode loop -------------------------------------------------------
+// Per-layer weights and cache of the persistent decode kernel (device array).
+struct LoopLayer {
+  const __half* wq;
+  const __half* wk;
+  const __half* wv;
+  const __half* wo;
+  const __half* q_norm;
+  const __half* k_norm;
+  const __half* gate;
+  const __half* up;
+  const __half* down;
+  const __half* in_norm;
+  const __half* post_norm;
+  __half* k_cache;  // [capacity, kvh, 128]
+  __half* v_cache;
+};
+// `steps` greedy decode steps of the whole model in one cooperative launch:
+// reads toks[*dev_len], writes each step's id to toks[pos + 1] and the last
+// step's logits, advances *dev_len by `steps`. The stage arithmetic is that
+// of the per-kernel decode chain (bit-identical results).
+struct DecodeLoop {
+  int hidden = 0, inter = 0, qh = 0, kvh = 0, vocab = 0, layers = 0;
+  float eps = 1e-6f, theta = 1e6f;
+  int round_norm = 0;  // FusionOptions::qk_rope_cache off: round the normed q/k
+  int add_norm = 1;    // FusionOptions::add_rms_norm: sum of squares of the unrounded sum
+  int block = 64;      // flash-decode keys per block
+  int attn_blocks = 0; // blocks per head the partial buffer holds
+  int steps = 0;
+  const LoopLayer* layer = nullptr;
+  const __half* embedding = nullptr;
+  const __half* final_norm = nullptr;
+  const __half* lm_head = nullptr;
+  const float2* rope = nullptr;
+  uint32_t* toks = nullptr;
+  uint32_t* dev_len = nullptr;
+  __half* hidden_buf = nullptr;  // [hidden] residual stream
+  __half* residual = nullptr;    // [hidden] after the attention add
+  __half* q_raw = nullptr;
+  __half* k_raw = nullptr;
+  __half* v_raw = nullptr;
+  __half* attn = nullptr;
+  __half* attn_o = nullptr;
+  __half* act = nullptr;
+  __half* logits = nullptr;
+  float* attn_part = nullptr;     // [kvh, attn_blocks, G, 130]
+  uint32_t* attn_count = nullptr; // [kvh], zero on entry and exit
+  uint32_t* argmax_key = nullptr; // [grid]
+  uint32_t* argmax_idx = nullptr; // [grid]
+  uint32_t* sync = nullptr;       // [2]: grid-barrier counter, abort flag
+  // plan (decode_loop_plan)
+  int slot_bytes = 0, slots = 0, x_bytes = 0, grid = 0;
+};
+// Fills the plan fields for `device`; false when the model shape or the
+// device's shared memory does not admit the persistent kernel.
+bool decode_loop_plan(DecodeLoop& p, int device);
+void decode_loop(cudaStream_t stream, const DecodeLoop& p);
+// Expired-wait code of the persistent kernel (0 = none), optionally cleared.
+unsigned decode_loop_status(bool reset);
+
 // ---- synthetic data ------------------------------------------------------------
 void fill_normal_f16(cudaStream_t s, __half* out, size_t n, uint64_t seed, uint64_t stream,
                      uint64_t offset, double std_dev);

@@ -18,6 +18,9 @@
 // step reads toks[len], writes its argmax to toks[len + 1] and increments
 // len. Kernels after the first are launched with programmatic dependent
 // launch so each one streams its weights while its predecessor finishes.
+//
+// By default the decode steps of a call run instead in one persistent
+// cooperative kernel (decode_loop.cu) with the same stages and arithmetic.
 
 #include <cstring>
 #include <map>
@@ -78,6 +81,7 @@ struct Layer {
 struct Workspace {
   TensorRef q_raw, k_raw, v_raw, attn, attn_o, residual, hidden, act, logits;
   TensorRef argmax_pv, argmax_pi, counters, attn_scratch;
+  TensorRef loop_sync;  // persistent decode: grid-barrier counter + abort flag
   int attn_splits = 0;  // flash-decode blocks for the largest cache seen
   int attn_block = 64;  // keys per flash-decode block
   size_t attn_cap = 0;
@@ -98,6 +102,9 @@ struct mi_qwen3 {
   mi_attention_kind attention_kind = MI_ATTENTION_TILED;
   mi_fusion_options fusion{1, 1, 1, 1};
   bool graphs = true;
+  bool persistent = true;  // decode through the persistent kernel when it fits
+  int loop_state = 0;      // 0 unplanned, 1 planned, -1 not admitted
+  k::DecodeLoop loop;
   Workspace ws;
   uint64_t plan_version = 1;  // bumps invalidate captured graphs
 };
@@ -113,6 +120,8 @@ struct mi_kv_cache {
   const float2* rope_table() const { return reinterpret_cast<const float2*>(rope.t->f32()); }
   cudaGraphExec_t graph = nullptr;
   uint64_t graph_version = 0;
+  std::vector<k::LoopLayer> loop_host;  // layer table of the persistent decode
+  TensorRef loop_layers;                // its device copy
   ~mi_kv_cache() {
     if (graph) cudaGraphExecDestroy(graph);
   }
@@ -198,16 +207,18 @@ void ensure_workspace(mi_qwen3* m, size_t capacity) {
     w.argmax_pi = TensorRef(new_tensor(ctx, {parts}, MI_U32, true));
     w.counters = TensorRef(new_tensor(ctx, {1 + c.num_key_value_heads}, MI_U32, true));
   }
-  if (capacity > w.attn_cap) {
+  const int cap_block = k::decode_block_for((int)capacity);
+  const int cap_splits = ((int)capacity + cap_block - 1) / cap_block;
+  if (capacity > w.attn_cap || cap_splits > w.attn_splits) {
     int kvh = (int)c.num_key_value_heads;
-    int block = k::decode_block_for((int)capacity);
-    int splits = ((int)capacity + block - 1) / block;
+    int block = cap_block;
+    int splits = std::max(cap_splits, w.attn_splits);
     int group = (int)(c.num_attention_heads / c.num_key_value_heads);
     size_t bytes = k::attention_decode_scratch(kvh, splits, group, (int)c.head_dim);
     w.attn_scratch = TensorRef(new_tensor(ctx, {bytes / 4}, MI_F32, true));
     w.attn_splits = splits;
     w.attn_block = block;
-    w.attn_cap = capacity;
+    w.attn_cap = std::max(capacity, w.attn_cap);
     m->plan_version++;
   }
 }
@@ -347,6 +358,103 @@ void encode_decode_step(mi_qwen3* m, mi_kv_cache* c) {
     p.step_counter = len;
     ProfileScope ps(m->ctx, "lm_head_argmax");
     k::gemv(dlaunch(m, true), p);
+  }
+}
+
+// Persistent decode (decode_loop.cu) unless disabled per model or by
+// MI_DECODE_LOOP=0; the planner rejects shapes it cannot hold on chip.
+bool persistent_env() {
+  static int on = -1;
+  if (on < 0) {
+    const char* e = getenv("MI_DECODE_LOOP");
+    on = (e && *e == '0') ? 0 : 1;
+  }
+  return on == 1;
+}
+
+bool decode_loop_ready(mi_qwen3* m) {
+  if (!m->persistent || !persistent_env() || !fused_decode_supported(m)) return false;
+  if (m->loop_state == 0) {
+    const auto& c = m->cfg;
+    k::DecodeLoop p;
+    p.hidden = (int)c.hidden_size;
+    p.inter = (int)c.intermediate_size;
+    p.qh = (int)c.num_attention_heads;
+    p.kvh = (int)c.num_key_value_heads;
+    p.vocab = (int)c.vocab_size;
+    p.layers = (int)c.num_hidden_layers;
+    p.eps = c.rms_norm_eps;
+    p.theta = c.rope_theta;
+    m->loop_state = k::decode_loop_plan(p, m->ctx->device) ? 1 : -1;
+    m->loop = p;
+  }
+  return m->loop_state == 1;
+}
+
+// `steps` decode steps from the cache's device position in persistent
+// launches (at most 2048 steps each, which bounds the grid-barrier counter).
+void run_decode_loop(mi_qwen3* m, mi_kv_cache* c, size_t steps) {
+  mi_context* ctx = m->ctx;
+  ensure_workspace(m, c->capacity);
+  auto& w = m->ws;
+  if (!w.loop_sync.t) w.loop_sync = TensorRef(new_tensor(ctx, {2}, MI_U32, true));
+  if (!c->loop_layers.t) {
+    c->loop_host.resize(m->layers.size());
+    for (size_t li = 0; li < m->layers.size(); ++li) {
+      const Layer& L = m->layers[li];
+      k::LoopLayer& d = c->loop_host[li];
+      d.wq = L.w[kQ].h();
+      d.wk = L.w[kK].h();
+      d.wv = L.w[kV].h();
+      d.wo = L.w[kO].h();
+      d.q_norm = L.w[kQNorm].h();
+      d.k_norm = L.w[kKNorm].h();
+      d.gate = L.w[kGate].h();
+      d.up = L.w[kUp].h();
+      d.down = L.w[kDown].h();
+      d.in_norm = L.w[kInputNorm].h();
+      d.post_norm = L.w[kPostNorm].h();
+      d.k_cache = c->key[li].h();
+      d.v_cache = c->value[li].h();
+    }
+    const size_t bytes = sizeof(k::LoopLayer) * c->loop_host.size();
+    c->loop_layers = TensorRef(new_tensor(ctx, {(bytes + 3) / 4}, MI_U32, false));
+    MI_CUDA(cudaMemcpyAsync(c->loop_layers.t->base(), c->loop_host.data(), bytes,
+                            cudaMemcpyHostToDevice, ctx->stream));
+  }
+  k::DecodeLoop p = m->loop;
+  p.round_norm = m->fusion.qk_rope_cache ? 0 : 1;
+  p.add_norm = m->fusion.add_rms_norm ? 1 : 0;
+  p.block = k::decode_block_for((int)c->capacity);
+  p.attn_blocks = w.attn_splits;
+  p.layer = reinterpret_cast<const k::LoopLayer*>(c->loop_layers.t->base());
+  p.embedding = m->embedding.h();
+  p.final_norm = m->final_norm.h();
+  p.lm_head = m->lm_head->f16();
+  p.rope = c->rope_table();
+  p.toks = c->toks.t->u32();
+  p.dev_len = c->dev_len.t->u32();
+  p.hidden_buf = w.hidden.h();
+  p.residual = w.residual.h();
+  p.q_raw = w.q_raw.h();
+  p.k_raw = w.k_raw.h();
+  p.v_raw = w.v_raw.h();
+  p.attn = w.attn.h();
+  p.attn_o = w.attn_o.h();
+  p.act = w.act.h();
+  p.logits = w.logits.h();
+  p.attn_part = w.attn_scratch.t->f32();
+  p.attn_count = w.counters.t->u32() + 1;
+  p.argmax_key = reinterpret_cast<uint32_t*>(w.argmax_pv.t->f32());
+  p.argmax_idx = w.argmax_pi.t->u32();
+  p.sync = w.loop_sync.t->u32();
+  MI_REQUIRE(w.argmax_pi.t->len() >= (size_t)p.grid, MI_ERR_RESOURCE,
+             "argmax partials smaller than the persistent grid");
+  for (size_t done = 0; done < steps;) {
+    p.steps = (int)std::min<size_t>(steps - done, 2048);
+    ProfileScope ps(ctx, "decode_loop");
+    k::decode_loop(ctx->stream, p);
+    done += (size_t)p.steps;
   }
 }
 
@@ -494,6 +602,11 @@ void forward_tokens(mi_qwen3* m, mi_kv_cache* c, size_t T) {
   const auto& cfg = m->cfg;
   ensure_workspace(m, c->capacity);
   size_t off = c->filled;
+  if (T == 1 && decode_loop_ready(m)) {
+    run_decode_loop(m, c, 1);
+    c->filled += 1;
+    return;
+  }
   if (T == 1 && fused_decode_supported(m)) {
     run_decode_step(m, c);
     c->filled += 1;
@@ -685,6 +798,21 @@ mi_status mi_qwen3_set_decode_graphs(mi_qwen3* m, int enabled) {
   });
 }
 
+mi_status mi_qwen3_set_decode_persistent(mi_qwen3* m, int enabled) {
+  return guard([&] {
+    require(m, "model");
+    m->persistent = enabled != 0;
+  });
+}
+
+mi_status mi_qwen3_decode_persistent(mi_qwen3* m, int* active) {
+  return guard([&] {
+    require(m, "model");
+    require(active, "active");
+    *active = decode_loop_ready(m) ? 1 : 0;
+  });
+}
+
 mi_status mi_kv_cache_create(mi_qwen3* m, size_t capacity, mi_kv_cache** out) {
   return guard([&] {
     require(m, "model");
@@ -854,6 +982,17 @@ mi_status mi_qwen3_decode_argmax(mi_qwen3* m, const mi_tensor* token, mi_kv_cach
 
 namespace {
 
+// `n` greedy decode steps from the cache's device position.
+void decode_steps(mi_qwen3* m, mi_kv_cache* c, size_t n) {
+  if (n == 0) return;
+  if (decode_loop_ready(m)) {
+    run_decode_loop(m, c, n);
+    c->filled += n;
+    return;
+  }
+  for (size_t i = 0; i < n; ++i) forward_tokens(m, c, 1);
+}
+
 // generate_greedy (qwen3.rs:475-555): prefill, then decode steps enqueued
 // back to back on the device. Without stop tokens or a callback all steps are
 // launched before the single readback; otherwise steps are checked in chunks
@@ -884,7 +1023,7 @@ size_t generate_greedy(mi_qwen3* m, mi_kv_cache* c, const uint32_t* prompt, size
   size_t seen = 0;      // ids examined
   while (stop_index == max_tokens && seen < max_tokens) {
     size_t n_new = std::min(chunk, steps - launched);
-    for (size_t i = 0; i < n_new; ++i) forward_tokens(m, c, 1);
+    decode_steps(m, c, n_new);
     launched += n_new;
     size_t avail = 1 + launched;  // ids at toks[prompt_len .. prompt_len + avail)
     MI_CUDA(cudaMemcpyAsync(ids.data() + have, c->toks.t->u32() + prompt_len + have,
@@ -928,7 +1067,7 @@ mi_status mi_qwen3_decode_steps(mi_qwen3* m, mi_kv_cache* cache, size_t steps) {
     if (cache->filled == 0)
       fail(MI_ERR_CONFIG, "invalid model configuration: decode needs a prefilled cache");
     check_capacity(cache, steps);
-    for (size_t i = 0; i < steps; ++i) forward_tokens(m, cache, 1);
+    decode_steps(m, cache, steps);
   });
 }
 

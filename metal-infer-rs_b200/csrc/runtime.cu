@@ -312,6 +312,7 @@ mi_status mi_context_kernel_status(mi_context* ctx, uint32_t* code) {
     *code = k::gemm_tc_status(true);
     if (unsigned g = k::gemv_status(true)) *code = *code ? *code : g;
     if (unsigned a = k::attention_status(true)) *code = *code ? *code : a;
+    if (unsigned d = k::decode_loop_status(true)) *code = *code ? *code : d;
   });
   if (st == MI_OK && *code != 0) {
     set_error("a bounded device wait expired (code %u)", *code);

@@ -160,7 +160,8 @@ EXPORTS = [
     "mi_attention_flash_decode_noalloc",
     "mi_qwen3_config_validate", "mi_qwen3_create_random", "mi_qwen3_load", "mi_qwen3_destroy",
     "mi_qwen3_get_config", "mi_qwen3_set_attention_kind", "mi_qwen3_set_fusion_options",
-    "mi_qwen3_fusion_options", "mi_qwen3_set_decode_graphs", "mi_kv_cache_create",
+    "mi_qwen3_fusion_options", "mi_qwen3_set_decode_graphs",
+    "mi_qwen3_set_decode_persistent", "mi_qwen3_decode_persistent", "mi_kv_cache_create",
     "mi_kv_cache_destroy", "mi_kv_cache_len", "mi_kv_cache_capacity", "mi_kv_cache_reset",
     "mi_kv_cache_layer", "mi_qwen3_prefill", "mi_qwen3_decode", "mi_qwen3_prefill_argmax",
     "mi_qwen3_decode_argmax", "mi_qwen3_decode_steps", "mi_kv_cache_tokens",
@@ -669,6 +670,15 @@ class Qwen3Model:
 
     def set_decode_graphs(self, enabled: bool) -> None:
         _check(lib().mi_qwen3_set_decode_graphs(self._h, ctypes.c_int(int(enabled))))
+
+    def set_decode_persistent(self, enabled: bool) -> None:
+        """Decode through the persistent kernel (default) or the kernel chain."""
+        _check(lib().mi_qwen3_set_decode_persistent(self._h, ctypes.c_int(int(enabled))))
+
+    def decode_persistent(self) -> bool:
+        active = ctypes.c_int(0)
+        _check(lib().mi_qwen3_decode_persistent(self._h, ctypes.byref(active)))
+        return bool(active.value)
 
     def kv_cache(self, capacity: int) -> KvCache:
         return KvCache(self, capacity)

@@ -74,10 +74,16 @@ def test_prefill_logits_and_cache_match_oracle(small, prompt_len):
     exact(v0.f16_bits().reshape(256, -1)[:prompt_len], ref.cache(1, True, prompt_len))
 
 
-@pytest.mark.parametrize("graphs", [True, False])
-def test_decode_logits_match_oracle(small, graphs):
+def set_path(model, path):
+    """Decode through the persistent kernel or the kernel chain (graph/eager)."""
+    model.set_decode_persistent(path == "persistent")
+    model.set_decode_graphs(path != "eager")
+
+
+@pytest.mark.parametrize("path", ["persistent", "graph", "eager"])
+def test_decode_logits_match_oracle(small, path):
     cfg, model, ref = small
-    model.set_decode_graphs(graphs)
+    set_path(model, path)
     try:
         prompt = O.gen_tokens(5, INPUT_STREAM + 1, 40, cfg["vocab_size"])
         cache = model.kv_cache(256)
@@ -91,7 +97,7 @@ def test_decode_logits_match_oracle(small, graphs):
             exact(logits, ref_logits)
         assert len(cache) == 52
     finally:
-        model.set_decode_graphs(True)
+        set_path(model, "persistent")
 
 
 def mi_argmax(bits):
@@ -143,6 +149,36 @@ def test_graph_and_eager_decode_are_bit_identical(small):
                               for t in (5, 77, 901, 4000)]))
     model.set_decode_graphs(True)
     np.testing.assert_array_equal(outs[0], outs[1])
+
+
+def test_persistent_decode_is_active_for_qwen3_shapes(small):
+    _, model, _ = small
+    assert model.decode_persistent()
+
+
+@pytest.mark.parametrize("capacity,prompt_len", [(128, 20), (9000, 150)])
+def test_decode_paths_bit_identical(small, capacity, prompt_len):
+    """Persistent kernel vs kernel chain: ids, last logits and the K/V cache."""
+    cfg, model, _ = small
+    prompt = O.gen_tokens(5, INPUT_STREAM + 6, prompt_len, cfg["vocab_size"])
+    outs = {}
+    try:
+        for path in ("persistent", "graph", "eager"):
+            set_path(model, path)
+            cache = model.kv_cache(capacity)
+            ids = model.generate(prompt, 24, cache)
+            logits = model.decode(int(ids[-1]), cache).f16_bits().ravel()
+            k1, v1 = cache.layer(1)
+            n = len(cache)
+            outs[path] = (ids, logits, k1.f16_bits().reshape(capacity, -1)[:n],
+                          v1.f16_bits().reshape(capacity, -1)[:n])
+    finally:
+        set_path(model, "persistent")
+    for path in ("graph", "eager"):
+        for a, b in zip(outs["persistent"], outs[path]):
+            np.testing.assert_array_equal(a, b)
+    ref_ids = O.Qwen3(cfg, seed=5, capacity=capacity).generate_greedy(prompt, 24)
+    np.testing.assert_array_equal(outs["persistent"][0], ref_ids)
 
 
 def test_pipelined_decode_argmax_matches_generate(ctx, small):
