@@ -43,8 +43,11 @@ constexpr int kConsumers = kConsumerWarps * 32;
 constexpr int kThreads = kConsumers + 32;  // + producer warp
 constexpr int kStreams = 8;
 constexpr int kTile = 64;                  // keys staged per attention tile
-constexpr int kAttnThreads = 128;          // warps 0..3 run the attention units
+constexpr int kAttnThreads = 256;          // warps 4..11 run the attention units
+constexpr int kAttnBase = 128;             // (warp 0 keeps the stage-input norms)
 constexpr int kMaxSlots = 16;
+constexpr int kSyncWords = 32;    // sync[]: [0] barrier counter, [1] abort flag
+constexpr int kMaxGrid = 256;
 constexpr int kMinSlotBytes = 32 * 1024;
 
 static __device__ unsigned g_loop_status = 0;
@@ -55,20 +58,28 @@ static __device__ unsigned g_loop_status = 0;
 // thread 0 after the preceding barrier / after the input / after its rows,
 // 3..4 = producer issue of the stage's first / last tile.
 constexpr int kTraceStages = 5 * 64 + 1;
-constexpr int kTraceEvents = 12;
+constexpr int kTraceEvents = 16;
 static __device__ unsigned long long g_trace[2][2][kTraceStages][kTraceEvents];
-__device__ int g_trace_step, g_trace_stage;  // set by consumer thread 0 of the traced CTAs
+__shared__ int g_trace_cur[2];  // step, stage of the running stage (traced CTAs)
 __device__ __forceinline__ void trace(int step, int stage, int ev) {
   const int c = blockIdx.x == 0 ? 0 : (blockIdx.x == gridDim.x - 1 ? 1 : -1);
   if (c < 0 || step >= 2 || stage >= kTraceStages) return;
   g_trace[c][step][stage][ev] = pipe::global_ns();
 }
+// every CTA: arrival at / release from the grid barriers of step 1, layer 3
+static __device__ unsigned long long g_arrive[256][5][2];
+__device__ __forceinline__ void trace_arrive(int step, int stage, int ev) {
+  if (step == 1 && stage >= 15 && stage < 20 && blockIdx.x < 256)
+    g_arrive[blockIdx.x][stage - 15][ev] = pipe::global_ns();
+}
 #define MI_TRACE(step, stage, ev) trace(step, stage, ev)
-#define MI_TRACE_CUR(ev) trace(g_trace_step, g_trace_stage, ev)
-#define MI_TRACE_SET(step, stage) (g_trace_step = (step), g_trace_stage = (stage))
+#define MI_TRACE_ARRIVE(ev) trace_arrive(g_trace_cur[0], g_trace_cur[1], ev)
+#define MI_TRACE_CUR(ev) trace(g_trace_cur[0], g_trace_cur[1], ev)
+#define MI_TRACE_SET(step, stage) (g_trace_cur[0] = (step), g_trace_cur[1] = (stage))
 #else
 #define MI_TRACE(step, stage, ev) ((void)0)
 #define MI_TRACE_CUR(ev) ((void)0)
+#define MI_TRACE_ARRIVE(ev) ((void)0)
 #define MI_TRACE_SET(step, stage) ((void)0)
 #endif
 
@@ -88,9 +99,10 @@ struct StageW {
   int pair;   // GU: gate and up rows per item
 };
 
-__device__ __forceinline__ StageW stage_weights(const DecodeLoop& p, int layer, int st) {
+__device__ __forceinline__ StageW stage_weights(const DecodeLoop& p, const LoopLayer* layers,
+                                                int layer, int st) {
   StageW s = {};
-  const LoopLayer* L = p.layer + (layer < p.layers ? layer : 0);
+  const LoopLayer* L = layers + (layer < p.layers ? layer : 0);
   switch (st) {
     case kQKV:
       s.w[0] = L->wq;
@@ -152,9 +164,14 @@ struct AttnSmem {
   __half v[kTile][HD];
   __half new_k[HD];
   __half new_v[HD];
+  __half qn_w[HD];        // QK-norm weights of the layer (prefetched)
+  __half kn_w[HD];
+  float2 rope[HD / 2];    // (cos, sin) at the step's position (prefetched)
   float q[G][HD];
   float m[kStreams][G];
   float l[kStreams][G];
+  float f[kStreams][G];   // stream merge factors
+  float M[G];
   float acc[kStreams][G][HD];
   int last;
 };
@@ -162,6 +179,7 @@ struct AttnSmem {
 struct Shared {
   uint64_t full[kMaxSlots];
   uint64_t empty[kMaxSlots];
+  Tiles tiles[5];  // this CTA's tiling of each stage (the same in every layer)
   float scale;
   uint32_t best_key[kConsumerWarps];
   uint32_t best_idx[kConsumerWarps];
@@ -176,11 +194,15 @@ __device__ __forceinline__ void attn_sync() {
   asm volatile("bar.sync 2, %0;" ::"n"(kAttnThreads) : "memory");
 }
 
-__device__ __forceinline__ uint32_t ld_acquire(const uint32_t* p) {
+__device__ __forceinline__ uint32_t ld_relaxed(const uint32_t* p) {
   uint32_t v;
-  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
+__device__ __forceinline__ void red_release_add(uint32_t* p, uint32_t v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
 
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(pipe::smem_u32(bar)) : "memory");
@@ -203,8 +225,11 @@ __device__ bool ring_wait(uint64_t* bar, uint32_t parity, Shared& sh, unsigned c
   return true;
 }
 
-// Grid barrier over all CTAs (consumer threads only). Returns false when the
-// kernel is aborting; the decision is uniform across the CTA.
+// Grid barrier over all CTAs (consumer threads only): thread 0 of each CTA
+// adds one to a counter in global memory with a release reduction and polls
+// it until it reaches epoch * gridDim.x (relaxed loads, one fence after).
+// Returns false when the kernel is aborting; the decision is uniform across
+// the CTA.
 __device__ bool grid_sync(const DecodeLoop& p, uint32_t& epoch, Shared& sh) {
   ++epoch;
   consumers_sync();
@@ -213,11 +238,11 @@ __device__ bool grid_sync(const DecodeLoop& p, uint32_t& epoch, Shared& sh) {
     if (sh.abort) {
       *abort_flag = 1u;
     } else {
-      __threadfence();
-      atomicAdd(p.sync, 1u);
+      MI_TRACE_ARRIVE(0);
       const uint32_t target = epoch * gridDim.x;
+      red_release_add(p.sync, 1u);
       uint64_t start = 0;
-      while (ld_acquire(p.sync) < target) {
+      while (ld_relaxed(p.sync) < target) {
         if (*abort_flag) {
           sh.abort = 1;
           break;
@@ -233,6 +258,7 @@ __device__ bool grid_sync(const DecodeLoop& p, uint32_t& epoch, Shared& sh) {
         }
       }
       __threadfence();
+      MI_TRACE_ARRIVE(1);
     }
   }
   consumers_sync();
@@ -265,7 +291,7 @@ __device__ void issue_tile(const StageW& s, const Tiles& t, int tile, uint8_t* d
   }
 }
 
-__device__ void produce(const DecodeLoop& p, uint8_t* ring, Shared& sh) {
+__device__ void produce(const DecodeLoop& p, const LoopLayer* layers, uint8_t* ring, Shared& sh) {
   const int S = p.slots;
   uint32_t g = 0;
   bool ok = true;
@@ -275,8 +301,8 @@ __device__ void produce(const DecodeLoop& p, uint8_t* ring, Shared& sh) {
       for (int j = 0; ok && j < nst; ++j) {
         const int st = layer < p.layers ? (j == 0 ? kQKV : j == 1 ? kO : j == 2 ? kGU : kDown)
                                         : kLM;
-        const StageW s = stage_weights(p, layer, st);
-        const Tiles t = tiles_of(p, s);
+        const StageW s = stage_weights(p, layers, layer, st);
+        const Tiles t = sh.tiles[st];
         const int trace_stage = layer < p.layers ? layer * 5 + (j == 0 ? 0 : j + 1) : p.layers * 5;
         (void)trace_stage;
         for (int tile = 0; tile < t.count; ++tile, ++g) {
@@ -311,9 +337,76 @@ __device__ void produce(const DecodeLoop& p, uint8_t* ring, Shared& sh) {
 // ---- consumers: stage input -------------------------------------------------------
 enum InMode : int { kPlainIn = 0, kNormIn = 1, kEmbedNormIn = 2, kAddNormIn = 3, kAddThenNormIn = 4 };
 
+// Chunk c of the stage input before the norm (gemv.cu build_input roundings).
+__device__ __forceinline__ uint4 input_chunk(int mode, const uint4* src, const uint4* src2, int c) {
+  if (mode == kAddNormIn || mode == kAddThenNormIn) {
+    const uint4 a = __ldcg(src + c);
+    const uint4 b = __ldcg(src2 + c);
+    const __half2* ha = reinterpret_cast<const __half2*>(&a);
+    const __half2* hb = reinterpret_cast<const __half2*>(&b);
+    uint4 v;
+    __half2* hv = reinterpret_cast<__half2*>(&v);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      if (mode == kAddNormIn) {
+        float2 fa = __half22float2(ha[i]);
+        float2 fb = __half22float2(hb[i]);
+        hv[i] = __floats2half2_rn(__fadd_rn(fa.x, fb.x), __fadd_rn(fa.y, fb.y));
+      } else {
+        hv[i] = __hadd2(ha[i], hb[i]);
+      }
+    }
+    return v;
+  }
+  if (mode == kEmbedNormIn) return src ? __ldg(src + c) : make_uint4(0, 0, 0, 0);
+  return __ldcg(src + c);
+}
+
+// Canonical sum of squares of the stage input, loaded by warp 0 itself so it
+// overlaps the fill instead of following it. kAddNormIn squares the
+// unrounded float sums (matvec2_add_rms_impl).
+__device__ __forceinline__ float input_sumsq(int mode, const uint4* src, const uint4* src2,
+                                             int kc, int lane) {
+  float acc = 0.f;
+#pragma unroll 4
+  for (int c = lane; c < kc; c += 32) {
+    if (mode == kAddNormIn) {
+      const uint4 a = __ldcg(src + c);
+      const uint4 b = __ldcg(src2 + c);
+      const __half2* ha = reinterpret_cast<const __half2*>(&a);
+      const __half2* hb = reinterpret_cast<const __half2*>(&b);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float2 fa = __half22float2(ha[i]);
+        float2 fb = __half22float2(hb[i]);
+        float s0 = __fadd_rn(fa.x, fb.x), s1 = __fadd_rn(fa.y, fb.y);
+        acc = __fmaf_rn(s0, s0, acc);
+        acc = __fmaf_rn(s1, s1, acc);
+      }
+    } else {
+      acc = chunk_sq(input_chunk(mode, src, src2, c), acc);
+    }
+  }
+  return acc;
+}
+
+__device__ __forceinline__ uint4 normalize_chunk(const uint4& v, const uint4& g, float scale) {
+  const __half2* hv = reinterpret_cast<const __half2*>(&v);
+  const __half2* hg = reinterpret_cast<const __half2*>(&g);
+  uint4 o;
+  __half2* ho = reinterpret_cast<__half2*>(&o);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float2 f = __half22float2(hv[i]);
+    float2 gg = __half22float2(hg[i]);
+    ho[i] = __floats2half2_rn(norm_mul(f.x, scale, gg.x), norm_mul(f.y, scale, gg.y));
+  }
+  return o;
+}
+
 // Builds the stage input (k halves) in xs with the prologue of the GEMV
-// family (gemv.cu build_input): the same roundings and the canonical sum of
-// squares by one warp.
+// family (gemv.cu build_input): the same roundings, the canonical sum of
+// squares by warp 0. One L2 round trip when k / 8 <= 480 chunks.
 __device__ void build_input(int mode, const __half* x, const __half* x2, const __half* norm_w,
                             int k, float eps, __half* write_back, uint4* xs, Shared& sh) {
   const int tid = threadIdx.x;
@@ -321,153 +414,171 @@ __device__ void build_input(int mode, const __half* x, const __half* x2, const _
   const int kc = k >> 3;
   const uint4* src = reinterpret_cast<const uint4*>(x);
   const uint4* src2 = reinterpret_cast<const uint4*>(x2);
-  for (int c = tid; c < kc; c += kConsumers) {
-    uint4 v;
-    if (mode == kAddNormIn || mode == kAddThenNormIn) {
-      uint4 a = __ldcg(src + c);
-      uint4 b = __ldcg(src2 + c);
-      const __half2* ha = reinterpret_cast<const __half2*>(&a);
-      const __half2* hb = reinterpret_cast<const __half2*>(&b);
-      __half2* hv = reinterpret_cast<__half2*>(&v);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        if (mode == kAddNormIn) {
-          float2 fa = __half22float2(ha[i]);
-          float2 fb = __half22float2(hb[i]);
-          hv[i] = __floats2half2_rn(__fadd_rn(fa.x, fb.x), __fadd_rn(fa.y, fb.y));
-        } else {
-          hv[i] = __hadd2(ha[i], hb[i]);
-        }
-      }
-    } else if (mode == kEmbedNormIn) {
-      v = src ? src[c] : make_uint4(0, 0, 0, 0);  // embedding rows are constant
-    } else {
-      v = __ldcg(src + c);
+  const uint4* g4 = reinterpret_cast<const uint4*>(norm_w);
+  uint4* wb = reinterpret_cast<uint4*>(write_back);
+  if (mode != kPlainIn && tid < 32) {
+    const float total = canon_reduce(input_sumsq(mode, src, src2, kc, lane), canon_lanes(k));
+    if (lane == 0) sh.scale = rms_scale(total, k, eps);
+  }
+  if (kc <= kConsumers) {
+    uint4 v = make_uint4(0, 0, 0, 0), g = make_uint4(0, 0, 0, 0);
+    if (tid < kc) {
+      v = input_chunk(mode, src, src2, tid);
+      if (mode != kPlainIn) g = __ldg(g4 + tid);
+      if (wb && blockIdx.x == 0) wb[tid] = v;
+      if (mode == kPlainIn) xs[tid] = v;
     }
-    if (write_back && blockIdx.x == 0) reinterpret_cast<uint4*>(write_back)[c] = v;
+    consumers_sync();
+    if (mode == kPlainIn) return;
+    if (tid < kc) xs[tid] = normalize_chunk(v, g, sh.scale);
+    consumers_sync();
+    return;
+  }
+  for (int c = tid; c < kc; c += kConsumers) {
+    const uint4 v = input_chunk(mode, src, src2, c);
+    if (wb && blockIdx.x == 0) wb[c] = v;
     xs[c] = v;
   }
   consumers_sync();
   if (mode == kPlainIn) return;
-  if (tid < 32) {
-    float acc = 0.f;
-    for (int c = lane; c < kc; c += 32) {
-      if (mode == kAddNormIn) {
-        // squares of the unrounded sums (matvec2_add_rms_impl)
-        uint4 a = __ldcg(src + c);
-        uint4 b = __ldcg(src2 + c);
-        const __half2* ha = reinterpret_cast<const __half2*>(&a);
-        const __half2* hb = reinterpret_cast<const __half2*>(&b);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          float2 fa = __half22float2(ha[i]);
-          float2 fb = __half22float2(hb[i]);
-          float s0 = __fadd_rn(fa.x, fb.x), s1 = __fadd_rn(fa.y, fb.y);
-          acc = __fmaf_rn(s0, s0, acc);
-          acc = __fmaf_rn(s1, s1, acc);
-        }
-      } else {
-        acc = chunk_sq(xs[c], acc);
-      }
-    }
-    float total = canon_reduce(acc, canon_lanes(k));
-    if (lane == 0) sh.scale = rms_scale(total, k, eps);
-  }
-  consumers_sync();
   const float scale = sh.scale;
-  const uint4* g4 = reinterpret_cast<const uint4*>(norm_w);
-  for (int c = tid; c < kc; c += kConsumers) {
-    uint4 v = xs[c];
-    uint4 g = g4[c];
-    const __half2* hv = reinterpret_cast<const __half2*>(&v);
-    const __half2* hg = reinterpret_cast<const __half2*>(&g);
-    uint4 o;
-    __half2* ho = reinterpret_cast<__half2*>(&o);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      float2 f = __half22float2(hv[i]);
-      float2 gg = __half22float2(hg[i]);
-      ho[i] = __floats2half2_rn(norm_mul(f.x, scale, gg.x), norm_mul(f.y, scale, gg.y));
-    }
-    xs[c] = o;
-  }
+  for (int c = tid; c < kc; c += kConsumers) xs[c] = normalize_chunk(xs[c], __ldg(g4 + c), scale);
   consumers_sync();
 }
 
 // ---- consumers: rows from the ring --------------------------------------------------
-// Reduces this CTA's rows of stage `st` (local row r goes to warp r mod 15)
-// and writes the stage outputs. `g` is the running tile counter.
-__device__ void reduce_rows(const DecodeLoop& p, int st, const StageW& s, const uint4* xs,
-                            const uint8_t* ring, Shared& sh, uint32_t& g, uint32_t& best_key,
-                            uint32_t& best_idx) {
+// Stage output of one reduced item (lane-local).
+template <int ST>
+__device__ __forceinline__ void put_item(const DecodeLoop& p, const StageW& s, int item, float a0,
+                                         float a1, uint32_t& best_key, uint32_t& best_idx) {
+  if (ST == kQKV) {
+    const int nq = s.n[0], nk = s.n[1];
+    const __half h0 = __float2half_rn(a0);
+    if (item < nq) p.q_raw[item] = h0;
+    else if (item < nq + nk) p.k_raw[item - nq] = h0;
+    else p.v_raw[item - nq - nk] = h0;
+  } else if (ST == kO) {
+    p.attn_o[item] = __float2half_rn(a0);
+  } else if (ST == kGU) {
+    const float gv = __half2float(__float2half_rn(a0));
+    const float uv = __half2float(__float2half_rn(a1));
+    p.act[item] = __float2half_rn(silu_mul(gv, uv));
+  } else if (ST == kDown) {
+    p.hidden_buf[item] = __hadd(__ldcg(p.residual + item), __float2half_rn(a0));
+  } else {
+    const __half h0 = __float2half_rn(a0);
+    p.logits[item] = h0;
+    const float v = __half2float(h0);
+    if (isfinite(v) && argmax_better(argmax_key(v), (uint32_t)item, best_key, best_idx)) {
+      best_key = argmax_key(v);
+      best_idx = (uint32_t)item;
+    }
+  }
+}
+
+// P consecutive rows (gate/up pairs for GU) reduced together: P independent
+// canonical FMA chains per lane and interleaved butterflies. Lane q writes
+// row q. Rows past `nr` repeat row 0 and are dropped.
+template <int ST, int P>
+__device__ __forceinline__ void rows_group(const DecodeLoop& p, const StageW& s, const uint4* xs,
+                                           const uint8_t* base, int r0, int nr, int cnt,
+                                           uint32_t row_bytes, int item0, int kc, int lanes,
+                                           uint32_t& best_key, uint32_t& best_idx) {
+  constexpr bool kPair = ST == kGU;
+  const int lane = threadIdx.x & 31;
+  const uint4* w[P];
+  const uint4* u[P];
+#pragma unroll
+  for (int q = 0; q < P; ++q) {
+    const int r = r0 + (q < nr ? q : 0);
+    w[q] = reinterpret_cast<const uint4*>(base + (size_t)r * row_bytes);
+    u[q] = reinterpret_cast<const uint4*>(base + (size_t)(cnt + r) * row_bytes);
+  }
+  float a[P], b[P];
+#pragma unroll
+  for (int q = 0; q < P; ++q) a[q] = b[q] = 0.f;
+  // Full blocks of kB chunks per lane with every shared-memory load issued
+  // before the block's FMA chains, then single chunks (chunk order per lane
+  // is unchanged).
+  constexpr int kB = (P == 1 && !kPair) ? 4 : (P == 2 && !kPair) ? 2 : 1;
+  int c = lane;
+  for (; c + 32 * (kB - 1) < kc; c += 32 * kB) {
+    uint4 xv[kB], wv[P][kB], uv[P][kB];
+#pragma unroll
+    for (int j = 0; j < kB; ++j) {
+      xv[j] = xs[c + 32 * j];
+#pragma unroll
+      for (int q = 0; q < P; ++q) {
+        wv[q][j] = w[q][c + 32 * j];
+        if (kPair) uv[q][j] = u[q][c + 32 * j];
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < kB; ++j)
+#pragma unroll
+      for (int q = 0; q < P; ++q) {
+        a[q] = chunk_dot(xv[j], wv[q][j], a[q]);
+        if (kPair) b[q] = chunk_dot(xv[j], uv[q][j], b[q]);
+      }
+  }
+  for (; c < kc; c += 32) {
+    const uint4 xv = xs[c];
+#pragma unroll
+    for (int q = 0; q < P; ++q) {
+      a[q] = chunk_dot(xv, w[q][c], a[q]);
+      if (kPair) b[q] = chunk_dot(xv, u[q][c], b[q]);
+    }
+  }
+  for (int o = lanes >> 1; o >= 1; o >>= 1) {
+#pragma unroll
+    for (int q = 0; q < P; ++q) {
+      a[q] = __fadd_rn(a[q], __shfl_xor_sync(0xffffffffu, a[q], o));
+      if (kPair) b[q] = __fadd_rn(b[q], __shfl_xor_sync(0xffffffffu, b[q], o));
+    }
+  }
+  if (lanes < 32) {
+#pragma unroll
+    for (int q = 0; q < P; ++q) {
+      a[q] = __shfl_sync(0xffffffffu, a[q], 0);
+      if (kPair) b[q] = __shfl_sync(0xffffffffu, b[q], 0);
+    }
+  }
+#pragma unroll
+  for (int q = 0; q < P; ++q)
+    if (lane == q && q < nr) put_item<ST>(p, s, item0 + q, a[q], b[q], best_key, best_idx);
+}
+
+// Reduces this CTA's rows of stage ST from the ring: groups of P local rows
+// (never straddling a tile) go round-robin to the 15 consumer warps; every
+// warp waits for every tile in order and releases it when done. `g` is the
+// running tile counter.
+template <int ST, int P>
+__device__ void reduce_rows_p(const DecodeLoop& p, const StageW& s, const Tiles& t,
+                              const uint4* xs, const uint8_t* ring, Shared& sh, uint32_t& g,
+                              uint32_t& best_key, uint32_t& best_idx) {
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
-  const Tiles t = tiles_of(p, s);
   const int kc = s.k >> 3;
   const int lanes = canon_lanes(s.k);
   const int S = p.slots;
+  const int rows = t.last - t.first;
   for (int tile = 0; tile < t.count; ++tile, ++g) {
     const int slot = (int)(g % S);
     const uint32_t use = g / S;
-    const bool ok = ring_wait(&sh.full[slot], use & 1u, sh, kCodeFull | st);
+    if (threadIdx.x == 0 && tile == 0) MI_TRACE_CUR(14);
+    const bool ok = ring_wait(&sh.full[slot], use & 1u, sh, kCodeFull | ST);
     if (threadIdx.x == 0 && tile == 0) MI_TRACE_CUR(5);
-    const int i0 = t.first + tile * t.per_tile;
-    const int cnt = min(t.per_tile, t.last - i0);
-    const uint8_t* base = ring + (size_t)slot * p.slot_bytes;
+    const int l0 = tile * t.per_tile;
+    const int cnt = min(t.per_tile, rows - l0);
     if (ok) {
-      const int lead = (warp - (tile * t.per_tile) % kConsumerWarps + kConsumerWarps) %
-                       kConsumerWarps;
-      for (int r = lead; r < cnt; r += kConsumerWarps) {
-        const uint4* w0 = reinterpret_cast<const uint4*>(base + (size_t)r * t.row_bytes);
-        float a0 = 0.f, a1 = 0.f;
-        if (st == kGU) {
-          const uint4* w1 = reinterpret_cast<const uint4*>(base + (size_t)(cnt + r) * t.row_bytes);
-          for (int c = lane; c < kc; c += 32) {
-            uint4 xv = xs[c];
-            a0 = chunk_dot(xv, w0[c], a0);
-            a1 = chunk_dot(xv, w1[c], a1);
-          }
-          a1 = canon_reduce(a1, lanes);
-        } else {
-          for (int c = lane; c < kc; c += 32) a0 = chunk_dot(xs[c], w0[c], a0);
-        }
-        a0 = canon_reduce(a0, lanes);
-        if (threadIdx.x == 0 && tile == 0 && r == lead) MI_TRACE_CUR(6);
-        if (lane == 0) {
-          const int item = i0 + r;
-          switch (st) {
-            case kQKV: {
-              const int nq = s.n[0], nk = s.n[1];
-              __half h0 = __float2half_rn(a0);
-              if (item < nq) p.q_raw[item] = h0;
-              else if (item < nq + nk) p.k_raw[item - nq] = h0;
-              else p.v_raw[item - nq - nk] = h0;
-              break;
-            }
-            case kO:
-              p.attn_o[item] = __float2half_rn(a0);
-              break;
-            case kGU: {
-              float gv = __half2float(__float2half_rn(a0));
-              float uv = __half2float(__float2half_rn(a1));
-              p.act[item] = __float2half_rn(silu_mul(gv, uv));
-              break;
-            }
-            case kDown:
-              p.hidden_buf[item] = __hadd(__ldcg(p.residual + item), __float2half_rn(a0));
-              break;
-            default: {
-              __half h0 = __float2half_rn(a0);
-              p.logits[item] = h0;
-              float v = __half2float(h0);
-              if (isfinite(v) && argmax_better(argmax_key(v), (uint32_t)item, best_key, best_idx)) {
-                best_key = argmax_key(v);
-                best_idx = (uint32_t)item;
-              }
-              break;
-            }
-          }
-        }
+      const uint8_t* base = ring + (size_t)slot * p.slot_bytes;
+      const int g0 = l0 / P;
+      const int g1 = (l0 + cnt + P - 1) / P;
+      for (int gi = g0 + (warp - g0 % kConsumerWarps + kConsumerWarps) % kConsumerWarps; gi < g1;
+           gi += kConsumerWarps) {
+        const int r0 = gi * P - l0;
+        rows_group<ST, P>(p, s, xs, base, r0, min(P, cnt - r0), cnt, t.row_bytes, t.first + l0 + r0,
+                          kc, lanes, best_key, best_idx);
       }
     }
     __syncwarp();
@@ -475,7 +586,24 @@ __device__ void reduce_rows(const DecodeLoop& p, int st, const StageW& s, const 
   }
 }
 
-// ---- consumers: attention units (warps 0..3) -------------------------------------------
+template <int ST>
+__device__ void reduce_rows(const DecodeLoop& p, const StageW& s, const uint4* xs,
+                            const uint8_t* ring, Shared& sh, uint32_t& g, uint32_t& best_key,
+                            uint32_t& best_idx) {
+  const Tiles t = sh.tiles[ST];
+  const int rows = t.last - t.first;
+  if (ST == kLM && t.per_tile % 4 == 0 && rows >= 4 * kConsumerWarps)
+    reduce_rows_p<ST, 4>(p, s, t, xs, ring, sh, g, best_key, best_idx);
+  else if (t.per_tile % 2 == 0 && rows >= 16)
+    reduce_rows_p<ST, 2>(p, s, t, xs, ring, sh, g, best_key, best_idx);
+  else
+    reduce_rows_p<ST, 1>(p, s, t, xs, ring, sh, g, best_key, best_idx);
+}
+
+// ---- consumers: attention units (warps 4..11) -------------------------------------------
+// Thread index within the attention warps.
+__device__ __forceinline__ int atid() { return (int)threadIdx.x - kAttnBase; }
+
 // Stages keys [j0, j1) of KV head g (cp.async, 16 bytes per copy), skipping
 // position `skip` (the new token, taken from shared memory).
 template <int G>
@@ -484,7 +612,7 @@ __device__ void stage_keys(const LoopLayer& L, int kvh, int g, int j0, int j1, i
   const int per_row = HD * 2 / 16;
   const int total = (j1 - j0) * per_row;
   const size_t stride = (size_t)kvh * HD;
-  for (int i = threadIdx.x; i < total; i += kAttnThreads) {
+  for (int i = atid(); i < total; i += kAttnThreads) {
     int r = i / per_row, c = i - r * per_row;
     int j = j0 + r;
     if (j == skip) continue;
@@ -494,13 +622,56 @@ __device__ void stage_keys(const LoopLayer& L, int kvh, int g, int j0, int j1, i
   pipe::cp_async_commit();
 }
 
-// One flash-decode unit: KV head g_kv, key block b of nb (attention.cu's
-// attention_decode_kernel with the fused front end, run by 128 threads).
+// During the QKV stage (whose outputs the attention needs) a CTA that owns
+// attention unit blockIdx.x stages that unit's first key tile, which is
+// already final, and loads the layer's QK-norm weights and the RoPE terms of
+// the position into shared memory. Warps 4..11.
+template <int G>
+__device__ void attention_prefetch(const DecodeLoop& p, const LoopLayer& L, int pos,
+                                   AttnSmem<G>& sm) {
+  const int nb = (pos + p.block) / p.block;
+  if ((int)blockIdx.x >= p.kvh * nb) return;
+  const int g_kv = blockIdx.x / nb, b = blockIdx.x % nb;
+  const int begin = b * p.block;
+  const int end = min(pos + 1, begin + p.block);
+  stage_keys<G>(L, p.kvh, g_kv, begin, min(end, begin + kTile), pos, sm);
+  const int tid = atid();
+  if (tid < 16) reinterpret_cast<uint4*>(sm.qn_w)[tid] = __ldg(reinterpret_cast<const uint4*>(L.q_norm) + tid);
+  else if (tid < 32) reinterpret_cast<uint4*>(sm.kn_w)[tid - 16] = __ldg(reinterpret_cast<const uint4*>(L.k_norm) + tid - 16);
+  else if (tid < 32 + HD / 2 && p.rope) sm.rope[tid - 32] = __ldg(p.rope + (size_t)pos * (HD / 2) + (tid - 32));
+}
+
+// QK-norm + RoPE of one head half-warp from the prefetched shared copies
+// (the RoPE row of `pos` is passed as a one-row table at position 0).
+template <int G>
+__device__ __forceinline__ void head_rope(const DecodeLoop& p, const AttnSmem<G>& sm,
+                                          const uint4& raw, const __half* w, int pos,
+                                          unsigned mask, float (&out)[8]) {
+  if (p.rope)
+    norm_rope_half(raw, w, 0u, p.theta, p.eps, p.round_norm != 0, mask, sm.rope, out);
+  else
+    norm_rope_half(raw, w, (uint32_t)pos, p.theta, p.eps, p.round_norm != 0, mask, nullptr, out);
+}
+
+constexpr int kKeyBatch = 4;  // keys of a stream scored together
+
+// One flash-decode unit: KV head g_kv, key block b of nb. The arithmetic is
+// attention.cu's attention_decode_kernel with the fused front end; the
+// independent parts of consecutive keys of a stream (scores, exponentials)
+// are computed together, the dependent online-softmax updates stay in key
+// order. Run by warps 4..11: for G >= 2 the two warpgroups each take half of
+// the query heads of the group over the same 8 key streams.
 template <int G>
 __device__ void attention_unit(const DecodeLoop& p, const LoopLayer& L, int g_kv, int b, int nb,
-                               int pos, AttnSmem<G>& sm, Shared& sh) {
+                               int pos, bool prefetched, AttnSmem<G>& sm) {
+  constexpr int NG = G >= 2 ? 2 : 1;  // warpgroups sharing the heads
+  constexpr int GS = G / NG;          // heads per warpgroup
+  const int t = atid();
+  const int wg = t >> 7;
+  const bool active = wg < NG;
+  const int g0 = wg * GS;
   const int lane = threadIdx.x & 31;
-  const int warp = threadIdx.x >> 5;
+  const int warp = (t & 127) >> 5;
   const int li = lane & 15;
   const int hw = warp * 2 + (lane >> 4);
   const int Lk = pos + 1;
@@ -508,41 +679,43 @@ __device__ void attention_unit(const DecodeLoop& p, const LoopLayer& L, int g_kv
   const int end = min(Lk, begin + p.block);
   const int ntiles = (end - begin + kTile - 1) / kTile;
 
-  if (hw < G) {
-    const unsigned mask = (warp * 2 + 1 < G) ? 0xffffffffu : 0x0000ffffu;
-    uint4 raw = __ldcg(reinterpret_cast<const uint4*>(p.q_raw + (size_t)(g_kv * G + hw) * HD) + li);
-    float qv[8];
-    norm_rope_half(raw, L.q_norm, (uint32_t)pos, p.theta, p.eps, p.round_norm != 0, mask, p.rope,
-                   qv);
+  {
+    const int hq = t >> 4;  // one query head per half-warp
+    if (hq < G) {
+      const unsigned mask = ((t >> 5) * 2 + 1 < G) ? 0xffffffffu : 0x0000ffffu;
+      const uint4 raw =
+          __ldcg(reinterpret_cast<const uint4*>(p.q_raw + (size_t)(g_kv * G + hq) * HD) + li);
+      float qv[8];
+      head_rope<G>(p, sm, raw, sm.qn_w, pos, mask, qv);
 #pragma unroll
-    for (int e = 0; e < 8; ++e) sm.q[hw][8 * li + e] = qv[e];
+      for (int e = 0; e < 8; ++e) sm.q[hq][8 * li + e] = qv[e];
+    }
   }
-  if (pos >= begin && pos < end && warp == 3 && lane >= 16) {
-    uint4 raw = __ldcg(reinterpret_cast<const uint4*>(p.k_raw + (size_t)g_kv * HD) + li);
+  if (pos >= begin && pos < end && t >= kAttnThreads - 16) {
+    const uint4 raw = __ldcg(reinterpret_cast<const uint4*>(p.k_raw + (size_t)g_kv * HD) + li);
+    const uint4 vv = __ldcg(reinterpret_cast<const uint4*>(p.v_raw + (size_t)g_kv * HD) + li);
     float kv[8];
-    norm_rope_half(raw, L.k_norm, (uint32_t)pos, p.theta, p.eps, p.round_norm != 0, 0xffff0000u,
-                   p.rope, kv);
+    head_rope<G>(p, sm, raw, sm.kn_w, pos, 0xffff0000u, kv);
     uint4 kk;
     __half2* hk = reinterpret_cast<__half2*>(&kk);
 #pragma unroll
     for (int i = 0; i < 4; ++i) hk[i] = __floats2half2_rn(kv[2 * i], kv[2 * i + 1]);
-    uint4 vv = __ldcg(reinterpret_cast<const uint4*>(p.v_raw + (size_t)g_kv * HD) + li);
     const size_t row = (size_t)pos * p.kvh * HD + (size_t)g_kv * HD;
     reinterpret_cast<uint4*>(L.k_cache + row)[li] = kk;
     reinterpret_cast<uint4*>(L.v_cache + row)[li] = vv;
     reinterpret_cast<uint4*>(sm.new_k)[li] = kk;
     reinterpret_cast<uint4*>(sm.new_v)[li] = vv;
   }
+  if (t == 0) MI_TRACE_CUR(5);
 
-  if (threadIdx.x == 0) MI_TRACE_CUR(5);
-  float qreg[G][8];
-  float m[G], l[G], acc[G][8];
+  float qreg[GS][8];
+  float m[GS], l[GS], acc[GS][8];
   attn_sync();
 #pragma unroll
-  for (int g = 0; g < G; ++g) {
+  for (int g = 0; g < GS; ++g) {
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
-      qreg[g][e] = sm.q[g][8 * li + e];
+      qreg[g][e] = active ? sm.q[g0 + g][8 * li + e] : 0.f;
       acc[g][e] = 0.f;
     }
     m[g] = -INFINITY;
@@ -550,138 +723,208 @@ __device__ void attention_unit(const DecodeLoop& p, const LoopLayer& L, int g_kv
   }
   const float scale = __frcp_rn(__fsqrt_rn((float)HD));
 
-  for (int t = 0; t < ntiles; ++t) {
-    const int j0 = begin + t * kTile;
+  for (int tl = 0; tl < ntiles; ++tl) {
+    const int j0 = begin + tl * kTile;
     const int j1 = min(end, j0 + kTile);
-    stage_keys<G>(L, p.kvh, g_kv, j0, j1, pos, sm);
+    if (tl > 0 || !prefetched) stage_keys<G>(L, p.kvh, g_kv, j0, j1, pos, sm);
     pipe::cp_async_wait_all();
     attn_sync();
-    if (threadIdx.x == 0 && t == 0) MI_TRACE_CUR(6);
-    // Stream hw takes block-relative keys hw, hw + 8, ...; both half-warps
-    // of a warp run the same trip count.
-    const int count = j1 - j0;
-    for (int base = warp * 2; base < count; base += kStreams) {
-      const int r = base + (lane >> 4);
-      const bool valid = r < count;
-      const int j = j0 + r;
-      uint4 kk = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
-      if (valid && j == pos) {
-        kk = reinterpret_cast<const uint4*>(sm.new_k)[li];
-        vv = reinterpret_cast<const uint4*>(sm.new_v)[li];
-      } else if (valid) {
-        kk = reinterpret_cast<const uint4*>(sm.k[r])[li];
-        vv = reinterpret_cast<const uint4*>(sm.v[r])[li];
+    if (t == 0 && tl == 0) MI_TRACE_CUR(6);
+    // Stream hw takes tile keys hw, hw + 8, ... in order; both half-warps of
+    // a warp run the same trip count (the score butterflies span the warp).
+    const int count = active ? j1 - j0 : 0;
+    for (int base = warp * 2; base < count; base += kStreams * kKeyBatch) {
+      uint4 kk[kKeyBatch];
+      bool valid[kKeyBatch];
+#pragma unroll
+      for (int q = 0; q < kKeyBatch; ++q) {
+        const int r = base + q * kStreams + (lane >> 4);
+        valid[q] = r < count;
+        const int rr = valid[q] ? r : 0;
+        kk[q] = (j0 + rr == pos) ? reinterpret_cast<const uint4*>(sm.new_k)[li]
+                                 : reinterpret_cast<const uint4*>(sm.k[rr])[li];
       }
-      float kf[8], vf[8];
-      const __half2* hk = reinterpret_cast<const __half2*>(&kk);
-      const __half2* hv = reinterpret_cast<const __half2*>(&vv);
+      float sc[GS][kKeyBatch];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        float2 fk = __half22float2(hk[i]);
-        float2 fv = __half22float2(hv[i]);
-        kf[2 * i] = fk.x;
-        kf[2 * i + 1] = fk.y;
-        vf[2 * i] = fv.x;
-        vf[2 * i + 1] = fv.y;
+      for (int q = 0; q < kKeyBatch; ++q) {
+        float kf[8];
+        const __half2* hk = reinterpret_cast<const __half2*>(&kk[q]);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          float2 f = __half22float2(hk[i]);
+          kf[2 * i] = f.x;
+          kf[2 * i + 1] = f.y;
+        }
+#pragma unroll
+        for (int g = 0; g < GS; ++g) {
+          float d = 0.f;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) d = __fmaf_rn(qreg[g][e], kf[e], d);
+          sc[g][q] = d;
+        }
       }
 #pragma unroll
-      for (int g = 0; g < G; ++g) {
-        float d = 0.f;
+      for (int o = 8; o >= 1; o >>= 1)
 #pragma unroll
-        for (int e = 0; e < 8; ++e) d = __fmaf_rn(qreg[g][e], kf[e], d);
-        float s = __fmul_rn(canon_butterfly(d, 16), scale);
-        if (!valid) continue;
-        float nm = fmaxf(m[g], s);
-        float pa = mi_exp(__fsub_rn(m[g], nm));
-        float pc = mi_exp(__fsub_rn(s, nm));
+        for (int q = 0; q < kKeyBatch; ++q)
 #pragma unroll
-        for (int e = 0; e < 8; ++e) acc[g][e] = __fmaf_rn(acc[g][e], pa, __fmul_rn(pc, vf[e]));
-        l[g] = __fmaf_rn(l[g], pa, pc);
-        m[g] = nm;
+          for (int g = 0; g < GS; ++g)
+            sc[g][q] = __fadd_rn(sc[g][q], __shfl_xor_sync(0xffffffffu, sc[g][q], o));
+      if (t == 0 && tl == 0 && base == 0) MI_TRACE_CUR(11);
+      // running maxima in key order, then every exponential at once
+      float mp[GS][kKeyBatch], mn[GS][kKeyBatch];
+#pragma unroll
+      for (int g = 0; g < GS; ++g) {
+        float mm = m[g];
+#pragma unroll
+        for (int q = 0; q < kKeyBatch; ++q) {
+          sc[g][q] = __fmul_rn(sc[g][q], scale);
+          mp[g][q] = mm;
+          if (valid[q]) mm = fmaxf(mm, sc[g][q]);
+          mn[g][q] = mm;
+        }
+        m[g] = mm;
       }
+      float pa[GS][kKeyBatch], pc[GS][kKeyBatch];
+#pragma unroll
+      for (int g = 0; g < GS; ++g)
+#pragma unroll
+        for (int q = 0; q < kKeyBatch; ++q) {
+          pa[g][q] = mi_exp(__fsub_rn(mp[g][q], mn[g][q]));
+          pc[g][q] = mi_exp(__fsub_rn(sc[g][q], mn[g][q]));
+        }
+      if (t == 0 && tl == 0 && base == 0) MI_TRACE_CUR(12);
+#pragma unroll
+      for (int q = 0; q < kKeyBatch; ++q) {
+        if (!valid[q]) continue;
+        const int r = base + q * kStreams + (lane >> 4);
+        const uint4 vv = (j0 + r == pos) ? reinterpret_cast<const uint4*>(sm.new_v)[li]
+                                         : reinterpret_cast<const uint4*>(sm.v[r])[li];
+        const __half2* hv = reinterpret_cast<const __half2*>(&vv);
+        float vf[8];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          float2 f = __half22float2(hv[i]);
+          vf[2 * i] = f.x;
+          vf[2 * i + 1] = f.y;
+        }
+#pragma unroll
+        for (int g = 0; g < GS; ++g) {
+#pragma unroll
+          for (int e = 0; e < 8; ++e)
+            acc[g][e] = __fmaf_rn(acc[g][e], pa[g][q], __fmul_rn(pc[g][q], vf[e]));
+          l[g] = __fmaf_rn(l[g], pa[g][q], pc[g][q]);
+        }
+      }
+      if (t == 0 && tl == 0 && base == 0) MI_TRACE_CUR(13);
     }
     attn_sync();
   }
+  if (t == 0) MI_TRACE_CUR(7);
 
-  if (threadIdx.x == 0) MI_TRACE_CUR(7);
-  // Stream merge (index order) -> block partial.
+  // Stream merge (index order) -> block partial; the factors once per (stream, head).
+  if (active) {
 #pragma unroll
-  for (int g = 0; g < G; ++g) {
-    if (li == 0) {
-      sm.m[hw][g] = m[g];
-      sm.l[hw][g] = l[g];
+    for (int g = 0; g < GS; ++g) {
+      if (li == 0) {
+        sm.m[hw][g0 + g] = m[g];
+        sm.l[hw][g0 + g] = l[g];
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) sm.acc[hw][g0 + g][8 * li + e] = acc[g][e];
     }
+  }
+  attn_sync();
+  if (t < kStreams * G) {
+    const int s = t / G, g = t % G;
+    float M = -INFINITY;
 #pragma unroll
-    for (int e = 0; e < 8; ++e) sm.acc[hw][g][8 * li + e] = acc[g][e];
+    for (int u = 0; u < kStreams; ++u) M = fmaxf(M, sm.m[u][g]);
+    sm.f[s][g] = sm.m[s][g] == -INFINITY ? 0.f : mi_exp(__fsub_rn(sm.m[s][g], M));
+    if (s == 0) sm.M[g] = M;
   }
   attn_sync();
   const int stride = HD + 2;
   float* part = p.attn_part + ((size_t)g_kv * p.attn_blocks + b) * G * stride;
-  for (int idx = threadIdx.x; idx < G * HD; idx += kAttnThreads) {
-    int g = idx / HD, d = idx - g * HD;
-    float M = -INFINITY;
-#pragma unroll
-    for (int s = 0; s < kStreams; ++s) M = fmaxf(M, sm.m[s][g]);
+  for (int idx = t; idx < G * HD; idx += kAttnThreads) {
+    const int g = idx / HD, d = idx - g * HD;
     float num = 0.f, den = 0.f;
 #pragma unroll
     for (int s = 0; s < kStreams; ++s) {
-      float f = sm.m[s][g] == -INFINITY ? 0.f : mi_exp(__fsub_rn(sm.m[s][g], M));
-      num = __fmaf_rn(sm.acc[s][g][d], f, num);
-      den = __fmaf_rn(sm.l[s][g], f, den);
+      num = __fmaf_rn(sm.acc[s][g][d], sm.f[s][g], num);
+      den = __fmaf_rn(sm.l[s][g], sm.f[s][g], den);
     }
     if (nb == 1) {
       p.attn[(size_t)(g_kv * G + g) * HD + d] = __float2half_rn(__fdiv_rn(num, den));
     } else {
       part[g * stride + 2 + d] = num;
       if (d == 0) {
-        part[g * stride] = M;
+        part[g * stride] = sm.M[g];
         part[g * stride + 1] = den;
       }
     }
   }
-  if (threadIdx.x == 0) MI_TRACE_CUR(8);
+  if (t == 0) MI_TRACE_CUR(8);
   if (nb == 1) {
     attn_sync();  // shared state is reused by the next unit
     return;
   }
   __threadfence();
   attn_sync();
-  if (threadIdx.x == 0) sm.last = atomicAdd(p.attn_count + g_kv, 1u) == (uint32_t)nb - 1;
+  if (t == 0) sm.last = atomicAdd(p.attn_count + g_kv, 1u) == (uint32_t)nb - 1;
   attn_sync();
   if (sm.last) {
+    // Last block of the head: log-sum-exp merge of all blocks in index order.
     __threadfence();
     const float* hb = p.attn_part + (size_t)g_kv * p.attn_blocks * G * stride;
-    for (int idx = threadIdx.x; idx < G * HD; idx += kAttnThreads) {
-      int g = idx / HD, d = idx - g * HD;
+    for (int idx = t; idx < G * HD; idx += kAttnThreads) {
+      const int g = idx / HD, d = idx - g * HD;
       float M = -INFINITY;
+#pragma unroll 8
       for (int s = 0; s < nb; ++s) M = fmaxf(M, __ldcg(hb + (size_t)(s * G + g) * stride));
       float num = 0.f, den = 0.f;
+#pragma unroll 8
       for (int s = 0; s < nb; ++s) {
         const float* ps = hb + (size_t)(s * G + g) * stride;
-        float mm = __ldcg(ps);
-        float f = mm == -INFINITY ? 0.f : mi_exp(__fsub_rn(mm, M));
+        const float mm = __ldcg(ps);
+        const float f = mm == -INFINITY ? 0.f : mi_exp(__fsub_rn(mm, M));
         den = __fmaf_rn(__ldcg(ps + 1), f, den);
         num = __fmaf_rn(__ldcg(ps + 2 + d), f, num);
       }
       p.attn[(size_t)(g_kv * G + g) * HD + d] = __float2half_rn(__fdiv_rn(num, den));
     }
-    if (threadIdx.x == 0) p.attn_count[g_kv] = 0u;
-    if (threadIdx.x == 0) MI_TRACE_CUR(10);
+    if (t == 0) p.attn_count[g_kv] = 0u;
+    if (t == 0) MI_TRACE_CUR(10);
   }
-  if (threadIdx.x == 0) MI_TRACE_CUR(9);
+  if (t == 0) MI_TRACE_CUR(9);
   attn_sync();
 }
 
 template <int G>
-__global__ void __launch_bounds__(kThreads, 1) decode_loop_kernel(DecodeLoop p) {
+__global__ void __launch_bounds__(kThreads, 1) decode_loop_kernel(DecodeLoop params) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ Shared sh;
+  // Parameters live in shared memory: a persistent kernel would otherwise
+  // miss the constant cache on them at every stage.
+  __shared__ DecodeLoop p;
+  if (threadIdx.x == 0) p = params;
+  __syncthreads();
   uint8_t* ring = smem;
   uint4* xs = reinterpret_cast<uint4*>(smem + (size_t)p.slots * p.slot_bytes);
   AttnSmem<G>& asm_ = *reinterpret_cast<AttnSmem<G>*>(smem + (size_t)p.slots * p.slot_bytes +
                                                         p.x_bytes);
+  LoopLayer* lay = reinterpret_cast<LoopLayer*>(smem + (size_t)p.slots * p.slot_bytes + p.x_bytes +
+                                                (sizeof(AttnSmem<G>) + 127) / 128 * 128);
   const int tid = threadIdx.x;
+  {
+    // per-layer pointer table -> shared memory (read at every stage)
+    const int words = p.layers * (int)(sizeof(LoopLayer) / 8);
+    const unsigned long long* src = reinterpret_cast<const unsigned long long*>(p.layer);
+    unsigned long long* dst = reinterpret_cast<unsigned long long*>(lay);
+    for (int i = tid; i < words; i += kThreads) dst[i] = src[i];
+  }
   if (tid == 0) {
+    for (int st = 0; st < 5; ++st) sh.tiles[st] = tiles_of(p, stage_weights(p, lay, 0, st));
     for (int s = 0; s < p.slots; ++s) {
       pipe::mbar_init(&sh.full[s], 1);
       pipe::mbar_init(&sh.empty[s], kConsumerWarps);
@@ -692,7 +935,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_loop_kernel(DecodeLoop p) 
   __syncthreads();
 
   if (tid >= kConsumers) {
-    if (tid == kConsumers) produce(p, ring, sh);
+    if (tid == kConsumers) produce(p, lay, ring, sh);
     return;
   }
 
@@ -703,12 +946,14 @@ __global__ void __launch_bounds__(kThreads, 1) decode_loop_kernel(DecodeLoop p) 
   for (int step = 0; step < p.steps; ++step) {
     const int pos = (int)len0 + step;
     for (int layer = 0; layer < p.layers; ++layer) {
-      const LoopLayer& L = p.layer[layer];
+      const LoopLayer& L = lay[layer];
       uint32_t bk = 0, bi = 0xFFFFFFFFu;
       // QKV
       {
         if (tid == 0) { MI_TRACE(step, layer * 5 + 0, 0); MI_TRACE_SET(step, layer * 5 + 0); }
-        StageW s = stage_weights(p, layer, kQKV);
+        if (tid >= kAttnBase && tid < kAttnBase + kAttnThreads)
+          attention_prefetch<G>(p, L, pos, asm_);
+        const StageW s = stage_weights(p, lay, layer, kQKV);
         if (layer == 0) {
           const bool zero = token == 0xFFFFFFFFu || token >= (uint32_t)p.vocab;
           build_input(kEmbedNormIn, zero ? nullptr : p.embedding + (size_t)token * p.hidden,
@@ -717,7 +962,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_loop_kernel(DecodeLoop p) 
           build_input(kNormIn, p.hidden_buf, nullptr, L.in_norm, p.hidden, p.eps, nullptr, xs, sh);
         }
         if (tid == 0) MI_TRACE(step, layer * 5 + 0, 1);
-        reduce_rows(p, kQKV, s, xs, ring, sh, g, bk, bi);
+        reduce_rows<kQKV>(p, s, xs, ring, sh, g, bk, bi);
         if (tid == 0) MI_TRACE(step, layer * 5 + 0, 2);
         if (!grid_sync(p, epoch, sh)) return;
       }
@@ -726,40 +971,40 @@ __global__ void __launch_bounds__(kThreads, 1) decode_loop_kernel(DecodeLoop p) 
         if (tid == 0) { MI_TRACE(step, layer * 5 + 1, 0); MI_TRACE_SET(step, layer * 5 + 1); }
         const int nb = (pos + p.block) / p.block;  // ceil((pos + 1) / block)
         const int units = p.kvh * nb;
-        if (tid < kAttnThreads)
+        if (tid >= kAttnBase && tid < kAttnBase + kAttnThreads)
           for (int u = blockIdx.x; u < units; u += gridDim.x)
-            attention_unit<G>(p, L, u / nb, u % nb, nb, pos, asm_, sh);
+            attention_unit<G>(p, L, u / nb, u % nb, nb, pos, u == (int)blockIdx.x, asm_);
         if (tid == 0) MI_TRACE(step, layer * 5 + 1, 2);
         if (!grid_sync(p, epoch, sh)) return;
       }
       // O
       {
         if (tid == 0) { MI_TRACE(step, layer * 5 + 2, 0); MI_TRACE_SET(step, layer * 5 + 2); }
-        StageW s = stage_weights(p, layer, kO);
+        const StageW s = stage_weights(p, lay, layer, kO);
         build_input(kPlainIn, p.attn, nullptr, nullptr, s.k, p.eps, nullptr, xs, sh);
         if (tid == 0) MI_TRACE(step, layer * 5 + 2, 1);
-        reduce_rows(p, kO, s, xs, ring, sh, g, bk, bi);
+        reduce_rows<kO>(p, s, xs, ring, sh, g, bk, bi);
         if (tid == 0) MI_TRACE(step, layer * 5 + 2, 2);
         if (!grid_sync(p, epoch, sh)) return;
       }
       // GU
       {
         if (tid == 0) { MI_TRACE(step, layer * 5 + 3, 0); MI_TRACE_SET(step, layer * 5 + 3); }
-        StageW s = stage_weights(p, layer, kGU);
+        const StageW s = stage_weights(p, lay, layer, kGU);
         build_input(p.add_norm ? kAddNormIn : kAddThenNormIn, p.hidden_buf, p.attn_o, L.post_norm,
                     p.hidden, p.eps, p.residual, xs, sh);
         if (tid == 0) MI_TRACE(step, layer * 5 + 3, 1);
-        reduce_rows(p, kGU, s, xs, ring, sh, g, bk, bi);
+        reduce_rows<kGU>(p, s, xs, ring, sh, g, bk, bi);
         if (tid == 0) MI_TRACE(step, layer * 5 + 3, 2);
         if (!grid_sync(p, epoch, sh)) return;
       }
       // DOWN
       {
         if (tid == 0) { MI_TRACE(step, layer * 5 + 4, 0); MI_TRACE_SET(step, layer * 5 + 4); }
-        StageW s = stage_weights(p, layer, kDown);
+        const StageW s = stage_weights(p, lay, layer, kDown);
         build_input(kPlainIn, p.act, nullptr, nullptr, s.k, p.eps, nullptr, xs, sh);
         if (tid == 0) MI_TRACE(step, layer * 5 + 4, 1);
-        reduce_rows(p, kDown, s, xs, ring, sh, g, bk, bi);
+        reduce_rows<kDown>(p, s, xs, ring, sh, g, bk, bi);
         if (tid == 0) MI_TRACE(step, layer * 5 + 4, 2);
         if (!grid_sync(p, epoch, sh)) return;
       }
@@ -768,11 +1013,21 @@ __global__ void __launch_bounds__(kThreads, 1) decode_loop_kernel(DecodeLoop p) 
     {
       if (tid == 0) { MI_TRACE(step, p.layers * 5, 0); MI_TRACE_SET(step, p.layers * 5); }
       uint32_t bk = 0, bi = 0xFFFFFFFFu;
-      StageW s = stage_weights(p, p.layers, kLM);
+      const StageW s = stage_weights(p, lay, p.layers, kLM);
       build_input(kNormIn, p.hidden_buf, nullptr, p.final_norm, p.hidden, p.eps, nullptr, xs, sh);
       if (tid == 0) MI_TRACE(step, p.layers * 5, 1);
-      reduce_rows(p, kLM, s, xs, ring, sh, g, bk, bi);
+      reduce_rows<kLM>(p, s, xs, ring, sh, g, bk, bi);
       if (tid == 0) MI_TRACE(step, p.layers * 5, 2);
+      // per-lane bests -> warp best -> CTA best -> grid partial
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const uint32_t ok = __shfl_xor_sync(0xffffffffu, bk, o);
+        const uint32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (argmax_better(ok, oi, bk, bi)) {
+          bk = ok;
+          bi = oi;
+        }
+      }
       if (lane == 0) {
         sh.best_key[warp] = bk;
         sh.best_idx[warp] = bi;
@@ -792,7 +1047,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_loop_kernel(DecodeLoop p) 
       if (warp == 0) {
         uint32_t ck = 0, ci = 0xFFFFFFFFu;
         for (int b = lane; b < (int)gridDim.x; b += 32) {
-          uint32_t k2 = __ldcg(p.argmax_key + b), i2 = __ldcg(p.argmax_idx + b);
+          const uint32_t k2 = __ldcg(p.argmax_key + b), i2 = __ldcg(p.argmax_idx + b);
           if (argmax_better(k2, i2, ck, ci)) {
             ck = k2;
             ci = i2;
@@ -800,8 +1055,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_loop_kernel(DecodeLoop p) 
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
-          uint32_t ok = __shfl_xor_sync(0xffffffffu, ck, o);
-          uint32_t oi = __shfl_xor_sync(0xffffffffu, ci, o);
+          const uint32_t ok = __shfl_xor_sync(0xffffffffu, ck, o);
+          const uint32_t oi = __shfl_xor_sync(0xffffffffu, ci, o);
           if (argmax_better(ok, oi, ck, ci)) {
             ck = ok;
             ci = oi;
@@ -833,6 +1088,8 @@ size_t attn_smem_for(int group) {
     default: return 0;
   }
 }
+
+size_t layer_table_bytes(int layers) { return (size_t)layers * sizeof(LoopLayer); }
 
 template <int G>
 cudaError_t launch_g(cudaStream_t stream, const DecodeLoop& p, int grid, size_t smem) {
@@ -867,25 +1124,27 @@ bool decode_loop_plan(DecodeLoop& p, int device) {
   if (cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device) !=
       cudaSuccess)
     return false;
-  const size_t fixed = (size_t)p.x_bytes + attn_smem_for(group) + sizeof(Shared) + 1024;
+  const size_t fixed = (size_t)p.x_bytes + attn_smem_for(group) + layer_table_bytes(p.layers) +
+                       sizeof(Shared) + 1024;
   if (fixed >= (size_t)optin) return false;
   p.slots = (int)std::min<size_t>(kMaxSlots, ((size_t)optin - fixed) / p.slot_bytes);
   if (p.slots < 2) return false;
   int sms = 0;
   if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess)
     return false;
-  p.grid = sms;
+  p.grid = std::min(sms, kMaxGrid);
   return true;
 }
 
 size_t decode_loop_smem(const DecodeLoop& p) {
-  return (size_t)p.slots * p.slot_bytes + p.x_bytes + attn_smem_for(p.qh / p.kvh);
+  return (size_t)p.slots * p.slot_bytes + p.x_bytes + attn_smem_for(p.qh / p.kvh) +
+         layer_table_bytes(p.layers);
 }
 
 void decode_loop(cudaStream_t stream, const DecodeLoop& p) {
   MI_REQUIRE(p.steps > 0 && p.grid > 0 && p.slots >= 2, MI_ERR_INVALID_ARGUMENT,
              "decode loop plan missing");
-  MI_CUDA(cudaMemsetAsync(p.sync, 0, 2 * sizeof(uint32_t), stream));
+  MI_CUDA(cudaMemsetAsync(p.sync, 0, kSyncWords * sizeof(uint32_t), stream));
   const size_t smem = decode_loop_smem(p);
   cudaError_t err = cudaErrorInvalidValue;
   switch (p.qh / p.kvh) {
@@ -901,8 +1160,10 @@ void decode_loop(cudaStream_t stream, const DecodeLoop& p) {
 
 #ifdef MI_DECODE_TRACE
 extern "C" int mi_debug_decode_trace(unsigned long long* out, size_t n) {
-  if (n < sizeof(g_trace) / 8) return -1;  // [2][2][321][12]
-  return cudaMemcpyFromSymbol(out, g_trace, sizeof(g_trace)) == cudaSuccess ? 0 : -2;
+  if (n < (sizeof(g_trace) + sizeof(g_arrive)) / 8) return -1;  // [2][2][321][16] + [256][5][2]
+  if (cudaMemcpyFromSymbol(out, g_trace, sizeof(g_trace)) != cudaSuccess) return -2;
+  return cudaMemcpyFromSymbol(out + sizeof(g_trace) / 8, g_arrive, sizeof(g_arrive)) == cudaSuccess
+             ? 0 : -2;
 }
 #endif
 

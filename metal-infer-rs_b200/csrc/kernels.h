@@ -212,7 +212,7 @@ struct DecodeLoop {
   uint32_t* attn_count = nullptr; // [kvh], zero on entry and exit
   uint32_t* argmax_key = nullptr; // [grid]
   uint32_t* argmax_idx = nullptr; // [grid]
-  uint32_t* sync = nullptr;       // [2]: grid-barrier counter, abort flag
+  uint32_t* sync = nullptr;       // [decode_loop_sync_words()]: barrier counter, abort flag
   // plan (decode_loop_plan)
   int slot_bytes = 0, slots = 0, x_bytes = 0, grid = 0;
 };
@@ -220,6 +220,8 @@ struct DecodeLoop {
 // device's shared memory does not admit the persistent kernel.
 bool decode_loop_plan(DecodeLoop& p, int device);
 void decode_loop(cudaStream_t stream, const DecodeLoop& p);
+// u32 words of DecodeLoop::sync.
+constexpr size_t decode_loop_sync_words() { return 32; }
 // Expired-wait code of the persistent kernel (0 = none), optionally cleared.
 unsigned decode_loop_status(bool reset);
 

@@ -24,14 +24,16 @@ namespace mi {
 namespace k {
 
 __device__ __forceinline__ float mi_exp(float x) {
-  if (x != x) return x;
-  if (x > 89.0f) return __int_as_float(0x7f800000);
-  if (x < -104.0f) return 0.0f;
+  // Branch-free: the reduction runs on x clamped to [-104, 89] and the
+  // out-of-range / NaN results are selected at the end. 2^n is applied as
+  // 2^(n >> 1) * 2^(n - (n >> 1)): the first product is exact, so the result
+  // carries the single rounding of p * 2^n, also where it is subnormal.
   const float kLog2e = 0x1.715476p+0f;
   const float kLn2Hi = 0x1.62e4p-1f;
   const float kLn2Lo = 0x1.7f7d1cp-20f;
-  float n = rintf(__fmul_rn(x, kLog2e));
-  float r = __fmaf_rn(n, -kLn2Hi, x);
+  const float xc = fminf(fmaxf(x, -104.0f), 89.0f);
+  float n = rintf(__fmul_rn(xc, kLog2e));
+  float r = __fmaf_rn(n, -kLn2Hi, xc);
   r = __fmaf_rn(n, -kLn2Lo, r);
   float p = 0x1.a01a02p-13f;
   p = __fmaf_rn(p, r, 0x1.6c16c2p-10f);
@@ -41,12 +43,14 @@ __device__ __forceinline__ float mi_exp(float x) {
   p = __fmaf_rn(p, r, 0.5f);
   p = __fmaf_rn(p, r, 1.0f);
   p = __fmaf_rn(p, r, 1.0f);
-  int ni = (int)n;
-  if (ni < -126)
-    return __fmul_rn(__fmul_rn(p, __int_as_float((ni + 64 + 127) << 23)),
-                     __int_as_float((-64 + 127) << 23));
-  if (ni > 127) return __fmul_rn(__fmul_rn(p, __int_as_float((127 + 127) << 23)), 2.0f);
-  return __fmul_rn(p, __int_as_float((ni + 127) << 23));
+  const int ni = (int)n;
+  const int n1 = ni >> 1;
+  const int n2 = ni - n1;
+  float res = __fmul_rn(__fmul_rn(p, __int_as_float((n1 + 127) << 23)),
+                        __int_as_float((n2 + 127) << 23));
+  res = x > 89.0f ? __int_as_float(0x7f800000) : res;
+  res = x < -104.0f ? 0.0f : res;
+  return x != x ? x : res;
 }
 
 // Lanes of the canonical reduction for n elements.

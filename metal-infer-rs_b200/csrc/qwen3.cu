@@ -397,7 +397,8 @@ void run_decode_loop(mi_qwen3* m, mi_kv_cache* c, size_t steps) {
   mi_context* ctx = m->ctx;
   ensure_workspace(m, c->capacity);
   auto& w = m->ws;
-  if (!w.loop_sync.t) w.loop_sync = TensorRef(new_tensor(ctx, {2}, MI_U32, true));
+  if (!w.loop_sync.t)
+    w.loop_sync = TensorRef(new_tensor(ctx, {k::decode_loop_sync_words()}, MI_U32, true));
   if (!c->loop_layers.t) {
     c->loop_host.resize(m->layers.size());
     for (size_t li = 0; li < m->layers.size(); ++li) {
