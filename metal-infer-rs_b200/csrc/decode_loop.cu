@@ -46,7 +46,15 @@ constexpr int kTile = 64;                  // keys staged per attention tile
 constexpr int kAttnThreads = 256;          // warps 4..11 run the attention units
 constexpr int kAttnBase = 128;             // (warp 0 keeps the stage-input norms)
 constexpr int kMaxSlots = 16;
-constexpr int kSyncWords = 32;    // sync[]: [0] barrier counter, [1] abort flag
+// sync[]: [0] barrier counter, [1] abort flag, [2] attention units finished,
+// [kHeadReady + h] QKV rows written for KV head h (counts cumulative over
+// the launch).
+constexpr int kUnitsDone = 2;
+constexpr int kHeadReady = 32;
+constexpr int kPart = HD + 4;  // partial record: max, denominator, 2 pad, 128 numerators
+constexpr int kSyncWords = 256;
+constexpr int kMaxKvHeads = 64;
+constexpr int kMaxDownRows = 64;
 constexpr int kMaxGrid = 256;
 constexpr int kMinSlotBytes = 32 * 1024;
 
@@ -90,6 +98,7 @@ constexpr unsigned kCodeFull = 0x0100;
 constexpr unsigned kCodeEmpty = 0x0200;
 constexpr unsigned kCodeGrid = 0x0300;
 constexpr unsigned kCodeDrain = 0x0400;
+constexpr unsigned kCodeHead = 0x0500;
 
 struct StageW {
   const __half* w[3];
@@ -181,10 +190,14 @@ struct Shared {
   uint64_t empty[kMaxSlots];
   Tiles tiles[5];  // this CTA's tiling of each stage (the same in every layer)
   float scale;
+  uint32_t qkv_rows[kMaxKvHeads];  // QKV rows this CTA writes per KV head
+  __half res[kMaxDownRows];         // DOWN: residual values of this CTA's rows
   uint32_t best_key[kConsumerWarps];
   uint32_t best_idx[kConsumerWarps];
   uint32_t token;
-  volatile int abort;
+  volatile int abort;  // raised by any warp (or the producer) that gives up
+  int stop;            // the consumers' uniform decision, written by one thread between barriers
+  int astop;           // the same for the attention warps
 };
 
 __device__ __forceinline__ void consumers_sync() {
@@ -260,9 +273,105 @@ __device__ bool grid_sync(const DecodeLoop& p, uint32_t& epoch, Shared& sh) {
       __threadfence();
       MI_TRACE_ARRIVE(1);
     }
+    sh.stop = sh.abort ? 1 : 0;
   }
   consumers_sync();
-  return !sh.abort;
+  return !sh.stop;
+}
+
+// Single-thread bounded wait until *ctr >= target (cumulative counters of
+// the per-head dataflow); false when the kernel is aborting.
+__device__ bool wait_counter(const DecodeLoop& p, const uint32_t* ctr, uint32_t target,
+                             Shared& sh) {
+  volatile uint32_t* abort_flag = p.sync + 1;
+  uint64_t start = 0;
+  while (ld_relaxed(ctr) < target) {
+    if (*abort_flag || sh.abort) {
+      sh.abort = 1;
+      return false;
+    }
+    const uint64_t now = pipe::global_ns();
+    if (!start) {
+      start = now;
+    } else if (now - start > pipe::kWaitNs) {
+      record(kCodeHead);
+      sh.abort = 1;
+      *abort_flag = 1u;
+      return false;
+    }
+  }
+  __threadfence();
+  return true;
+}
+
+// End of the QKV stage: publish this CTA's rows per KV head (no barrier; the
+// attention units of a head wait for exactly its rows).
+__device__ bool publish_qkv(const DecodeLoop& p, Shared& sh) {
+  consumers_sync();
+  if (threadIdx.x == 0) {
+    if (!sh.abort)
+      for (int h = 0; h < p.kvh; ++h)
+        if (sh.qkv_rows[h]) red_release_add(p.sync + kHeadReady + h, sh.qkv_rows[h]);
+    sh.stop = sh.abort ? 1 : 0;
+  }
+  consumers_sync();
+  return !sh.stop;
+}
+
+// Start of the O stage: wait until `units` attention units (cumulative over
+// the launch) have published their block partials.
+__device__ bool wait_units(const DecodeLoop& p, uint32_t units, Shared& sh) {
+  if (threadIdx.x == 0) {
+    const bool ok = !sh.abort && wait_counter(p, p.sync + kUnitsDone, units, sh);
+    sh.stop = ok ? 0 : 1;
+  }
+  consumers_sync();
+  return !sh.stop;
+}
+
+// O-stage input: the attention output of every query head, the log-sum-exp
+// merge of its nb block partials in block order (the arithmetic of
+// attention.cu's final merge), written to xs as FP16.
+__device__ void build_attn_input(const DecodeLoop& p, int nb, uint4* xs) {
+  const int G = p.qh / p.kvh;
+  const int kc = p.qh * HD / 8;
+  const size_t block_stride = (size_t)G * kPart;
+  for (int c = threadIdx.x; c < kc; c += kConsumers) {
+    const int qi = c / (HD / 8);
+    const int d0 = (c % (HD / 8)) * 8;
+    const float* hb = p.attn_part + ((size_t)(qi / G) * p.attn_blocks * G + qi % G) * kPart;
+    float M = -INFINITY;
+#pragma unroll 4
+    for (int b = 0; b < nb; ++b) M = fmaxf(M, __ldcg(hb + b * block_stride));
+    float num[8], den = 0.f;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) num[e] = 0.f;
+#pragma unroll 4
+    for (int b = 0; b < nb; ++b) {
+      const float* rec = hb + b * block_stride;
+      const float mm = __ldcg(rec);
+      const float f = mm == -INFINITY ? 0.f : mi_exp(__fsub_rn(mm, M));
+      den = __fmaf_rn(__ldcg(rec + 1), f, den);
+      const float4 n0 = __ldcg(reinterpret_cast<const float4*>(rec + 4 + d0));
+      const float4 n1 = __ldcg(reinterpret_cast<const float4*>(rec + 8 + d0));
+      num[0] = __fmaf_rn(n0.x, f, num[0]);
+      num[1] = __fmaf_rn(n0.y, f, num[1]);
+      num[2] = __fmaf_rn(n0.z, f, num[2]);
+      num[3] = __fmaf_rn(n0.w, f, num[3]);
+      num[4] = __fmaf_rn(n1.x, f, num[4]);
+      num[5] = __fmaf_rn(n1.y, f, num[5]);
+      num[6] = __fmaf_rn(n1.z, f, num[6]);
+      num[7] = __fmaf_rn(n1.w, f, num[7]);
+    }
+    uint4 v;
+    __half2* hv = reinterpret_cast<__half2*>(&v);
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      hv[i] = __halves2half2(__float2half_rn(__fdiv_rn(num[2 * i], den)),
+                             __float2half_rn(__fdiv_rn(num[2 * i + 1], den)));
+    xs[c] = v;
+  }
+  consumers_sync();
 }
 
 // ---- producer -------------------------------------------------------------------
@@ -450,7 +559,8 @@ __device__ void build_input(int mode, const __half* x, const __half* x2, const _
 // Stage output of one reduced item (lane-local).
 template <int ST>
 __device__ __forceinline__ void put_item(const DecodeLoop& p, const StageW& s, int item, float a0,
-                                         float a1, uint32_t& best_key, uint32_t& best_idx) {
+                                         float a1, const __half* res, int res_first,
+                                         uint32_t& best_key, uint32_t& best_idx) {
   if (ST == kQKV) {
     const int nq = s.n[0], nk = s.n[1];
     const __half h0 = __float2half_rn(a0);
@@ -464,7 +574,9 @@ __device__ __forceinline__ void put_item(const DecodeLoop& p, const StageW& s, i
     const float uv = __half2float(__float2half_rn(a1));
     p.act[item] = __float2half_rn(silu_mul(gv, uv));
   } else if (ST == kDown) {
-    p.hidden_buf[item] = __hadd(__ldcg(p.residual + item), __float2half_rn(a0));
+    const int local = item - res_first;
+    const __half r = local < kMaxDownRows ? res[local] : __ldcg(p.residual + item);
+    p.hidden_buf[item] = __hadd(r, __float2half_rn(a0));
   } else {
     const __half h0 = __float2half_rn(a0);
     p.logits[item] = h0;
@@ -481,6 +593,7 @@ __device__ __forceinline__ void put_item(const DecodeLoop& p, const StageW& s, i
 // row q. Rows past `nr` repeat row 0 and are dropped.
 template <int ST, int P>
 __device__ __forceinline__ void rows_group(const DecodeLoop& p, const StageW& s, const uint4* xs,
+                                           const __half* res, int res_first,
                                            const uint8_t* base, int r0, int nr, int cnt,
                                            uint32_t row_bytes, int item0, int kc, int lanes,
                                            uint32_t& best_key, uint32_t& best_idx) {
@@ -545,7 +658,8 @@ __device__ __forceinline__ void rows_group(const DecodeLoop& p, const StageW& s,
   }
 #pragma unroll
   for (int q = 0; q < P; ++q)
-    if (lane == q && q < nr) put_item<ST>(p, s, item0 + q, a[q], b[q], best_key, best_idx);
+    if (lane == q && q < nr)
+      put_item<ST>(p, s, item0 + q, a[q], b[q], res, res_first, best_key, best_idx);
 }
 
 // Reduces this CTA's rows of stage ST from the ring: groups of P local rows
@@ -577,7 +691,8 @@ __device__ void reduce_rows_p(const DecodeLoop& p, const StageW& s, const Tiles&
       for (int gi = g0 + (warp - g0 % kConsumerWarps + kConsumerWarps) % kConsumerWarps; gi < g1;
            gi += kConsumerWarps) {
         const int r0 = gi * P - l0;
-        rows_group<ST, P>(p, s, xs, base, r0, min(P, cnt - r0), cnt, t.row_bytes, t.first + l0 + r0,
+        rows_group<ST, P>(p, s, xs, sh.res, t.first, base, r0, min(P, cnt - r0), cnt, t.row_bytes,
+                          t.first + l0 + r0,
                           kc, lanes, best_key, best_idx);
       }
     }
@@ -662,8 +777,9 @@ constexpr int kKeyBatch = 4;  // keys of a stream scored together
 // order. Run by warps 4..11: for G >= 2 the two warpgroups each take half of
 // the query heads of the group over the same 8 key streams.
 template <int G>
-__device__ void attention_unit(const DecodeLoop& p, const LoopLayer& L, int g_kv, int b, int nb,
-                               int pos, bool prefetched, AttnSmem<G>& sm) {
+__device__ bool attention_unit(const DecodeLoop& p, const LoopLayer& L, int g_kv, int b, int nb,
+                               int pos, bool prefetched, uint32_t ls, AttnSmem<G>& sm,
+                               Shared& sh) {
   constexpr int NG = G >= 2 ? 2 : 1;  // warpgroups sharing the heads
   constexpr int GS = G / NG;          // heads per warpgroup
   const int t = atid();
@@ -678,6 +794,13 @@ __device__ void attention_unit(const DecodeLoop& p, const LoopLayer& L, int g_kv
   const int begin = b * p.block;
   const int end = min(Lk, begin + p.block);
   const int ntiles = (end - begin + kTile - 1) / kTile;
+
+  // this head's Q/K/V rows of layer-step ls are all written
+  if (t == 0)
+    sh.astop = wait_counter(p, p.sync + kHeadReady + g_kv, (ls + 1u) * (uint32_t)((G + 2) * HD),
+                            sh) ? 0 : 1;
+  attn_sync();
+  if (sh.astop) return false;
 
   {
     const int hq = t >> 4;  // one query head per half-warp
@@ -844,8 +967,9 @@ __device__ void attention_unit(const DecodeLoop& p, const LoopLayer& L, int g_kv
     if (s == 0) sm.M[g] = M;
   }
   attn_sync();
-  const int stride = HD + 2;
-  float* part = p.attn_part + ((size_t)g_kv * p.attn_blocks + b) * G * stride;
+  // Block partial (max, denominator, numerators) of every head; the O stage
+  // merges the blocks.
+  float* part = p.attn_part + ((size_t)g_kv * p.attn_blocks + b) * G * kPart;
   for (int idx = t; idx < G * HD; idx += kAttnThreads) {
     const int g = idx / HD, d = idx - g * HD;
     float num = 0.f, den = 0.f;
@@ -854,50 +978,16 @@ __device__ void attention_unit(const DecodeLoop& p, const LoopLayer& L, int g_kv
       num = __fmaf_rn(sm.acc[s][g][d], sm.f[s][g], num);
       den = __fmaf_rn(sm.l[s][g], sm.f[s][g], den);
     }
-    if (nb == 1) {
-      p.attn[(size_t)(g_kv * G + g) * HD + d] = __float2half_rn(__fdiv_rn(num, den));
-    } else {
-      part[g * stride + 2 + d] = num;
-      if (d == 0) {
-        part[g * stride] = sm.M[g];
-        part[g * stride + 1] = den;
-      }
+    part[g * kPart + 4 + d] = num;
+    if (d == 0) {
+      part[g * kPart] = sm.M[g];
+      part[g * kPart + 1] = den;
     }
   }
   if (t == 0) MI_TRACE_CUR(8);
-  if (nb == 1) {
-    attn_sync();  // shared state is reused by the next unit
-    return;
-  }
-  __threadfence();
-  attn_sync();
-  if (t == 0) sm.last = atomicAdd(p.attn_count + g_kv, 1u) == (uint32_t)nb - 1;
-  attn_sync();
-  if (sm.last) {
-    // Last block of the head: log-sum-exp merge of all blocks in index order.
-    __threadfence();
-    const float* hb = p.attn_part + (size_t)g_kv * p.attn_blocks * G * stride;
-    for (int idx = t; idx < G * HD; idx += kAttnThreads) {
-      const int g = idx / HD, d = idx - g * HD;
-      float M = -INFINITY;
-#pragma unroll 8
-      for (int s = 0; s < nb; ++s) M = fmaxf(M, __ldcg(hb + (size_t)(s * G + g) * stride));
-      float num = 0.f, den = 0.f;
-#pragma unroll 8
-      for (int s = 0; s < nb; ++s) {
-        const float* ps = hb + (size_t)(s * G + g) * stride;
-        const float mm = __ldcg(ps);
-        const float f = mm == -INFINITY ? 0.f : mi_exp(__fsub_rn(mm, M));
-        den = __fmaf_rn(__ldcg(ps + 1), f, den);
-        num = __fmaf_rn(__ldcg(ps + 2 + d), f, num);
-      }
-      p.attn[(size_t)(g_kv * G + g) * HD + d] = __float2half_rn(__fdiv_rn(num, den));
-    }
-    if (t == 0) p.attn_count[g_kv] = 0u;
-    if (t == 0) MI_TRACE_CUR(10);
-  }
-  if (t == 0) MI_TRACE_CUR(9);
-  attn_sync();
+  attn_sync();  // partial written; shared state is reused by the next unit
+  if (t == 0) red_release_add(p.sync + kUnitsDone, 1u);
+  return true;
 }
 
 template <int G>
@@ -925,6 +1015,14 @@ __global__ void __launch_bounds__(kThreads, 1) decode_loop_kernel(DecodeLoop par
   }
   if (tid == 0) {
     for (int st = 0; st < 5; ++st) sh.tiles[st] = tiles_of(p, stage_weights(p, lay, 0, st));
+    for (int h = 0; h < kMaxKvHeads; ++h) sh.qkv_rows[h] = 0;
+    const int qw = p.qh * HD, kw = p.kvh * HD, gw = (p.qh / p.kvh) * HD;
+    for (int item = sh.tiles[kQKV].first; item < sh.tiles[kQKV].last; ++item) {
+      const int h = item < qw ? item / gw : item < qw + kw ? (item - qw) / HD : (item - qw - kw) / HD;
+      sh.qkv_rows[h] += 1u;
+    }
+    sh.stop = 0;
+    sh.astop = 0;
     for (int s = 0; s < p.slots; ++s) {
       pipe::mbar_init(&sh.full[s], 1);
       pipe::mbar_init(&sh.empty[s], kConsumerWarps);
@@ -942,6 +1040,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_loop_kernel(DecodeLoop par
   const uint32_t len0 = __ldcg(p.dev_len);
   uint32_t token = __ldcg(p.toks + len0);
   uint32_t g = 0, epoch = 0;
+  uint32_t units_total = 0;  // attention units published so far (all CTAs agree)
   const int warp = tid >> 5, lane = tid & 31;
   for (int step = 0; step < p.steps; ++step) {
     const int pos = (int)len0 + step;
@@ -964,24 +1063,28 @@ __global__ void __launch_bounds__(kThreads, 1) decode_loop_kernel(DecodeLoop par
         if (tid == 0) MI_TRACE(step, layer * 5 + 0, 1);
         reduce_rows<kQKV>(p, s, xs, ring, sh, g, bk, bi);
         if (tid == 0) MI_TRACE(step, layer * 5 + 0, 2);
-        if (!grid_sync(p, epoch, sh)) return;
+        if (!publish_qkv(p, sh)) return;
       }
       // ATTN
+      const uint32_t ls = (uint32_t)(step * p.layers + layer);  // layer-step index
       {
         if (tid == 0) { MI_TRACE(step, layer * 5 + 1, 0); MI_TRACE_SET(step, layer * 5 + 1); }
         const int nb = (pos + p.block) / p.block;  // ceil((pos + 1) / block)
         const int units = p.kvh * nb;
         if (tid >= kAttnBase && tid < kAttnBase + kAttnThreads)
           for (int u = blockIdx.x; u < units; u += gridDim.x)
-            attention_unit<G>(p, L, u / nb, u % nb, nb, pos, u == (int)blockIdx.x, asm_);
+            if (!attention_unit<G>(p, L, u / nb, u % nb, nb, pos, u == (int)blockIdx.x, ls, asm_,
+                                   sh))
+              break;
         if (tid == 0) MI_TRACE(step, layer * 5 + 1, 2);
-        if (!grid_sync(p, epoch, sh)) return;
       }
-      // O
+      // O (waits for every attention unit's partial instead of a grid barrier)
       {
+        units_total += (uint32_t)(p.kvh * ((pos + p.block) / p.block));
+        if (!wait_units(p, units_total, sh)) return;
         if (tid == 0) { MI_TRACE(step, layer * 5 + 2, 0); MI_TRACE_SET(step, layer * 5 + 2); }
         const StageW s = stage_weights(p, lay, layer, kO);
-        build_input(kPlainIn, p.attn, nullptr, nullptr, s.k, p.eps, nullptr, xs, sh);
+        build_attn_input(p, (pos + p.block) / p.block, xs);
         if (tid == 0) MI_TRACE(step, layer * 5 + 2, 1);
         reduce_rows<kO>(p, s, xs, ring, sh, g, bk, bi);
         if (tid == 0) MI_TRACE(step, layer * 5 + 2, 2);
@@ -1001,6 +1104,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_loop_kernel(DecodeLoop par
       // DOWN
       {
         if (tid == 0) { MI_TRACE(step, layer * 5 + 4, 0); MI_TRACE_SET(step, layer * 5 + 4); }
+        {
+          // residuals of this CTA's rows, read while the stage input loads
+          const Tiles& td = sh.tiles[kDown];
+          if (tid < min(td.last - td.first, kMaxDownRows))
+            sh.res[tid] = __ldcg(p.residual + td.first + tid);
+        }
         const StageW s = stage_weights(p, lay, layer, kDown);
         build_input(kPlainIn, p.act, nullptr, nullptr, s.k, p.eps, nullptr, xs, sh);
         if (tid == 0) MI_TRACE(step, layer * 5 + 4, 1);
@@ -1116,6 +1225,7 @@ bool decode_loop_plan(DecodeLoop& p, int device) {
   const int group = p.kvh > 0 ? p.qh / p.kvh : 0;
   if (attn_smem_for(group) == 0 || p.qh % p.kvh) return false;
   if (p.hidden % 8 || p.inter % 8 || p.hidden <= 0 || p.inter <= 0) return false;
+  if (p.kvh > kMaxKvHeads) return false;
   const int max_k = std::max(std::max(p.hidden, p.inter), p.qh * HD);
   int max_item = std::max(std::max(p.hidden * 4, p.inter * 2), p.qh * HD * 2);
   p.slot_bytes = std::max(kMinSlotBytes, (max_item + 127) / 128 * 128);
@@ -1145,6 +1255,7 @@ void decode_loop(cudaStream_t stream, const DecodeLoop& p) {
   MI_REQUIRE(p.steps > 0 && p.grid > 0 && p.slots >= 2, MI_ERR_INVALID_ARGUMENT,
              "decode loop plan missing");
   MI_CUDA(cudaMemsetAsync(p.sync, 0, kSyncWords * sizeof(uint32_t), stream));
+  static_assert(kSyncWords == decode_loop_sync_words(), "sync buffer size");
   const size_t smem = decode_loop_smem(p);
   cudaError_t err = cudaErrorInvalidValue;
   switch (p.qh / p.kvh) {

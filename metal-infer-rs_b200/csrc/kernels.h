@@ -204,15 +204,13 @@ struct DecodeLoop {
   __half* q_raw = nullptr;
   __half* k_raw = nullptr;
   __half* v_raw = nullptr;
-  __half* attn = nullptr;
   __half* attn_o = nullptr;
   __half* act = nullptr;
   __half* logits = nullptr;
-  float* attn_part = nullptr;     // [kvh, attn_blocks, G, 130]
-  uint32_t* attn_count = nullptr; // [kvh], zero on entry and exit
+  float* attn_part = nullptr;     // [kvh, attn_blocks, G, 132] block partials
   uint32_t* argmax_key = nullptr; // [grid]
   uint32_t* argmax_idx = nullptr; // [grid]
-  uint32_t* sync = nullptr;       // [decode_loop_sync_words()]: barrier counter, abort flag
+  uint32_t* sync = nullptr;       // [decode_loop_sync_words()]: barrier counter, abort flag, per-head counters
   // plan (decode_loop_plan)
   int slot_bytes = 0, slots = 0, x_bytes = 0, grid = 0;
 };
@@ -220,8 +218,13 @@ struct DecodeLoop {
 // device's shared memory does not admit the persistent kernel.
 bool decode_loop_plan(DecodeLoop& p, int device);
 void decode_loop(cudaStream_t stream, const DecodeLoop& p);
+// Floats of DecodeLoop::attn_part for kvh KV heads, `blocks` key blocks and
+// `group` query heads per KV head.
+inline size_t decode_loop_part_floats(int kvh, int blocks, int group) {
+  return (size_t)kvh * blocks * group * (128 + 4);
+}
 // u32 words of DecodeLoop::sync.
-constexpr size_t decode_loop_sync_words() { return 32; }
+constexpr size_t decode_loop_sync_words() { return 256; }
 // Expired-wait code of the persistent kernel (0 = none), optionally cleared.
 unsigned decode_loop_status(bool reset);
 

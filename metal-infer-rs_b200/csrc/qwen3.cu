@@ -82,6 +82,7 @@ struct Workspace {
   TensorRef q_raw, k_raw, v_raw, attn, attn_o, residual, hidden, act, logits;
   TensorRef argmax_pv, argmax_pi, counters, attn_scratch;
   TensorRef loop_sync;  // persistent decode: grid-barrier counter + abort flag
+  TensorRef loop_part;  // persistent decode: attention block partials
   int attn_splits = 0;  // flash-decode blocks for the largest cache seen
   int attn_block = 64;  // keys per flash-decode block
   size_t attn_cap = 0;
@@ -440,12 +441,13 @@ void run_decode_loop(mi_qwen3* m, mi_kv_cache* c, size_t steps) {
   p.q_raw = w.q_raw.h();
   p.k_raw = w.k_raw.h();
   p.v_raw = w.v_raw.h();
-  p.attn = w.attn.h();
   p.attn_o = w.attn_o.h();
   p.act = w.act.h();
   p.logits = w.logits.h();
-  p.attn_part = w.attn_scratch.t->f32();
-  p.attn_count = w.counters.t->u32() + 1;
+  const size_t part = k::decode_loop_part_floats(p.kvh, w.attn_splits, p.qh / p.kvh);
+  if (!w.loop_part.t || w.loop_part.t->len() < part)
+    w.loop_part = TensorRef(new_tensor(ctx, {part}, MI_F32, false));
+  p.attn_part = w.loop_part.t->f32();
   p.argmax_key = reinterpret_cast<uint32_t*>(w.argmax_pv.t->f32());
   p.argmax_idx = w.argmax_pi.t->u32();
   p.sync = w.loop_sync.t->u32();
