@@ -18,14 +18,20 @@
 // consumer warps arrive on), never by the grid barriers between stages, so
 // HBM keeps streaming weights while the consumers wait on their
 // predecessors. Consumers build each stage's input vector in shared memory,
-// reduce their rows from the ring and write the outputs to global memory
-// (L2-resident activations are read with L1-bypassing loads), then meet at a
-// grid barrier (a monotonic counter in global memory).
+// reduce their rows from the ring and write the outputs to global memory.
 //
-// Every wait is bounded in time: a ring wait, a grid-barrier wait or an
-// attention merge that gives up records a code in g_loop_status and raises a
-// device-wide abort flag; all warps leave at the next stage boundary and the
-// producer waits (bounded) for its copies in flight before the CTA exits.
+// There are no grid barriers. Activations that cross CTAs are stored as
+// epoch-tagged words (tag << 16 | FP16 bits) that validate themselves; each
+// CTA bumps a per-stage counter with a relaxed reduction after its rows, and
+// one thread per CTA polls the counter of the stage it consumes before the
+// CTA reads (and checks) the tagged words. Attention units publish their
+// block partials with a release reduction, and the O stage merges the
+// partials of every head while building its input.
+//
+// Every wait is bounded in time: a ring wait, a counter or tag poll that
+// gives up records a code in g_loop_status and raises a device-wide abort
+// flag; all warps leave at the next stage boundary and the producer waits
+// (bounded) for its copies in flight before the CTA exits.
 
 #include <algorithm>
 
@@ -46,11 +52,10 @@ constexpr int kTile = 64;                  // keys staged per attention tile
 constexpr int kAttnThreads = 256;          // warps 4..11 run the attention units
 constexpr int kAttnBase = 128;             // (warp 0 keeps the stage-input norms)
 constexpr int kMaxSlots = 16;
-// sync[]: [0] barrier counter, [1] abort flag, [2] attention units finished,
-// [kHeadReady + h] QKV rows written for KV head h (counts cumulative over
-// the launch).
+// sync[]: [1] abort flag, [2] attention units finished, [kStageDone + st]
+// CTAs that finished stage st (all cumulative over the launch).
 constexpr int kUnitsDone = 2;
-constexpr int kHeadReady = 32;
+constexpr int kStageDone = 8;
 constexpr int kPart = HD + 4;  // partial record: max, denominator, 2 pad, 128 numerators
 constexpr int kSyncWords = 256;
 constexpr int kMaxKvHeads = 64;
@@ -96,9 +101,9 @@ enum Stage : int { kQKV = 0, kO = 1, kGU = 2, kDown = 3, kLM = 4 };
 // Failure codes (high byte: place, low byte: stage).
 constexpr unsigned kCodeFull = 0x0100;
 constexpr unsigned kCodeEmpty = 0x0200;
-constexpr unsigned kCodeGrid = 0x0300;
 constexpr unsigned kCodeDrain = 0x0400;
 constexpr unsigned kCodeHead = 0x0500;
+constexpr unsigned kCodeTag = 0x0600;
 
 struct StageW {
   const __half* w[3];
@@ -190,7 +195,6 @@ struct Shared {
   uint64_t empty[kMaxSlots];
   Tiles tiles[5];  // this CTA's tiling of each stage (the same in every layer)
   float scale;
-  uint32_t qkv_rows[kMaxKvHeads];  // QKV rows this CTA writes per KV head
   __half res[kMaxDownRows];         // DOWN: residual values of this CTA's rows
   uint32_t best_key[kConsumerWarps];
   uint32_t best_idx[kConsumerWarps];
@@ -211,6 +215,9 @@ __device__ __forceinline__ uint32_t ld_relaxed(const uint32_t* p) {
   uint32_t v;
   asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
+}
+__device__ __forceinline__ void red_relaxed_add(uint32_t* p, uint32_t v) {
+  asm volatile("red.relaxed.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 __device__ __forceinline__ void red_release_add(uint32_t* p, uint32_t v) {
   asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
@@ -238,45 +245,120 @@ __device__ bool ring_wait(uint64_t* bar, uint32_t parity, Shared& sh, unsigned c
   return true;
 }
 
-// Grid barrier over all CTAs (consumer threads only): thread 0 of each CTA
-// adds one to a counter in global memory with a release reduction and polls
-// it until it reaches epoch * gridDim.x (relaxed loads, one fence after).
-// Returns false when the kernel is aborting; the decision is uniform across
-// the CTA.
-__device__ bool grid_sync(const DecodeLoop& p, uint32_t& epoch, Shared& sh) {
-  ++epoch;
-  consumers_sync();
-  if (threadIdx.x == 0) {
-    volatile uint32_t* abort_flag = p.sync + 1;
-    if (sh.abort) {
-      *abort_flag = 1u;
-    } else {
-      MI_TRACE_ARRIVE(0);
-      const uint32_t target = epoch * gridDim.x;
-      red_release_add(p.sync, 1u);
-      uint64_t start = 0;
-      while (ld_relaxed(p.sync) < target) {
-        if (*abort_flag) {
-          sh.abort = 1;
-          break;
-        }
-        const uint64_t now = pipe::global_ns();
-        if (!start) {
-          start = now;
-        } else if (now - start > pipe::kWaitNs) {
-          record(kCodeGrid);
-          sh.abort = 1;
-          *abort_flag = 1u;
-          break;
-        }
-      }
-      __threadfence();
-      MI_TRACE_ARRIVE(1);
+// ---- epoch-tagged activations ----------------------------------------------------
+// Every activation vector that crosses CTAs is stored as one u32 per FP16
+// value: (16-bit tag << 16) | value bits, written with a single store. A
+// reader polls the words it needs until all carry the tag of the layer-step
+// it wants, so each word validates itself and no grid barrier is needed.
+// Overwrites are ordered by the data dependencies of the stages: a buffer is
+// written again only by a stage that first consumed complete vectors from
+// every CTA, each of which had finished reading the previous contents.
+// tag(e, slot): e = layer-step counter (host base + step * layers + layer),
+// slot 1 marks the DOWN output, which shares the hidden buffer with the
+// embedding written at layer 0.
+__device__ __forceinline__ uint32_t tagv(uint32_t e, int slot) {
+  return ((e * 2u + (uint32_t)slot) & 0xFFFFu) << 16;
+}
+__device__ __forceinline__ uint4 ld_relaxed_v4(const uint32_t* p) {
+  uint4 v;
+  asm volatile("ld.relaxed.gpu.global.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p)
+               : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_relaxed(uint32_t* p, uint32_t v) {
+  asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void st_relaxed_v4(uint32_t* p, uint4 v) {
+  asm volatile("st.relaxed.gpu.global.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y),
+               "r"(v.z), "r"(v.w)
+               : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_relaxed_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_relaxed_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+// Bounded-poll bookkeeping shared by the tag waits: false once the kernel
+// is aborting (the caller then continues on zeros until the next decision).
+struct PollClock {
+  uint64_t start = 0;
+  __device__ __forceinline__ bool keep_going(const DecodeLoop& p, Shared& sh) {
+    if (sh.abort || *reinterpret_cast<volatile uint32_t*>(p.sync + 1)) {
+      sh.abort = 1;
+      return false;
     }
-    sh.stop = sh.abort ? 1 : 0;
+    const uint64_t now = pipe::global_ns();
+    if (!start) {
+      start = now;
+    } else if (now - start > pipe::kWaitNs) {
+      record(kCodeTag);
+      sh.abort = 1;
+      *reinterpret_cast<volatile uint32_t*>(p.sync + 1) = 1u;
+      return false;
+    }
+    return true;
   }
-  consumers_sync();
-  return !sh.stop;
+};
+
+// Chunk c (8 FP16 values) of a tagged vector, once all 8 carry `tag`.
+__device__ uint4 take8(const DecodeLoop& p, const uint32_t* src, int c, uint32_t tag,
+                                   Shared& sh) {
+  const uint32_t* q = src + 8 * c;
+  PollClock clock;
+  while (true) {
+    const uint4 a = ld_relaxed_v4(q), b = ld_relaxed_v4(q + 4);
+    const uint32_t miss = (a.x ^ tag) | (a.y ^ tag) | (a.z ^ tag) | (a.w ^ tag) | (b.x ^ tag) |
+                          (b.y ^ tag) | (b.z ^ tag) | (b.w ^ tag);
+    if ((miss >> 16) == 0)
+      return make_uint4((a.x & 0xFFFFu) | (a.y << 16), (a.z & 0xFFFFu) | (a.w << 16),
+                        (b.x & 0xFFFFu) | (b.y << 16), (b.z & 0xFFFFu) | (b.w << 16));
+    if (!clock.keep_going(p, sh)) return make_uint4(0, 0, 0, 0);
+  }
+}
+
+// Two-phase form for batching: issue the raw loads of several chunks first,
+// then validate (re-polling only chunks whose tags were not there yet).
+struct Raw8 {
+  uint4 a, b;
+};
+__device__ __forceinline__ Raw8 raw8(const uint32_t* src, int c) {
+  return {ld_relaxed_v4(src + 8 * c), ld_relaxed_v4(src + 8 * c + 4)};
+}
+__device__ __forceinline__ uint4 take8_from(const DecodeLoop& p, const Raw8& r,
+                                            const uint32_t* src, int c, uint32_t tag,
+                                            Shared& sh) {
+  const uint32_t miss = (r.a.x ^ tag) | (r.a.y ^ tag) | (r.a.z ^ tag) | (r.a.w ^ tag) |
+                        (r.b.x ^ tag) | (r.b.y ^ tag) | (r.b.z ^ tag) | (r.b.w ^ tag);
+  if ((miss >> 16) == 0)
+    return make_uint4((r.a.x & 0xFFFFu) | (r.a.y << 16), (r.a.z & 0xFFFFu) | (r.a.w << 16),
+                      (r.b.x & 0xFFFFu) | (r.b.y << 16), (r.b.z & 0xFFFFu) | (r.b.w << 16));
+  return take8(p, src, c, tag, sh);
+}
+
+// Element i of a tagged vector.
+__device__ __half take1(const DecodeLoop& p, const uint32_t* src, int i, uint32_t tag, Shared& sh) {
+  PollClock clock;
+  while (true) {
+    const uint32_t w = ld_relaxed(src + i);
+    if ((w >> 16) == (tag >> 16)) return __ushort_as_half((unsigned short)(w & 0xFFFFu));
+    if (!clock.keep_going(p, sh)) return __float2half_rn(0.f);
+  }
+}
+
+__device__ __forceinline__ void put1(uint32_t* dst, int i, __half h, uint32_t tag) {
+  st_relaxed(dst + i, tag | __half_as_ushort(h));
+}
+__device__ __forceinline__ void put8(uint32_t* dst, int c, const uint4& v, uint32_t tag) {
+  st_relaxed_v4(dst + 8 * c, make_uint4(tag | (v.x & 0xFFFFu), tag | (v.x >> 16),
+                                         tag | (v.y & 0xFFFFu), tag | (v.y >> 16)));
+  st_relaxed_v4(dst + 8 * c + 4, make_uint4(tag | (v.z & 0xFFFFu), tag | (v.z >> 16),
+                                             tag | (v.w & 0xFFFFu), tag | (v.w >> 16)));
 }
 
 // Single-thread bounded wait until *ctr >= target (cumulative counters of
@@ -304,18 +386,12 @@ __device__ bool wait_counter(const DecodeLoop& p, const uint32_t* ctr, uint32_t 
   return true;
 }
 
-// End of the QKV stage: publish this CTA's rows per KV head (no barrier; the
-// attention units of a head wait for exactly its rows).
-__device__ bool publish_qkv(const DecodeLoop& p, Shared& sh) {
-  consumers_sync();
-  if (threadIdx.x == 0) {
-    if (!sh.abort)
-      for (int h = 0; h < p.kvh; ++h)
-        if (sh.qkv_rows[h]) red_release_add(p.sync + kHeadReady + h, sh.qkv_rows[h]);
-    sh.stop = sh.abort ? 1 : 0;
-  }
-  consumers_sync();
-  return !sh.stop;
+__device__ bool wait_counter_relaxed(const DecodeLoop& p, const uint32_t* ctr, uint32_t target,
+                                     Shared& sh) {
+  PollClock clock;
+  while (ld_relaxed(ctr) < target)
+    if (!clock.keep_going(p, sh)) return false;
+  return true;
 }
 
 // Start of the O stage: wait until `units` attention units (cumulative over
@@ -327,6 +403,23 @@ __device__ bool wait_units(const DecodeLoop& p, uint32_t units, Shared& sh) {
   }
   consumers_sync();
   return !sh.stop;
+}
+
+// End of a stage: after every warp has issued its tagged stores, count the
+// CTA in (a relaxed reduction: the tags, not the counter, carry
+// correctness; the counter only tells readers when to look).
+__device__ __forceinline__ void stage_done(const DecodeLoop& p, int st) {
+  consumers_sync();
+  if (threadIdx.x == 0) {
+    MI_TRACE_ARRIVE(0);
+    red_relaxed_add(p.sync + kStageDone + st, 1u);
+  }
+}
+
+// Thread 0: wait until `n` CTAs have finished stage st (cumulative), so the
+// tagged reads that follow find their words (bounded; false when aborting).
+__device__ __forceinline__ bool stage_ready(const DecodeLoop& p, int st, uint32_t n, Shared& sh) {
+  return wait_counter_relaxed(p, p.sync + kStageDone + st, n, sh);
 }
 
 // O-stage input: the attention output of every query head, the log-sum-exp
@@ -446,42 +539,62 @@ __device__ void produce(const DecodeLoop& p, const LoopLayer* layers, uint8_t* r
 // ---- consumers: stage input -------------------------------------------------------
 enum InMode : int { kPlainIn = 0, kNormIn = 1, kEmbedNormIn = 2, kAddNormIn = 3, kAddThenNormIn = 4 };
 
-// Chunk c of the stage input before the norm (gemv.cu build_input roundings).
-__device__ __forceinline__ uint4 input_chunk(int mode, const uint4* src, const uint4* src2, int c) {
-  if (mode == kAddNormIn || mode == kAddThenNormIn) {
-    const uint4 a = __ldcg(src + c);
-    const uint4 b = __ldcg(src2 + c);
-    const __half2* ha = reinterpret_cast<const __half2*>(&a);
-    const __half2* hb = reinterpret_cast<const __half2*>(&b);
-    uint4 v;
-    __half2* hv = reinterpret_cast<__half2*>(&v);
+// A stage input: tagged vector x (+ x2 for the residual adds, or an
+// embedding row), the norm weights, and where CTA 0 writes back the
+// un-normalized input (hidden stream / residual).
+struct StageIn {
+  int mode;
+  int k;
+  const uint32_t* x;
+  uint32_t xtag;
+  const uint32_t* x2;
+  uint32_t x2tag;
+  const __half* embed;  // kEmbedNormIn: table row, null for an out-of-range token
+  const __half* norm_w;
+  uint32_t* wb;
+  uint32_t wbtag;
+};
+
+__device__ __forceinline__ uint4 add_chunk(int mode, const uint4& a, const uint4& b) {
+  const __half2* ha = reinterpret_cast<const __half2*>(&a);
+  const __half2* hb = reinterpret_cast<const __half2*>(&b);
+  uint4 v;
+  __half2* hv = reinterpret_cast<__half2*>(&v);
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      if (mode == kAddNormIn) {
-        float2 fa = __half22float2(ha[i]);
-        float2 fb = __half22float2(hb[i]);
-        hv[i] = __floats2half2_rn(__fadd_rn(fa.x, fb.x), __fadd_rn(fa.y, fb.y));
-      } else {
-        hv[i] = __hadd2(ha[i], hb[i]);
-      }
+  for (int i = 0; i < 4; ++i) {
+    if (mode == kAddNormIn) {
+      float2 fa = __half22float2(ha[i]);
+      float2 fb = __half22float2(hb[i]);
+      hv[i] = __floats2half2_rn(__fadd_rn(fa.x, fb.x), __fadd_rn(fa.y, fb.y));
+    } else {
+      hv[i] = __hadd2(ha[i], hb[i]);
     }
-    return v;
   }
-  if (mode == kEmbedNormIn) return src ? __ldg(src + c) : make_uint4(0, 0, 0, 0);
-  return __ldcg(src + c);
+  return v;
 }
 
-// Canonical sum of squares of the stage input, loaded by warp 0 itself so it
-// overlaps the fill instead of following it. kAddNormIn squares the
-// unrounded float sums (matvec2_add_rms_impl).
-__device__ __forceinline__ float input_sumsq(int mode, const uint4* src, const uint4* src2,
-                                             int kc, int lane) {
+// Chunk c of the stage input before the norm (gemv.cu build_input roundings).
+__device__ __forceinline__ uint4 input_chunk(const DecodeLoop& p, const StageIn& in, int c,
+                                             Shared& sh) {
+  if (in.mode == kAddNormIn || in.mode == kAddThenNormIn) {
+    const Raw8 ra = raw8(in.x, c), rb = raw8(in.x2, c);
+    return add_chunk(in.mode, take8_from(p, ra, in.x, c, in.xtag, sh),
+                     take8_from(p, rb, in.x2, c, in.x2tag, sh));
+  }
+  if (in.mode == kEmbedNormIn)
+    return in.embed ? __ldg(reinterpret_cast<const uint4*>(in.embed) + c) : make_uint4(0, 0, 0, 0);
+  return take8(p, in.x, c, in.xtag, sh);
+}
+
+// Canonical sum of squares of the staged input (warp 0, from shared memory):
+// xs holds x (or the embedding row), xs2 holds x2 for the residual adds;
+// kAddNormIn squares the unrounded float sums (matvec2_add_rms_impl).
+__device__ __forceinline__ float staged_sumsq(int mode, const uint4* xs, const uint4* xs2, int kc,
+                                              int lane) {
   float acc = 0.f;
-#pragma unroll 4
   for (int c = lane; c < kc; c += 32) {
     if (mode == kAddNormIn) {
-      const uint4 a = __ldcg(src + c);
-      const uint4 b = __ldcg(src2 + c);
+      const uint4 a = xs[c], b = xs2[c];
       const __half2* ha = reinterpret_cast<const __half2*>(&a);
       const __half2* hb = reinterpret_cast<const __half2*>(&b);
 #pragma unroll
@@ -492,8 +605,10 @@ __device__ __forceinline__ float input_sumsq(int mode, const uint4* src, const u
         acc = __fmaf_rn(s0, s0, acc);
         acc = __fmaf_rn(s1, s1, acc);
       }
+    } else if (mode == kAddThenNormIn) {
+      acc = chunk_sq(add_chunk(mode, xs[c], xs2[c]), acc);
     } else {
-      acc = chunk_sq(input_chunk(mode, src, src2, c), acc);
+      acc = chunk_sq(xs[c], acc);
     }
   }
   return acc;
@@ -514,45 +629,59 @@ __device__ __forceinline__ uint4 normalize_chunk(const uint4& v, const uint4& g,
 }
 
 // Builds the stage input (k halves) in xs with the prologue of the GEMV
-// family (gemv.cu build_input): the same roundings, the canonical sum of
-// squares by warp 0. One L2 round trip when k / 8 <= 480 chunks.
-__device__ void build_input(int mode, const __half* x, const __half* x2, const __half* norm_w,
-                            int k, float eps, __half* write_back, uint4* xs, Shared& sh) {
+// family (gemv.cu build_input): the same roundings and the canonical sum of
+// squares. One poller per CTA waits on the producing stage's counter; then
+// every thread stages its chunks in shared memory (one L2 round trip, the
+// tags validate each word), warp 0 reduces the squares from shared memory
+// and the chunks are normalized in place. The first barrier also orders
+// this stage's writes of xs after the previous stage's reads. Returns the
+// CTA's uniform decision to continue (false when the kernel is aborting).
+__device__ bool build_input(const DecodeLoop& p, const StageIn& in, int wait_st,
+                            uint32_t wait_n, uint4* xs, uint4* xs2, Shared& sh) {
   const int tid = threadIdx.x;
   const int lane = tid & 31;
-  const int kc = k >> 3;
-  const uint4* src = reinterpret_cast<const uint4*>(x);
-  const uint4* src2 = reinterpret_cast<const uint4*>(x2);
-  const uint4* g4 = reinterpret_cast<const uint4*>(norm_w);
-  uint4* wb = reinterpret_cast<uint4*>(write_back);
-  if (mode != kPlainIn && tid < 32) {
-    const float total = canon_reduce(input_sumsq(mode, src, src2, kc, lane), canon_lanes(k));
-    if (lane == 0) sh.scale = rms_scale(total, k, eps);
+  const int kc = in.k >> 3;
+  const bool two = in.mode == kAddNormIn || in.mode == kAddThenNormIn;
+  const bool norm = in.mode != kPlainIn;
+  const uint4* g4 = reinterpret_cast<const uint4*>(in.norm_w);
+  if (tid == 0 && wait_st >= 0) {
+    stage_ready(p, wait_st, wait_n, sh);
+    MI_TRACE_ARRIVE(1);
   }
-  if (kc <= kConsumers) {
-    uint4 v = make_uint4(0, 0, 0, 0), g = make_uint4(0, 0, 0, 0);
-    if (tid < kc) {
-      v = input_chunk(mode, src, src2, tid);
-      if (mode != kPlainIn) g = __ldg(g4 + tid);
-      if (wb && blockIdx.x == 0) wb[tid] = v;
-      if (mode == kPlainIn) xs[tid] = v;
+  consumers_sync();
+  uint4 g_first = make_uint4(0, 0, 0, 0);
+  if (norm && tid < kc) g_first = __ldg(g4 + tid);
+  for (int c = tid; c < kc; c += kConsumers) {
+    uint4 v;
+    if (two) {
+      const Raw8 ra = raw8(in.x, c), rb = raw8(in.x2, c);
+      const uint4 a = take8_from(p, ra, in.x, c, in.xtag, sh);
+      const uint4 b = take8_from(p, rb, in.x2, c, in.x2tag, sh);
+      xs[c] = a;
+      xs2[c] = b;
+      v = add_chunk(in.mode, a, b);
+    } else {
+      v = input_chunk(p, in, c, sh);
+      xs[c] = v;
+    }
+    if (in.wb && blockIdx.x == 0) put8(in.wb, c, v, in.wbtag);
+  }
+  consumers_sync();
+  if (norm) {
+    if (tid < 32) {
+      const float total = canon_reduce(staged_sumsq(in.mode, xs, xs2, kc, lane), canon_lanes(in.k));
+      if (lane == 0) sh.scale = rms_scale(total, in.k, p.eps);
     }
     consumers_sync();
-    if (mode == kPlainIn) return;
-    if (tid < kc) xs[tid] = normalize_chunk(v, g, sh.scale);
-    consumers_sync();
-    return;
+    const float scale = sh.scale;
+    for (int c = tid; c < kc; c += kConsumers) {
+      const uint4 v = two ? add_chunk(in.mode, xs[c], xs2[c]) : xs[c];
+      xs[c] = normalize_chunk(v, c == tid ? g_first : __ldg(g4 + c), scale);
+    }
   }
-  for (int c = tid; c < kc; c += kConsumers) {
-    const uint4 v = input_chunk(mode, src, src2, c);
-    if (wb && blockIdx.x == 0) wb[c] = v;
-    xs[c] = v;
-  }
+  if (tid == 0) sh.stop = sh.abort ? 1 : 0;
   consumers_sync();
-  if (mode == kPlainIn) return;
-  const float scale = sh.scale;
-  for (int c = tid; c < kc; c += kConsumers) xs[c] = normalize_chunk(xs[c], __ldg(g4 + c), scale);
-  consumers_sync();
+  return !sh.stop;
 }
 
 // ---- consumers: rows from the ring --------------------------------------------------
@@ -560,23 +689,18 @@ __device__ void build_input(int mode, const __half* x, const __half* x2, const _
 template <int ST>
 __device__ __forceinline__ void put_item(const DecodeLoop& p, const StageW& s, int item, float a0,
                                          float a1, const __half* res, int res_first,
-                                         uint32_t& best_key, uint32_t& best_idx) {
+                                         uint32_t tag, uint32_t& best_key, uint32_t& best_idx) {
   if (ST == kQKV) {
-    const int nq = s.n[0], nk = s.n[1];
-    const __half h0 = __float2half_rn(a0);
-    if (item < nq) p.q_raw[item] = h0;
-    else if (item < nq + nk) p.k_raw[item - nq] = h0;
-    else p.v_raw[item - nq - nk] = h0;
+    put1(p.t_qkv, item, __float2half_rn(a0), tag);
   } else if (ST == kO) {
-    p.attn_o[item] = __float2half_rn(a0);
+    put1(p.t_attn_o, item, __float2half_rn(a0), tag);
   } else if (ST == kGU) {
     const float gv = __half2float(__float2half_rn(a0));
     const float uv = __half2float(__float2half_rn(a1));
-    p.act[item] = __float2half_rn(silu_mul(gv, uv));
+    put1(p.t_act, item, __float2half_rn(silu_mul(gv, uv)), tag);
   } else if (ST == kDown) {
     const int local = item - res_first;
-    const __half r = local < kMaxDownRows ? res[local] : __ldcg(p.residual + item);
-    p.hidden_buf[item] = __hadd(r, __float2half_rn(a0));
+    put1(p.t_hidden, item, __hadd(res[local], __float2half_rn(a0)), tag);
   } else {
     const __half h0 = __float2half_rn(a0);
     p.logits[item] = h0;
@@ -593,7 +717,7 @@ __device__ __forceinline__ void put_item(const DecodeLoop& p, const StageW& s, i
 // row q. Rows past `nr` repeat row 0 and are dropped.
 template <int ST, int P>
 __device__ __forceinline__ void rows_group(const DecodeLoop& p, const StageW& s, const uint4* xs,
-                                           const __half* res, int res_first,
+                                           const __half* res, int res_first, uint32_t tag,
                                            const uint8_t* base, int r0, int nr, int cnt,
                                            uint32_t row_bytes, int item0, int kc, int lanes,
                                            uint32_t& best_key, uint32_t& best_idx) {
@@ -659,7 +783,7 @@ __device__ __forceinline__ void rows_group(const DecodeLoop& p, const StageW& s,
 #pragma unroll
   for (int q = 0; q < P; ++q)
     if (lane == q && q < nr)
-      put_item<ST>(p, s, item0 + q, a[q], b[q], res, res_first, best_key, best_idx);
+      put_item<ST>(p, s, item0 + q, a[q], b[q], res, res_first, tag, best_key, best_idx);
 }
 
 // Reduces this CTA's rows of stage ST from the ring: groups of P local rows
@@ -669,7 +793,7 @@ __device__ __forceinline__ void rows_group(const DecodeLoop& p, const StageW& s,
 template <int ST, int P>
 __device__ void reduce_rows_p(const DecodeLoop& p, const StageW& s, const Tiles& t,
                               const uint4* xs, const uint8_t* ring, Shared& sh, uint32_t& g,
-                              uint32_t& best_key, uint32_t& best_idx) {
+                              uint32_t tag, uint32_t& best_key, uint32_t& best_idx) {
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   const int kc = s.k >> 3;
@@ -691,7 +815,7 @@ __device__ void reduce_rows_p(const DecodeLoop& p, const StageW& s, const Tiles&
       for (int gi = g0 + (warp - g0 % kConsumerWarps + kConsumerWarps) % kConsumerWarps; gi < g1;
            gi += kConsumerWarps) {
         const int r0 = gi * P - l0;
-        rows_group<ST, P>(p, s, xs, sh.res, t.first, base, r0, min(P, cnt - r0), cnt, t.row_bytes,
+        rows_group<ST, P>(p, s, xs, sh.res, t.first, tag, base, r0, min(P, cnt - r0), cnt, t.row_bytes,
                           t.first + l0 + r0,
                           kc, lanes, best_key, best_idx);
       }
@@ -703,16 +827,16 @@ __device__ void reduce_rows_p(const DecodeLoop& p, const StageW& s, const Tiles&
 
 template <int ST>
 __device__ void reduce_rows(const DecodeLoop& p, const StageW& s, const uint4* xs,
-                            const uint8_t* ring, Shared& sh, uint32_t& g, uint32_t& best_key,
-                            uint32_t& best_idx) {
+                            const uint8_t* ring, Shared& sh, uint32_t& g, uint32_t tag,
+                            uint32_t& best_key, uint32_t& best_idx) {
   const Tiles t = sh.tiles[ST];
   const int rows = t.last - t.first;
   if (ST == kLM && t.per_tile % 4 == 0 && rows >= 4 * kConsumerWarps)
-    reduce_rows_p<ST, 4>(p, s, t, xs, ring, sh, g, best_key, best_idx);
+    reduce_rows_p<ST, 4>(p, s, t, xs, ring, sh, g, tag, best_key, best_idx);
   else if (t.per_tile % 2 == 0 && rows >= 16)
-    reduce_rows_p<ST, 2>(p, s, t, xs, ring, sh, g, best_key, best_idx);
+    reduce_rows_p<ST, 2>(p, s, t, xs, ring, sh, g, tag, best_key, best_idx);
   else
-    reduce_rows_p<ST, 1>(p, s, t, xs, ring, sh, g, best_key, best_idx);
+    reduce_rows_p<ST, 1>(p, s, t, xs, ring, sh, g, tag, best_key, best_idx);
 }
 
 // ---- consumers: attention units (warps 4..11) -------------------------------------------
@@ -777,9 +901,9 @@ constexpr int kKeyBatch = 4;  // keys of a stream scored together
 // order. Run by warps 4..11: for G >= 2 the two warpgroups each take half of
 // the query heads of the group over the same 8 key streams.
 template <int G>
-__device__ bool attention_unit(const DecodeLoop& p, const LoopLayer& L, int g_kv, int b, int nb,
-                               int pos, bool prefetched, uint32_t ls, AttnSmem<G>& sm,
-                               Shared& sh) {
+__device__ void attention_unit(const DecodeLoop& p, const LoopLayer& L, int g_kv, int b, int nb,
+                               int pos, bool prefetched, uint32_t qkv_tag, uint32_t qkv_ctas,
+                               AttnSmem<G>& sm, Shared& sh) {
   constexpr int NG = G >= 2 ? 2 : 1;  // warpgroups sharing the heads
   constexpr int GS = G / NG;          // heads per warpgroup
   const int t = atid();
@@ -795,19 +919,14 @@ __device__ bool attention_unit(const DecodeLoop& p, const LoopLayer& L, int g_kv
   const int end = min(Lk, begin + p.block);
   const int ntiles = (end - begin + kTile - 1) / kTile;
 
-  // this head's Q/K/V rows of layer-step ls are all written
-  if (t == 0)
-    sh.astop = wait_counter(p, p.sync + kHeadReady + g_kv, (ls + 1u) * (uint32_t)((G + 2) * HD),
-                            sh) ? 0 : 1;
+  // every CTA's QKV rows are out (the tags then validate each word)
+  if (t == 0) stage_ready(p, kQKV, qkv_ctas, sh);
   attn_sync();
-  if (sh.astop) return false;
-
   {
     const int hq = t >> 4;  // one query head per half-warp
     if (hq < G) {
       const unsigned mask = ((t >> 5) * 2 + 1 < G) ? 0xffffffffu : 0x0000ffffu;
-      const uint4 raw =
-          __ldcg(reinterpret_cast<const uint4*>(p.q_raw + (size_t)(g_kv * G + hq) * HD) + li);
+      const uint4 raw = take8(p, p.t_qkv, (g_kv * G + hq) * (HD / 8) + li, qkv_tag, sh);
       float qv[8];
       head_rope<G>(p, sm, raw, sm.qn_w, pos, mask, qv);
 #pragma unroll
@@ -815,8 +934,9 @@ __device__ bool attention_unit(const DecodeLoop& p, const LoopLayer& L, int g_kv
     }
   }
   if (pos >= begin && pos < end && t >= kAttnThreads - 16) {
-    const uint4 raw = __ldcg(reinterpret_cast<const uint4*>(p.k_raw + (size_t)g_kv * HD) + li);
-    const uint4 vv = __ldcg(reinterpret_cast<const uint4*>(p.v_raw + (size_t)g_kv * HD) + li);
+    const int kc0 = (p.qh * HD + g_kv * HD) / 8;
+    const uint4 raw = take8(p, p.t_qkv, kc0 + li, qkv_tag, sh);
+    const uint4 vv = take8(p, p.t_qkv, kc0 + p.kvh * HD / 8 + li, qkv_tag, sh);
     float kv[8];
     head_rope<G>(p, sm, raw, sm.kn_w, pos, 0xffff0000u, kv);
     uint4 kk;
@@ -987,7 +1107,11 @@ __device__ bool attention_unit(const DecodeLoop& p, const LoopLayer& L, int g_kv
   if (t == 0) MI_TRACE_CUR(8);
   attn_sync();  // partial written; shared state is reused by the next unit
   if (t == 0) red_release_add(p.sync + kUnitsDone, 1u);
-  return true;
+}
+
+// Bytes of the shared-memory copy of the layer table.
+__host__ __device__ size_t layer_table_bytes(int layers) {
+  return ((size_t)layers * sizeof(LoopLayer) + 127) / 128 * 128;
 }
 
 template <int G>
@@ -1005,6 +1129,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_loop_kernel(DecodeLoop par
                                                         p.x_bytes);
   LoopLayer* lay = reinterpret_cast<LoopLayer*>(smem + (size_t)p.slots * p.slot_bytes + p.x_bytes +
                                                 (sizeof(AttnSmem<G>) + 127) / 128 * 128);
+  // second operand of the residual-add inputs (hidden halves)
+  uint4* xs2 = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(lay) +
+                                        layer_table_bytes(p.layers));
   const int tid = threadIdx.x;
   {
     // per-layer pointer table -> shared memory (read at every stage)
@@ -1015,12 +1142,6 @@ __global__ void __launch_bounds__(kThreads, 1) decode_loop_kernel(DecodeLoop par
   }
   if (tid == 0) {
     for (int st = 0; st < 5; ++st) sh.tiles[st] = tiles_of(p, stage_weights(p, lay, 0, st));
-    for (int h = 0; h < kMaxKvHeads; ++h) sh.qkv_rows[h] = 0;
-    const int qw = p.qh * HD, kw = p.kvh * HD, gw = (p.qh / p.kvh) * HD;
-    for (int item = sh.tiles[kQKV].first; item < sh.tiles[kQKV].last; ++item) {
-      const int h = item < qw ? item / gw : item < qw + kw ? (item - qw) / HD : (item - qw - kw) / HD;
-      sh.qkv_rows[h] += 1u;
-    }
     sh.stop = 0;
     sh.astop = 0;
     for (int s = 0; s < p.slots; ++s) {
@@ -1039,95 +1160,128 @@ __global__ void __launch_bounds__(kThreads, 1) decode_loop_kernel(DecodeLoop par
 
   const uint32_t len0 = __ldcg(p.dev_len);
   uint32_t token = __ldcg(p.toks + len0);
-  uint32_t g = 0, epoch = 0;
+  uint32_t g = 0;
   uint32_t units_total = 0;  // attention units published so far (all CTAs agree)
+  const uint32_t grid = gridDim.x;
   const int warp = tid >> 5, lane = tid & 31;
   for (int step = 0; step < p.steps; ++step) {
     const int pos = (int)len0 + step;
+    const int nb = (pos + p.block) / p.block;  // key blocks: ceil((pos + 1) / block)
     for (int layer = 0; layer < p.layers; ++layer) {
       const LoopLayer& L = lay[layer];
+      const uint32_t ls = (uint32_t)(step * p.layers + layer);  // layer-step of this launch
+      const uint32_t e = p.epoch0 + ls;                             // its tag epoch
+      const uint32_t hidden_in = layer == 0 ? tagv(e, 0) : tagv(e - 1u, 1);
       uint32_t bk = 0, bi = 0xFFFFFFFFu;
-      // QKV
+      // QKV (layer 0: the embedding row, written back as the hidden stream)
       {
         if (tid == 0) { MI_TRACE(step, layer * 5 + 0, 0); MI_TRACE_SET(step, layer * 5 + 0); }
         if (tid >= kAttnBase && tid < kAttnBase + kAttnThreads)
           attention_prefetch<G>(p, L, pos, asm_);
         const StageW s = stage_weights(p, lay, layer, kQKV);
+        StageIn in = {};
+        in.k = p.hidden;
+        in.norm_w = L.in_norm;
         if (layer == 0) {
           const bool zero = token == 0xFFFFFFFFu || token >= (uint32_t)p.vocab;
-          build_input(kEmbedNormIn, zero ? nullptr : p.embedding + (size_t)token * p.hidden,
-                      nullptr, L.in_norm, p.hidden, p.eps, p.hidden_buf, xs, sh);
+          in.mode = kEmbedNormIn;
+          in.embed = zero ? nullptr : p.embedding + (size_t)token * p.hidden;
+          in.wb = p.t_hidden;
+          in.wbtag = tagv(e, 0);
         } else {
-          build_input(kNormIn, p.hidden_buf, nullptr, L.in_norm, p.hidden, p.eps, nullptr, xs, sh);
+          in.mode = kNormIn;
+          in.x = p.t_hidden;
+          in.xtag = hidden_in;
         }
+        if (!build_input(p, in, layer == 0 ? -1 : kDown, ls * grid, xs, xs2, sh)) return;
         if (tid == 0) MI_TRACE(step, layer * 5 + 0, 1);
-        reduce_rows<kQKV>(p, s, xs, ring, sh, g, bk, bi);
+        reduce_rows<kQKV>(p, s, xs, ring, sh, g, tagv(e, 0), bk, bi);
+        stage_done(p, kQKV);
         if (tid == 0) MI_TRACE(step, layer * 5 + 0, 2);
-        if (!publish_qkv(p, sh)) return;
       }
-      // ATTN
-      const uint32_t ls = (uint32_t)(step * p.layers + layer);  // layer-step index
+      // ATTN (units read their head's tagged Q/K/V rows)
       {
         if (tid == 0) { MI_TRACE(step, layer * 5 + 1, 0); MI_TRACE_SET(step, layer * 5 + 1); }
-        const int nb = (pos + p.block) / p.block;  // ceil((pos + 1) / block)
         const int units = p.kvh * nb;
         if (tid >= kAttnBase && tid < kAttnBase + kAttnThreads)
           for (int u = blockIdx.x; u < units; u += gridDim.x)
-            if (!attention_unit<G>(p, L, u / nb, u % nb, nb, pos, u == (int)blockIdx.x, ls, asm_,
-                                   sh))
-              break;
+            attention_unit<G>(p, L, u / nb, u % nb, nb, pos, u == (int)blockIdx.x, tagv(e, 0),
+                              (ls + 1u) * grid, asm_, sh);
         if (tid == 0) MI_TRACE(step, layer * 5 + 1, 2);
       }
-      // O (waits for every attention unit's partial instead of a grid barrier)
+      // O (waits for every attention unit's partial, merges them as its input)
       {
-        units_total += (uint32_t)(p.kvh * ((pos + p.block) / p.block));
+        units_total += (uint32_t)(p.kvh * nb);
         if (!wait_units(p, units_total, sh)) return;
         if (tid == 0) { MI_TRACE(step, layer * 5 + 2, 0); MI_TRACE_SET(step, layer * 5 + 2); }
+        if (tid == 0) MI_TRACE_ARRIVE(1);
         const StageW s = stage_weights(p, lay, layer, kO);
-        build_attn_input(p, (pos + p.block) / p.block, xs);
+        build_attn_input(p, nb, xs);
         if (tid == 0) MI_TRACE(step, layer * 5 + 2, 1);
-        reduce_rows<kO>(p, s, xs, ring, sh, g, bk, bi);
+        reduce_rows<kO>(p, s, xs, ring, sh, g, tagv(e, 0), bk, bi);
+        stage_done(p, kO);
         if (tid == 0) MI_TRACE(step, layer * 5 + 2, 2);
-        if (!grid_sync(p, epoch, sh)) return;
       }
       // GU
       {
         if (tid == 0) { MI_TRACE(step, layer * 5 + 3, 0); MI_TRACE_SET(step, layer * 5 + 3); }
         const StageW s = stage_weights(p, lay, layer, kGU);
-        build_input(p.add_norm ? kAddNormIn : kAddThenNormIn, p.hidden_buf, p.attn_o, L.post_norm,
-                    p.hidden, p.eps, p.residual, xs, sh);
+        StageIn in = {};
+        in.mode = p.add_norm ? kAddNormIn : kAddThenNormIn;
+        in.k = p.hidden;
+        in.x = p.t_hidden;
+        in.xtag = hidden_in;
+        in.x2 = p.t_attn_o;
+        in.x2tag = tagv(e, 0);
+        in.norm_w = L.post_norm;
+        in.wb = p.t_res;
+        in.wbtag = tagv(e, 0);
+        if (!build_input(p, in, kO, (ls + 1u) * grid, xs, xs2, sh)) return;
         if (tid == 0) MI_TRACE(step, layer * 5 + 3, 1);
-        reduce_rows<kGU>(p, s, xs, ring, sh, g, bk, bi);
+        reduce_rows<kGU>(p, s, xs, ring, sh, g, tagv(e, 0), bk, bi);
+        stage_done(p, kGU);
         if (tid == 0) MI_TRACE(step, layer * 5 + 3, 2);
-        if (!grid_sync(p, epoch, sh)) return;
       }
       // DOWN
       {
         if (tid == 0) { MI_TRACE(step, layer * 5 + 4, 0); MI_TRACE_SET(step, layer * 5 + 4); }
-        {
-          // residuals of this CTA's rows, read while the stage input loads
-          const Tiles& td = sh.tiles[kDown];
-          if (tid < min(td.last - td.first, kMaxDownRows))
-            sh.res[tid] = __ldcg(p.residual + td.first + tid);
-        }
         const StageW s = stage_weights(p, lay, layer, kDown);
-        build_input(kPlainIn, p.act, nullptr, nullptr, s.k, p.eps, nullptr, xs, sh);
+        StageIn in = {};
+        in.mode = kPlainIn;
+        in.k = p.inter;
+        in.x = p.t_act;
+        in.xtag = tagv(e, 0);
+        if (!build_input(p, in, kGU, (ls + 1u) * grid, xs, xs2, sh)) return;
+        {
+          // residuals of this CTA's rows (written back by CTA 0 in GU)
+          const Tiles& td = sh.tiles[kDown];
+          if (tid < td.last - td.first) sh.res[tid] = take1(p, p.t_res, td.first + tid, tagv(e, 0), sh);
+          consumers_sync();
+        }
         if (tid == 0) MI_TRACE(step, layer * 5 + 4, 1);
-        reduce_rows<kDown>(p, s, xs, ring, sh, g, bk, bi);
+        reduce_rows<kDown>(p, s, xs, ring, sh, g, tagv(e, 1), bk, bi);
+        stage_done(p, kDown);
         if (tid == 0) MI_TRACE(step, layer * 5 + 4, 2);
-        if (!grid_sync(p, epoch, sh)) return;
       }
     }
     // final norm + LM head + argmax
     {
       if (tid == 0) { MI_TRACE(step, p.layers * 5, 0); MI_TRACE_SET(step, p.layers * 5); }
+      const uint32_t e = p.epoch0 + (uint32_t)(step * p.layers + p.layers - 1);
       uint32_t bk = 0, bi = 0xFFFFFFFFu;
       const StageW s = stage_weights(p, lay, p.layers, kLM);
-      build_input(kNormIn, p.hidden_buf, nullptr, p.final_norm, p.hidden, p.eps, nullptr, xs, sh);
+      StageIn in = {};
+      in.mode = kNormIn;
+      in.k = p.hidden;
+      in.x = p.t_hidden;
+      in.xtag = tagv(e, 1);
+      in.norm_w = p.final_norm;
+      const uint32_t ls_last = (uint32_t)(step * p.layers + p.layers - 1);
+      if (!build_input(p, in, kDown, (ls_last + 1u) * grid, xs, xs2, sh)) return;
       if (tid == 0) MI_TRACE(step, p.layers * 5, 1);
-      reduce_rows<kLM>(p, s, xs, ring, sh, g, bk, bi);
+      reduce_rows<kLM>(p, s, xs, ring, sh, g, 0u, bk, bi);
       if (tid == 0) MI_TRACE(step, p.layers * 5, 2);
-      // per-lane bests -> warp best -> CTA best -> grid partial
+      // per-lane bests -> warp best -> CTA best -> tagged record per CTA
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) {
         const uint32_t ok = __shfl_xor_sync(0xffffffffu, bk, o);
@@ -1142,21 +1296,31 @@ __global__ void __launch_bounds__(kThreads, 1) decode_loop_kernel(DecodeLoop par
         sh.best_idx[warp] = bi;
       }
       consumers_sync();
-      if (tid == 0) {
-        uint32_t ck = 0, ci = 0xFFFFFFFFu;
-        for (int w = 0; w < kConsumerWarps; ++w)
-          if (argmax_better(sh.best_key[w], sh.best_idx[w], ck, ci)) {
-            ck = sh.best_key[w];
-            ci = sh.best_idx[w];
-          }
-        p.argmax_key[blockIdx.x] = ck;
-        p.argmax_idx[blockIdx.x] = ci;
-      }
-      if (!grid_sync(p, epoch, sh)) return;
+      const unsigned long long rtag = e & 0x3FFFu;
       if (warp == 0) {
+        if (lane == 0) {
+          uint32_t ck = 0, ci = 0xFFFFFFFFu;
+          for (int w = 0; w < kConsumerWarps; ++w)
+            if (argmax_better(sh.best_key[w], sh.best_idx[w], ck, ci)) {
+              ck = sh.best_key[w];
+              ci = sh.best_idx[w];
+            }
+          const unsigned long long idx = ci == 0xFFFFFFFFu ? 0x3FFFFull : (unsigned long long)ci;
+          st_relaxed_u64(p.t_argmax + blockIdx.x,
+                         ((unsigned long long)ck << 32) | (idx << 14) | rtag);
+          red_relaxed_add(p.sync + kStageDone + kLM, 1u);
+          stage_ready(p, kLM, (uint32_t)(step + 1) * grid, sh);
+        }
+        __syncwarp();
+        // every CTA reduces all records (argmax order is total: any order)
         uint32_t ck = 0, ci = 0xFFFFFFFFu;
         for (int b = lane; b < (int)gridDim.x; b += 32) {
-          const uint32_t k2 = __ldcg(p.argmax_key + b), i2 = __ldcg(p.argmax_idx + b);
+          unsigned long long r = ld_relaxed_u64(p.t_argmax + b);
+          PollClock clock;
+          while ((r & 0x3FFFull) != rtag && clock.keep_going(p, sh)) r = ld_relaxed_u64(p.t_argmax + b);
+          const uint32_t k2 = (uint32_t)(r >> 32);
+          uint32_t i2 = (uint32_t)((r >> 14) & 0x3FFFFull);
+          if (i2 == 0x3FFFFu) i2 = 0xFFFFFFFFu;
           if (argmax_better(k2, i2, ck, ci)) {
             ck = k2;
             ci = i2;
@@ -1174,9 +1338,11 @@ __global__ void __launch_bounds__(kThreads, 1) decode_loop_kernel(DecodeLoop par
         if (lane == 0) {
           sh.token = ci;
           if (blockIdx.x == 0) p.toks[pos + 1] = ci;
+          sh.stop = sh.abort ? 1 : 0;
         }
       }
       consumers_sync();
+      if (sh.stop) return;
       token = sh.token;
     }
   }
@@ -1198,7 +1364,7 @@ size_t attn_smem_for(int group) {
   }
 }
 
-size_t layer_table_bytes(int layers) { return (size_t)layers * sizeof(LoopLayer); }
+size_t x2_bytes(int hidden) { return ((size_t)hidden * 2 + 127) / 128 * 128; }
 
 template <int G>
 cudaError_t launch_g(cudaStream_t stream, const DecodeLoop& p, int grid, size_t smem) {
@@ -1226,6 +1392,7 @@ bool decode_loop_plan(DecodeLoop& p, int device) {
   if (attn_smem_for(group) == 0 || p.qh % p.kvh) return false;
   if (p.hidden % 8 || p.inter % 8 || p.hidden <= 0 || p.inter <= 0) return false;
   if (p.kvh > kMaxKvHeads) return false;
+  if (p.vocab >= 0x3FFFF) return false;  // argmax records carry an 18-bit index
   const int max_k = std::max(std::max(p.hidden, p.inter), p.qh * HD);
   int max_item = std::max(std::max(p.hidden * 4, p.inter * 2), p.qh * HD * 2);
   p.slot_bytes = std::max(kMinSlotBytes, (max_item + 127) / 128 * 128);
@@ -1235,7 +1402,7 @@ bool decode_loop_plan(DecodeLoop& p, int device) {
       cudaSuccess)
     return false;
   const size_t fixed = (size_t)p.x_bytes + attn_smem_for(group) + layer_table_bytes(p.layers) +
-                       sizeof(Shared) + 1024;
+                       x2_bytes(p.hidden) + sizeof(Shared) + 1024;
   if (fixed >= (size_t)optin) return false;
   p.slots = (int)std::min<size_t>(kMaxSlots, ((size_t)optin - fixed) / p.slot_bytes);
   if (p.slots < 2) return false;
@@ -1243,12 +1410,13 @@ bool decode_loop_plan(DecodeLoop& p, int device) {
   if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess)
     return false;
   p.grid = std::min(sms, kMaxGrid);
+  if ((p.hidden + p.grid - 1) / p.grid > kMaxDownRows) return false;  // DOWN residual cache
   return true;
 }
 
 size_t decode_loop_smem(const DecodeLoop& p) {
   return (size_t)p.slots * p.slot_bytes + p.x_bytes + attn_smem_for(p.qh / p.kvh) +
-         layer_table_bytes(p.layers);
+         layer_table_bytes(p.layers) + x2_bytes(p.hidden);
 }
 
 void decode_loop(cudaStream_t stream, const DecodeLoop& p) {

@@ -199,18 +199,18 @@ struct DecodeLoop {
   const float2* rope = nullptr;
   uint32_t* toks = nullptr;
   uint32_t* dev_len = nullptr;
-  __half* hidden_buf = nullptr;  // [hidden] residual stream
-  __half* residual = nullptr;    // [hidden] after the attention add
-  __half* q_raw = nullptr;
-  __half* k_raw = nullptr;
-  __half* v_raw = nullptr;
-  __half* attn_o = nullptr;
-  __half* act = nullptr;
+  // Activations that cross CTAs, one u32 per FP16 value: (16-bit epoch tag
+  // << 16) | bits, so readers validate every word (no grid barriers).
+  uint32_t epoch0 = 1;               // tag base: layer-steps run on these buffers + 1
+  uint32_t* t_hidden = nullptr;      // [hidden] residual stream
+  uint32_t* t_res = nullptr;         // [hidden] after the attention add
+  uint32_t* t_qkv = nullptr;         // [qh * 128 + 2 * kvh * 128]
+  uint32_t* t_attn_o = nullptr;      // [hidden]
+  uint32_t* t_act = nullptr;         // [inter]
+  unsigned long long* t_argmax = nullptr;  // [grid]: key << 32 | index << 14 | 14-bit tag
   __half* logits = nullptr;
   float* attn_part = nullptr;     // [kvh, attn_blocks, G, 132] block partials
-  uint32_t* argmax_key = nullptr; // [grid]
-  uint32_t* argmax_idx = nullptr; // [grid]
-  uint32_t* sync = nullptr;       // [decode_loop_sync_words()]: barrier counter, abort flag, per-head counters
+  uint32_t* sync = nullptr;       // [decode_loop_sync_words()]: abort flag, attention-unit counter
   // plan (decode_loop_plan)
   int slot_bytes = 0, slots = 0, x_bytes = 0, grid = 0;
 };

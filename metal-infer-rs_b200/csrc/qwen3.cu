@@ -81,8 +81,11 @@ struct Layer {
 struct Workspace {
   TensorRef q_raw, k_raw, v_raw, attn, attn_o, residual, hidden, act, logits;
   TensorRef argmax_pv, argmax_pi, counters, attn_scratch;
-  TensorRef loop_sync;  // persistent decode: grid-barrier counter + abort flag
+  TensorRef loop_sync;  // persistent decode: abort flag + attention-unit counter
   TensorRef loop_part;  // persistent decode: attention block partials
+  // persistent decode: epoch-tagged activations and per-CTA argmax records
+  TensorRef t_hidden, t_res, t_qkv, t_attn_o, t_act, t_argmax;
+  uint64_t loop_epoch = 1;  // layer-steps run through the tagged buffers + 1
   int attn_splits = 0;  // flash-decode blocks for the largest cache seen
   int attn_block = 64;  // keys per flash-decode block
   size_t attn_cap = 0;
@@ -436,27 +439,33 @@ void run_decode_loop(mi_qwen3* m, mi_kv_cache* c, size_t steps) {
   p.rope = c->rope_table();
   p.toks = c->toks.t->u32();
   p.dev_len = c->dev_len.t->u32();
-  p.hidden_buf = w.hidden.h();
-  p.residual = w.residual.h();
-  p.q_raw = w.q_raw.h();
-  p.k_raw = w.k_raw.h();
-  p.v_raw = w.v_raw.h();
-  p.attn_o = w.attn_o.h();
-  p.act = w.act.h();
+  if (!w.t_hidden.t) {
+    const auto& c = m->cfg;
+    w.t_hidden = TensorRef(new_tensor(ctx, {c.hidden_size}, MI_U32, true));
+    w.t_res = TensorRef(new_tensor(ctx, {c.hidden_size}, MI_U32, true));
+    w.t_qkv = TensorRef(new_tensor(ctx, {qwidth(c) + 2 * kvwidth(c)}, MI_U32, true));
+    w.t_attn_o = TensorRef(new_tensor(ctx, {c.hidden_size}, MI_U32, true));
+    w.t_act = TensorRef(new_tensor(ctx, {c.intermediate_size}, MI_U32, true));
+    w.t_argmax = TensorRef(new_tensor(ctx, {2 * (size_t)p.grid}, MI_U32, true));
+  }
+  p.t_hidden = w.t_hidden.t->u32();
+  p.t_res = w.t_res.t->u32();
+  p.t_qkv = w.t_qkv.t->u32();
+  p.t_attn_o = w.t_attn_o.t->u32();
+  p.t_act = w.t_act.t->u32();
+  p.t_argmax = reinterpret_cast<unsigned long long*>(w.t_argmax.t->u32());
   p.logits = w.logits.h();
   const size_t part = k::decode_loop_part_floats(p.kvh, w.attn_splits, p.qh / p.kvh);
   if (!w.loop_part.t || w.loop_part.t->len() < part)
     w.loop_part = TensorRef(new_tensor(ctx, {part}, MI_F32, false));
   p.attn_part = w.loop_part.t->f32();
-  p.argmax_key = reinterpret_cast<uint32_t*>(w.argmax_pv.t->f32());
-  p.argmax_idx = w.argmax_pi.t->u32();
   p.sync = w.loop_sync.t->u32();
-  MI_REQUIRE(w.argmax_pi.t->len() >= (size_t)p.grid, MI_ERR_RESOURCE,
-             "argmax partials smaller than the persistent grid");
   for (size_t done = 0; done < steps;) {
     p.steps = (int)std::min<size_t>(steps - done, 2048);
+    p.epoch0 = (uint32_t)w.loop_epoch;
     ProfileScope ps(ctx, "decode_loop");
     k::decode_loop(ctx->stream, p);
+    w.loop_epoch += (uint64_t)p.steps * (uint64_t)p.layers;
     done += (size_t)p.steps;
   }
 }
