@@ -338,6 +338,30 @@ mi_status mi_qwen3_config_validate(const mi_qwen3_config* config);
  * synthetic runs. */
 mi_status mi_qwen3_create_random(mi_context* ctx, const mi_qwen3_config* config, uint64_t seed,
                                  double std_dev, mi_qwen3** out);
+/* ---- tensor parallelism (no counterpart in the reference, which runs on
+ * one GPU). Megatron-style sharding over tp ranks, one process (context)
+ * per GPU: rank r holds query heads [q_head0, q_head0 + q_heads), KV heads
+ * [kv_head0, ...), MLP columns [inter0, ...) and LM-head rows (vocabulary)
+ * [vocab0, ...); the O and down projections are row-parallel: each rank's
+ * FP32 partial products are gathered over NCCL and summed in rank order,
+ * then rounded once to FP16; the greedy id is the best of the ranks'
+ * candidates. Every rank calls the same model functions in the same order
+ * (prefill, decode, generate return identical ids on all ranks; logits are
+ * gathered over the full vocabulary). */
+typedef struct mi_tp_shard_info {
+  size_t q_heads, kv_heads, intermediate, vocab;
+  size_t q_head0, kv_head0, inter0, vocab0;
+} mi_tp_shard_info;
+/* This rank's shard of `config` (host only; no device needed). */
+mi_status mi_tp_shard(const mi_qwen3_config* config, int tp, int rank, mi_tp_shard_info* out);
+/* A fresh NCCL unique id (128 bytes) for rank 0 to share with the others. */
+mi_status mi_nccl_unique_id(uint8_t* out, size_t len);
+/* mi_qwen3_create_random's model, this rank's shard of it; joins the NCCL
+ * communicator of `nccl_id` (collective: every rank must call it). tp = 1
+ * is mi_qwen3_create_random. */
+mi_status mi_qwen3_create_random_tp(mi_context* ctx, const mi_qwen3_config* config,
+                                    uint64_t seed, double std_dev, int tp, int rank,
+                                    const uint8_t* nccl_id, mi_qwen3** out);
 /* Qwen3Model::load from a directory with config.json + *.safetensors
  * (qwen3.rs:155-240, weights.rs:21-75). F16 and BF16 tensors. */
 mi_status mi_qwen3_load(mi_context* ctx, const char* directory, mi_qwen3** out);

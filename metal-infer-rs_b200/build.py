@@ -33,8 +33,8 @@ def nvcc() -> str:
 def nccl_dirs():
     """Include and library directories of the NCCL that torch ships with."""
     try:
-        import nvidia.nccl  # type: ignore
-        base = os.path.dirname(nvidia.nccl.__file__)
+        import nvidia.nccl  # type: ignore  (a namespace package: no __file__)
+        base = list(nvidia.nccl.__path__)[0]
         inc, lib = os.path.join(base, "include"), os.path.join(base, "lib")
         if os.path.exists(os.path.join(inc, "nccl.h")):
             return inc, lib

@@ -23,7 +23,7 @@ constexpr int kCanonRows = 512;
 // butterfly completes each of the 64 dots.
 __global__ void __launch_bounds__(256) gemm_canon_kernel(const __half* x, const __half* w,
                                                          __half* out, int m, int n, int k,
-                                                         int ldo) {
+                                                         int ldo, float* outf) {
   pdl_wait();
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
@@ -66,7 +66,10 @@ __global__ void __launch_bounds__(256) gemm_canon_kernel(const __half* x, const 
 #pragma unroll
       for (int jj = 0; jj < 8; ++jj)
         if (ii == i && jj == j) v = acc[ii][jj];
-    if (m0 + i < m && n0 + j < n) out[(size_t)(m0 + i) * ldo + n0 + j] = __float2half_rn(v);
+    if (m0 + i < m && n0 + j < n) {
+      if (outf) outf[(size_t)(m0 + i) * ldo + n0 + j] = v;
+      else out[(size_t)(m0 + i) * ldo + n0 + j] = __float2half_rn(v);
+    }
   }
 }
 
@@ -132,12 +135,23 @@ void gemm(const Launch& l, const __half* x, const __half* w, __half* out, int m,
   const bool vec = k % 8 == 0 && aligned16(x) && aligned16(w);
   if (vec && m <= kCanonRows) {
     dim3 grid((n + 31) / 32, (m + 15) / 16);
-    launch_kernel(l, grid, dim3(256), 0, gemm_canon_kernel, x, w, out, m, n, k, ldo);
+    launch_kernel(l, grid, dim3(256), 0, gemm_canon_kernel, x, w, out, m, n, k, ldo,
+                  static_cast<float*>(nullptr));
     return;
   }
   if (gemm_tc(l, x, w, out, m, n, k, ldo)) return;
   dim3 grid((n + BN - 1) / BN, (m + BM - 1) / BM);
   launch_kernel(l, grid, dim3(256), 0, gemm_simt_kernel, x, w, out, m, n, k, ldo);
+}
+
+void gemm_partial_f32(const Launch& l, const __half* x, const __half* w, float* out, int m, int n,
+                      int k) {
+  if (m <= 0 || n <= 0) return;
+  MI_REQUIRE(k % 8 == 0 && aligned16(x) && aligned16(w), MI_ERR_SHAPE,
+             "tensor-parallel partial products need K %% 8 == 0 and 16-byte aligned operands");
+  dim3 grid((n + 31) / 32, (m + 15) / 16);
+  launch_kernel(l, grid, dim3(256), 0, gemm_canon_kernel, x, w, static_cast<__half*>(nullptr), m,
+                n, k, n, out);
 }
 
 }  // namespace k

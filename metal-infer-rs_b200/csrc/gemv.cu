@@ -229,6 +229,8 @@ __global__ void __launch_bounds__(kThreads) gemv_staged_kernel(GemvProblem p, Pl
           p.out[0][item] = __float2half_rn(silu_mul(g, u));
         } else if (OUT == kOutResidual) {
           p.out[0][item] = __hadd(p.res[item], __float2half_rn(a0));
+        } else if (OUT == kOutF32) {
+          p.outf[item] = a0;
         } else {
           int seg = 0, row = item;
           if (row >= p.n[0]) {
@@ -301,7 +303,12 @@ __global__ void __launch_bounds__(kThreads) gemv_staged_kernel(GemvProblem p, Pl
             bk = best_key_s[w];
             bi = best_idx_s[w];
           }
-        p.token_out[p.token_pos ? *p.token_pos + 1u : 0u] = bi;
+        if (p.best_out) {
+          p.best_out[0] = bk;
+          p.best_out[1] = bi == 0xFFFFFFFFu ? bi : bi + p.index_base;
+        } else {
+          p.token_out[p.token_pos ? *p.token_pos + 1u : 0u] = bi;
+        }
         __threadfence();
         if (p.step_counter) *p.step_counter += 1u;
         *p.counter = 0u;
@@ -437,6 +444,7 @@ void gemv(const Launch& l, const GemvProblem& p) {
   MI_GEMV_CASE(kInPlain, kOutSwiglu)
   MI_GEMV_CASE(kInNorm, kOutArgmax)
   MI_GEMV_CASE(kInPlain, kOutArgmax)
+  MI_GEMV_CASE(kInPlain, kOutF32)
 #undef MI_GEMV_CASE
   fail(MI_ERR_SHAPE, "unsupported GEMV fusion (%d, %d)", p.in_mode, p.out_mode);
 }

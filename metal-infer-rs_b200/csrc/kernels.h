@@ -39,7 +39,8 @@ enum GemvOut : int {
   kOutPlain = 0,     // out[s][row] = half(dot)
   kOutResidual = 1,  // out0[row] = res[row] + half(dot)  (half add)
   kOutSwiglu = 2,    // out0[i] = half(silu(g) * u), g/u = half dots of rows i of w0/w1
-  kOutArgmax = 3     // out0 = logits; greedy id of the logits -> token_out
+  kOutArgmax = 3,    // out0 = logits; greedy id of the logits -> token_out
+  kOutF32 = 4        // outf[row] = dot (FP32, unrounded: a tensor-parallel partial)
 };
 
 struct GemvProblem {
@@ -68,6 +69,9 @@ struct GemvProblem {
   uint32_t* argmax_index = nullptr;   // kOutArgmax: [grid] indices
   uint32_t* counter = nullptr;        // kOutArgmax: zero before, zero after
   uint32_t* step_counter = nullptr;   // kOutArgmax: optional +1 of a decode state
+  uint32_t* best_out = nullptr;       // kOutArgmax: optional {key, index + index_base}
+  uint32_t index_base = 0;            // kOutArgmax: global index of row 0 (vocab shard)
+  float* outf = nullptr;              // kOutF32
 };
 // True when the fast kernel accepts the problem (K % 8 == 0, 16-byte
 // aligned pointers, K <= 16384); otherwise gemv() uses the generic kernel.
@@ -79,6 +83,10 @@ void matmul_reference(const Launch& l, const __half* x, const __half* w, __half*
 // Prefill GEMM (M > 1): out[m, n] = x[m, :] . w[n, :], FP32 accumulate.
 void gemm(const Launch& l, const __half* x, const __half* w, __half* out, int m, int n, int k,
           int ldo);
+// Tensor-parallel partial product: out[m, n] = DOT(x[m], w[n]) in FP32 with
+// the canonical reduction (any m), unrounded.
+void gemm_partial_f32(const Launch& l, const __half* x, const __half* w, float* out, int m, int n,
+                      int k);
 // Expired-wait code of the tensor-core GEMM (0 = none); optionally cleared.
 unsigned gemm_tc_status(bool reset);
 bool gemm_tc_available();
@@ -162,6 +170,16 @@ unsigned attention_status(bool reset);
 // round_p the flash-prefill semantics (FP16 probabilities), without it the
 // FP32 online softmax of the tiled kernel.
 void attention_prefill(const Launch& l, const AttnProblem& p);
+
+// ---- tensor parallelism -----------------------------------------------------------
+// out[i] = half(parts[0][i] + parts[1][i] + ... + parts[tp-1][i]), summed in
+// rank order in FP32 (parts: [tp, n] as gathered from the ranks).
+void rank_sum_round(cudaStream_t s, const float* parts, int tp, size_t n, __half* out);
+// Greedy id over the ranks' {key, index} pairs ([tp, 2]): writes it to
+// token_out[*token_pos + 1] (or token_out[0] without token_pos) and adds one
+// to *step_counter when given.
+void argmax_combine(cudaStream_t s, const uint32_t* pairs, int tp, uint32_t* token_out,
+                    const uint32_t* token_pos, uint32_t* step_counter);
 
 // ---- persistent decode loop -------------------------------------------------------
 // Per-layer weights and cache of the persistent decode kernel (device array).

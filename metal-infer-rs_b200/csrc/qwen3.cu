@@ -26,6 +26,10 @@
 #include <map>
 #include <memory>
 
+#ifdef MI_HAVE_NCCL
+#include <nccl.h>
+#endif
+
 #include "kernels.h"
 #include "mi_internal.h"
 
@@ -81,6 +85,9 @@ struct Layer {
 struct Workspace {
   TensorRef q_raw, k_raw, v_raw, attn, attn_o, residual, hidden, act, logits;
   TensorRef argmax_pv, argmax_pi, counters, attn_scratch;
+  // tensor parallelism: FP32 partials of this rank, all ranks' partials,
+  // the rounded sum, this rank's greedy candidate and all ranks' candidates
+  TensorRef tp_part, tp_gather, tp_sum, tp_best, tp_best_all, tp_logits;
   TensorRef loop_sync;  // persistent decode: abort flag + attention-unit counter
   TensorRef loop_part;  // persistent decode: attention block partials
   // persistent decode: epoch-tagged activations and per-CTA argmax records
@@ -106,6 +113,13 @@ struct mi_qwen3 {
   mi_attention_kind attention_kind = MI_ATTENTION_TILED;
   mi_fusion_options fusion{1, 1, 1, 1};
   bool graphs = true;
+  // Tensor parallelism: cfg holds this rank's shard (heads, intermediate,
+  // vocabulary divided by tp); full_cfg the model's configuration.
+  int tp = 1, rank = 0;
+  mi_qwen3_config full_cfg{};
+#ifdef MI_HAVE_NCCL
+  ncclComm_t comm = nullptr;
+#endif
   bool persistent = true;  // decode through the persistent kernel when it fits
   int loop_state = 0;      // 0 unplanned, 1 planned, -1 not admitted
   k::DecodeLoop loop;
@@ -142,6 +156,9 @@ void model_release(mi_qwen3* m) {
   mi_context* ctx = m->ctx;
   cudaSetDevice(ctx->device);
   cudaStreamSynchronize(ctx->stream);
+#ifdef MI_HAVE_NCCL
+  if (m->comm) ncclCommDestroy(m->comm);
+#endif
   delete m;
   context_release(ctx);
 }
@@ -178,11 +195,44 @@ bool pdl_enabled() {
 }
 
 k::Launch dlaunch(mi_qwen3* m, bool pdl) {
-  return launch(m, pdl && !m->ctx->profiling && pdl_enabled());
+  return launch(m, pdl && !m->ctx->profiling && pdl_enabled() && m->tp == 1);
 }
 
 size_t qwidth(const mi_qwen3_config& c) { return c.num_attention_heads * c.head_dim; }
 size_t kvwidth(const mi_qwen3_config& c) { return c.num_key_value_heads * c.head_dim; }
+
+// Tokens index the full vocabulary (the embedding is replicated).
+uint32_t vocab_full(const mi_qwen3* m) { return (uint32_t)m->full_cfg.vocab_size; }
+
+// All-gather of `count` elements per rank on the engine stream.
+void tp_allgather(mi_qwen3* m, const void* send, void* recv, size_t count, int dtype_bytes) {
+#ifdef MI_HAVE_NCCL
+  ncclDataType_t t = dtype_bytes == 4 ? ncclFloat32 : ncclFloat16;
+  ncclResult_t r = ncclAllGather(send, recv, count, t, m->comm, m->ctx->stream);
+  if (r != ncclSuccess)
+    fail(MI_ERR_COLLECTIVE, "NCCL all-gather failed: %s", ncclGetErrorString(r));
+#else
+  (void)m, (void)send, (void)recv, (void)count, (void)dtype_bytes;
+  fail(MI_ERR_UNSUPPORTED, "built without NCCL: tensor parallelism is unavailable");
+#endif
+}
+
+// Row-parallel projection result: this rank's FP32 partials `part` ([n])
+// are gathered from every rank into `gather` ([tp, n]) and summed in rank
+// order into `out` (FP16).
+void tp_reduce(mi_qwen3* m, const float* part, size_t n, float* gather, __half* out) {
+  tp_allgather(m, part, gather, n, 4);
+  k::rank_sum_round(m->ctx->stream, gather, m->tp, n, out);
+}
+
+// Vocab-parallel greedy id: the ranks' {key, index} candidates in
+// w.tp_best are gathered and the best goes to tokens[*pos + 1] (or
+// tokens[0] without pos); *step_counter advances when given.
+void tp_argmax(mi_qwen3* m, uint32_t* tokens, const uint32_t* pos, uint32_t* step_counter) {
+  auto& w = m->ws;
+  tp_allgather(m, w.tp_best.t->u32(), w.tp_best_all.t->u32(), 2, 4);
+  k::argmax_combine(m->ctx->stream, w.tp_best_all.t->u32(), m->tp, tokens, pos, step_counter);
+}
 
 bool fused_decode_supported(const mi_qwen3* m) {
   const auto& c = m->cfg;
@@ -210,6 +260,14 @@ void ensure_workspace(mi_qwen3* m, size_t capacity) {
     w.argmax_pv = TensorRef(new_tensor(ctx, {parts}, MI_F32, true));
     w.argmax_pi = TensorRef(new_tensor(ctx, {parts}, MI_U32, true));
     w.counters = TensorRef(new_tensor(ctx, {1 + c.num_key_value_heads}, MI_U32, true));
+    if (m->tp > 1) {
+      w.tp_part = TensorRef(new_tensor(ctx, {c.hidden_size}, MI_F32, true));
+      w.tp_sum = TensorRef(new_tensor(ctx, {c.hidden_size}, MI_F16, true));
+      w.tp_best = TensorRef(new_tensor(ctx, {2}, MI_U32, true));
+      w.tp_best_all = TensorRef(new_tensor(ctx, {2 * (size_t)m->tp}, MI_U32, true));
+      // fixed for the captured decode graph (prefill gathers into its own)
+      w.tp_gather = TensorRef(new_tensor(ctx, {(size_t)m->tp * c.hidden_size}, MI_F32, true));
+    }
   }
   const int cap_block = k::decode_block_for((int)capacity);
   const int cap_splits = ((int)capacity + cap_block - 1) / cap_block;
@@ -265,7 +323,7 @@ void encode_decode_step(mi_qwen3* m, mi_kv_cache* c) {
         p.token = c->toks.t->u32();
         p.token_pos = len;
         p.table = m->embedding.h();
-        p.table_rows = (uint32_t)cfg.vocab_size;
+        p.table_rows = vocab_full(m);
         p.embed_out = w.hidden.h();
       } else {
         p.in_mode = k::kInNorm;
@@ -297,7 +355,7 @@ void encode_decode_step(mi_qwen3* m, mi_kv_cache* c) {
       k::attention_decode_fused(dlaunch(m, true), d, w.attn_splits, w.attn_scratch.t->f32(),
                                 w.counters.t->u32() + 1, k::decode_block_for((int)c->capacity));
     }
-    // 3. O projection
+    // 3. O projection (row-parallel under tensor parallelism)
     {
       k::GemvProblem p;
       p.k = qw;
@@ -305,8 +363,13 @@ void encode_decode_step(mi_qwen3* m, mi_kv_cache* c) {
       p.w[0] = L.w[kO].h();
       p.n[0] = h;
       p.out[0] = w.attn_o.h();
+      if (m->tp > 1) {
+        p.out_mode = k::kOutF32;
+        p.outf = w.tp_part.t->f32();
+      }
       ProfileScope ps(m->ctx, "o_gemv");
       k::gemv(dlaunch(m, true), p);
+      if (m->tp > 1) tp_reduce(m, w.tp_part.t->f32(), (size_t)h, w.tp_gather.t->f32(), w.attn_o.h());
     }
     // 4. residual + RMSNorm + gate/up + SwiGLU
     {
@@ -328,7 +391,7 @@ void encode_decode_step(mi_qwen3* m, mi_kv_cache* c) {
       ProfileScope ps(m->ctx, "gate_up_gemv");
       k::gemv(dlaunch(m, true), p);
     }
-    // 5. down + residual
+    // 5. down + residual (row-parallel under tensor parallelism)
     {
       k::GemvProblem p;
       p.k = I;
@@ -338,8 +401,16 @@ void encode_decode_step(mi_qwen3* m, mi_kv_cache* c) {
       p.out_mode = k::kOutResidual;
       p.res = w.residual.h();
       p.out[0] = w.hidden.h();
+      if (m->tp > 1) {
+        p.out_mode = k::kOutF32;
+        p.outf = w.tp_part.t->f32();
+      }
       ProfileScope ps(m->ctx, "down_gemv");
       k::gemv(dlaunch(m, true), p);
+      if (m->tp > 1) {
+        tp_reduce(m, w.tp_part.t->f32(), (size_t)h, w.tp_gather.t->f32(), w.tp_sum.h());
+        k::add(launch(m, false), w.residual.h(), w.tp_sum.h(), w.hidden.h(), (size_t)h);
+      }
     }
   }
   // final norm + LM head + argmax; advances the device length.
@@ -360,8 +431,15 @@ void encode_decode_step(mi_qwen3* m, mi_kv_cache* c) {
     p.argmax_index = w.argmax_pi.t->u32();
     p.counter = w.counters.t->u32();
     p.step_counter = len;
+    if (m->tp > 1) {
+      // vocab-parallel: this rank's candidate, then the combine over ranks
+      p.best_out = w.tp_best.t->u32();
+      p.index_base = (uint32_t)(m->rank * cfg.vocab_size);
+      p.step_counter = nullptr;
+    }
     ProfileScope ps(m->ctx, "lm_head_argmax");
     k::gemv(dlaunch(m, true), p);
+    if (m->tp > 1) tp_argmax(m, c->toks.t->u32(), len, len);
   }
 }
 
@@ -377,7 +455,8 @@ bool persistent_env() {
 }
 
 bool decode_loop_ready(mi_qwen3* m) {
-  if (!m->persistent || !persistent_env() || !fused_decode_supported(m)) return false;
+  if (m->tp > 1 || !m->persistent || !persistent_env() || !fused_decode_supported(m))
+    return false;
   if (m->loop_state == 0) {
     const auto& c = m->cfg;
     k::DecodeLoop p;
@@ -527,6 +606,21 @@ mi_attention_kind prefill_kind(mi_attention_kind configured, size_t tokens) {
   }
 }
 
+// out[t, n] of a row-parallel projection: the plain GEMM on one GPU; under
+// tensor parallelism each rank's canonical FP32 partials over its slice of
+// the input columns, summed in rank order and rounded once.
+void row_parallel_gemm(mi_qwen3* m, const k::Launch& l, const __half* x, const __half* w,
+                       __half* out, int t, int n, int k_local) {
+  if (m->tp == 1) {
+    k::gemm(l, x, w, out, t, n, k_local, n);
+    return;
+  }
+  TensorRef part(new_tensor(m->ctx, {(size_t)t * n}, MI_F32, false));
+  TensorRef gather(new_tensor(m->ctx, {(size_t)m->tp * t * n}, MI_F32, false));
+  k::gemm_partial_f32(l, x, w, part.t->f32(), t, n, k_local);
+  tp_reduce(m, part.t->f32(), (size_t)t * n, gather.t->f32(), out);
+}
+
 // One layer on hidden [T, h] at cache offset `off` (prefill semantics).
 void layer_prefill(mi_qwen3* m, mi_kv_cache* c, size_t li, __half* hidden, size_t T, size_t off,
                    Scratch& s) {
@@ -581,7 +675,7 @@ void layer_prefill(mi_qwen3* m, mi_kv_cache* c, size_t li, __half* hidden, size_
     k::attention_prefill(l, a);
   }
   __half* attn_o = s.f16({T, (size_t)h});
-  k::gemm(l, attn, L.w[kO].h(), attn_o, t, h, qw, h);
+  row_parallel_gemm(m, l, attn, L.w[kO].h(), attn_o, t, h, qw);
   __half* residual = s.f16({T, (size_t)h});
   if (m->fusion.add_rms_norm) {
     k::add_rms_norm(l, hidden, attn_o, L.w[kPostNorm].h(), residual, normalized, t, h, eps);
@@ -596,7 +690,7 @@ void layer_prefill(mi_qwen3* m, mi_kv_cache* c, size_t li, __half* hidden, size_
   __half* act = s.f16({T, (size_t)I});
   k::swiglu(l, gate, up, act, T * I);
   __half* down = s.f16({T, (size_t)h});
-  k::gemm(l, act, L.w[kDown].h(), down, t, h, I, h);
+  row_parallel_gemm(m, l, act, L.w[kDown].h(), down, t, h, I);
   k::add(l, residual, down, hidden, T * h);
 }
 
@@ -628,8 +722,7 @@ void forward_tokens(mi_qwen3* m, mi_kv_cache* c, size_t T) {
   k::Launch l = launch(m, false);
   const int h = (int)cfg.hidden_size;
   __half* hidden = s.f16({T, (size_t)h});
-  k::embedding(l, c->toks.t->u32() + off, m->embedding.h(), hidden, (int)T, h,
-               (uint32_t)cfg.vocab_size);
+  k::embedding(l, c->toks.t->u32() + off, m->embedding.h(), hidden, (int)T, h, vocab_full(m));
   for (size_t li = 0; li < m->layers.size(); ++li) layer_prefill(m, c, li, hidden, T, off, s);
   auto& w = m->ws;
   k::GemvProblem p;
@@ -646,7 +739,12 @@ void forward_tokens(mi_qwen3* m, mi_kv_cache* c, size_t T) {
   p.argmax_partial = w.argmax_pv.t->f32();
   p.argmax_index = w.argmax_pi.t->u32();
   p.counter = w.counters.t->u32();
+  if (m->tp > 1) {
+    p.best_out = w.tp_best.t->u32();
+    p.index_base = (uint32_t)(m->rank * cfg.vocab_size);
+  }
   k::gemv(l, p);
+  if (m->tp > 1) tp_argmax(m, c->toks.t->u32() + off + T, nullptr, nullptr);
   c->filled = off + T;
   set_dev_len(c, c->filled);
 }
@@ -656,8 +754,14 @@ void upload_tokens(mi_kv_cache* c, const uint32_t* tokens, size_t count, size_t 
                           c->model->ctx->stream));
 }
 
+// The last logits over the full vocabulary (gathered from the vocab shards
+// under tensor parallelism).
 mi_tensor* copy_logits(mi_qwen3* m) {
-  mi_tensor* out = new_tensor(m->ctx, {1, m->cfg.vocab_size}, MI_F16);
+  mi_tensor* out = new_tensor(m->ctx, {1, m->full_cfg.vocab_size}, MI_F16);
+  if (m->tp > 1) {
+    tp_allgather(m, m->ws.logits.t->base(), out->base(), m->cfg.vocab_size, 2);
+    return out;
+  }
   MI_CUDA(cudaMemcpyAsync(out->base(), m->ws.logits.t->base(), out->bytes(),
                           cudaMemcpyDeviceToDevice, m->ctx->stream));
   return out;
@@ -709,65 +813,175 @@ mi_status mi_qwen3_config_validate(const mi_qwen3_config* config) {
   });
 }
 
+mi_status mi_tp_shard(const mi_qwen3_config* config, int tp, int rank, mi_tp_shard_info* out) {
+  return guard([&] {
+    require(config, "config");
+    require(out, "out");
+    validate_config(*config);
+    const auto& c = *config;
+    if (tp < 1 || rank < 0 || rank >= tp)
+      fail(MI_ERR_CONFIG, "invalid model configuration: rank %d outside tensor-parallel size %d",
+           rank, tp);
+    if (c.num_attention_heads % tp || c.num_key_value_heads % tp || c.intermediate_size % tp ||
+        c.vocab_size % tp)
+      fail(MI_ERR_CONFIG,
+           "invalid model configuration: heads, KV heads, intermediate size and vocabulary must "
+           "divide by the tensor-parallel size %d", tp);
+    if (tp > 1 && ((c.intermediate_size / tp) % 8 || (c.num_attention_heads / tp * c.head_dim) % 8))
+      fail(MI_ERR_CONFIG,
+           "invalid model configuration: per-rank input slices must be multiples of 8");
+    mi_tp_shard_info s{};
+    s.q_heads = c.num_attention_heads / tp;
+    s.kv_heads = c.num_key_value_heads / tp;
+    s.intermediate = c.intermediate_size / tp;
+    s.vocab = c.vocab_size / tp;
+    s.q_head0 = (size_t)rank * s.q_heads;
+    s.kv_head0 = (size_t)rank * s.kv_heads;
+    s.inter0 = (size_t)rank * s.intermediate;
+    s.vocab0 = (size_t)rank * s.vocab;
+    *out = s;
+  });
+}
+
+mi_status mi_nccl_unique_id(uint8_t* out, size_t len) {
+  return guard([&] {
+    require(out, "out");
+#ifdef MI_HAVE_NCCL
+    MI_REQUIRE(len >= sizeof(ncclUniqueId), MI_ERR_INVALID_ARGUMENT,
+               "the NCCL id needs %zu bytes", sizeof(ncclUniqueId));
+    ncclUniqueId id;
+    ncclResult_t r = ncclGetUniqueId(&id);
+    if (r != ncclSuccess) fail(MI_ERR_COLLECTIVE, "ncclGetUniqueId: %s", ncclGetErrorString(r));
+    std::memcpy(out, &id, sizeof id);
+#else
+    (void)len;
+    fail(MI_ERR_UNSUPPORTED, "built without NCCL: tensor parallelism is unavailable");
+#endif
+  });
+}
+
+}  // extern "C"
+
+namespace {
+
+// Seeded random-init model, this rank's shard of it under tensor
+// parallelism (tp ranks): every shard is the corresponding block of the
+// full tensors of the one-GPU model (same generator streams and indices).
+mi_qwen3* build_random(mi_context* ctx, const mi_qwen3_config& config, uint64_t seed,
+                       double std_dev, int tp, int rank, const uint8_t* nccl_id) {
+  validate_config(config);
+  mi_tp_shard_info sh{};
+  {
+    mi_status st = mi_tp_shard(&config, tp, rank, &sh);
+    if (st != MI_OK) fail(st, "%s", mi_last_error_message());
+  }
+  auto m = std::make_unique<mi_qwen3>();
+  m->ctx = ctx;
+  m->full_cfg = config;
+  m->cfg = config;
+  m->cfg.num_attention_heads = (uint32_t)sh.q_heads;
+  m->cfg.num_key_value_heads = (uint32_t)sh.kv_heads;
+  m->cfg.intermediate_size = (uint32_t)sh.intermediate;
+  m->cfg.vocab_size = (uint32_t)sh.vocab;
+  m->tp = tp;
+  m->rank = rank;
+  context_retain(ctx);
+  struct CtxGuard {
+    mi_qwen3* m;
+    ~CtxGuard() {
+      if (m) context_release(m->ctx);
+    }
+  } ctx_guard{m.get()};
+  const auto& fc = m->full_cfg;
+  const size_t h = fc.hidden_size, hd = fc.head_dim, V = fc.vocab_size;
+  const size_t qw = qwidth(fc), kw = kvwidth(fc), I = fc.intermediate_size;
+  const size_t qw_l = qwidth(m->cfg), kw_l = kvwidth(m->cfg), I_l = m->cfg.intermediate_size;
+  cudaStream_t st = ctx->stream;
+  // rows x cols block at (row0, col0) of the full [*, full_cols] tensor
+  auto block = [&](int layer, int role, size_t rows, size_t cols, size_t full_cols, size_t row0,
+                   size_t col0) {
+    TensorRef t(new_tensor(ctx, {rows, cols}, MI_F16));
+    k::fill_normal_f16_block(st, t.h(), rows, cols, full_cols, row0, col0, seed,
+                             (uint64_t)((layer + 1) * 16 + role), std_dev);
+    return t;
+  };
+  auto ones = [&](size_t n) {
+    TensorRef t(new_tensor(ctx, {n}, MI_F16));
+    k::fill_f16(st, t.h(), n, 0x3c00);
+    return t;
+  };
+  m->embedding = block(-1, kEmbedding, V, h, h, 0, 0);
+  m->final_norm = ones(h);
+  if (fc.tie_word_embeddings) {
+    if (tp == 1) {
+      m->lm_head = m->embedding.t;
+    } else {
+      m->lm_head_own = TensorRef(view(m->embedding.t, {sh.vocab, h}, sh.vocab0 * h * 2));
+      m->lm_head = m->lm_head_own.t;
+    }
+  } else {
+    m->lm_head_own = block(-1, kLmHead, sh.vocab, h, h, sh.vocab0, 0);
+    m->lm_head = m->lm_head_own.t;
+  }
+  m->layers.resize(fc.num_hidden_layers);
+  for (size_t l = 0; l < fc.num_hidden_layers; ++l) {
+    Layer& L = m->layers[l];
+    const int li = (int)l;
+    L.w[kQ] = block(li, kQ, qw_l, h, h, sh.q_head0 * hd, 0);
+    L.w[kK] = block(li, kK, kw_l, h, h, sh.kv_head0 * hd, 0);
+    L.w[kV] = block(li, kV, kw_l, h, h, sh.kv_head0 * hd, 0);
+    L.w[kO] = block(li, kO, h, qw_l, qw, 0, sh.q_head0 * hd);
+    L.w[kQNorm] = ones(hd);
+    L.w[kKNorm] = ones(hd);
+    L.w[kGate] = block(li, kGate, I_l, h, h, sh.inter0, 0);
+    L.w[kUp] = block(li, kUp, I_l, h, h, sh.inter0, 0);
+    L.w[kDown] = block(li, kDown, h, I_l, I, 0, sh.inter0);
+    L.w[kInputNorm] = ones(h);
+    L.w[kPostNorm] = ones(h);
+  }
+  (void)kw;
+  if (tp > 1) {
+#ifdef MI_HAVE_NCCL
+    require(nccl_id, "nccl_id");
+    ncclUniqueId id;
+    std::memcpy(&id, nccl_id, sizeof id);
+    MI_CUDA(cudaSetDevice(ctx->device));
+    ncclResult_t r = ncclCommInitRank(&m->comm, tp, id, rank);
+    if (r != ncclSuccess)
+      fail(MI_ERR_COLLECTIVE, "ncclCommInitRank (rank %d of %d): %s", rank, tp,
+           ncclGetErrorString(r));
+#else
+    (void)nccl_id;
+    fail(MI_ERR_UNSUPPORTED, "built without NCCL: tensor parallelism is unavailable");
+#endif
+  }
+  sync_context(ctx);
+  ctx_guard.m = nullptr;
+  return m.release();
+}
+
+}  // namespace
+
+extern "C" {
+
 mi_status mi_qwen3_create_random(mi_context* ctx, const mi_qwen3_config* config, uint64_t seed,
                                  double std_dev, mi_qwen3** out) {
   return guard([&] {
     require(ctx, "ctx");
     require(config, "config");
     require(out, "out");
-    validate_config(*config);
-    auto m = std::make_unique<mi_qwen3>();
-    m->ctx = ctx;
-    m->cfg = *config;
-    context_retain(ctx);
-    struct CtxGuard {
-      mi_qwen3* m;
-      ~CtxGuard() {
-        if (m) context_release(m->ctx);
-      }
-    } ctx_guard{m.get()};
-    const auto& c = m->cfg;
-    size_t h = c.hidden_size, hd = c.head_dim, qw = qwidth(c), kw = kvwidth(c),
-           I = c.intermediate_size, V = c.vocab_size;
-    cudaStream_t st = ctx->stream;
-    auto matrix = [&](int layer, int role, size_t rows, size_t cols) {
-      TensorRef t(new_tensor(ctx, {rows, cols}, MI_F16));
-      k::fill_normal_f16(st, t.h(), rows * cols, seed, (uint64_t)((layer + 1) * 16 + role), 0,
-                         std_dev);
-      return t;
-    };
-    auto ones = [&](size_t n) {
-      TensorRef t(new_tensor(ctx, {n}, MI_F16));
-      k::fill_f16(st, t.h(), n, 0x3c00);
-      return t;
-    };
-    m->embedding = matrix(-1, kEmbedding, V, h);
-    m->final_norm = ones(h);
-    if (c.tie_word_embeddings) {
-      m->lm_head = m->embedding.t;
-    } else {
-      m->lm_head_own = matrix(-1, kLmHead, V, h);
-      m->lm_head = m->lm_head_own.t;
-    }
-    m->layers.resize(c.num_hidden_layers);
-    for (size_t l = 0; l < c.num_hidden_layers; ++l) {
-      Layer& L = m->layers[l];
-      int li = (int)l;
-      L.w[kQ] = matrix(li, kQ, qw, h);
-      L.w[kK] = matrix(li, kK, kw, h);
-      L.w[kV] = matrix(li, kV, kw, h);
-      L.w[kO] = matrix(li, kO, h, qw);
-      L.w[kQNorm] = ones(hd);
-      L.w[kKNorm] = ones(hd);
-      L.w[kGate] = matrix(li, kGate, I, h);
-      L.w[kUp] = matrix(li, kUp, I, h);
-      L.w[kDown] = matrix(li, kDown, h, I);
-      L.w[kInputNorm] = ones(h);
-      L.w[kPostNorm] = ones(h);
-    }
-    sync_context(ctx);
-    ctx_guard.m = nullptr;
-    *out = m.release();
+    *out = build_random(ctx, *config, seed, std_dev, 1, 0, nullptr);
+  });
+}
+
+mi_status mi_qwen3_create_random_tp(mi_context* ctx, const mi_qwen3_config* config,
+                                    uint64_t seed, double std_dev, int tp, int rank,
+                                    const uint8_t* nccl_id, mi_qwen3** out) {
+  return guard([&] {
+    require(ctx, "ctx");
+    require(config, "config");
+    require(out, "out");
+    *out = build_random(ctx, *config, seed, std_dev, tp, rank, nccl_id);
   });
 }
 
@@ -777,7 +991,7 @@ mi_status mi_qwen3_get_config(const mi_qwen3* m, mi_qwen3_config* out) {
   return guard([&] {
     require(m, "model");
     require(out, "out");
-    *out = m->cfg;
+    *out = m->full_cfg;
   });
 }
 
@@ -1148,7 +1362,7 @@ mi_status mi_qwen3_run_first_block(mi_qwen3* m, const uint32_t* tokens, size_t c
     const int h = (int)m->cfg.hidden_size;
     TensorRef hidden(new_tensor(m->ctx, {count, (size_t)h}, MI_F16));
     k::embedding(launch(m, false), c->toks.t->u32(), m->embedding.h(), hidden.h(), (int)count, h,
-                 (uint32_t)m->cfg.vocab_size);
+                 vocab_full(m));
     Scratch sc(m->ctx);
     layer_prefill(m, c, 0, hidden.h(), count, 0, sc);
     sync_context(m->ctx);

@@ -118,6 +118,41 @@ class FusionOptions(ctypes.Structure):
         return cls(0, 0, 0, 0)
 
 
+class TpShard(ctypes.Structure):
+    """mi_tp_shard_info: one tensor-parallel rank's slice of a config."""
+    _fields_ = [(n, ctypes.c_size_t) for n in ("q_heads", "kv_heads", "intermediate", "vocab",
+                                                "q_head0", "kv_head0", "inter0", "vocab0")]
+
+
+def tp_shard(config: dict, tp: int, rank: int) -> dict:
+    """This rank's shard of `config` (host only, no GPU needed)."""
+    c = Qwen3Config.from_dict(config)
+    out = TpShard()
+    _check(lib().mi_tp_shard(ctypes.byref(c), ctypes.c_int(tp), ctypes.c_int(rank),
+                             ctypes.byref(out)))
+    return {n: getattr(out, n) for n, _ in TpShard._fields_}
+
+
+def nccl_unique_id() -> bytes:
+    """A fresh NCCL unique id (rank 0 creates it and shares it)."""
+    buf = (ctypes.c_uint8 * 128)()
+    _check(lib().mi_nccl_unique_id(buf, ctypes.c_size_t(128)))
+    return bytes(buf)
+
+
+def share_nccl_id(group=None) -> bytes:
+    """Rank 0's NCCL id broadcast over an initialized torch.distributed group
+    (any backend; gloo works on CPU)."""
+    import torch
+    import torch.distributed as dist
+    rank = dist.get_rank(group)
+    t = torch.zeros(128, dtype=torch.uint8)
+    if rank == 0:
+        t.copy_(torch.frombuffer(bytearray(nccl_unique_id()), dtype=torch.uint8))
+    dist.broadcast(t, src=0, group=group)
+    return bytes(t.tolist())
+
+
 class GenerationOptions(ctypes.Structure):
     _fields_ = [("max_tokens", ctypes.c_size_t), ("temperature", ctypes.c_float),
                 ("top_p", ctypes.c_float), ("top_k", ctypes.c_size_t),
@@ -161,7 +196,8 @@ EXPORTS = [
     "mi_qwen3_config_validate", "mi_qwen3_create_random", "mi_qwen3_load", "mi_qwen3_destroy",
     "mi_qwen3_get_config", "mi_qwen3_set_attention_kind", "mi_qwen3_set_fusion_options",
     "mi_qwen3_fusion_options", "mi_qwen3_set_decode_graphs",
-    "mi_qwen3_set_decode_persistent", "mi_qwen3_decode_persistent", "mi_kv_cache_create",
+    "mi_qwen3_set_decode_persistent", "mi_qwen3_decode_persistent",
+    "mi_tp_shard", "mi_nccl_unique_id", "mi_qwen3_create_random_tp", "mi_kv_cache_create",
     "mi_kv_cache_destroy", "mi_kv_cache_len", "mi_kv_cache_capacity", "mi_kv_cache_reset",
     "mi_kv_cache_layer", "mi_qwen3_prefill", "mi_qwen3_decode", "mi_qwen3_prefill_argmax",
     "mi_qwen3_decode_argmax", "mi_qwen3_decode_steps", "mi_kv_cache_tokens",
@@ -638,6 +674,19 @@ class Qwen3Model:
         h = _vp()
         _check(lib().mi_qwen3_create_random(context.handle, ctypes.byref(c), ctypes.c_uint64(seed),
                                             ctypes.c_double(std), ctypes.byref(h)))
+        return cls(h, context)
+
+    @classmethod
+    def random_tp(cls, context: MetalContext, config: dict, seed: int, tp: int, rank: int,
+                  nccl_id: bytes, std: float = 0.02):
+        """This rank's shard of the random-init model (collective over the tp ranks)."""
+        c = Qwen3Config.from_dict(config)
+        h = _vp()
+        ident = (ctypes.c_uint8 * 128).from_buffer_copy(nccl_id[:128])
+        _check(lib().mi_qwen3_create_random_tp(context.handle, ctypes.byref(c),
+                                               ctypes.c_uint64(seed), ctypes.c_double(std),
+                                               ctypes.c_int(tp), ctypes.c_int(rank), ident,
+                                               ctypes.byref(h)))
         return cls(h, context)
 
     @classmethod

@@ -741,6 +741,7 @@ struct or_qwen3 {
   size_t decode_block = 64;
   bool fuse_qk_rope_cache = true;
   bool fuse_add_rms_norm = true;
+  size_t tp = 1;  // tensor-parallel ranks whose arithmetic the row-parallel products follow
 };
 
 namespace {
@@ -754,6 +755,34 @@ std::vector<uint16_t> random_matrix(uint64_t seed, int layer, int role, size_t c
 }
 
 std::vector<uint16_t> ones(size_t n) { return std::vector<uint16_t>(n, 0x3c00); }
+
+// Row-parallel product of tensor parallelism over `tp` ranks: rank t owns
+// input columns [t k / tp, (t + 1) k / tp) and produces the canonical DOT
+// over its slice in FP32; the partials are summed in rank order and the sum
+// is rounded once to FP16. tp = 1 is or_matmul.
+void row_parallel_matmul(const uint16_t* x, size_t m, size_t k, const uint16_t* w, size_t n,
+                         size_t tp, uint16_t* out) {
+  if (tp <= 1) {
+    or_matmul(x, m, k, w, n, out);
+    return;
+  }
+  const size_t ks = k / tp;
+  std::vector<float> xf(m * k);
+  widen(x, xf.data(), m * k);
+#pragma omp parallel for schedule(static)
+  for (long long row = 0; row < static_cast<long long>(n); ++row) {
+    std::vector<float> wf(k);
+    widen(w + static_cast<size_t>(row) * k, wf.data(), k);
+    for (size_t r = 0; r < m; ++r) {
+      float acc = 0.f;
+      for (size_t t = 0; t < tp; ++t) {
+        const float part = dot_canon(xf.data() + r * k + t * ks, wf.data() + t * ks, ks);
+        acc = t == 0 ? part : acc + part;
+      }
+      out[r * n + static_cast<size_t>(row)] = h(acc);
+    }
+  }
+}
 
 // One transformer layer on hidden [T, h] (qwen3.rs:647-796), fusion options
 // RECOMMENDED (= ALL) unless changed.
@@ -804,7 +833,7 @@ void layer_forward(or_qwen3* m, or_qwen3::Layer& L, std::vector<uint16_t>& hidde
     attention_prefill(query.data(), L.key_cache.data(), L.value_cache.data(), T, qh, kvh, hd,
                       active, 1, offset, T >= 32, attn.data());
   std::vector<uint16_t> attn_o(T * hs);
-  or_matmul(attn.data(), T, qw, L.w[kO].data(), hs, attn_o.data());
+  row_parallel_matmul(attn.data(), T, qw, L.w[kO].data(), hs, m->tp, attn_o.data());
   std::vector<uint16_t> residual(T * hs);
   if (m->fuse_add_rms_norm) {
     or_add_rms_norm(hidden.data(), attn_o.data(), T, hs, L.w[kPostNorm].data(), eps,
@@ -822,7 +851,7 @@ void layer_forward(or_qwen3* m, or_qwen3::Layer& L, std::vector<uint16_t>& hidde
   }
   or_swiglu(gate.data(), up.data(), T * I, act.data());
   std::vector<uint16_t> down(T * hs);
-  or_matmul(act.data(), T, I, L.w[kDown].data(), hs, down.data());
+  row_parallel_matmul(act.data(), T, I, L.w[kDown].data(), hs, m->tp, down.data());
   or_add(residual.data(), down.data(), T * hs, hidden.data());
 }
 
@@ -869,6 +898,8 @@ void or_qwen3_set_fusion(or_qwen3* m, int qk_rope_cache, int add_rms_norm) {
   m->fuse_qk_rope_cache = qk_rope_cache != 0;
   m->fuse_add_rms_norm = add_rms_norm != 0;
 }
+
+void or_qwen3_set_tp(or_qwen3* m, size_t tp) { m->tp = tp ? tp : 1; }
 
 void or_qwen3_reset(or_qwen3* m) { m->filled = 0; }
 

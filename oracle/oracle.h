@@ -139,6 +139,11 @@ or_qwen3* or_qwen3_create_random(const or_qwen3_config* cfg, uint64_t seed,
 void or_qwen3_destroy(or_qwen3* m);
 /* FusionOptions flags that change rounding (qwen3.rs:42-66). */
 void or_qwen3_set_fusion(or_qwen3* m, int qk_rope_cache, int add_rms_norm);
+/* Tensor-parallel arithmetic of the engine's TP path (no counterpart in the
+ * reference, which runs on one GPU): the O and down products become the sum,
+ * in rank order, of each rank's canonical DOT over its 1/tp slice of the
+ * input columns, rounded once to FP16. Everything else is unchanged. */
+void or_qwen3_set_tp(or_qwen3* m, size_t tp);
 void or_qwen3_reset(or_qwen3* m);
 size_t or_qwen3_len(const or_qwen3* m);
 /* Embeds tokens and runs the model; logits of the last row (half[vocab]).

@@ -59,6 +59,7 @@ def lib():
                                              ctypes.c_double, _sz]
         L.or_qwen3_destroy.argtypes = [ctypes.c_void_p]
         L.or_qwen3_set_fusion.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int]
+        L.or_qwen3_set_tp.argtypes = [ctypes.c_void_p, ctypes.c_size_t]
         L.or_qwen3_reset.argtypes = [ctypes.c_void_p]
         L.or_qwen3_len.argtypes = [ctypes.c_void_p]
         L.or_qwen3_len.restype = _sz
@@ -325,6 +326,10 @@ class Qwen3:
 
     def set_fusion(self, qk_rope_cache: bool = True, add_rms_norm: bool = True):
         lib().or_qwen3_set_fusion(self.h, int(qk_rope_cache), int(add_rms_norm))
+
+    def set_tp(self, tp: int) -> None:
+        """Follow the arithmetic of `tp` tensor-parallel ranks (O and down)."""
+        lib().or_qwen3_set_tp(self.h, tp)
 
     def reset(self):
         lib().or_qwen3_reset(self.h)

@@ -1,0 +1,94 @@
+"""Tensor parallelism on 2 GPUs against the oracle's TP arithmetic
+(bit-exact logits, caches' ids). Skipped on hosts with fewer than 2 GPUs.
+
+Each rank is its own process (spawned), owns one GPU and one context, and
+joins the NCCL communicator whose id rank 0 shares over a gloo group.
+"""
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as tmp
+
+import metal_infer as mi
+import oracle as O
+from conftest import INPUT_STREAM
+
+pytestmark = pytest.mark.gpu
+
+TP = 2
+
+
+def small_cfg():
+    cfg = dict(mi.QWEN3_0_6B)
+    cfg.update(num_hidden_layers=2, vocab_size=4096)
+    return cfg
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank_main(rank, port, cfg, prompt, steps, out):
+    import torch.distributed as dist
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                            world_size=TP)
+    try:
+        ident = mi.share_nccl_id()
+        ctx = mi.MetalContext(rank)
+        model = mi.Qwen3Model.random_tp(ctx, cfg, seed=11, tp=TP, rank=rank, nccl_id=ident)
+        res = {}
+        cache = model.kv_cache(128)
+        res["prefill"] = model.prefill(prompt, cache).f16_bits().ravel()
+        res["decode"] = [model.decode(int(t), cache).f16_bits().ravel() for t in (7, 900)]
+        for graphs in (True, False):
+            model.set_decode_graphs(graphs)
+            res[f"ids_{graphs}"] = model.generate(prompt, steps, model.kv_cache(128))
+        res["config"] = model.config()
+        out.put((rank, res))
+        del model, cache
+        ctx.synchronize()
+    except Exception as e:  # report instead of hanging the peer
+        out.put((rank, {"error": repr(e)}))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < TP, reason="needs 2 GPUs")
+def test_tp2_matches_oracle_tp_arithmetic():
+    cfg = small_cfg()
+    prompt = O.gen_tokens(11, INPUT_STREAM, 20, cfg["vocab_size"])
+    steps = 16
+    ctx = tmp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_main, args=(r, port, cfg, prompt, steps, q))
+             for r in range(TP)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(TP):
+        rank, r = q.get(timeout=300)
+        res[rank] = r
+    for p in procs:
+        p.join(timeout=120)
+    for r in range(TP):
+        assert "error" not in res[r], res[r]["error"]
+    ref = O.Qwen3(cfg, seed=11, capacity=128)
+    ref.set_tp(TP)
+    want_prefill = ref.forward(prompt)
+    want_decode = [ref.forward(np.array([t], np.uint32)) for t in (7, 900)]
+    ref_ids = O.Qwen3(cfg, seed=11, capacity=128)
+    ref_ids.set_tp(TP)
+    want_ids = ref_ids.generate_greedy(prompt, steps)
+    for r in range(TP):
+        got = res[r]
+        assert got["config"]["num_attention_heads"] == cfg["num_attention_heads"]
+        np.testing.assert_array_equal(got["prefill"], want_prefill)
+        for a, b in zip(got["decode"], want_decode):
+            np.testing.assert_array_equal(a, b)
+        np.testing.assert_array_equal(got["ids_True"], want_ids)
+        np.testing.assert_array_equal(got["ids_False"], want_ids)
