@@ -385,8 +385,80 @@ def run_reference(args, rank):
     print(json.dumps(line), flush=True)
 
 
+# ---- tensor-parallel workload (Qwen3-8B) ----------------------------
+CONFIG_8B = dict(hidden_size=4096, intermediate_size=12288, num_hidden_layers=36,
+                 num_attention_heads=32, num_key_value_heads=8, head_dim=128, rms_norm_eps=1e-6,
+                 rope_theta=1e6, vocab_size=151936, tie_word_embeddings=0)
+
+
+def run_tp(args, rank, world, local_rank):
+    """Qwen3-8B (config 3 shapes) sharded over the torchrun ranks: a
+    2048-token prompt, then `--decode-steps` greedy steps (capacity 4096).
+    value = decode tokens/s of the one sequence (all ranks serve it; max over
+    ranks of the device time)."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+    import metal_infer as mi
+    import oracle as O
+
+    torch.cuda.set_device(local_rank)
+    if world > 1:
+        dist.init_process_group("gloo", timeout=timedelta(seconds=300))
+        ident = mi.share_nccl_id()
+    else:
+        ident = bytes(128)  # one GPU: no communicator (tp = 1 is the plain model)
+    ctx = mi.MetalContext(local_rank)
+    model = mi.Qwen3Model.random_tp(ctx, CONFIG_8B, seed=3, tp=world, rank=rank, nccl_id=ident)
+    prompt = O.gen_tokens(3, INPUT_STREAM, 2048, CONFIG_8B["vocab_size"])
+    stream = torch.cuda.ExternalStream(ctx.stream())
+    decode = args.decode_steps if args.decode_steps != DECODE else 512
+    times = []
+    for i in range(args.warmup + args.steps):
+        cache = model.kv_cache(4096)
+        slot = ctx.empty([1], mi.DType.U32)
+        e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+        e0.record(stream)
+        model.prefill_argmax(prompt, cache, slot)
+        e1.record(stream)
+        model.decode_steps(cache, decode)
+        e2.record(stream)
+        e2.synchronize()
+        if i >= args.warmup:
+            times.append((e0.elapsed_time(e1), e1.elapsed_time(e2)))
+        del cache
+    prefill_ms = sum(t[0] for t in times)
+    decode_ms = sum(t[1] for t in times)
+    if world > 1:
+        t = torch.tensor([prefill_ms, decode_ms], dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        prefill_ms, decode_ms = t.tolist()
+    if rank == 0:
+        print(json.dumps({
+            "metric": "decode tokens/s (batch 1, greedy)", "impl": "ours",
+            "value": round(decode * args.steps / (decode_ms / 1e3), 2), "unit": "tokens/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round((prefill_ms + decode_ms) / args.steps, 3),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f16",
+            "data": "synthetic (random-init FP16 N(0,0.02) weights, uniform prompt ids)",
+            "config": {"workload": f"Qwen3-8B tensor-parallel TP{world}: 2048-token prompt + "
+                                   f"{decode} decode steps (BASELINE config 3)",
+                       "parallelism": f"tp{world}", "kv_capacity": 4096},
+            "prefill_tokens_per_s": round(2048 * args.steps / (prefill_ms / 1e3), 1),
+            "decode_path": "persistent kernel" if model.decode_persistent()
+                           else "per-kernel chain + NCCL all-gathers"}), flush=True)
+    del model
+    ctx.synchronize()
+    if world > 1:
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
+    ap.add_argument("--workload", choices=["0.6b", "8b-tp"], default="0.6b",
+                    help="0.6b: the headline config (replicas over GPUs); 8b-tp: Qwen3-8B "
+                         "sharded over the GPUs")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
@@ -407,6 +479,9 @@ def main():
         return
     if args.warmup < 3:
         args.warmup = 3
+    if args.workload == "8b-tp":
+        run_tp(args, rank, world, local_rank)
+        return
     run_ours(args, rank, world, local_rank)
 
 

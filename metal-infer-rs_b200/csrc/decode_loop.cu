@@ -275,11 +275,6 @@ __device__ __forceinline__ void st_relaxed_v4(uint32_t* p, uint4 v) {
                "r"(v.z), "r"(v.w)
                : "memory");
 }
-__device__ __forceinline__ unsigned long long ld_relaxed_u64(const unsigned long long* p) {
-  unsigned long long v;
-  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-  return v;
-}
 __device__ __forceinline__ void st_relaxed_u64(unsigned long long* p, unsigned long long v) {
   asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
@@ -361,6 +356,75 @@ __device__ __forceinline__ void put8(uint32_t* dst, int c, const uint4& v, uint3
                                              tag | (v.w & 0xFFFFu), tag | (v.w >> 16)));
 }
 
+// ---- tensor-parallel exchange through peer memory ------------------------------------
+// Partials are pushed with plain stores into every rank's mailbox (NVLink
+// peer mappings); readers poll their own mailbox. System-scope relaxed
+// accesses: the tags validate every word, the counters only say when to look.
+__device__ __forceinline__ void st_sys_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_sys_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void red_sys_add_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("red.relaxed.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+// This rank's FP32 partial of row `item` into region `region` of every rank.
+__device__ __forceinline__ void push_partial(const DecodeLoop& p, size_t region, int item,
+                                             float v, uint32_t tag) {
+  const unsigned long long w = ((unsigned long long)tag << 32) | __float_as_uint(v);
+  for (int r = 0; r < p.tp; ++r) st_sys_u64(p.peers[r] + region + (size_t)p.rank * p.hidden + item, w);
+}
+
+// Count this CTA into mailbox counter k (0 O, 1 DOWN, 2 LM) of every rank.
+__device__ __forceinline__ void push_count(const DecodeLoop& p, int k) {
+  const MailboxLayout mb = mailbox_layout(p.tp, p.hidden, gridDim.x);
+  for (int r = 0; r < p.tp; ++r) red_sys_add_u64(p.peers[r] + mb.ctr + 16 * k, 1ull);
+}
+
+// Single thread: wait until this rank's mailbox counter k reaches target.
+__device__ bool wait_mbox(const DecodeLoop& p, int k, unsigned long long target, Shared& sh) {
+  const MailboxLayout mb = mailbox_layout(p.tp, p.hidden, gridDim.x);
+  PollClock clock;
+  while (ld_sys_u64(p.mbox + mb.ctr + 16 * k) < target)
+    if (!clock.keep_going(p, sh)) return false;
+  return true;
+}
+
+// Chunk c (8 values) of the ranks' partials in region `region`, summed in
+// rank order in FP32 and rounded once to FP16 (the row-parallel result).
+__device__ uint4 take_partials8(const DecodeLoop& p, size_t region, int c, uint32_t tag,
+                                Shared& sh) {
+  float acc[8];
+  for (int r = 0; r < p.tp; ++r) {
+    const unsigned long long* q = p.mbox + region + (size_t)r * p.hidden + 8 * c;
+    unsigned long long w[8];
+    PollClock clock;
+    while (true) {
+      bool ok = true;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        w[e] = ld_sys_u64(q + e);
+        ok &= (uint32_t)(w[e] >> 32) == tag;
+      }
+      if (ok || !clock.keep_going(p, sh)) break;
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float v = __uint_as_float((uint32_t)w[e]);
+      acc[e] = r == 0 ? v : __fadd_rn(acc[e], v);
+    }
+  }
+  uint4 out;
+  __half2* ho = reinterpret_cast<__half2*>(&out);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) ho[i] = __floats2half2_rn(acc[2 * i], acc[2 * i + 1]);
+  return out;
+}
+
 // Single-thread bounded wait until *ctr >= target (cumulative counters of
 // the per-head dataflow); false when the kernel is aborting.
 __device__ bool wait_counter(const DecodeLoop& p, const uint32_t* ctr, uint32_t target,
@@ -412,7 +476,10 @@ __device__ __forceinline__ void stage_done(const DecodeLoop& p, int st) {
   consumers_sync();
   if (threadIdx.x == 0) {
     MI_TRACE_ARRIVE(0);
-    red_relaxed_add(p.sync + kStageDone + st, 1u);
+    if (p.tp > 1 && (st == kO || st == kDown))
+      push_count(p, st == kO ? 0 : 1);
+    else
+      red_relaxed_add(p.sync + kStageDone + st, 1u);
   }
 }
 
@@ -549,6 +616,9 @@ struct StageIn {
   uint32_t xtag;
   const uint32_t* x2;
   uint32_t x2tag;
+  long long x2_part;  // >= 0: x2 is the ranks' summed partials in this mailbox region
+  int mb_wait;        // >= 0: first wait until mailbox counter mb_wait reaches mb_target
+  unsigned long long mb_target;
   const __half* embed;  // kEmbedNormIn: table row, null for an out-of-range token
   const __half* norm_w;
   uint32_t* wb;
@@ -644,8 +714,11 @@ __device__ bool build_input(const DecodeLoop& p, const StageIn& in, int wait_st,
   const bool two = in.mode == kAddNormIn || in.mode == kAddThenNormIn;
   const bool norm = in.mode != kPlainIn;
   const uint4* g4 = reinterpret_cast<const uint4*>(in.norm_w);
-  if (tid == 0 && wait_st >= 0) {
-    stage_ready(p, wait_st, wait_n, sh);
+  if (tid == 0) {
+    if (in.mb_wait >= 0)
+      wait_mbox(p, in.mb_wait, in.mb_target, sh);
+    else if (wait_st >= 0)
+      stage_ready(p, wait_st, wait_n, sh);
     MI_TRACE_ARRIVE(1);
   }
   consumers_sync();
@@ -653,7 +726,14 @@ __device__ bool build_input(const DecodeLoop& p, const StageIn& in, int wait_st,
   if (norm && tid < kc) g_first = __ldg(g4 + tid);
   for (int c = tid; c < kc; c += kConsumers) {
     uint4 v;
-    if (two) {
+    if (two && in.x2_part >= 0) {
+      const Raw8 ra = raw8(in.x, c);
+      const uint4 b = take_partials8(p, (size_t)in.x2_part, c, in.x2tag, sh);
+      const uint4 a = take8_from(p, ra, in.x, c, in.xtag, sh);
+      xs[c] = a;
+      xs2[c] = b;
+      v = add_chunk(in.mode, a, b);
+    } else if (two) {
       const Raw8 ra = raw8(in.x, c), rb = raw8(in.x2, c);
       const uint4 a = take8_from(p, ra, in.x, c, in.xtag, sh);
       const uint4 b = take8_from(p, rb, in.x2, c, in.x2tag, sh);
@@ -693,14 +773,24 @@ __device__ __forceinline__ void put_item(const DecodeLoop& p, const StageW& s, i
   if (ST == kQKV) {
     put1(p.t_qkv, item, __float2half_rn(a0), tag);
   } else if (ST == kO) {
-    put1(p.t_attn_o, item, __float2half_rn(a0), tag);
+    if (p.tp > 1) {
+      const MailboxLayout mb = mailbox_layout(p.tp, p.hidden, gridDim.x);
+      push_partial(p, mb.o, item, a0, tag);
+    } else {
+      put1(p.t_attn_o, item, __float2half_rn(a0), tag);
+    }
   } else if (ST == kGU) {
     const float gv = __half2float(__float2half_rn(a0));
     const float uv = __half2float(__float2half_rn(a1));
     put1(p.t_act, item, __float2half_rn(silu_mul(gv, uv)), tag);
   } else if (ST == kDown) {
-    const int local = item - res_first;
-    put1(p.t_hidden, item, __hadd(res[local], __float2half_rn(a0)), tag);
+    if (p.tp > 1) {
+      const MailboxLayout mb = mailbox_layout(p.tp, p.hidden, gridDim.x);
+      push_partial(p, mb.d, item, a0, tag);
+    } else {
+      const int local = item - res_first;
+      put1(p.t_hidden, item, __hadd(res[local], __float2half_rn(a0)), tag);
+    }
   } else {
     const __half h0 = __float2half_rn(a0);
     p.logits[item] = h0;
@@ -1171,7 +1261,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_loop_kernel(DecodeLoop par
       const LoopLayer& L = lay[layer];
       const uint32_t ls = (uint32_t)(step * p.layers + layer);  // layer-step of this launch
       const uint32_t e = p.epoch0 + ls;                             // its tag epoch
-      const uint32_t hidden_in = layer == 0 ? tagv(e, 0) : tagv(e - 1u, 1);
+      // hidden stream read by GU: under tensor parallelism every QKV stage
+      // writes it back (it is assembled from the ranks' down partials there)
+      const uint32_t hidden_in = (layer == 0 || p.tp > 1) ? tagv(e, 0) : tagv(e - 1u, 1);
+      const unsigned long long per_ls = (unsigned long long)p.tp * grid;  // mailbox counts
       uint32_t bk = 0, bi = 0xFFFFFFFFu;
       // QKV (layer 0: the embedding row, written back as the hidden stream)
       {
@@ -1180,12 +1273,25 @@ __global__ void __launch_bounds__(kThreads, 1) decode_loop_kernel(DecodeLoop par
           attention_prefetch<G>(p, L, pos, asm_);
         const StageW s = stage_weights(p, lay, layer, kQKV);
         StageIn in = {};
+        in.x2_part = -1;
+        in.mb_wait = -1;
         in.k = p.hidden;
         in.norm_w = L.in_norm;
         if (layer == 0) {
-          const bool zero = token == 0xFFFFFFFFu || token >= (uint32_t)p.vocab;
+          const bool zero = token == 0xFFFFFFFFu || token >= p.vocab_full;
           in.mode = kEmbedNormIn;
           in.embed = zero ? nullptr : p.embedding + (size_t)token * p.hidden;
+          in.wb = p.t_hidden;
+          in.wbtag = tagv(e, 0);
+        } else if (p.tp > 1) {
+          // hidden = residual + half(sum of the ranks' down partials)
+          in.mode = kAddThenNormIn;
+          in.x = p.t_res;
+          in.xtag = tagv(e - 1u, 0);
+          in.x2_part = (long long)mailbox_layout(p.tp, p.hidden, grid).d;
+          in.x2tag = tagv(e - 1u, 1);  // as the DOWN stage tagged its partials
+          in.mb_wait = 1;
+          in.mb_target = p.ctr_base[1] + (unsigned long long)ls * per_ls;
           in.wb = p.t_hidden;
           in.wbtag = tagv(e, 0);
         } else {
@@ -1227,12 +1333,21 @@ __global__ void __launch_bounds__(kThreads, 1) decode_loop_kernel(DecodeLoop par
         if (tid == 0) { MI_TRACE(step, layer * 5 + 3, 0); MI_TRACE_SET(step, layer * 5 + 3); }
         const StageW s = stage_weights(p, lay, layer, kGU);
         StageIn in = {};
+        in.x2_part = -1;
+        in.mb_wait = -1;
         in.mode = p.add_norm ? kAddNormIn : kAddThenNormIn;
         in.k = p.hidden;
         in.x = p.t_hidden;
         in.xtag = hidden_in;
         in.x2 = p.t_attn_o;
         in.x2tag = tagv(e, 0);
+        if (p.tp > 1) {
+          // attention output = half(sum of the ranks' O partials)
+          in.x2_part = (long long)mailbox_layout(p.tp, p.hidden, grid).o;
+          in.x2tag = tagv(e, 0);  // as the O stage tagged its partials
+          in.mb_wait = 0;
+          in.mb_target = p.ctr_base[0] + (unsigned long long)(ls + 1u) * per_ls;
+        }
         in.norm_w = L.post_norm;
         in.wb = p.t_res;
         in.wbtag = tagv(e, 0);
@@ -1247,13 +1362,16 @@ __global__ void __launch_bounds__(kThreads, 1) decode_loop_kernel(DecodeLoop par
         if (tid == 0) { MI_TRACE(step, layer * 5 + 4, 0); MI_TRACE_SET(step, layer * 5 + 4); }
         const StageW s = stage_weights(p, lay, layer, kDown);
         StageIn in = {};
+        in.x2_part = -1;
+        in.mb_wait = -1;
         in.mode = kPlainIn;
         in.k = p.inter;
         in.x = p.t_act;
         in.xtag = tagv(e, 0);
         if (!build_input(p, in, kGU, (ls + 1u) * grid, xs, xs2, sh)) return;
-        {
-          // residuals of this CTA's rows (written back by CTA 0 in GU)
+        if (p.tp == 1) {
+          // residuals of this CTA's rows (written back by CTA 0 in GU); under
+          // tensor parallelism the next QKV stage adds them
           const Tiles& td = sh.tiles[kDown];
           if (tid < td.last - td.first) sh.res[tid] = take1(p, p.t_res, td.first + tid, tagv(e, 0), sh);
           consumers_sync();
@@ -1271,12 +1389,23 @@ __global__ void __launch_bounds__(kThreads, 1) decode_loop_kernel(DecodeLoop par
       uint32_t bk = 0, bi = 0xFFFFFFFFu;
       const StageW s = stage_weights(p, lay, p.layers, kLM);
       StageIn in = {};
+      in.x2_part = -1;
+      in.mb_wait = -1;
       in.mode = kNormIn;
       in.k = p.hidden;
       in.x = p.t_hidden;
       in.xtag = tagv(e, 1);
       in.norm_w = p.final_norm;
       const uint32_t ls_last = (uint32_t)(step * p.layers + p.layers - 1);
+      if (p.tp > 1) {
+        in.mode = kAddThenNormIn;
+        in.x = p.t_res;
+        in.xtag = tagv(e, 0);
+        in.x2_part = (long long)mailbox_layout(p.tp, p.hidden, grid).d;
+        in.x2tag = tagv(e, 1);
+        in.mb_wait = 1;
+        in.mb_target = p.ctr_base[1] + (unsigned long long)(ls_last + 1u) * p.tp * grid;
+      }
       if (!build_input(p, in, kDown, (ls_last + 1u) * grid, xs, xs2, sh)) return;
       if (tid == 0) MI_TRACE(step, p.layers * 5, 1);
       reduce_rows<kLM>(p, s, xs, ring, sh, g, 0u, bk, bi);
@@ -1305,19 +1434,32 @@ __global__ void __launch_bounds__(kThreads, 1) decode_loop_kernel(DecodeLoop par
               ck = sh.best_key[w];
               ci = sh.best_idx[w];
             }
-          const unsigned long long idx = ci == 0xFFFFFFFFu ? 0x3FFFFull : (unsigned long long)ci;
-          st_relaxed_u64(p.t_argmax + blockIdx.x,
-                         ((unsigned long long)ck << 32) | (idx << 14) | rtag);
-          red_relaxed_add(p.sync + kStageDone + kLM, 1u);
-          stage_ready(p, kLM, (uint32_t)(step + 1) * grid, sh);
+          const unsigned long long idx =
+              ci == 0xFFFFFFFFu ? 0x3FFFFull : (unsigned long long)(ci + p.vocab0);
+          const unsigned long long rec = ((unsigned long long)ck << 32) | (idx << 14) | rtag;
+          if (p.tp > 1) {
+            // vocab-parallel: the record goes to every rank's mailbox
+            const MailboxLayout mb = mailbox_layout(p.tp, p.hidden, grid);
+            for (int r = 0; r < p.tp; ++r)
+              st_sys_u64(p.peers[r] + mb.rec + (size_t)p.rank * grid + blockIdx.x, rec);
+            push_count(p, 2);
+            wait_mbox(p, 2, p.ctr_base[2] + (unsigned long long)(step + 1) * p.tp * grid, sh);
+          } else {
+            st_relaxed_u64(p.t_argmax + blockIdx.x, rec);
+            red_relaxed_add(p.sync + kStageDone + kLM, 1u);
+            stage_ready(p, kLM, (uint32_t)(step + 1) * grid, sh);
+          }
         }
         __syncwarp();
         // every CTA reduces all records (argmax order is total: any order)
+        const unsigned long long* recs =
+            p.tp > 1 ? p.mbox + mailbox_layout(p.tp, p.hidden, grid).rec : p.t_argmax;
+        const int nrec = p.tp * (int)gridDim.x;
         uint32_t ck = 0, ci = 0xFFFFFFFFu;
-        for (int b = lane; b < (int)gridDim.x; b += 32) {
-          unsigned long long r = ld_relaxed_u64(p.t_argmax + b);
+        for (int b = lane; b < nrec; b += 32) {
+          unsigned long long r = ld_sys_u64(recs + b);
           PollClock clock;
-          while ((r & 0x3FFFull) != rtag && clock.keep_going(p, sh)) r = ld_relaxed_u64(p.t_argmax + b);
+          while ((r & 0x3FFFull) != rtag && clock.keep_going(p, sh)) r = ld_sys_u64(recs + b);
           const uint32_t k2 = (uint32_t)(r >> 32);
           uint32_t i2 = (uint32_t)((r >> 14) & 0x3FFFFull);
           if (i2 == 0x3FFFFu) i2 = 0xFFFFFFFFu;
@@ -1392,7 +1534,7 @@ bool decode_loop_plan(DecodeLoop& p, int device) {
   if (attn_smem_for(group) == 0 || p.qh % p.kvh) return false;
   if (p.hidden % 8 || p.inter % 8 || p.hidden <= 0 || p.inter <= 0) return false;
   if (p.kvh > kMaxKvHeads) return false;
-  if (p.vocab >= 0x3FFFF) return false;  // argmax records carry an 18-bit index
+  if (p.vocab_full >= 0x3FFFF) return false;  // argmax records carry an 18-bit index
   const int max_k = std::max(std::max(p.hidden, p.inter), p.qh * HD);
   int max_item = std::max(std::max(p.hidden * 4, p.inter * 2), p.qh * HD * 2);
   p.slot_bytes = std::max(kMinSlotBytes, (max_item + 127) / 128 * 128);

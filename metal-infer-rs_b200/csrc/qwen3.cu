@@ -120,6 +120,15 @@ struct mi_qwen3 {
 #ifdef MI_HAVE_NCCL
   ncclComm_t comm = nullptr;
 #endif
+  // Tensor-parallel persistent decode: this rank's mailbox (cudaMalloc, IPC
+  // exported) and every rank's mailbox mapped here (peer[rank] = local).
+  struct Mailbox {
+    void* local = nullptr;
+    std::vector<void*> peer;
+    TensorRef table;  // device array of the tp mailbox pointers
+    int grid = 0;
+    unsigned long long ctr_base[3] = {0, 0, 0};
+  } mbox;
   bool persistent = true;  // decode through the persistent kernel when it fits
   int loop_state = 0;      // 0 unplanned, 1 planned, -1 not admitted
   k::DecodeLoop loop;
@@ -156,6 +165,10 @@ void model_release(mi_qwen3* m) {
   mi_context* ctx = m->ctx;
   cudaSetDevice(ctx->device);
   cudaStreamSynchronize(ctx->stream);
+  for (size_t r = 0; r < m->mbox.peer.size(); ++r)
+    if ((int)r != m->rank && m->mbox.peer[r]) cudaIpcCloseMemHandle(m->mbox.peer[r]);
+  m->mbox.table = TensorRef();
+  if (m->mbox.local) cudaFree(m->mbox.local);
 #ifdef MI_HAVE_NCCL
   if (m->comm) ncclCommDestroy(m->comm);
 #endif
@@ -455,7 +468,8 @@ bool persistent_env() {
 }
 
 bool decode_loop_ready(mi_qwen3* m) {
-  if (m->tp > 1 || !m->persistent || !persistent_env() || !fused_decode_supported(m))
+  if ((m->tp > 1 && !m->mbox.local) || !m->persistent || !persistent_env() ||
+      !fused_decode_supported(m))
     return false;
   if (m->loop_state == 0) {
     const auto& c = m->cfg;
@@ -468,7 +482,9 @@ bool decode_loop_ready(mi_qwen3* m) {
     p.layers = (int)c.num_hidden_layers;
     p.eps = c.rms_norm_eps;
     p.theta = c.rope_theta;
+    p.vocab_full = (uint32_t)m->full_cfg.vocab_size;
     m->loop_state = k::decode_loop_plan(p, m->ctx->device) ? 1 : -1;
+    if (m->tp > 1 && p.grid != m->mbox.grid) m->loop_state = -1;  // mailbox sized for another grid
     m->loop = p;
   }
   return m->loop_state == 1;
@@ -539,12 +555,24 @@ void run_decode_loop(mi_qwen3* m, mi_kv_cache* c, size_t steps) {
     w.loop_part = TensorRef(new_tensor(ctx, {part}, MI_F32, false));
   p.attn_part = w.loop_part.t->f32();
   p.sync = w.loop_sync.t->u32();
+  p.tp = m->tp;
+  p.rank = m->rank;
+  p.vocab0 = (uint32_t)(m->rank * m->cfg.vocab_size);
+  if (m->tp > 1) {
+    p.peers = reinterpret_cast<unsigned long long* const*>(m->mbox.table.t->base());
+    p.mbox = static_cast<unsigned long long*>(m->mbox.local);
+  }
   for (size_t done = 0; done < steps;) {
     p.steps = (int)std::min<size_t>(steps - done, 2048);
     p.epoch0 = (uint32_t)w.loop_epoch;
+    for (int i = 0; i < 3; ++i) p.ctr_base[i] = m->mbox.ctr_base[i];
     ProfileScope ps(ctx, "decode_loop");
     k::decode_loop(ctx->stream, p);
     w.loop_epoch += (uint64_t)p.steps * (uint64_t)p.layers;
+    const unsigned long long per_step = (unsigned long long)m->tp * p.grid;
+    m->mbox.ctr_base[0] += per_step * p.steps * p.layers;
+    m->mbox.ctr_base[1] += per_step * p.steps * p.layers;
+    m->mbox.ctr_base[2] += per_step * p.steps;
     done += (size_t)p.steps;
   }
 }
@@ -864,6 +892,48 @@ mi_status mi_nccl_unique_id(uint8_t* out, size_t len) {
 
 namespace {
 
+// Persistent tensor-parallel decode: allocate this rank's mailbox, export it
+// (CUDA IPC), gather every rank's handle over NCCL and map the peers'
+// mailboxes here. The mailbox starts zeroed (no tag matches zero).
+void setup_mailbox(mi_qwen3* m) {
+#ifdef MI_HAVE_NCCL
+  mi_context* ctx = m->ctx;
+  auto& mb = m->mbox;
+  mb.grid = std::min(ctx->sm_count, 256);
+  const k::MailboxLayout lay =
+      k::mailbox_layout(m->tp, (int)m->full_cfg.hidden_size, mb.grid);
+  const size_t bytes = lay.words * 8;
+  MI_CUDA(cudaMalloc(&mb.local, bytes));
+  MI_CUDA(cudaMemset(mb.local, 0, bytes));
+  cudaIpcMemHandle_t mine;
+  MI_CUDA(cudaIpcGetMemHandle(&mine, mb.local));
+  TensorRef dev_mine(new_tensor(ctx, {sizeof mine}, MI_F16, false));  // byte carrier
+  TensorRef dev_all(new_tensor(ctx, {sizeof mine * (size_t)m->tp}, MI_F16, false));
+  MI_CUDA(cudaMemcpy(dev_mine.t->base(), &mine, sizeof mine, cudaMemcpyHostToDevice));
+  ncclResult_t r = ncclAllGather(dev_mine.t->base(), dev_all.t->base(), sizeof mine, ncclUint8,
+                                 m->comm, ctx->stream);
+  if (r != ncclSuccess)
+    fail(MI_ERR_COLLECTIVE, "NCCL all-gather of IPC handles: %s", ncclGetErrorString(r));
+  std::vector<cudaIpcMemHandle_t> all(m->tp);
+  MI_CUDA(cudaMemcpyAsync(all.data(), dev_all.t->base(), sizeof mine * m->tp,
+                          cudaMemcpyDeviceToHost, ctx->stream));
+  MI_CUDA(cudaStreamSynchronize(ctx->stream));
+  mb.peer.assign(m->tp, nullptr);
+  for (int q = 0; q < m->tp; ++q) {
+    if (q == m->rank) {
+      mb.peer[q] = mb.local;
+      continue;
+    }
+    MI_CUDA(cudaIpcOpenMemHandle(&mb.peer[q], all[q], cudaIpcMemLazyEnablePeerAccess));
+  }
+  mb.table = TensorRef(new_tensor(ctx, {(size_t)m->tp * 2}, MI_U32, false));
+  MI_CUDA(cudaMemcpy(mb.table.t->base(), mb.peer.data(), sizeof(void*) * m->tp,
+                     cudaMemcpyHostToDevice));
+#else
+  (void)m;
+#endif
+}
+
 // Seeded random-init model, this rank's shard of it under tensor
 // parallelism (tp ranks): every shard is the corresponding block of the
 // full tensors of the one-GPU model (same generator streams and indices).
@@ -950,6 +1020,7 @@ mi_qwen3* build_random(mi_context* ctx, const mi_qwen3_config& config, uint64_t 
     if (r != ncclSuccess)
       fail(MI_ERR_COLLECTIVE, "ncclCommInitRank (rank %d of %d): %s", rank, tp,
            ncclGetErrorString(r));
+    setup_mailbox(m.get());
 #else
     (void)nccl_id;
     fail(MI_ERR_UNSUPPORTED, "built without NCCL: tensor parallelism is unavailable");

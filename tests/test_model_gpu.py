@@ -181,6 +181,29 @@ def test_decode_paths_bit_identical(small, capacity, prompt_len):
     np.testing.assert_array_equal(outs["persistent"][0], ref_ids)
 
 
+def test_decode_paths_bit_identical_8b_shapes(ctx):
+    """Qwen3-8B layer shapes (hidden 4096, intermediate 12288, 32/8 heads):
+    persistent kernel vs kernel chain vs the oracle."""
+    cfg = dict(mi.QWEN3_8B)
+    cfg.update(num_hidden_layers=2, vocab_size=4096)
+    model = mi.Qwen3Model.random(ctx, cfg, seed=13)
+    assert model.decode_persistent()
+    prompt = O.gen_tokens(13, INPUT_STREAM, 24, cfg["vocab_size"])
+    outs = {}
+    try:
+        for path in ("persistent", "graph"):
+            set_path(model, path)
+            cache = model.kv_cache(128)
+            ids = model.generate(prompt, 12, cache)
+            outs[path] = (ids, model.decode(int(ids[-1]), cache).f16_bits().ravel())
+    finally:
+        set_path(model, "persistent")
+    for a, b in zip(outs["persistent"], outs["graph"]):
+        np.testing.assert_array_equal(a, b)
+    ref = O.Qwen3(cfg, seed=13, capacity=128)
+    np.testing.assert_array_equal(outs["persistent"][0], ref.generate_greedy(prompt, 12))
+
+
 def test_pipelined_decode_argmax_matches_generate(ctx, small):
     cfg, model, _ = small
     prompt = O.gen_tokens(5, INPUT_STREAM + 4, 24, cfg["vocab_size"])

@@ -1,5 +1,7 @@
 """Tensor parallelism on 2 GPUs against the oracle's TP arithmetic
-(bit-exact logits, caches' ids). Skipped on hosts with fewer than 2 GPUs.
+(bit-exact logits and greedy ids through the persistent kernel, which
+exchanges partials through peer memory, and through the NCCL kernel chain).
+Skipped on hosts with fewer than 2 GPUs.
 
 Each rank is its own process (spawned), owns one GPU and one context, and
 joins the NCCL communicator whose id rank 0 shares over a gloo group.
@@ -44,10 +46,13 @@ def _rank_main(rank, port, cfg, prompt, steps, out):
         cache = model.kv_cache(128)
         res["prefill"] = model.prefill(prompt, cache).f16_bits().ravel()
         res["decode"] = [model.decode(int(t), cache).f16_bits().ravel() for t in (7, 900)]
-        for graphs in (True, False):
-            model.set_decode_graphs(graphs)
-            res[f"ids_{graphs}"] = model.generate(prompt, steps, model.kv_cache(128))
+        res["persistent"] = model.decode_persistent()
+        for path in ("persistent", "graph", "eager"):
+            model.set_decode_persistent(path == "persistent")
+            model.set_decode_graphs(path != "eager")
+            res[f"ids_{path}"] = model.generate(prompt, steps, model.kv_cache(128))
         res["config"] = model.config()
+        res["status"] = ctx.kernel_status()
         out.put((rank, res))
         del model, cache
         ctx.synchronize()
@@ -90,5 +95,7 @@ def test_tp2_matches_oracle_tp_arithmetic():
         np.testing.assert_array_equal(got["prefill"], want_prefill)
         for a, b in zip(got["decode"], want_decode):
             np.testing.assert_array_equal(a, b)
-        np.testing.assert_array_equal(got["ids_True"], want_ids)
-        np.testing.assert_array_equal(got["ids_False"], want_ids)
+        assert got["status"] == 0
+        assert got["persistent"]  # decode runs in the persistent kernel with peer exchange
+        for path in ("persistent", "graph", "eager"):
+            np.testing.assert_array_equal(got[f"ids_{path}"], want_ids, err_msg=path)
