@@ -362,9 +362,19 @@ mi_status mi_nccl_unique_id(uint8_t* out, size_t len);
 mi_status mi_qwen3_create_random_tp(mi_context* ctx, const mi_qwen3_config* config,
                                     uint64_t seed, double std_dev, int tp, int rank,
                                     const uint8_t* nccl_id, mi_qwen3** out);
-/* Qwen3Model::load from a directory with config.json + *.safetensors
- * (qwen3.rs:155-240, weights.rs:21-75). F16 and BF16 tensors. */
+/* Qwen3Model::load from a directory with config.json + model.safetensors
+ * or the shards named by model.safetensors.index.json (qwen3.rs:155-240,
+ * weights.rs:21-75, config.rs:23-57). F16 tensors are used as stored, BF16
+ * ones converted to FP16 through FP32 with round-to-nearest-even; other
+ * dtypes, model_type other than qwen3 and attention biases return
+ * MI_ERR_UNSUPPORTED, a missing tensor MI_ERR_MISSING_TENSOR, a wrong shape
+ * MI_ERR_CONFIG, unreadable files MI_ERR_IO. Tensor names as the
+ * reference's (model.layers.{i}.self_attn.q_proj.weight, ...). */
 mi_status mi_qwen3_load(mi_context* ctx, const char* directory, mi_qwen3** out);
+/* No counterpart in the reference: mi_qwen3_load reading only this rank's
+ * tensor-parallel shard of every weight (see mi_qwen3_create_random_tp). */
+mi_status mi_qwen3_load_tp(mi_context* ctx, const char* directory, int tp, int rank,
+                           const uint8_t* nccl_id, mi_qwen3** out);
 void mi_qwen3_destroy(mi_qwen3* m);
 mi_status mi_qwen3_get_config(const mi_qwen3* m, mi_qwen3_config* out);
 /* Qwen3Model::set_attention_kind / set_fusion_options (qwen3.rs:330-346) */

@@ -23,6 +23,7 @@
 // cooperative kernel (decode_loop.cu) with the same stages and arithmetic.
 
 #include <cstring>
+#include <functional>
 #include <map>
 #include <memory>
 
@@ -31,6 +32,7 @@
 #endif
 
 #include "kernels.h"
+#include "loader.h"
 #include "mi_internal.h"
 
 using namespace mi;
@@ -934,11 +936,17 @@ void setup_mailbox(mi_qwen3* m) {
 #endif
 }
 
-// Seeded random-init model, this rank's shard of it under tensor
-// parallelism (tp ranks): every shard is the corresponding block of the
-// full tensors of the one-GPU model (same generator streams and indices).
-mi_qwen3* build_random(mi_context* ctx, const mi_qwen3_config& config, uint64_t seed,
-                       double std_dev, int tp, int rank, const uint8_t* nccl_id) {
+// Fills `dst` ([rows, cols] FP16) with the block at (row0, col0) of the full
+// [*, full_cols] weight (layer, role); 1-D norms come as one row.
+using WeightFill = std::function<void(int layer, int role, __half* dst, size_t rows, size_t cols,
+                                      size_t full_cols, size_t row0, size_t col0)>;
+
+// A model, or this rank's shard of it under tensor parallelism (tp ranks):
+// every shard is the corresponding block of the full tensors, taken from
+// `fill`. Embedding and norms are replicated; a tied LM head is a view of
+// the embedding rows of the rank's vocabulary shard.
+mi_qwen3* build_model(mi_context* ctx, const mi_qwen3_config& config, int tp, int rank,
+                      const uint8_t* nccl_id, const WeightFill& fill) {
   validate_config(config);
   mi_tp_shard_info sh{};
   {
@@ -964,24 +972,21 @@ mi_qwen3* build_random(mi_context* ctx, const mi_qwen3_config& config, uint64_t 
   } ctx_guard{m.get()};
   const auto& fc = m->full_cfg;
   const size_t h = fc.hidden_size, hd = fc.head_dim, V = fc.vocab_size;
-  const size_t qw = qwidth(fc), kw = kvwidth(fc), I = fc.intermediate_size;
+  const size_t qw = qwidth(fc), I = fc.intermediate_size;
   const size_t qw_l = qwidth(m->cfg), kw_l = kvwidth(m->cfg), I_l = m->cfg.intermediate_size;
-  cudaStream_t st = ctx->stream;
-  // rows x cols block at (row0, col0) of the full [*, full_cols] tensor
   auto block = [&](int layer, int role, size_t rows, size_t cols, size_t full_cols, size_t row0,
                    size_t col0) {
     TensorRef t(new_tensor(ctx, {rows, cols}, MI_F16));
-    k::fill_normal_f16_block(st, t.h(), rows, cols, full_cols, row0, col0, seed,
-                             (uint64_t)((layer + 1) * 16 + role), std_dev);
+    fill(layer, role, t.h(), rows, cols, full_cols, row0, col0);
     return t;
   };
-  auto ones = [&](size_t n) {
+  auto vec = [&](int layer, int role, size_t n) {
     TensorRef t(new_tensor(ctx, {n}, MI_F16));
-    k::fill_f16(st, t.h(), n, 0x3c00);
+    fill(layer, role, t.h(), 1, n, n, 0, 0);
     return t;
   };
   m->embedding = block(-1, kEmbedding, V, h, h, 0, 0);
-  m->final_norm = ones(h);
+  m->final_norm = vec(-1, kFinalNorm, h);
   if (fc.tie_word_embeddings) {
     if (tp == 1) {
       m->lm_head = m->embedding.t;
@@ -1001,15 +1006,14 @@ mi_qwen3* build_random(mi_context* ctx, const mi_qwen3_config& config, uint64_t 
     L.w[kK] = block(li, kK, kw_l, h, h, sh.kv_head0 * hd, 0);
     L.w[kV] = block(li, kV, kw_l, h, h, sh.kv_head0 * hd, 0);
     L.w[kO] = block(li, kO, h, qw_l, qw, 0, sh.q_head0 * hd);
-    L.w[kQNorm] = ones(hd);
-    L.w[kKNorm] = ones(hd);
+    L.w[kQNorm] = vec(li, kQNorm, hd);
+    L.w[kKNorm] = vec(li, kKNorm, hd);
     L.w[kGate] = block(li, kGate, I_l, h, h, sh.inter0, 0);
     L.w[kUp] = block(li, kUp, I_l, h, h, sh.inter0, 0);
     L.w[kDown] = block(li, kDown, h, I_l, I, 0, sh.inter0);
-    L.w[kInputNorm] = ones(h);
-    L.w[kPostNorm] = ones(h);
+    L.w[kInputNorm] = vec(li, kInputNorm, h);
+    L.w[kPostNorm] = vec(li, kPostNorm, h);
   }
-  (void)kw;
   if (tp > 1) {
 #ifdef MI_HAVE_NCCL
     require(nccl_id, "nccl_id");
@@ -1029,6 +1033,56 @@ mi_qwen3* build_random(mi_context* ctx, const mi_qwen3_config& config, uint64_t 
   sync_context(ctx);
   ctx_guard.m = nullptr;
   return m.release();
+}
+
+// Seeded N(0, std) matrices and unit norm gains (mi_qwen3_create_random).
+WeightFill random_fill(cudaStream_t st, uint64_t seed, double std_dev) {
+  return [=](int layer, int role, __half* dst, size_t rows, size_t cols, size_t full_cols,
+             size_t row0, size_t col0) {
+    if (role == kQNorm || role == kKNorm || role == kInputNorm || role == kPostNorm ||
+        role == kFinalNorm) {
+      k::fill_f16(st, dst, rows * cols, 0x3c00);
+      return;
+    }
+    k::fill_normal_f16_block(st, dst, rows, cols, full_cols, row0, col0, seed,
+                             (uint64_t)((layer + 1) * 16 + role), std_dev);
+  };
+}
+
+// Weights from a safetensors checkpoint (qwen3.rs:155-240): each tensor is
+// checked against the full config's shape, then the shard block is read.
+WeightFill checkpoint_fill(const load::Checkpoint& ck, cudaStream_t st) {
+  const mi_qwen3_config& c = ck.config();
+  const size_t h = c.hidden_size, hd = c.head_dim, V = c.vocab_size, I = c.intermediate_size;
+  const size_t qw = qwidth(c), kw = kvwidth(c);
+  return [&ck, st, h, hd, V, I, qw, kw](int layer, int role, __half* dst, size_t rows,
+                                          size_t cols, size_t, size_t row0, size_t col0) {
+    std::vector<size_t> shape;
+    switch (role) {
+      case kEmbedding: case kLmHead: shape = {V, h}; break;
+      case kQ: shape = {qw, h}; break;
+      case kK: case kV: shape = {kw, h}; break;
+      case kO: shape = {h, qw}; break;
+      case kQNorm: case kKNorm: shape = {hd}; break;
+      case kGate: case kUp: shape = {I, h}; break;
+      case kDown: shape = {h, I}; break;
+      default: shape = {h}; break;
+    }
+    const std::string name = load::weight_name(layer, role);
+    ck.expect(name, shape);
+    ck.read_block(name, rows, cols, row0, col0, dst, st);
+  };
+}
+
+mi_qwen3* build_random(mi_context* ctx, const mi_qwen3_config& config, uint64_t seed,
+                       double std_dev, int tp, int rank, const uint8_t* nccl_id) {
+  return build_model(ctx, config, tp, rank, nccl_id, random_fill(ctx->stream, seed, std_dev));
+}
+
+mi_qwen3* build_loaded(mi_context* ctx, const char* directory, int tp, int rank,
+                       const uint8_t* nccl_id) {
+  auto ck = load::Checkpoint::open(directory);
+  return build_model(ctx, ck->config(), tp, rank, nccl_id, checkpoint_fill(*ck, ctx->stream));
 }
 
 }  // namespace
@@ -1491,7 +1545,17 @@ mi_status mi_qwen3_load(mi_context* ctx, const char* directory, mi_qwen3** out) 
     require(ctx, "ctx");
     require(directory, "directory");
     require(out, "out");
-    fail(MI_ERR_UNSUPPORTED, "unsupported model: safetensors loading is not built yet");
+    *out = build_loaded(ctx, directory, 1, 0, nullptr);
+  });
+}
+
+mi_status mi_qwen3_load_tp(mi_context* ctx, const char* directory, int tp, int rank,
+                           const uint8_t* nccl_id, mi_qwen3** out) {
+  return guard([&] {
+    require(ctx, "ctx");
+    require(directory, "directory");
+    require(out, "out");
+    *out = build_loaded(ctx, directory, tp, rank, nccl_id);
   });
 }
 

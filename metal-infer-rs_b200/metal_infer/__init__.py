@@ -197,7 +197,7 @@ EXPORTS = [
     "mi_qwen3_get_config", "mi_qwen3_set_attention_kind", "mi_qwen3_set_fusion_options",
     "mi_qwen3_fusion_options", "mi_qwen3_set_decode_graphs",
     "mi_qwen3_set_decode_persistent", "mi_qwen3_decode_persistent",
-    "mi_tp_shard", "mi_nccl_unique_id", "mi_qwen3_create_random_tp", "mi_kv_cache_create",
+    "mi_tp_shard", "mi_nccl_unique_id", "mi_qwen3_create_random_tp", "mi_qwen3_load_tp", "mi_kv_cache_create",
     "mi_kv_cache_destroy", "mi_kv_cache_len", "mi_kv_cache_capacity", "mi_kv_cache_reset",
     "mi_kv_cache_layer", "mi_qwen3_prefill", "mi_qwen3_decode", "mi_qwen3_prefill_argmax",
     "mi_qwen3_decode_argmax", "mi_qwen3_decode_steps", "mi_kv_cache_tokens",
@@ -693,6 +693,15 @@ class Qwen3Model:
     def load(cls, directory: str, context: MetalContext):
         h = _vp()
         _check(lib().mi_qwen3_load(context.handle, directory.encode(), ctypes.byref(h)))
+        return cls(h, context)
+
+    @classmethod
+    def load_tp(cls, directory: str, context: MetalContext, tp: int, rank: int, nccl_id: bytes):
+        """This rank's tensor-parallel shard of a safetensors checkpoint."""
+        h = _vp()
+        ident = (ctypes.c_uint8 * 128).from_buffer_copy(nccl_id[:128])
+        _check(lib().mi_qwen3_load_tp(context.handle, directory.encode(), ctypes.c_int(tp),
+                                      ctypes.c_int(rank), ident, ctypes.byref(h)))
         return cls(h, context)
 
     def __del__(self):

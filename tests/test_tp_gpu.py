@@ -34,7 +34,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _rank_main(rank, port, cfg, prompt, steps, out):
+def _rank_main(rank, port, cfg, prompt, steps, out, ckpt=None):
     import torch.distributed as dist
     dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
                             world_size=TP)
@@ -52,6 +52,11 @@ def _rank_main(rank, port, cfg, prompt, steps, out):
             model.set_decode_graphs(path != "eager")
             res[f"ids_{path}"] = model.generate(prompt, steps, model.kv_cache(128))
         res["config"] = model.config()
+        if ckpt:
+            # the same shard read from a checkpoint of the full model
+            loaded = mi.Qwen3Model.load_tp(ckpt, ctx, TP, rank, mi.share_nccl_id())
+            res["loaded_prefill"] = loaded.prefill(prompt, loaded.kv_cache(128)).f16_bits().ravel()
+            del loaded
         res["status"] = ctx.kernel_status()
         out.put((rank, res))
         del model, cache
@@ -63,14 +68,20 @@ def _rank_main(rank, port, cfg, prompt, steps, out):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < TP, reason="needs 2 GPUs")
-def test_tp2_matches_oracle_tp_arithmetic():
+def test_tp2_matches_oracle_tp_arithmetic(tmp_path):
     cfg = small_cfg()
     prompt = O.gen_tokens(11, INPUT_STREAM, 20, cfg["vocab_size"])
     steps = 16
+    # a checkpoint of the full (one-GPU) model for the shard-on-load check
+    import safetensors_io as st
+    from test_loader_gpu import export
+    full = mi.Qwen3Model.random(mi.MetalContext(0), cfg, seed=11)
+    export(full, cfg, str(tmp_path))
+    del full
     ctx = tmp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank_main, args=(r, port, cfg, prompt, steps, q))
+    procs = [ctx.Process(target=_rank_main, args=(r, port, cfg, prompt, steps, q, str(tmp_path)))
              for r in range(TP)]
     for p in procs:
         p.start()
@@ -93,6 +104,7 @@ def test_tp2_matches_oracle_tp_arithmetic():
         got = res[r]
         assert got["config"]["num_attention_heads"] == cfg["num_attention_heads"]
         np.testing.assert_array_equal(got["prefill"], want_prefill)
+        np.testing.assert_array_equal(got["loaded_prefill"], want_prefill)
         for a, b in zip(got["decode"], want_decode):
             np.testing.assert_array_equal(a, b)
         assert got["status"] == 0
