@@ -313,8 +313,8 @@ typedef struct mi_fusion_options {
   int qk_rope_cache;
 } mi_fusion_options;
 
-/* GenerationOptions (qwen3.rs:132-152). Only temperature 0 (greedy) is on
- * the device path; other temperatures return MI_ERR_UNSUPPORTED. */
+/* GenerationOptions (qwen3.rs:132-152). Temperature 0 is greedy; a
+ * temperature > 0 samples on the device (mi_sample_logits). */
 typedef struct mi_generation_options {
   size_t max_tokens;
   float temperature;
@@ -324,6 +324,20 @@ typedef struct mi_generation_options {
   const uint32_t* stop_token_ids;
   size_t stop_token_count;
 } mi_generation_options;
+
+/* sample_token (qwen3.rs:909-925) / sample_token_f16 + sample_candidates
+ * (qwen3.rs:927-1005) on the device: one token from FP16 logits ([n] or
+ * [1, n]) under temperature / top_p / top_k as GenerationOptions, drawing
+ * from the XorShift64 state *state (in/out, qwen3.rs:1011-1034; seed it with
+ * mi_xorshift_seed). Temperature 0 is the greedy argmax and leaves *state.
+ * Candidates are ordered by descending value, equal logits by ascending
+ * index; every FP64 sum is the reference's sequential one. Synchronous.
+ * Errors: MI_ERR_CONFIG "logits contain no finite value" / "failed to sample
+ * a token" and the validate_generation_options messages. */
+mi_status mi_sample_logits(mi_context* ctx, const mi_tensor* logits, float temperature,
+                           float top_p, size_t top_k, uint64_t* state, uint32_t* token);
+/* XorShift64::new (qwen3.rs:1016-1024): seed 0 becomes 0x9e3779b97f4a7c15. */
+uint64_t mi_xorshift_seed(uint64_t seed);
 
 typedef struct mi_qwen3 mi_qwen3;
 typedef struct mi_kv_cache mi_kv_cache;
@@ -433,7 +447,11 @@ mi_status mi_qwen3_generate(mi_qwen3* m, const uint32_t* prompt, size_t prompt_l
                             size_t max_tokens, mi_kv_cache* cache, uint32_t* out_ids,
                             size_t* out_count);
 /* Qwen3Model::generate_with (qwen3.rs:441-473): on_token returns non-zero
- * to continue; it may be NULL. */
+ * to continue; it may be NULL. Temperature > 0 draws every token on the
+ * device (prefill and decode lm_heads followed by the sampler, one
+ * XorShift64 stream per call) through the same pipelined loop as greedy; the
+ * persistent decode kernel is greedy-only, so sampled decode steps run the
+ * per-kernel chain (captured as its own CUDA graph). */
 typedef int (*mi_token_callback)(uint32_t token, void* user);
 mi_status mi_qwen3_generate_with(mi_qwen3* m, const uint32_t* prompt, size_t prompt_len,
                                  const mi_generation_options* options, mi_kv_cache* cache,

@@ -64,6 +64,12 @@ __device__ __forceinline__ bool argmax_better(uint32_t ck, uint32_t ci, uint32_t
   return ck > bk || (ck == bk && ci > bi);
 }
 
+// Sampling order key of finite FP16 bits: descending key = descending
+// total_cmp value (-0 below +0).
+__device__ __forceinline__ uint32_t sample_key16(uint16_t b) {
+  return (b & 0x8000u) ? (uint32_t)(~b & 0xffffu) : (uint32_t)(b | 0x8000u);
+}
+
 __device__ __forceinline__ uint32_t pos_of(const Pos& p) {
   return p.dev ? (*p.dev + p.base) : p.base;
 }

@@ -243,7 +243,11 @@ __global__ void __launch_bounds__(kThreads) gemv_staged_kernel(GemvProblem p, Pl
           }
           __half h0 = __float2half_rn(a0);
           p.out[seg][row] = h0;
-          if (OUT == kOutArgmax) argmax_take(__half2float(h0), (uint32_t)item, best_key, best_idx);
+          if (OUT == kOutArgmax) {
+            argmax_take(__half2float(h0), (uint32_t)item, best_key, best_idx);
+            const uint16_t hb = __half_as_ushort(h0);
+            if (p.hist && (hb & 0x7c00u) != 0x7c00u) atomicAdd(p.hist + sample_key16(hb), 1u);
+          }
         }
       }
     }

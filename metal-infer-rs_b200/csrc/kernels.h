@@ -72,11 +72,34 @@ struct GemvProblem {
   uint32_t* best_out = nullptr;       // kOutArgmax: optional {key, index + index_base}
   uint32_t index_base = 0;            // kOutArgmax: global index of row 0 (vocab shard)
   float* outf = nullptr;              // kOutF32
+  uint32_t* hist = nullptr;           // kOutArgmax: optional +1 per finite logit at its order key
 };
 // True when the fast kernel accepts the problem (K % 8 == 0, 16-byte
 // aligned pointers, K <= 16384); otherwise gemv() uses the generic kernel.
 bool gemv_fast_ok(const GemvProblem& p);
 void gemv(const Launch& l, const GemvProblem& p);
+// ---- sampling (sample_token_f16, qwen3.rs:927-1005) -----------------------
+// Order key of a finite FP16 logit: total_cmp order as an unsigned 16-bit key.
+constexpr int kSampleBins = 65536;
+struct SampleProblem {
+  const __half* logits = nullptr;
+  uint32_t n = 0;
+  uint32_t* hist = nullptr;     // [kSampleBins] counts per order key; cleared by sample()
+  uint32_t* groups = nullptr;   // scratch [3 * kSampleBins]
+  // device words: {bits of 1 / temperature (FP32, correctly rounded), bits of
+  // top_p, top_k (0: all)}; read at run time, so a captured graph serves any
+  const uint32_t* opts = nullptr;
+  uint64_t* state = nullptr;    // XorShift64 state, advanced once per token drawn
+  // token_out[token_pos ? *token_pos : 0] = token, 0xFFFFFFFF when no logit is
+  // finite, 0xFFFFFFFE when the walk ends without a token
+  uint32_t* token_out = nullptr;
+  const uint32_t* token_pos = nullptr;
+};
+// hist[key(logit)] += 1 for every finite logit (hist zero before).
+void logit_histogram(const Launch& l, const __half* logits, uint32_t n, uint32_t* hist);
+// One CTA: draws one token from the histogram and the logits.
+void sample(const Launch& l, const SampleProblem& p);
+
 // Plain tiled reference kernel (MatmulBackend::Reference), any shape, M rows.
 void matmul_reference(const Launch& l, const __half* x, const __half* w, __half* out, int m,
                       int n, int k);

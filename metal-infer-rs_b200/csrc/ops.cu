@@ -3,6 +3,7 @@
 // validation and error messages; outputs are new stream-ordered tensors.
 
 #include <cmath>
+#include <cstring>
 
 #include "kernels.h"
 #include "mi_internal.h"
@@ -597,6 +598,77 @@ mi_status mi_batch_copy_into_cache(mi_batch* b, const mi_tensor* source, mi_tens
                to_int(source->shape[1] * source->shape[2], "stride"), pos);
   });
 }
+
+// sample_token (qwen3.rs:909-925) / sample_token_f16 (qwen3.rs:927-939) on
+// the device, synchronous: the key histogram, then the one-CTA sampler.
+mi_status mi_sample_logits(mi_context* ctx, const mi_tensor* logits, float temperature,
+                           float top_p, size_t top_k, uint64_t* state, uint32_t* token) {
+  return guard([&] {
+    require(ctx, "ctx");
+    require_f16(logits);
+    require(state, "state");
+    require(token, "token");
+    if (!std::isfinite(temperature) || temperature < 0.f)
+      fail(MI_ERR_CONFIG, "invalid model configuration: temperature must be finite and non-negative");
+    if (!std::isfinite(top_p) || !(top_p >= 0.f && top_p <= 1.f))
+      fail(MI_ERR_CONFIG, "invalid model configuration: top_p must be between 0 and 1");
+    const size_t n = logits->len();
+    const bool vector_shape = logits->shape.size() == 1 ||
+                              (logits->shape.size() == 2 && logits->shape[0] == 1);
+    if (!vector_shape || n == 0)
+      fail(MI_ERR_SHAPE, "invalid tensor shape: sampling expects nonempty logits [n] or [1, n]");
+    MI_REQUIRE(n < 0x80000000ull, MI_ERR_SHAPE, "invalid tensor shape: %zu logits exceed 2^31", n);
+    if (top_k > 0xFFFFFFFFull)
+      fail(MI_ERR_CONFIG, "invalid model configuration: top_k does not fit in u32");
+    Out out;
+    out.t = new_tensor(ctx, {2}, MI_U32);
+    if (temperature == 0.f) {
+      int groups = k::argmax_partials(n);
+      Out pv, pi;
+      pv.t = new_tensor(ctx, {(size_t)groups}, MI_F32);
+      pi.t = new_tensor(ctx, {(size_t)groups}, MI_U32);
+      k::argmax(launch_of(ctx), logits->f16(), n, pv.t->f32(), pi.t->u32(), out.t->u32());
+    } else {
+      Out hist, groups, opts, st;
+      hist.t = new_tensor(ctx, {(size_t)k::kSampleBins}, MI_U32);
+      groups.t = new_tensor(ctx, {3 * (size_t)k::kSampleBins}, MI_U32);
+      opts.t = new_tensor(ctx, {4}, MI_U32);
+      st.t = new_tensor(ctx, {2}, MI_U32);
+      const float inv = 1.0f / temperature;
+      uint32_t host_opts[4];
+      std::memcpy(&host_opts[0], &inv, 4);
+      std::memcpy(&host_opts[1], &top_p, 4);
+      host_opts[2] = (uint32_t)top_k;
+      host_opts[3] = 0;
+      MI_CUDA(cudaMemsetAsync(hist.t->base(), 0, hist.t->bytes(), ctx->stream));
+      MI_CUDA(cudaMemcpyAsync(opts.t->base(), host_opts, sizeof(host_opts),
+                              cudaMemcpyHostToDevice, ctx->stream));
+      MI_CUDA(cudaMemcpyAsync(st.t->base(), state, 8, cudaMemcpyHostToDevice, ctx->stream));
+      ProfileScope ps(ctx, "sample");
+      k::logit_histogram(launch_of(ctx), logits->f16(), (uint32_t)n, hist.t->u32());
+      k::SampleProblem p;
+      p.logits = logits->f16();
+      p.n = (uint32_t)n;
+      p.hist = hist.t->u32();
+      p.groups = groups.t->u32();
+      p.opts = opts.t->u32();
+      p.state = reinterpret_cast<uint64_t*>(st.t->u32());
+      p.token_out = out.t->u32();
+      k::sample(launch_of(ctx), p);
+      MI_CUDA(cudaMemcpyAsync(state, st.t->base(), 8, cudaMemcpyDeviceToHost, ctx->stream));
+    }
+    uint32_t tok = 0;
+    MI_CUDA(cudaMemcpyAsync(&tok, out.t->base(), 4, cudaMemcpyDeviceToHost, ctx->stream));
+    MI_CUDA(cudaStreamSynchronize(ctx->stream));
+    if (tok == 0xFFFFFFFFu)
+      fail(MI_ERR_CONFIG, "invalid model configuration: logits contain no finite value");
+    if (tok == 0xFFFFFFFEu)
+      fail(MI_ERR_CONFIG, "invalid model configuration: failed to sample a token");
+    *token = tok;
+  });
+}
+
+uint64_t mi_xorshift_seed(uint64_t seed) { return seed == 0 ? 0x9e3779b97f4a7c15ull : seed; }
 
 mi_status mi_fill_normal_f16(mi_context* ctx, mi_tensor* t, uint64_t seed, uint64_t stream,
                              uint64_t offset, double std_dev) {

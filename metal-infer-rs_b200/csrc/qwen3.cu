@@ -94,6 +94,9 @@ struct Workspace {
   TensorRef loop_part;  // persistent decode: attention block partials
   // persistent decode: epoch-tagged activations and per-CTA argmax records
   TensorRef t_hidden, t_res, t_qkv, t_attn_o, t_act, t_argmax;
+  // sampling: key histogram, group scratch, options, XorShift64 state and
+  // (tensor parallelism) the gathered full-vocabulary logits
+  TensorRef smp_hist, smp_groups, smp_opts, smp_state, smp_logits;
   uint64_t loop_epoch = 1;  // layer-steps run through the tagged buffers + 1
   int attn_splits = 0;  // flash-decode blocks for the largest cache seen
   int attn_block = 64;  // keys per flash-decode block
@@ -132,6 +135,7 @@ struct mi_qwen3 {
     unsigned long long ctr_base[3] = {0, 0, 0};
   } mbox;
   bool persistent = true;  // decode through the persistent kernel when it fits
+  bool sampling = false;   // LM heads draw tokens (generate_with, temperature > 0)
   int loop_state = 0;      // 0 unplanned, 1 planned, -1 not admitted
   k::DecodeLoop loop;
   Workspace ws;
@@ -147,12 +151,15 @@ struct mi_kv_cache {
   TensorRef dev_len;  // u32 [1]
   TensorRef rope;     // f32 [capacity, head_dim / 2, 2]: (cos, sin) per position and pair
   const float2* rope_table() const { return reinterpret_cast<const float2*>(rope.t->f32()); }
-  cudaGraphExec_t graph = nullptr;
+  cudaGraphExec_t graph = nullptr;  // decode step: [0] greedy, [1] sampled
   uint64_t graph_version = 0;
+  cudaGraphExec_t graph_sampled = nullptr;
+  uint64_t graph_sampled_version = 0;
   std::vector<k::LoopLayer> loop_host;  // layer table of the persistent decode
   TensorRef loop_layers;                // its device copy
   ~mi_kv_cache() {
     if (graph) cudaGraphExecDestroy(graph);
+    if (graph_sampled) cudaGraphExecDestroy(graph_sampled);
   }
 };
 
@@ -247,6 +254,44 @@ void tp_argmax(mi_qwen3* m, uint32_t* tokens, const uint32_t* pos, uint32_t* ste
   auto& w = m->ws;
   tp_allgather(m, w.tp_best.t->u32(), w.tp_best_all.t->u32(), 2, 4);
   k::argmax_combine(m->ctx->stream, w.tp_best_all.t->u32(), m->tp, tokens, pos, step_counter);
+}
+
+// Sampling buffers (the histogram starts zeroed; the sampler clears it).
+void ensure_sampling(mi_qwen3* m) {
+  auto& w = m->ws;
+  if (w.smp_hist.t) return;
+  mi_context* ctx = m->ctx;
+  w.smp_hist = TensorRef(new_tensor(ctx, {(size_t)k::kSampleBins}, MI_U32, true));
+  w.smp_groups = TensorRef(new_tensor(ctx, {3 * (size_t)k::kSampleBins}, MI_U32, true));
+  w.smp_opts = TensorRef(new_tensor(ctx, {4}, MI_U32, true));
+  w.smp_state = TensorRef(new_tensor(ctx, {2}, MI_U32, true));
+  if (m->tp > 1)
+    w.smp_logits = TensorRef(new_tensor(ctx, {m->full_cfg.vocab_size}, MI_F16, true));
+  MI_CUDA(cudaMemsetAsync(w.smp_hist.t->base(), 0, w.smp_hist.t->bytes(), ctx->stream));
+}
+
+// The lm_head's logits -> tokens[*pos] (tokens[0] without pos), drawn by the
+// sampler. One GPU: the lm_head GEMV filled the key histogram. Tensor
+// parallelism: every rank gathers the full logits and draws the same token.
+void encode_sample(mi_qwen3* m, uint32_t* tokens, const uint32_t* pos) {
+  auto& w = m->ws;
+  k::SampleProblem sp;
+  sp.logits = w.logits.h();
+  sp.n = (uint32_t)m->cfg.vocab_size;
+  sp.hist = w.smp_hist.t->u32();
+  if (m->tp > 1) {
+    tp_allgather(m, w.logits.t->base(), w.smp_logits.t->base(), m->cfg.vocab_size, 2);
+    sp.logits = w.smp_logits.h();
+    sp.n = (uint32_t)m->full_cfg.vocab_size;
+    k::logit_histogram(launch(m, false), sp.logits, sp.n, sp.hist);
+  }
+  sp.groups = w.smp_groups.t->u32();
+  sp.opts = w.smp_opts.t->u32();
+  sp.state = reinterpret_cast<uint64_t*>(w.smp_state.t->u32());
+  sp.token_out = tokens;
+  sp.token_pos = pos;
+  ProfileScope ps(m->ctx, "sample");
+  k::sample(launch(m, false), sp);
 }
 
 bool fused_decode_supported(const mi_qwen3* m) {
@@ -452,9 +497,14 @@ void encode_decode_step(mi_qwen3* m, mi_kv_cache* c) {
       p.index_base = (uint32_t)(m->rank * cfg.vocab_size);
       p.step_counter = nullptr;
     }
-    ProfileScope ps(m->ctx, "lm_head_argmax");
-    k::gemv(dlaunch(m, true), p);
+    if (m->sampling && m->tp == 1) p.hist = w.smp_hist.t->u32();
+    {
+      ProfileScope ps(m->ctx, "lm_head_argmax");
+      k::gemv(dlaunch(m, true), p);
+    }
     if (m->tp > 1) tp_argmax(m, c->toks.t->u32(), len, len);
+    // the step counter has advanced: the token goes to toks[*len]
+    if (m->sampling) encode_sample(m, c->toks.t->u32(), len);
   }
 }
 
@@ -471,7 +521,7 @@ bool persistent_env() {
 
 bool decode_loop_ready(mi_qwen3* m) {
   if ((m->tp > 1 && !m->mbox.local) || !m->persistent || !persistent_env() ||
-      !fused_decode_supported(m))
+      !fused_decode_supported(m) || m->sampling)
     return false;
   if (m->loop_state == 0) {
     const auto& c = m->cfg;
@@ -586,10 +636,12 @@ void run_decode_step(mi_qwen3* m, mi_kv_cache* c) {
     encode_decode_step(m, c);
     return;
   }
-  if (!c->graph || c->graph_version != m->plan_version) {
-    if (c->graph) {
-      cudaGraphExecDestroy(c->graph);
-      c->graph = nullptr;
+  cudaGraphExec_t& graph = m->sampling ? c->graph_sampled : c->graph;
+  uint64_t& version = m->sampling ? c->graph_sampled_version : c->graph_version;
+  if (!graph || version != m->plan_version) {
+    if (graph) {
+      cudaGraphExecDestroy(graph);
+      graph = nullptr;
     }
     cudaGraph_t g = nullptr;
     MI_CUDA(cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal));
@@ -601,15 +653,15 @@ void run_decode_step(mi_qwen3* m, mi_kv_cache* c) {
       throw;
     }
     MI_CUDA(cudaStreamEndCapture(ctx->stream, &g));
-    cudaError_t err = cudaGraphInstantiate(&c->graph, g, 0);
+    cudaError_t err = cudaGraphInstantiate(&graph, g, 0);
     cudaGraphDestroy(g);
     if (err != cudaSuccess) {
-      c->graph = nullptr;
+      graph = nullptr;
       fail(MI_ERR_COMMAND, "graph instantiation failed: %s", cudaGetErrorString(err));
     }
-    c->graph_version = m->plan_version;
+    version = m->plan_version;
   }
-  MI_CUDA(cudaGraphLaunch(c->graph, ctx->stream));
+  MI_CUDA(cudaGraphLaunch(graph, ctx->stream));
 }
 
 // ---- prefill / eager forward ---------------------------------------------------
@@ -773,8 +825,10 @@ void forward_tokens(mi_qwen3* m, mi_kv_cache* c, size_t T) {
     p.best_out = w.tp_best.t->u32();
     p.index_base = (uint32_t)(m->rank * cfg.vocab_size);
   }
+  if (m->sampling && m->tp == 1) p.hist = w.smp_hist.t->u32();
   k::gemv(l, p);
   if (m->tp > 1) tp_argmax(m, c->toks.t->u32() + off + T, nullptr, nullptr);
+  if (m->sampling) encode_sample(m, c->toks.t->u32() + off + T, nullptr);
   c->filled = off + T;
   set_dev_len(c, c->filled);
 }
@@ -1385,6 +1439,8 @@ size_t generate_greedy(mi_qwen3* m, mi_kv_cache* c, const uint32_t* prompt, size
       uint32_t tok = ids[seen];
       if (tok == 0xFFFFFFFFu)
         fail(MI_ERR_CONFIG, "invalid model configuration: logits contain no finite value");
+      if (tok == 0xFFFFFFFEu)
+        fail(MI_ERR_CONFIG, "invalid model configuration: failed to sample a token");
       bool is_stop = false;
       for (size_t s = 0; s < nstops; ++s) is_stop |= stops[s] == tok;
       if (is_stop) {
@@ -1461,10 +1517,37 @@ mi_status mi_qwen3_generate_with(mi_qwen3* m, const uint32_t* prompt, size_t pro
     require(prompt, "prompt");
     if (!std::isfinite(options->temperature) || options->temperature < 0.f)
       fail(MI_ERR_CONFIG, "invalid model configuration: temperature must be finite and non-negative");
-    if (!(options->top_p > 0.f && options->top_p <= 1.f))
-      fail(MI_ERR_CONFIG, "invalid model configuration: top_p must be in (0, 1]");
-    if (options->temperature != 0.f)
-      fail(MI_ERR_UNSUPPORTED, "unsupported model: sampling with temperature > 0 is not on the device path");
+    // validate_generation_options (qwen3.rs:897-907)
+    if (!std::isfinite(options->top_p) || !(options->top_p >= 0.f && options->top_p <= 1.f))
+      fail(MI_ERR_CONFIG, "invalid model configuration: top_p must be between 0 and 1");
+    if (options->temperature == 0.f || options->max_tokens == 0) {
+      *out_count = generate_greedy(m, cache, prompt, prompt_len, options->max_tokens,
+                                   options->stop_token_ids, options->stop_token_count, on_token,
+                                   user, out_ids, capacity);
+      return;
+    }
+    // Sampled (qwen3.rs:455-472): the same pipelined loop, each lm_head
+    // followed by the sampler, one XorShift64 stream for the whole call.
+    if (options->top_k > 0xFFFFFFFFull)
+      fail(MI_ERR_CONFIG, "invalid model configuration: top_k does not fit in u32");
+    ensure_sampling(m);
+    const float inv = 1.0f / options->temperature;
+    uint32_t opts[4];
+    std::memcpy(&opts[0], &inv, 4);
+    std::memcpy(&opts[1], &options->top_p, 4);
+    opts[2] = (uint32_t)options->top_k;
+    opts[3] = 0;
+    const uint64_t state = options->seed == 0 ? 0x9e3779b97f4a7c15ull : options->seed;
+    MI_CUDA(cudaMemcpyAsync(m->ws.smp_opts.t->base(), opts, sizeof(opts), cudaMemcpyHostToDevice,
+                            m->ctx->stream));
+    MI_CUDA(cudaMemcpyAsync(m->ws.smp_state.t->base(), &state, 8, cudaMemcpyHostToDevice,
+                            m->ctx->stream));
+    // the host copies above read pageable memory before returning
+    struct Scope {
+      mi_qwen3* m;
+      ~Scope() { m->sampling = false; }
+    } scope{m};
+    m->sampling = true;
     *out_count = generate_greedy(m, cache, prompt, prompt_len, options->max_tokens,
                                  options->stop_token_ids, options->stop_token_count, on_token,
                                  user, out_ids, capacity);

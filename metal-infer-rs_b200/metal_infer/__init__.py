@@ -173,6 +173,11 @@ QWEN3_32B = dict(hidden_size=5120, intermediate_size=25600, num_hidden_layers=64
                  rms_norm_eps=1e-6, rope_theta=1e6, vocab_size=151936, tie_word_embeddings=0)
 
 # Every symbol the header declares (checked by the CPU tests).
+def xorshift_seed(seed: int) -> int:
+    """XorShift64::new (qwen3.rs:1016-1024): seed 0 becomes 0x9e3779b97f4a7c15."""
+    return int(lib().mi_xorshift_seed(ctypes.c_uint64(seed)))
+
+
 EXPORTS = [
     "mi_last_error_message", "mi_version", "mi_context_create", "mi_context_destroy",
     "mi_context_device_name", "mi_context_allocated_bytes", "mi_context_set_matmul_backend",
@@ -203,7 +208,7 @@ EXPORTS = [
     "mi_qwen3_decode_argmax", "mi_qwen3_decode_steps", "mi_kv_cache_tokens",
     "mi_qwen3_generate", "mi_qwen3_generate_with",
     "mi_qwen3_run_first_block", "mi_qwen3_forward_hidden", "mi_qwen3_weight",
-    "mi_fill_normal_f16", "mi_fill_tokens_u32",
+    "mi_fill_normal_f16", "mi_fill_tokens_u32", "mi_sample_logits", "mi_xorshift_seed",
 ]
 
 _lib = None
@@ -228,6 +233,8 @@ def lib() -> ctypes.CDLL:
         getattr(L, name).restype = _sz
     L.mi_tensor_device_ptr.restype = _vp
     L.mi_context_stream.restype = _vp
+    L.mi_xorshift_seed.restype = ctypes.c_uint64
+    L.mi_xorshift_seed.argtypes = [ctypes.c_uint64]
     for name in ("mi_context_destroy", "mi_tensor_release", "mi_batch_abandon", "mi_qwen3_destroy",
                  "mi_kv_cache_destroy", "mi_kv_cache_reset"):
         getattr(L, name).restype = None
@@ -455,6 +462,17 @@ class MetalContext:
     def fill_tokens_u32(self, t: Tensor, seed: int, stream: int, vocab: int) -> None:
         _check(lib().mi_fill_tokens_u32(self._h, t.handle, ctypes.c_uint64(seed),
                                         ctypes.c_uint64(stream), ctypes.c_uint32(vocab)))
+
+    def sample_logits(self, logits: Tensor, temperature: float, top_p: float = 1.0,
+                      top_k: int = 0, state: int = 1) -> tuple:
+        """sample_token / sample_token_f16 (qwen3.rs:909-1005) on the device:
+        returns (token, next XorShift64 state)."""
+        st = ctypes.c_uint64(state)
+        tok = ctypes.c_uint32(0)
+        _check(lib().mi_sample_logits(self._h, logits.handle, ctypes.c_float(temperature),
+                                      ctypes.c_float(top_p), _sz(top_k), ctypes.byref(st),
+                                      ctypes.byref(tok)))
+        return int(tok.value), int(st.value)
 
     # batches
     def begin_batch(self) -> "CommandBatch":

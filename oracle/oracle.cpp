@@ -649,6 +649,79 @@ uint32_t or_argmax(const uint16_t* logits, size_t n) {
   return best_index;
 }
 
+// XorShift64::new (qwen3.rs:1016-1024)
+uint64_t or_xorshift_seed(uint64_t seed) { return seed == 0 ? 0x9e3779b97f4a7c15ull : seed; }
+
+// sample_token (qwen3.rs:909-925), sample_token_f16 (qwen3.rs:927-939) and
+// sample_candidates (qwen3.rs:941-1005) as one sequential pass:
+//  * finite logits become candidates; they are ordered by descending
+//    total_cmp (the sign-flipped bit key below, so +0 precedes -0) and, among
+//    equal bit patterns, by ascending index (the reference's unstable sort
+//    leaves that order open; both of its top-k branches reduce to "the first
+//    top_k in this order");
+//  * weights exp((v - max) * (1 / temperature)) in FP32, summed in FP64 in
+//    that order; with top_p < 1 the prefix whose running sum first reaches
+//    total * top_p is kept and its running sum becomes the total;
+//  * target = next_f64() * total; the first candidate at which
+//    target -= weight drops to <= 0 is the token.
+uint32_t or_sample_f16(const uint16_t* logits, size_t n, float temperature, float top_p,
+                       size_t top_k, uint64_t* state) {
+  if (temperature == 0.0f) return or_argmax(logits, n);
+  struct Cand {
+    uint16_t key;
+    uint32_t index;
+  };
+  std::vector<Cand> cand;
+  cand.reserve(n);
+  for (size_t i = 0; i < n; ++i) {
+    uint16_t b = logits[i];
+    if ((b & 0x7c00u) == 0x7c00u) continue;  // infinity or NaN
+    uint16_t key = (b & 0x8000u) ? static_cast<uint16_t>(~b) : static_cast<uint16_t>(b | 0x8000u);
+    cand.push_back({key, static_cast<uint32_t>(i)});
+  }
+  if (cand.empty()) return 0xFFFFFFFFu;
+  std::stable_sort(cand.begin(), cand.end(),
+                   [](const Cand& a, const Cand& b) { return a.key > b.key; });
+  if (top_k > 0 && cand.size() > top_k) cand.resize(top_k);
+  auto value = [&](const Cand& c) {
+    uint16_t b = (c.key & 0x8000u) ? static_cast<uint16_t>(c.key & 0x7fffu)
+                                    : static_cast<uint16_t>(~c.key);
+    return f(b);
+  };
+  const float max_logit = value(cand[0]);
+  const float inverse = 1.0f / temperature;
+  std::vector<float> weight(cand.size());
+  double total = 0.0;
+  for (size_t i = 0; i < cand.size(); ++i) {
+    weight[i] = mi_exp((value(cand[i]) - max_logit) * inverse);
+    total += static_cast<double>(weight[i]);
+  }
+  size_t keep = cand.size();
+  if (top_p < 1.0f) {
+    const double threshold = total * static_cast<double>(top_p);
+    double cumulative = 0.0;
+    keep = 0;
+    for (size_t i = 0; i < cand.size(); ++i) {
+      cumulative += static_cast<double>(weight[i]);
+      ++keep;
+      if (cumulative >= threshold) break;
+    }
+    total = 0.0;
+    for (size_t i = 0; i < keep; ++i) total += static_cast<double>(weight[i]);
+  }
+  uint64_t v = *state;
+  v ^= v << 13;
+  v ^= v >> 7;
+  v ^= v << 17;
+  *state = v;
+  double target = (static_cast<double>(v) / 18446744073709551616.0) * total;
+  for (size_t i = 0; i < keep; ++i) {
+    target -= static_cast<double>(weight[i]);
+    if (target <= 0.0) return cand[i].index;
+  }
+  return 0xFFFFFFFEu;
+}
+
 // rope_f16 (transformer.metal:1514-1531)
 void or_rope(const uint16_t* in, size_t tokens, size_t heads, size_t head_dim, size_t offset,
              float theta, uint16_t* out) {
@@ -946,6 +1019,26 @@ size_t or_qwen3_generate_greedy(or_qwen3* m, const uint32_t* prompt, size_t prom
     if (step + 1 == max_tokens) break;
     if (or_qwen3_forward(m, &token, 1, logits.data()) != 0) break;
     token = or_argmax(logits.data(), logits.size());
+  }
+  return produced;
+}
+
+// generate_with, temperature > 0 branch (qwen3.rs:455-472), no stop tokens.
+size_t or_qwen3_generate_sampled(or_qwen3* m, const uint32_t* prompt, size_t prompt_len,
+                                 size_t max_tokens, float temperature, float top_p,
+                                 size_t top_k, uint64_t seed, uint32_t* out_ids) {
+  if (max_tokens == 0) return 0;
+  std::vector<uint16_t> logits(m->c.vocab_size);
+  m->filled = 0;
+  if (or_qwen3_forward(m, prompt, prompt_len, logits.data()) != 0) return 0;
+  uint64_t state = or_xorshift_seed(seed);
+  size_t produced = 0;
+  for (size_t step = 0; step < max_tokens; ++step) {
+    uint32_t token = or_sample_f16(logits.data(), logits.size(), temperature, top_p, top_k, &state);
+    if (token >= 0xFFFFFFFEu) break;
+    out_ids[produced++] = token;
+    if (step + 1 == max_tokens) break;
+    if (or_qwen3_forward(m, &token, 1, logits.data()) != 0) break;
   }
   return produced;
 }

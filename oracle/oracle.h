@@ -74,6 +74,18 @@ void or_embedding(const uint32_t* tokens, size_t count, const uint16_t* table,
                   size_t rows, size_t width, uint16_t* out);
 /* transformer.metal:1396-1512; returns 0xFFFFFFFF when nothing is finite */
 uint32_t or_argmax(const uint16_t* logits, size_t n);
+/* sample_token / sample_token_f16 + sample_candidates (qwen3.rs:909-1005)
+ * with the XorShift64 stream of qwen3.rs:1011-1034 (`state` in/out, already
+ * seeded: see or_xorshift_seed). Temperature 0 is the argmax of sample_token.
+ * Candidates are ordered by descending total_cmp value; equal bit patterns
+ * in ascending index (slice::sort_unstable_by leaves their order open); the
+ * exponential is the engine's exp. Returns the token, 0xFFFFFFFF when no
+ * logit is finite, 0xFFFFFFFE when the walk ends without a token ("failed to
+ * sample a token"). */
+uint32_t or_sample_f16(const uint16_t* logits, size_t n, float temperature,
+                       float top_p, size_t top_k, uint64_t* state);
+/* XorShift64::new (qwen3.rs:1016-1024): seed 0 becomes 0x9e3779b97f4a7c15. */
+uint64_t or_xorshift_seed(uint64_t seed);
 /* transformer.metal:1514-1531 */
 void or_rope(const uint16_t* in, size_t tokens, size_t heads, size_t head_dim,
              size_t offset, float theta, uint16_t* out);
@@ -159,6 +171,14 @@ int or_qwen3_forward_hidden(or_qwen3* m, const uint16_t* hidden, size_t count,
 size_t or_qwen3_generate_greedy(or_qwen3* m, const uint32_t* prompt,
                                 size_t prompt_len, size_t max_tokens,
                                 uint32_t* out_ids);
+/* Sampled generation as generate_with with temperature > 0 (qwen3.rs:441-473)
+ * without stop tokens: token 0 from the prefill logits, each later token from
+ * the logits of decoding the previous one, one XorShift64 stream seeded by
+ * `seed`. Stops early (returning the count) on a sampling failure. */
+size_t or_qwen3_generate_sampled(or_qwen3* m, const uint32_t* prompt,
+                                 size_t prompt_len, size_t max_tokens,
+                                 float temperature, float top_p, size_t top_k,
+                                 uint64_t seed, uint32_t* out_ids);
 /* Access to one weight tensor by stream role (for op-level checks). */
 const uint16_t* or_qwen3_weight(const or_qwen3* m, int layer, int role);
 const uint16_t* or_qwen3_cache(const or_qwen3* m, int layer, int value);

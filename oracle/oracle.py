@@ -67,6 +67,14 @@ def lib():
         L.or_qwen3_forward_hidden.argtypes = [ctypes.c_void_p, _u16p, _sz, _u16p]
         L.or_qwen3_generate_greedy.argtypes = [ctypes.c_void_p, _u32p, _sz, _sz, _u32p]
         L.or_qwen3_generate_greedy.restype = _sz
+        L.or_qwen3_generate_sampled.argtypes = [ctypes.c_void_p, _u32p, _sz, _sz, ctypes.c_float,
+                                                ctypes.c_float, _sz, ctypes.c_uint64, _u32p]
+        L.or_qwen3_generate_sampled.restype = _sz
+        L.or_sample_f16.argtypes = [_u16p, _sz, ctypes.c_float, ctypes.c_float, _sz,
+                                    ctypes.POINTER(ctypes.c_uint64)]
+        L.or_sample_f16.restype = ctypes.c_uint32
+        L.or_xorshift_seed.argtypes = [ctypes.c_uint64]
+        L.or_xorshift_seed.restype = ctypes.c_uint64
         L.or_qwen3_weight.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int]
         L.or_qwen3_weight.restype = _u16p
         L.or_qwen3_cache.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int]
@@ -200,6 +208,22 @@ def embedding(tokens, table):
 def argmax(logits) -> int:
     logits = np.ascontiguousarray(logits, np.uint16)
     return int(lib().or_argmax(_p16(logits), _sz(logits.size)))
+
+
+def xorshift_seed(seed: int) -> int:
+    """XorShift64::new (qwen3.rs:1016-1024)."""
+    return int(lib().or_xorshift_seed(seed))
+
+
+def sample(logits, temperature: float, top_p: float = 1.0, top_k: int = 0, state: int = 1):
+    """One sampled token from FP16 logit bits (qwen3.rs:909-1005); returns
+    (token, next state). Token 0xFFFFFFFF: no finite logit; 0xFFFFFFFE: the
+    walk ended without a token."""
+    logits = np.ascontiguousarray(logits, np.uint16)
+    st = ctypes.c_uint64(state)
+    tok = lib().or_sample_f16(_p16(logits), _sz(logits.size), temperature, top_p, top_k,
+                              ctypes.byref(st))
+    return int(tok), int(st.value)
 
 
 def rope(x, offset, theta):
@@ -359,6 +383,15 @@ class Qwen3:
         out = np.empty(max_tokens, np.uint32)
         n = lib().or_qwen3_generate_greedy(self.h, _p32(prompt), _sz(prompt.size),
                                            _sz(max_tokens), _p32(out))
+        return out[:n]
+
+    def generate_sampled(self, prompt, max_tokens: int, temperature: float, top_p: float = 1.0,
+                         top_k: int = 0, seed: int = 0) -> np.ndarray:
+        prompt = np.ascontiguousarray(prompt, np.uint32)
+        out = np.empty(max(1, max_tokens), np.uint32)
+        n = lib().or_qwen3_generate_sampled(self.h, _p32(prompt), _sz(prompt.size),
+                                            _sz(max_tokens), temperature, top_p, top_k, seed,
+                                            _p32(out))
         return out[:n]
 
     def weight(self, layer: int, role: str, shape) -> np.ndarray:

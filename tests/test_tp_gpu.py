@@ -20,6 +20,7 @@ from conftest import INPUT_STREAM
 pytestmark = pytest.mark.gpu
 
 TP = 2
+SAMPLED = dict(temperature=0.9, top_p=0.95, top_k=64, seed=13)
 
 
 def small_cfg():
@@ -51,6 +52,9 @@ def _rank_main(rank, port, cfg, prompt, steps, out, ckpt=None):
             model.set_decode_persistent(path == "persistent")
             model.set_decode_graphs(path != "eager")
             res[f"ids_{path}"] = model.generate(prompt, steps, model.kv_cache(128))
+        # sampled: every rank gathers the full logits and draws the same token
+        res["sampled"] = model.generate_with(prompt, dict(SAMPLED, max_tokens=steps),
+                                             model.kv_cache(128))
         res["config"] = model.config()
         if ckpt:
             # the same shard read from a checkpoint of the full model
@@ -100,6 +104,8 @@ def test_tp2_matches_oracle_tp_arithmetic(tmp_path):
     ref_ids = O.Qwen3(cfg, seed=11, capacity=128)
     ref_ids.set_tp(TP)
     want_ids = ref_ids.generate_greedy(prompt, steps)
+    want_sampled = ref_ids.generate_sampled(prompt, steps, SAMPLED["temperature"],
+                                            SAMPLED["top_p"], SAMPLED["top_k"], SAMPLED["seed"])
     for r in range(TP):
         got = res[r]
         assert got["config"]["num_attention_heads"] == cfg["num_attention_heads"]
@@ -111,3 +117,4 @@ def test_tp2_matches_oracle_tp_arithmetic(tmp_path):
         assert got["persistent"]  # decode runs in the persistent kernel with peer exchange
         for path in ("persistent", "graph", "eager"):
             np.testing.assert_array_equal(got[f"ids_{path}"], want_ids, err_msg=path)
+        np.testing.assert_array_equal(got["sampled"], want_sampled)
