@@ -255,6 +255,35 @@ def run_ours(args, rank, world, local_rank):
     achieved = dom_bytes / dom_avg / 1e9
     traffic = read_traffic(dominant)
 
+    # Sampled decode (generate_with, temperature > 0): the kernel chain with
+    # the lm_head's key histogram and the one-CTA sampler after every head.
+    # Decode rate = 64 steps / (time of a 65-token call - a 1-token call).
+    sampled = {}
+    for label, opts in (("top_k20_top_p0.95_t0.6", dict(temperature=0.6, top_p=0.95, top_k=20)),
+                        ("full_vocab_t1.0", dict(temperature=1.0, top_p=1.0, top_k=0))):
+        opts = dict(opts, seed=SEED)
+        model.generate_with(prompt_ptr, dict(opts, max_tokens=17), cache)  # graph capture
+        spans = []
+        for n in (1, 65):
+            torch.cuda.synchronize()
+            t = time.perf_counter()
+            model.generate_with(prompt_ptr, dict(opts, max_tokens=n), cache)
+            spans.append(time.perf_counter() - t)
+        ctx.set_kernel_profiling(True)
+        ctx.take_kernel_profiles()
+        model.generate_with(prompt_ptr, dict(opts, max_tokens=17), cache)
+        ctx.synchronize()
+        prof_s = ctx.take_kernel_profiles()
+        ctx.set_kernel_profiling(False)
+        smp = [s for n, s in prof_s if n == "sample"]
+        head = [s for n, s in prof_s if n == "lm_head_argmax"]
+        sampled[label] = {
+            "decode_tokens_per_s": round(64 / max(spans[1] - spans[0], 1e-9), 1),
+            "note": "generate_with, host clock, decode chain (CUDA graph) + sampler",
+            "sample_kernel_us": round(sum(smp) / len(smp) * 1e6, 2) if smp else None,
+            "lm_head_with_histogram_us": round(sum(head) / len(head) * 1e6, 2) if head else None,
+        }
+
     kv_mean = PROMPT + (DECODE + 1) / 2.0
     bytes_tok = decode_bytes_per_token(CONFIG, kv_mean)
     per_gpu_tps = decode_tps / world
@@ -293,6 +322,7 @@ def run_ours(args, rank, world, local_rank):
                          "traffic": traffic, "bytes_per_launch": dom_bytes,
                          "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"},
             "decode_path": "persistent kernel" if persistent else "kernel chain (CUDA graph)",
+            "sampled_decode": sampled,
             "kernels": kernels,
             "gpu_launches": launches,
             "clocks": clocks.summary(),

@@ -70,6 +70,78 @@ __device__ __forceinline__ uint32_t sample_key16(uint16_t b) {
   return (b & 0x8000u) ? (uint32_t)(~b & 0xffffu) : (uint32_t)(b | 0x8000u);
 }
 
+// Bitonic sort (ascending) of n 16-bit keys in shared memory, n a power of
+// two, by every thread of the block; ends with a barrier.
+__device__ __forceinline__ void block_sort_u16(uint16_t* keys, int n) {
+  for (int k = 2; k <= n; k <<= 1)
+    for (int j = k >> 1; j > 0; j >>= 1) {
+      for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const int ixj = i ^ j;
+        if (ixj > i) {
+          const uint16_t a = keys[i], b = keys[ixj];
+          if ((a > b) == ((i & k) == 0)) {
+            keys[i] = b;
+            keys[ixj] = a;
+          }
+        }
+      }
+      __syncthreads();
+    }
+}
+
+// Adds the run lengths of the sorted keys[0, n) to hist (0xFFFF marks an
+// empty slot: it is the key of no finite value): the last element of each
+// run finds the run's first by binary search and adds its length, so there
+// is one global atomic per distinct key. The run lengths also go to the
+// block's coarse counts `coarse_s` (shared, one per 64 keys).
+__device__ __forceinline__ void emit_key_runs(const uint16_t* keys, int n, uint32_t* hist,
+                                              uint32_t* coarse_s) {
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const uint16_t k = keys[i];
+    if (k == 0xFFFFu || (i + 1 < n && keys[i + 1] == k)) continue;
+    int lo = 0, hi = i;  // first index with keys[index] == k
+    while (lo < hi) {
+      const int mid = (lo + hi) >> 1;
+      if (keys[mid] < k) lo = mid + 1;
+      else hi = mid;
+    }
+    const uint32_t len = (uint32_t)(i + 1 - lo);
+    atomicAdd(hist + k, len);
+    atomicAdd(coarse_s + (k >> 6), len);
+  }
+}
+
+// Sampling histogram of logits[first, last) (this block's rows): the keys of
+// the finite values are sorted in `scratch` (>= 2 * seg + 4096 bytes of
+// shared memory, seg a power of two) segment by segment and added as runs;
+// the per-64-key block counts hist[65536 + b] get one atomic per non-empty
+// block.
+__device__ __forceinline__ void hist_add_rows(const uint16_t* logits, int first, int last,
+                                              uint16_t* scratch, int seg, uint32_t* hist) {
+  uint32_t* coarse_s = reinterpret_cast<uint32_t*>(scratch + seg);
+  for (int b = threadIdx.x; b < 1024; b += blockDim.x) coarse_s[b] = 0;
+  for (int base = first; base < last; base += seg) {
+    const int n = min(seg, last - base);
+    int np2 = 1;
+    while (np2 < n) np2 <<= 1;
+    for (int i = threadIdx.x; i < np2; i += blockDim.x) {
+      uint16_t key = 0xFFFFu;
+      if (i < n) {
+        const uint16_t b = logits[base + i];
+        if ((b & 0x7c00u) != 0x7c00u) key = (uint16_t)sample_key16(b);
+      }
+      scratch[i] = key;
+    }
+    __syncthreads();
+    block_sort_u16(scratch, np2);
+    emit_key_runs(scratch, np2, hist, coarse_s);
+    __syncthreads();
+  }
+  for (int b = threadIdx.x; b < 1024; b += blockDim.x)
+    if (coarse_s[b]) atomicAdd(hist + 65536 + b, coarse_s[b]);
+  __syncthreads();
+}
+
 __device__ __forceinline__ uint32_t pos_of(const Pos& p) {
   return p.dev ? (*p.dev + p.base) : p.base;
 }

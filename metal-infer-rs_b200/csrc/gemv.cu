@@ -29,6 +29,10 @@ constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
 constexpr int kSmemBudget = 112 * 1024;  // two GEMV CTAs fit on one SM
 constexpr int kMaxStages = 6;
+#ifndef MI_GEMV_LARGE_CTAS_PER_SM
+#define MI_GEMV_LARGE_CTAS_PER_SM 2
+#endif
+constexpr int kLargeCtasPerSm = MI_GEMV_LARGE_CTAS_PER_SM;
 
 struct Plan {
   int rpc;      // items per CTA
@@ -243,11 +247,7 @@ __global__ void __launch_bounds__(kThreads) gemv_staged_kernel(GemvProblem p, Pl
           }
           __half h0 = __float2half_rn(a0);
           p.out[seg][row] = h0;
-          if (OUT == kOutArgmax) {
-            argmax_take(__half2float(h0), (uint32_t)item, best_key, best_idx);
-            const uint16_t hb = __half_as_ushort(h0);
-            if (p.hist && (hb & 0x7c00u) != 0x7c00u) atomicAdd(p.hist + sample_key16(hb), 1u);
-          }
+          if (OUT == kOutArgmax) argmax_take(__half2float(h0), (uint32_t)item, best_key, best_idx);
         }
       }
     }
@@ -256,6 +256,16 @@ __global__ void __launch_bounds__(kThreads) gemv_staged_kernel(GemvProblem p, Pl
       issue_stage<OUT>(p, plan, stages, full, first, last, chunk + plan.stages);
   }
 
+  if (OUT == kOutArgmax && p.hist) {
+    // sampling: key histogram of this block's logits, sorted in the idle
+    // weight ring (the last stage has been consumed)
+    __syncthreads();
+    const uint32_t ring = (uint32_t)plan.stages * plan.stage_bytes;
+    int seg = 4096;
+    while (seg > 64 && (uint32_t)seg * 2u + 4096u > ring) seg >>= 1;
+    hist_add_rows(reinterpret_cast<const uint16_t*>(p.out[0]), first, last,
+                  reinterpret_cast<uint16_t*>(stages), seg, p.hist);
+  }
   if (OUT == kOutArgmax) {
     if (lane == 0) {
       best_key_s[warp] = best_key;
@@ -391,7 +401,9 @@ template <int IN, int OUT>
 void launch_staged(const Launch& l, const GemvProblem& p) {
   int items = (OUT == kOutSwiglu) ? p.n[0] : p.n[0] + p.n[1] + p.n[2];
   if (items <= 0) return;
+  // large problems (the lm_head) run kLargeCtasPerSm CTAs per SM
   int grid = items < l.sm_count ? items : l.sm_count;
+  if (items >= 64 * l.sm_count) grid = kLargeCtasPerSm * l.sm_count;
   Plan plan = make_plan(p, items, grid, OUT == kOutSwiglu);
   grid = (items + plan.rpc - 1) / plan.rpc;
   size_t smem = (size_t)plan.x_bytes + (size_t)plan.stages * plan.stage_bytes;

@@ -81,11 +81,15 @@ void gemv(const Launch& l, const GemvProblem& p);
 // ---- sampling (sample_token_f16, qwen3.rs:927-1005) -----------------------
 // Order key of a finite FP16 logit: total_cmp order as an unsigned 16-bit key.
 constexpr int kSampleBins = 65536;
+constexpr int kSampleBlocks = kSampleBins / 64;
+// Histogram words: kSampleBins counts per order key, then kSampleBlocks
+// counts per block of 64 keys.
+constexpr int kSampleHistWords = kSampleBins + kSampleBlocks;
 struct SampleProblem {
   const __half* logits = nullptr;
   uint32_t n = 0;
-  uint32_t* hist = nullptr;     // [kSampleBins] counts per order key; cleared by sample()
-  uint32_t* groups = nullptr;   // scratch [3 * kSampleBins]
+  uint32_t* hist = nullptr;     // [kSampleHistWords], zero before; cleared by sample()
+  uint32_t* groups = nullptr;   // scratch [2 * kSampleBins]: {key, count} per group
   // device words: {bits of 1 / temperature (FP32, correctly rounded), bits of
   // top_p, top_k (0: all)}; read at run time, so a captured graph serves any
   const uint32_t* opts = nullptr;

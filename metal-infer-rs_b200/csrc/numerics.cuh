@@ -82,16 +82,23 @@ __device__ __forceinline__ float canon_butterfly_mask(float v, int lanes, unsign
   return v;
 }
 
+// a * b + c for FP16 a, b and FP32 c with one rounding: the mixed-precision
+// FMA of sm_100 (the FP16 operands widen exactly, so this equals
+// __fmaf_rn(float(a), float(b), c) without the two conversions).
+__device__ __forceinline__ float fma_f16_f32(unsigned short a, unsigned short b, float c) {
+  float d;
+  asm("fma.rn.f32.f16 %0, %1, %2, %3;" : "=f"(d) : "h"(a), "h"(b), "f"(c));
+  return d;
+}
+
 // 8 sequential fused multiply-adds of one chunk (FP16 x FP16).
 __device__ __forceinline__ float chunk_dot(const uint4& a, const uint4& b, float acc) {
-  const __half2* x = reinterpret_cast<const __half2*>(&a);
-  const __half2* y = reinterpret_cast<const __half2*>(&b);
+  const uint32_t x[4] = {a.x, a.y, a.z, a.w};
+  const uint32_t y[4] = {b.x, b.y, b.z, b.w};
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    float2 fx = __half22float2(x[i]);
-    float2 fy = __half22float2(y[i]);
-    acc = __fmaf_rn(fx.x, fy.x, acc);
-    acc = __fmaf_rn(fx.y, fy.y, acc);
+    acc = fma_f16_f32((unsigned short)(x[i] & 0xffffu), (unsigned short)(y[i] & 0xffffu), acc);
+    acc = fma_f16_f32((unsigned short)(x[i] >> 16), (unsigned short)(y[i] >> 16), acc);
   }
   return acc;
 }

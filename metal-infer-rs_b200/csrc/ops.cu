@@ -630,8 +630,8 @@ mi_status mi_sample_logits(mi_context* ctx, const mi_tensor* logits, float tempe
       k::argmax(launch_of(ctx), logits->f16(), n, pv.t->f32(), pi.t->u32(), out.t->u32());
     } else {
       Out hist, groups, opts, st;
-      hist.t = new_tensor(ctx, {(size_t)k::kSampleBins}, MI_U32);
-      groups.t = new_tensor(ctx, {3 * (size_t)k::kSampleBins}, MI_U32);
+      hist.t = new_tensor(ctx, {(size_t)k::kSampleHistWords}, MI_U32);
+      groups.t = new_tensor(ctx, {2 * (size_t)k::kSampleBins}, MI_U32);
       opts.t = new_tensor(ctx, {4}, MI_U32);
       st.t = new_tensor(ctx, {2}, MI_U32);
       const float inv = 1.0f / temperature;

@@ -261,8 +261,8 @@ void ensure_sampling(mi_qwen3* m) {
   auto& w = m->ws;
   if (w.smp_hist.t) return;
   mi_context* ctx = m->ctx;
-  w.smp_hist = TensorRef(new_tensor(ctx, {(size_t)k::kSampleBins}, MI_U32, true));
-  w.smp_groups = TensorRef(new_tensor(ctx, {3 * (size_t)k::kSampleBins}, MI_U32, true));
+  w.smp_hist = TensorRef(new_tensor(ctx, {(size_t)k::kSampleHistWords}, MI_U32, true));
+  w.smp_groups = TensorRef(new_tensor(ctx, {2 * (size_t)k::kSampleBins}, MI_U32, true));
   w.smp_opts = TensorRef(new_tensor(ctx, {4}, MI_U32, true));
   w.smp_state = TensorRef(new_tensor(ctx, {2}, MI_U32, true));
   if (m->tp > 1)

@@ -37,11 +37,27 @@ constexpr int kWarps = kThreads / 32;
 constexpr int kPerThread = 4;  // groups per thread per chunk
 constexpr int kChunk = kThreads * kPerThread;
 constexpr int kCheckpoints = 256;
+constexpr uint32_t kSeqRun = 32;  // groups run by one thread after each event
 constexpr long long kSat = 1ll << 60;
 constexpr long long kTwo52 = 1ll << 52;
 constexpr long long kTwo53 = 1ll << 53;
 
 enum PassMode : int { kAdd = 0, kTopP = 1, kSub = 2 };
+
+#ifdef MI_SAMPLE_TRACE
+// Diagnostic build only: %globaltimer after each phase of the last draw.
+static __device__ unsigned long long g_sample_trace[16];
+__device__ __forceinline__ void sample_trace(int i) {
+  if (threadIdx.x == 0) {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    g_sample_trace[i] = t;
+  }
+}
+#define MI_SAMPLE_TRACE_AT(i) sample_trace(i)
+#else
+#define MI_SAMPLE_TRACE_AT(i) ((void)0)
+#endif
 
 // Value of an order key (inverse of sample_key16).
 __device__ __forceinline__ float key_value(uint32_t key) {
@@ -205,6 +221,8 @@ struct Shared {
   uint32_t ckpt_group[kCheckpoints];
   double ckpt_t[kCheckpoints];
   uint32_t result;
+  uint32_t next;
+  uint2 seq[kSeqRun + 1];  // groups of a one-thread run, staged
 };
 
 // Exclusive block scan of composable elements; `total` gets the whole block's.
@@ -271,11 +289,55 @@ __device__ unsigned long long scan_u64(unsigned long long x, unsigned long long&
   return ex;
 }
 
+// Weight of a group: exp((v - max) * (1 / T)) in FP32 (sample_candidates'
+// `(value - max_logit) * inverse_temperature).exp()`), from its key.
+struct Weights {
+  float max_logit, inv_temperature;
+  __device__ __forceinline__ double of(uint32_t key) const {
+    return (double)mi_exp(__fmul_rn(__fsub_rn(key_value(key), max_logit), inv_temperature));
+  }
+};
+
+// Groups [g, limit) by thread 0, in order, from s.t, reading the staged
+// copies s.seq[g - g_seq]; stops early at a stop (recorded in s) and returns
+// the next group.
+__device__ uint32_t run_sequential(int mode, uint32_t g, uint32_t limit, uint32_t g_seq,
+                                   const Weights& w, double thr, Shared& s) {
+  double t = s.t;
+  for (; g < limit; ++g) {
+    const uint2 kc = s.seq[g - g_seq];
+    uint32_t pos;
+    if (run_steps(t, w.of(kc.x), kc.y, mode, thr, pos)) {
+      s.stopped = 1;
+      s.stop_group = g;
+      s.stop_pos = pos;
+      ++g;
+      break;
+    }
+  }
+  s.t = t;
+  return g;
+}
+
+// Stages groups [g, g + kSeqRun + 1) and runs them on thread 0 (block-wide
+// call, ends with the next group in s.next after a barrier).
+__device__ void sequential_burst(int mode, uint32_t g, uint32_t ngroups, const uint2* g_kc,
+                                 const Weights& w, double thr, Shared& s) {
+  const uint32_t limit = min(ngroups, g + kSeqRun + 1);
+  if (threadIdx.x < limit - g) s.seq[threadIdx.x] = g_kc[g + threadIdx.x];
+  __syncthreads();
+  if (threadIdx.x == 0) s.next = run_sequential(mode, g, limit, g, w, thr, s);
+  __syncthreads();
+}
+
 // One sequential FP64 pass over groups [g_start, ngroups) from t_start.
 // Leaves the final value in s.t and a stop (kTopP, kSub) in s.stopped /
-// s.stop_group / s.stop_pos. `record` keeps chunk-start checkpoints.
+// s.stop_group / s.stop_pos. `record` keeps chunk-start checkpoints. A group
+// that may cross a binade or hold the stop, with the groups after it, runs
+// on one thread (cheap for the common single-count groups); the rest are
+// scanned by the block, kChunk groups at a time.
 __device__ void run_pass(int mode, double t_start, uint32_t g_start, uint32_t ngroups,
-                         const uint32_t* g_count, const float* g_p, double thr, bool record,
+                         const uint2* g_kc, const Weights& w, double thr, bool record,
                          Shared& s) {
   const int tid = threadIdx.x;
   if (tid == 0) {
@@ -296,33 +358,34 @@ __device__ void run_pass(int mode, double t_start, uint32_t g_start, uint32_t ng
     long long T0;
     int e;
     if (!decode(t, T0, e)) {
-      // zero or subnormal running value: one group by real steps
-      if (tid == 0) {
-        double tt = t;
-        uint32_t pos;
-        if (run_steps(tt, (double)g_p[g0], g_count[g0], mode, thr, pos)) {
-          s.stopped = 1;
-          s.stop_group = g0;
-          s.stop_pos = pos;
-        }
-        s.t = tt;
-      }
+      // zero or subnormal running value: the next groups on one thread
+      sequential_burst(mode, g0, ngroups, g_kc, w, thr, s);
+      const uint32_t nx = s.next;
+      const int stopped = s.stopped;
       __syncthreads();
-      if (s.stopped) return;
-      ++g0;
+      if (stopped) return;
+      g0 = nx;
       continue;
     }
     if (tid == 0) s.bad = 0x7fffffff;
     const uint32_t base = g0 + (uint32_t)tid * kPerThread;
+    uint2 kc[kPerThread];
+    double p[kPerThread];
     Elem acc = identity();
 #pragma unroll
     for (int j = 0; j < kPerThread; ++j) {
-      uint32_t g = base + j;
-      if (g < ngroups) {
+      const uint32_t g = base + j;
+      kc[j] = g < ngroups ? g_kc[g] : make_uint2(0, 0);
+    }
+#pragma unroll
+    for (int j = 0; j < kPerThread; ++j) {
+      p[j] = 0.0;
+      if (base + j < ngroups) {
+        p[j] = w.of(kc[j].x);
         long long m;
         int cls;
-        classify((double)g_p[g], e, m, cls);
-        acc = compose(acc, group_elem(m, cls, g_count[g], sub));
+        classify(p[j], e, m, cls);
+        acc = compose(acc, group_elem(m, cls, kc[j].y, sub));
       }
     }
     Elem total;
@@ -332,12 +395,12 @@ __device__ void run_pass(int mode, double t_start, uint32_t g_start, uint32_t ng
     long long t_bad = 0;
 #pragma unroll
     for (int j = 0; j < kPerThread; ++j) {
-      uint32_t g = base + j;
+      const uint32_t g = base + j;
       if (g < ngroups && bad == 0x7fffffff) {
         long long m;
         int cls;
-        classify((double)g_p[g], e, m, cls);
-        long long tend = apply(T, group_elem(m, cls, g_count[g], sub));
+        classify(p[j], e, m, cls);
+        long long tend = apply(T, group_elem(m, cls, kc[j].y, sub));
         bool ok;
         if (cls == 3) {
           ok = false;
@@ -358,101 +421,101 @@ __device__ void run_pass(int mode, double t_start, uint32_t g_start, uint32_t ng
     if (bad != 0x7fffffff) atomicMin(&s.bad, bad);
     __syncthreads();
     const int first = s.bad;
-    if (first != 0x7fffffff && bad == first) s.t_bad = t_bad;
-    __syncthreads();
+    if (first != 0x7fffffff && bad == first) s.t = scalbn((double)t_bad, e);
     if (first == 0x7fffffff) {
+      __syncthreads();  // every thread has read s.t and s.bad
       if (tid == 0) s.t = scalbn((double)apply(T0, total), e);
       g0 = min(ngroups, g0 + (uint32_t)kChunk);
+      __syncthreads();
     } else {
-      if (tid == 0) {
-        double tt = scalbn((double)s.t_bad, e);
-        uint32_t pos;
-        if (run_steps(tt, (double)g_p[first], g_count[first], mode, thr, pos)) {
-          s.stopped = 1;
-          s.stop_group = (uint32_t)first;
-          s.stop_pos = pos;
-        }
-        s.t = tt;
-      }
-      g0 = (uint32_t)first + 1;
+      sequential_burst(mode, (uint32_t)first, ngroups, g_kc, w, thr, s);  // barrier first
+      const uint32_t nx = s.next;
+      const int stopped = s.stopped;
+      __syncthreads();
+      if (stopped) return;
+      g0 = nx;
     }
-    __syncthreads();
-    if (s.stopped) return;
   }
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
-    sample_kernel(const __half* logits, uint32_t n, uint32_t* hist, uint32_t* g_key,
-                  uint32_t* g_count, float* g_p, const uint32_t* opts,
-                  unsigned long long* state, uint32_t* token_out, const uint32_t* token_pos) {
+    sample_kernel(const __half* logits, uint32_t n, uint32_t* hist, uint2* g_kc,
+                  const uint32_t* opts, unsigned long long* state, uint32_t* token_out,
+                  const uint32_t* token_pos) {
   __shared__ Shared s;
   const int tid = threadIdx.x;
   pdl_wait();
-  const float inv_temperature = __uint_as_float(opts[0]);
   const float top_p = __uint_as_float(opts[1]);
   const uint32_t top_k = opts[2];
+  MI_SAMPLE_TRACE_AT(0);
   if (tid == 0) {
     s.ngroups_written = 0;
     s.result = 0xFFFFFFFFu;
   }
-  __syncthreads();
 
-  // 1. Groups in descending key order (first top_k candidates), histogram
-  //    cleared for the next use.
+  // 1. Groups in descending key order (the first top_k candidates); the
+  //    histogram is cleared for the next draw. Thread t owns the block of 64
+  //    keys below 65536 - 64 t: its coarse count, then (for the blocks before
+  //    the top_k cut) its 64 bins, scanned twice (candidates, groups).
   const unsigned long long cut = top_k > 0 ? (unsigned long long)top_k : ~0ull;
-  unsigned long long groups_before = 0, cands_before = 0;
-  bool cut_done = false;
-  for (int r = 0; r < 16; ++r) {
-    const int hi = 65535 - 4096 * r - 4 * tid;  // this thread: keys hi, hi-1, hi-2, hi-3
-    uint4* slot = reinterpret_cast<uint4*>(hist + (hi - 3));
-    if (!cut_done) {
-      uint4 v = *slot;
-      uint32_t c[4] = {v.w, v.z, v.y, v.x};
-      uint32_t ne = 0;
-      unsigned long long cc = 0;
+  uint32_t* coarse = hist + kSampleBins;
+  const int blk = kSampleBlocks - 1 - tid;
+  const uint32_t cblk = coarse[blk];
+  unsigned long long tot;
+  const unsigned long long c_before = scan_u64(cblk, tot, s);  // ends with a barrier
+  const unsigned long long cands_total = tot;
+  const bool needed = cblk != 0 && c_before < cut;
+  uint4* mine = reinterpret_cast<uint4*>(hist + 64 * blk);  // mine[j]: keys 64 blk + 4j .. + 3
+  uint32_t ne = 0;
+  if (needed) {
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        ne += c[i] != 0;
-        cc += c[i];
-      }
-      unsigned long long tot;
-      unsigned long long ex = scan_u64((cc << 13) | ne, tot, s);
-      unsigned long long g = groups_before + (ex & 0x1fff);
-      unsigned long long cb = cands_before + (ex >> 13);
+    for (int j = 0; j < 16; ++j) {
+      const uint4 v = mine[j];
+      ne += (v.x != 0) + (v.y != 0) + (v.z != 0) + (v.w != 0);
+    }
+  }
+  const unsigned long long g_before = scan_u64(ne, tot, s);
+  const uint32_t groups_total = (uint32_t)tot;
+  if (needed) {
+    unsigned long long g = g_before, cb = c_before;
+    for (int j = 15; j >= 0; --j) {
+      const uint4 v = mine[j];
+      const uint32_t c[4] = {v.w, v.z, v.y, v.x};  // descending keys
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         if (c[i] == 0) continue;
         if (cb < cut) {
-          unsigned long long keep = cut - cb;
-          g_key[g] = (uint32_t)(hi - i);
-          g_count[g] = keep < c[i] ? (uint32_t)keep : c[i];
-          atomicMax(&s.ngroups_written, (uint32_t)(g + 1));
+          const unsigned long long keep = cut - cb;
+          g_kc[g] = make_uint2((uint32_t)(64 * blk + 4 * j + 3 - i),
+                               keep < c[i] ? (uint32_t)keep : c[i]);
+          if (keep <= c[i]) s.ngroups_written = (uint32_t)(g + 1);  // the group reaching top_k
         }
         ++g;
         cb += c[i];
       }
-      groups_before += tot & 0x1fff;
-      cands_before += tot >> 13;
-      cut_done = cands_before >= cut;
     }
-    *slot = make_uint4(0, 0, 0, 0);
+  }
+  if (cblk != 0) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) mine[j] = make_uint4(0, 0, 0, 0);
+    coarse[blk] = 0;
   }
   __syncthreads();
-  const uint32_t ngroups = s.ngroups_written;
+  MI_SAMPLE_TRACE_AT(1);
+  const uint32_t ngroups = cands_total >= cut ? s.ngroups_written : groups_total;
   if (ngroups == 0) {
     if (tid == 0) token_out[token_pos ? *token_pos : 0] = 0xFFFFFFFFu;
     return;
   }
-
-  // 2. Weights exp((v - max) * (1 / T)) in FP32.
-  const float max_logit = key_value(g_key[0]);
-  for (uint32_t g = tid; g < ngroups; g += kThreads)
-    g_p[g] = mi_exp(__fmul_rn(__fsub_rn(key_value(g_key[g]), max_logit), inv_temperature));
-  __syncthreads();
+  Weights w;
+  w.max_logit = key_value(g_kc[0].x);
+  w.inv_temperature = __uint_as_float(opts[0]);
+  MI_SAMPLE_TRACE_AT(2);
 
   // 3. Total.
-  run_pass(kAdd, 0.0, 0, ngroups, g_count, g_p, 0.0, true, s);
+  run_pass(kAdd, 0.0, 0, ngroups, g_kc, w, 0.0, true, s);
   double total = s.t;
+  MI_SAMPLE_TRACE_AT(3);
   uint32_t kept = ngroups;
 
   // 4. Top-p: the prefix whose running sum first reaches total * top_p, from
@@ -467,36 +530,40 @@ __global__ void __launch_bounds__(kThreads, 1)
         t_start = s.ckpt_t[i];
       }
     __syncthreads();
-    run_pass(kTopP, t_start, g_start, ngroups, g_count, g_p, thr, false, s);
+    run_pass(kTopP, t_start, g_start, ngroups, g_kc, w, thr, false, s);
     if (s.stopped) {  // always, as the full sum reaches the threshold
       kept = s.stop_group + 1;
-      if (tid == 0) g_count[s.stop_group] = s.stop_pos + 1;
+      if (tid == 0) g_kc[s.stop_group].y = s.stop_pos + 1;
       total = s.t;
     }
     __syncthreads();
   }
 
+  MI_SAMPLE_TRACE_AT(4);
   // 5. XorShift64 draw and the walk.
   __shared__ double s_target;
   if (tid == 0) {
-    unsigned long long v = *state;
-    v ^= v << 13;
-    v ^= v >> 7;
-    v ^= v << 17;
-    *state = v;
-    s_target = __dmul_rn(__ull2double_rn(v) * 0x1p-64, total);
+    unsigned long long x = *state;
+    x ^= x << 13;
+    x ^= x >> 7;
+    x ^= x << 17;
+    *state = x;
+    s_target = __dmul_rn(__ull2double_rn(x) * 0x1p-64, total);
   }
   __syncthreads();
-  run_pass(kSub, s_target, 0, kept, g_count, g_p, 0.0, false, s);
+  run_pass(kSub, s_target, 0, kept, g_kc, w, 0.0, false, s);
+  MI_SAMPLE_TRACE_AT(5);
   if (!s.stopped) {
     if (tid == 0) token_out[token_pos ? *token_pos : 0] = 0xFFFFFFFEu;
     return;
   }
-  const uint32_t key = g_key[s.stop_group];
+  const uint32_t key = g_kc[s.stop_group].x;
   const uint32_t want = s.stop_pos;
-  const uint16_t bits = key_bits(key);
+  const uint32_t bits = key_bits(key);
 
-  // 6. The want-th occurrence (index order) of the chosen value.
+  // 6. The want-th occurrence (index order) of the chosen value: counts over
+  //    contiguous per-thread ranges (loads batched), a block scan, then the
+  //    owning thread finds it.
   const uint32_t per = (((n + kThreads - 1) / kThreads) + 7) & ~7u;
   const uint32_t begin = min(n, (uint32_t)tid * per);
   const uint32_t end = min(n, begin + per);
@@ -505,19 +572,29 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t cnt = 0;
   uint32_t i = begin;
   if (vec) {
-    for (; i + 8 <= end; i += 8) {
-      uint4 v = *reinterpret_cast<const uint4*>(lb + i);
-      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    const uint32_t bb = bits | (bits << 16);
+    for (; i + 64 <= end; i += 64) {
+      uint4 q4[8];
 #pragma unroll
-      for (int q = 0; q < 4; ++q)
-        cnt += ((w[q] & 0xffffu) == bits) + ((w[q] >> 16) == bits);
+      for (int q = 0; q < 8; ++q) q4[q] = *reinterpret_cast<const uint4*>(lb + i + 8 * q);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const uint32_t x4[4] = {q4[q].x ^ bb, q4[q].y ^ bb, q4[q].z ^ bb, q4[q].w ^ bb};
+#pragma unroll
+        for (int r = 0; r < 4; ++r) cnt += ((x4[r] & 0xffffu) == 0) + ((x4[r] >> 16) == 0);
+      }
+    }
+    for (; i + 8 <= end; i += 8) {
+      const uint4 q4 = *reinterpret_cast<const uint4*>(lb + i);
+      const uint32_t x4[4] = {q4.x ^ bb, q4.y ^ bb, q4.z ^ bb, q4.w ^ bb};
+#pragma unroll
+      for (int r = 0; r < 4; ++r) cnt += ((x4[r] & 0xffffu) == 0) + ((x4[r] >> 16) == 0);
     }
   }
   for (; i < end; ++i) cnt += lb[i] == bits;
-  unsigned long long tot;
-  const unsigned long long ex = scan_u64(cnt, tot, s);
-  if (want >= ex && want < ex + cnt) {
-    uint32_t left = want - (uint32_t)ex;
+  const unsigned long long before = scan_u64(cnt, tot, s);
+  if (want >= before && want < before + cnt) {
+    uint32_t left = want - (uint32_t)before;
     for (uint32_t j = begin; j < end; ++j)
       if (lb[j] == bits) {
         if (left == 0) {
@@ -528,31 +605,39 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
   }
   __syncthreads();
+  MI_SAMPLE_TRACE_AT(6);
   if (tid == 0) token_out[token_pos ? *token_pos : 0] = s.result;
 }
 
-__global__ void logit_histogram_kernel(const __half* logits, uint32_t n, uint32_t* hist) {
+// Blocks of kHistSeg logits: keys sorted in shared memory, one pair of
+// atomics per distinct key (no contention on frequent values).
+constexpr int kHistSeg = 2048;
+__global__ void __launch_bounds__(256) logit_histogram_kernel(const __half* logits, uint32_t n,
+                                                              uint32_t* hist) {
+  __shared__ __align__(16) uint16_t keys[kHistSeg + 2048];  // keys, then 1024 block counts
   pdl_wait();
-  const uint16_t* lb = reinterpret_cast<const uint16_t*>(logits);
-  for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
-    uint16_t b = lb[i];
-    if ((b & 0x7c00u) != 0x7c00u) atomicAdd(hist + sample_key16(b), 1u);
-  }
+  const int first = (int)(blockIdx.x * kHistSeg);
+  hist_add_rows(reinterpret_cast<const uint16_t*>(logits), first,
+                (int)min(n, (uint32_t)first + kHistSeg), keys, kHistSeg, hist);
 }
 
 }  // namespace
 
+#ifdef MI_SAMPLE_TRACE
+extern "C" int mi_debug_sample_trace(unsigned long long* out) {
+  return cudaMemcpyFromSymbol(out, g_sample_trace, sizeof(g_sample_trace)) == cudaSuccess ? 0 : -1;
+}
+#endif
+
 void logit_histogram(const Launch& l, const __half* logits, uint32_t n, uint32_t* hist) {
-  int grid = min(l.sm_count * 4, (int)((n + 255) / 256));
-  if (grid < 1) grid = 1;
-  launch_kernel(l, dim3(grid), dim3(256), 0, logit_histogram_kernel, logits, n, hist);
+  const int grid = (int)((n + kHistSeg - 1) / kHistSeg);
+  if (grid > 0) launch_kernel(l, dim3(grid), dim3(256), 0, logit_histogram_kernel, logits, n, hist);
 }
 
 void sample(const Launch& l, const SampleProblem& p) {
   launch_kernel(l, dim3(1), dim3(kThreads), 0, sample_kernel, p.logits, p.n, p.hist,
-                p.groups, p.groups + kSampleBins, reinterpret_cast<float*>(p.groups + 2 * kSampleBins),
-                p.opts, reinterpret_cast<unsigned long long*>(p.state), p.token_out,
-                p.token_pos);
+                reinterpret_cast<uint2*>(p.groups), p.opts,
+                reinterpret_cast<unsigned long long*>(p.state), p.token_out, p.token_pos);
 }
 
 }  // namespace k
