@@ -259,8 +259,10 @@ def run_ours(args, rank, world, local_rank):
     # the lm_head's key histogram and the one-CTA sampler after every head.
     # Decode rate = 64 steps / (time of a 65-token call - a 1-token call).
     sampled = {}
-    for label, opts in (("top_k20_top_p0.95_t0.6", dict(temperature=0.6, top_p=0.95, top_k=20)),
-                        ("full_vocab_t1.0", dict(temperature=1.0, top_p=1.0, top_k=0))):
+    sampled_cases = [] if args.no_sampled_report else [
+        ("top_k20_top_p0.95_t0.6", dict(temperature=0.6, top_p=0.95, top_k=20)),
+        ("full_vocab_t1.0", dict(temperature=1.0, top_p=1.0, top_k=0))]
+    for label, opts in sampled_cases:
         opts = dict(opts, seed=SEED)
         model.generate_with(prompt_ptr, dict(opts, max_tokens=17), cache)  # graph capture
         spans = []
@@ -494,6 +496,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-sampled-report", action="store_true",
+                    help="skip the untimed sampled-decode report (short profiling runs)")
     ap.add_argument("--cpu-sample-steps", type=int, default=48)
     ap.add_argument("--cpu-sample-steps-ref", type=int, default=8)
     ap.add_argument("--decode-steps", type=int, default=DECODE,
