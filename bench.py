@@ -278,12 +278,12 @@ def run_ours(args, rank, world, local_rank):
         prof_s = ctx.take_kernel_profiles()
         ctx.set_kernel_profiling(False)
         smp = [s for n, s in prof_s if n == "sample"]
-        head = [s for n, s in prof_s if n == "lm_head_argmax"]
+        hist = [s for n, s in prof_s if n == "sample_histogram"]
         sampled[label] = {
             "decode_tokens_per_s": round(64 / max(spans[1] - spans[0], 1e-9), 1),
-            "note": "generate_with, host clock, decode chain (CUDA graph) + sampler",
+            "note": "generate_with, host clock: persistent kernel one step per launch + histogram + sampler",
             "sample_kernel_us": round(sum(smp) / len(smp) * 1e6, 2) if smp else None,
-            "lm_head_with_histogram_us": round(sum(head) / len(head) * 1e6, 2) if head else None,
+            "histogram_kernel_us": round(sum(hist) / len(hist) * 1e6, 2) if hist else None,
         }
 
     kv_mean = PROMPT + (DECODE + 1) / 2.0

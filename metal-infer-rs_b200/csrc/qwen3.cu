@@ -271,9 +271,10 @@ void ensure_sampling(mi_qwen3* m) {
 }
 
 // The lm_head's logits -> tokens[*pos] (tokens[0] without pos), drawn by the
-// sampler. One GPU: the lm_head GEMV filled the key histogram. Tensor
-// parallelism: every rank gathers the full logits and draws the same token.
-void encode_sample(mi_qwen3* m, uint32_t* tokens, const uint32_t* pos) {
+// sampler. One GPU: the lm_head GEMV filled the key histogram (hist_built),
+// else the histogram kernel builds it. Tensor parallelism: every rank gathers
+// the full logits and draws the same token.
+void encode_sample(mi_qwen3* m, uint32_t* tokens, const uint32_t* pos, bool hist_built) {
   auto& w = m->ws;
   k::SampleProblem sp;
   sp.logits = w.logits.h();
@@ -283,6 +284,10 @@ void encode_sample(mi_qwen3* m, uint32_t* tokens, const uint32_t* pos) {
     tp_allgather(m, w.logits.t->base(), w.smp_logits.t->base(), m->cfg.vocab_size, 2);
     sp.logits = w.smp_logits.h();
     sp.n = (uint32_t)m->full_cfg.vocab_size;
+    ProfileScope ph(m->ctx, "sample_histogram");
+    k::logit_histogram(launch(m, false), sp.logits, sp.n, sp.hist);
+  } else if (!hist_built) {
+    ProfileScope ph(m->ctx, "sample_histogram");
     k::logit_histogram(launch(m, false), sp.logits, sp.n, sp.hist);
   }
   sp.groups = w.smp_groups.t->u32();
@@ -504,7 +509,7 @@ void encode_decode_step(mi_qwen3* m, mi_kv_cache* c) {
     }
     if (m->tp > 1) tp_argmax(m, c->toks.t->u32(), len, len);
     // the step counter has advanced: the token goes to toks[*len]
-    if (m->sampling) encode_sample(m, c->toks.t->u32(), len);
+    if (m->sampling) encode_sample(m, c->toks.t->u32(), len, true);
   }
 }
 
@@ -521,7 +526,7 @@ bool persistent_env() {
 
 bool decode_loop_ready(mi_qwen3* m) {
   if ((m->tp > 1 && !m->mbox.local) || !m->persistent || !persistent_env() ||
-      !fused_decode_supported(m) || m->sampling)
+      !fused_decode_supported(m))
     return false;
   if (m->loop_state == 0) {
     const auto& c = m->cfg;
@@ -626,6 +631,23 @@ void run_decode_loop(mi_qwen3* m, mi_kv_cache* c, size_t steps) {
     m->mbox.ctr_base[1] += per_step * p.steps * p.layers;
     m->mbox.ctr_base[2] += per_step * p.steps;
     done += (size_t)p.steps;
+  }
+}
+
+// `n` steps through the persistent kernel: one launch when greedy; when
+// sampling, one launch per step, each followed by the histogram and the
+// sampler, which overwrite the greedy id at toks[*dev_len] before the next
+// launch embeds it.
+void run_persistent_steps(mi_qwen3* m, mi_kv_cache* c, size_t n) {
+  if (!m->sampling) {
+    run_decode_loop(m, c, n);
+    c->filled += n;
+    return;
+  }
+  for (size_t i = 0; i < n; ++i) {
+    run_decode_loop(m, c, 1);
+    encode_sample(m, c->toks.t->u32(), c->dev_len.t->u32(), false);
+    c->filled += 1;
   }
 }
 
@@ -791,8 +813,7 @@ void forward_tokens(mi_qwen3* m, mi_kv_cache* c, size_t T) {
   ensure_workspace(m, c->capacity);
   size_t off = c->filled;
   if (T == 1 && decode_loop_ready(m)) {
-    run_decode_loop(m, c, 1);
-    c->filled += 1;
+    run_persistent_steps(m, c, 1);
     return;
   }
   if (T == 1 && fused_decode_supported(m)) {
@@ -828,7 +849,7 @@ void forward_tokens(mi_qwen3* m, mi_kv_cache* c, size_t T) {
   if (m->sampling && m->tp == 1) p.hist = w.smp_hist.t->u32();
   k::gemv(l, p);
   if (m->tp > 1) tp_argmax(m, c->toks.t->u32() + off + T, nullptr, nullptr);
-  if (m->sampling) encode_sample(m, c->toks.t->u32() + off + T, nullptr);
+  if (m->sampling) encode_sample(m, c->toks.t->u32() + off + T, nullptr, true);
   c->filled = off + T;
   set_dev_len(c, c->filled);
 }
@@ -1387,12 +1408,11 @@ mi_status mi_qwen3_decode_argmax(mi_qwen3* m, const mi_tensor* token, mi_kv_cach
 
 namespace {
 
-// `n` greedy decode steps from the cache's device position.
+// `n` decode steps from the cache's device position.
 void decode_steps(mi_qwen3* m, mi_kv_cache* c, size_t n) {
   if (n == 0) return;
   if (decode_loop_ready(m)) {
-    run_decode_loop(m, c, n);
-    c->filled += n;
+    run_persistent_steps(m, c, n);
     return;
   }
   for (size_t i = 0; i < n; ++i) forward_tokens(m, c, 1);
