@@ -37,7 +37,8 @@ constexpr int kWarps = kThreads / 32;
 constexpr int kPerThread = 4;  // groups per thread per chunk
 constexpr int kChunk = kThreads * kPerThread;
 constexpr int kCheckpoints = 256;
-constexpr uint32_t kSeqRun = 32;  // groups run by one thread after each event
+constexpr uint32_t kSeqTail = 64;  // a tail this short runs on one thread
+constexpr uint32_t kBurst = 32;    // one-thread run after an event close to the last
 constexpr long long kSat = 1ll << 60;
 constexpr long long kTwo52 = 1ll << 52;
 constexpr long long kTwo53 = 1ll << 53;
@@ -71,9 +72,12 @@ __device__ __forceinline__ uint16_t key_bits(uint32_t key) {
 __device__ __forceinline__ long long sat(long long v) {
   return v > kSat ? kSat : (v < -kSat ? -kSat : v);
 }
+// n * d for n, d >= 0, saturated at kSat (no division: the high half of the
+// 128-bit product).
 __device__ __forceinline__ long long mul_sat(long long n, long long d) {
-  if (d != 0 && n > kSat / d) return kSat;
-  return n * d;
+  const unsigned long long un = (unsigned long long)n, ud = (unsigned long long)d;
+  const unsigned long long lo = un * ud;
+  return (__umul64hi(un, ud) != 0 || lo > (unsigned long long)kSat) ? kSat : (long long)lo;
 }
 
 // t = T * 2^e with T in [2^52, 2^53); false for zero, subnormal, negative or
@@ -87,9 +91,16 @@ __device__ __forceinline__ bool decode(double t, long long& T, int& e) {
   return true;
 }
 
+// v * 2^k, exact: one multiply by a power of two built from its exponent
+// bits when 2^k is a normal double, scalbn otherwise.
+__device__ __forceinline__ double times_pow2(double v, int k) {
+  if (k >= -1022 && k <= 1023) return v * __longlong_as_double((long long)(k + 1023) << 52);
+  return scalbn(v, k);
+}
+
 // p / 2^e = m + f: class 0 (f < 1/2), 1 (f > 1/2), 2 (f == 1/2), 3 (too large).
 __device__ __forceinline__ void classify(double p, int e, long long& m, int& cls) {
-  double x = scalbn(p, -e);
+  double x = times_pow2(p, -e);
   if (!(x < 0x1p62)) {
     m = 0;
     cls = 3;
@@ -186,13 +197,13 @@ __device__ bool run_steps(double& t, double p, uint32_t count, int mode, double 
       if (room < 0) continue;
       n = d == 0 ? rem : min(rem, room / d + 1);
       if (mode == kTopP && d > 0) {
-        double thr_t = scalbn(thr, -e);
+        double thr_t = times_pow2(thr, -e);
         if (thr_t < 0x1p62) {
           long long need = (long long)ceil(thr_t) - T;  // >= 1 since t < thr
           long long jt = (need + d - 1) / d;
           if (jt <= n) {
             T += jt * d;
-            t = scalbn((double)T, e);
+            t = times_pow2((double)T, e);
             done += (uint32_t)jt;
             pos = done - 1;
             return true;
@@ -201,7 +212,7 @@ __device__ bool run_steps(double& t, double p, uint32_t count, int mode, double 
       }
       T += n * d;
     }
-    t = scalbn((double)T, e);
+    t = times_pow2((double)T, e);
     done += (uint32_t)n;
   }
   pos = count;
@@ -222,7 +233,7 @@ struct Shared {
   double ckpt_t[kCheckpoints];
   uint32_t result;
   uint32_t next;
-  uint2 seq[kSeqRun + 1];  // groups of a one-thread run, staged
+  uint2 seq[kSeqTail];  // groups of a one-thread run, staged
 };
 
 // Exclusive block scan of composable elements; `total` gets the whole block's.
@@ -299,10 +310,9 @@ struct Weights {
 };
 
 // Groups [g, limit) by thread 0, in order, from s.t, reading the staged
-// copies s.seq[g - g_seq]; stops early at a stop (recorded in s) and returns
-// the next group.
-__device__ uint32_t run_sequential(int mode, uint32_t g, uint32_t limit, uint32_t g_seq,
-                                   const Weights& w, double thr, Shared& s) {
+// copies s.seq[g - g_seq]; stops early at a stop (recorded in s).
+__device__ void run_sequential(int mode, uint32_t g, uint32_t limit, uint32_t g_seq,
+                               const Weights& w, double thr, Shared& s) {
   double t = s.t;
   for (; g < limit; ++g) {
     const uint2 kc = s.seq[g - g_seq];
@@ -311,31 +321,20 @@ __device__ uint32_t run_sequential(int mode, uint32_t g, uint32_t limit, uint32_
       s.stopped = 1;
       s.stop_group = g;
       s.stop_pos = pos;
-      ++g;
       break;
     }
   }
   s.t = t;
-  return g;
-}
-
-// Stages groups [g, g + kSeqRun + 1) and runs them on thread 0 (block-wide
-// call, ends with the next group in s.next after a barrier).
-__device__ void sequential_burst(int mode, uint32_t g, uint32_t ngroups, const uint2* g_kc,
-                                 const Weights& w, double thr, Shared& s) {
-  const uint32_t limit = min(ngroups, g + kSeqRun + 1);
-  if (threadIdx.x < limit - g) s.seq[threadIdx.x] = g_kc[g + threadIdx.x];
-  __syncthreads();
-  if (threadIdx.x == 0) s.next = run_sequential(mode, g, limit, g, w, thr, s);
-  __syncthreads();
 }
 
 // One sequential FP64 pass over groups [g_start, ngroups) from t_start.
 // Leaves the final value in s.t and a stop (kTopP, kSub) in s.stopped /
-// s.stop_group / s.stop_pos. `record` keeps chunk-start checkpoints. A group
-// that may cross a binade or hold the stop, with the groups after it, runs
-// on one thread (cheap for the common single-count groups); the rest are
-// scanned by the block, kChunk groups at a time.
+// s.stop_group / s.stop_pos. `record` keeps checkpoints (group, value).
+// Chunks of kChunk groups are loaded once into registers (key, count,
+// weight); the block scans the chunk in the current binade, one thread runs
+// the first group that may cross the binade or hold the stop, and the scan
+// resumes behind it in the new binade. A short tail (top_k lists) runs on
+// one thread from shared memory.
 __device__ void run_pass(int mode, double t_start, uint32_t g_start, uint32_t ngroups,
                          const uint2* g_kc, const Weights& w, double thr, bool record,
                          Shared& s) {
@@ -348,93 +347,117 @@ __device__ void run_pass(int mode, double t_start, uint32_t g_start, uint32_t ng
   __syncthreads();
   const bool sub = mode == kSub;
   uint32_t g0 = g_start;
+  uint32_t last_event = 0xffffffffu;  // where the previous one-thread run began
   while (g0 < ngroups) {
-    const double t = s.t;
-    if (record && tid == 0 && s.ckpt_count < kCheckpoints) {
-      s.ckpt_group[s.ckpt_count] = g0;
-      s.ckpt_t[s.ckpt_count] = t;
-      ++s.ckpt_count;
-    }
-    long long T0;
-    int e;
-    if (!decode(t, T0, e)) {
-      // zero or subnormal running value: the next groups on one thread
-      sequential_burst(mode, g0, ngroups, g_kc, w, thr, s);
-      const uint32_t nx = s.next;
-      const int stopped = s.stopped;
+    if (ngroups - g0 <= kSeqTail) {
+      if (tid < ngroups - g0) s.seq[tid] = g_kc[g0 + tid];
+      if (record && tid == 0 && s.ckpt_count < kCheckpoints) {
+        s.ckpt_group[s.ckpt_count] = g0;
+        s.ckpt_t[s.ckpt_count] = s.t;
+        ++s.ckpt_count;
+      }
       __syncthreads();
-      if (stopped) return;
-      g0 = nx;
-      continue;
+      if (tid == 0) run_sequential(mode, g0, ngroups, g0, w, thr, s);
+      __syncthreads();
+      return;
     }
-    if (tid == 0) s.bad = 0x7fffffff;
+    const uint32_t chunk_end = min(ngroups, g0 + (uint32_t)kChunk);
     const uint32_t base = g0 + (uint32_t)tid * kPerThread;
     uint2 kc[kPerThread];
-    double p[kPerThread];
-    Elem acc = identity();
+    double pw[kPerThread];
 #pragma unroll
     for (int j = 0; j < kPerThread; ++j) {
       const uint32_t g = base + j;
-      kc[j] = g < ngroups ? g_kc[g] : make_uint2(0, 0);
+      kc[j] = g < chunk_end ? g_kc[g] : make_uint2(0, 0);
+      pw[j] = g < chunk_end ? w.of(kc[j].x) : 0.0;
     }
-#pragma unroll
-    for (int j = 0; j < kPerThread; ++j) {
-      p[j] = 0.0;
-      if (base + j < ngroups) {
-        p[j] = w.of(kc[j].x);
-        long long m;
-        int cls;
-        classify(p[j], e, m, cls);
-        acc = compose(acc, group_elem(m, cls, kc[j].y, sub));
+    uint32_t start = g0;  // first group of the chunk still to run
+    while (start < chunk_end) {
+      const double t = s.t;
+      if (record && tid == 0 && s.ckpt_count < kCheckpoints) {
+        s.ckpt_group[s.ckpt_count] = start;
+        s.ckpt_t[s.ckpt_count] = t;
+        ++s.ckpt_count;
       }
-    }
-    Elem total;
-    Elem ex = scan_elems(acc, total, s);  // ends with a barrier (s.bad is set)
-    long long T = apply(T0, ex);
-    int bad = 0x7fffffff;
-    long long t_bad = 0;
+      long long T0;
+      int e;
+      const bool normal = decode(t, T0, e);
+      if (tid == 0) s.bad = normal ? 0x7fffffff : (int)start;  // zero / subnormal: one thread
+      long long gm[kPerThread];
+      int gc[kPerThread];
+      Elem acc = identity();
 #pragma unroll
-    for (int j = 0; j < kPerThread; ++j) {
-      const uint32_t g = base + j;
-      if (g < ngroups && bad == 0x7fffffff) {
-        long long m;
-        int cls;
-        classify(p[j], e, m, cls);
-        long long tend = apply(T, group_elem(m, cls, kc[j].y, sub));
-        bool ok;
-        if (cls == 3) {
-          ok = false;
-        } else if (sub) {
-          ok = tend >= kTwo52 + 1;
-        } else {
-          ok = tend + m <= kTwo53 - 1;
-          if (ok && mode == kTopP) ok = scalbn((double)tend, e) < thr;
-        }
-        if (!ok) {
-          bad = (int)g;
-          t_bad = T;
-        } else {
-          T = tend;
+      for (int j = 0; j < kPerThread; ++j) {
+        const uint32_t g = base + j;
+        gm[j] = 0;
+        gc[j] = 0;
+        if (normal && g >= start && g < chunk_end) {
+          classify(pw[j], e, gm[j], gc[j]);
+          acc = compose(acc, group_elem(gm[j], gc[j], kc[j].y, sub));
         }
       }
-    }
-    if (bad != 0x7fffffff) atomicMin(&s.bad, bad);
-    __syncthreads();
-    const int first = s.bad;
-    if (first != 0x7fffffff && bad == first) s.t = scalbn((double)t_bad, e);
-    if (first == 0x7fffffff) {
-      __syncthreads();  // every thread has read s.t and s.bad
-      if (tid == 0) s.t = scalbn((double)apply(T0, total), e);
-      g0 = min(ngroups, g0 + (uint32_t)kChunk);
+      Elem total;
+      const Elem ex = scan_elems(acc, total, s);  // ends with a barrier (s.bad is set)
+      int bad = 0x7fffffff;
+      long long t_bad = 0;
+      if (normal) {
+        long long T = apply(T0, ex);
+#pragma unroll
+        for (int j = 0; j < kPerThread; ++j) {
+          const uint32_t g = base + j;
+          if (g >= start && g < chunk_end && bad == 0x7fffffff) {
+            const long long m = gm[j];
+            const int cls = gc[j];
+            const long long tend = apply(T, group_elem(m, cls, kc[j].y, sub));
+            bool ok;
+            if (cls == 3) {
+              ok = false;
+            } else if (sub) {
+              ok = tend >= kTwo52 + 1;
+            } else {
+              ok = tend + m <= kTwo53 - 1;
+              if (ok && mode == kTopP) ok = times_pow2((double)tend, e) < thr;
+            }
+            if (!ok) {
+              bad = (int)g;
+              t_bad = T;
+            } else {
+              T = tend;
+            }
+          }
+        }
+        if (bad != 0x7fffffff) atomicMin(&s.bad, bad);
+      }
       __syncthreads();
-    } else {
-      sequential_burst(mode, (uint32_t)first, ngroups, g_kc, w, thr, s);  // barrier first
-      const uint32_t nx = s.next;
+      const int first = s.bad;
+      if (first == 0x7fffffff) {
+        __syncthreads();  // every thread has read s.bad
+        if (tid == 0) s.t = times_pow2((double)apply(T0, total), e);
+        start = chunk_end;
+        __syncthreads();
+        break;
+      }
+      // One thread runs the group, and, where events come close together
+      // (the first binades of a sum), the kBurst groups after it: a block
+      // scan per event would cost more there. The owners stage the groups
+      // (and, in a binade, the value before the first).
+      const uint32_t f = (uint32_t)first;
+      const uint32_t len =
+          min(chunk_end - f, (last_event != 0xffffffffu && f - last_event <= 64u) ? kBurst : 1u);
+      last_event = f;
+#pragma unroll
+      for (int j = 0; j < kPerThread; ++j)
+        if (base + j >= f && base + j < f + len) s.seq[base + j - f] = kc[j];
+      if (normal && f >= base && f < base + kPerThread) s.t = times_pow2((double)t_bad, e);
+      __syncthreads();
+      if (tid == 0) run_sequential(mode, f, f + len, f, w, thr, s);
+      __syncthreads();
       const int stopped = s.stopped;
       __syncthreads();
       if (stopped) return;
-      g0 = nx;
+      start = f + len;
     }
+    g0 = chunk_end;
   }
 }
 
