@@ -959,10 +959,14 @@ __device__ void attention_prefetch(const DecodeLoop& p, const LoopLayer& L, int 
   const int begin = b * p.block;
   const int end = min(pos + 1, begin + p.block);
   stage_keys<G>(L, p.kvh, g_kv, begin, min(end, begin + kTile), pos, sm);
+  // the norms and the RoPE row are copied asynchronously too: these warps
+  // join the QKV stage's input barrier next, which must not wait on them
   const int tid = atid();
-  if (tid < 16) reinterpret_cast<uint4*>(sm.qn_w)[tid] = __ldg(reinterpret_cast<const uint4*>(L.q_norm) + tid);
-  else if (tid < 32) reinterpret_cast<uint4*>(sm.kn_w)[tid - 16] = __ldg(reinterpret_cast<const uint4*>(L.k_norm) + tid - 16);
-  else if (tid < 32 + HD / 2 && p.rope) sm.rope[tid - 32] = __ldg(p.rope + (size_t)pos * (HD / 2) + (tid - 32));
+  if (tid < 16) pipe::cp_async16(&sm.qn_w[8 * tid], L.q_norm + 8 * tid);
+  else if (tid < 32) pipe::cp_async16(&sm.kn_w[8 * (tid - 16)], L.k_norm + 8 * (tid - 16));
+  else if (tid < 32 + HD / 4 && p.rope)
+    pipe::cp_async16(&sm.rope[2 * (tid - 32)], p.rope + (size_t)pos * (HD / 2) + 2 * (tid - 32));
+  pipe::cp_async_commit();
 }
 
 // QK-norm + RoPE of one head half-warp from the prefetched shared copies
@@ -1004,8 +1008,10 @@ __device__ void attention_unit(const DecodeLoop& p, const LoopLayer& L, int g_kv
   const int end = min(Lk, begin + p.block);
   const int ntiles = (end - begin + kTile - 1) / kTile;
 
-  // every CTA's QKV rows are out (the tags then validate each word)
+  // every CTA's QKV rows are out (the tags then validate each word); this
+  // thread's prefetched copies (norms, RoPE row, first key tile) have landed
   if (t == 0) stage_ready(p, kQKV, sh);
+  pipe::cp_async_wait_all();
   attn_sync();
   {
     const int hq = t >> 4;  // one query head per half-warp
