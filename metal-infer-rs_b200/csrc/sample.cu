@@ -634,7 +634,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // Blocks of kHistSeg logits: keys sorted in shared memory, one pair of
 // atomics per distinct key (no contention on frequent values).
-constexpr int kHistSeg = 2048;
+constexpr int kHistSeg = 256;  // keys per block (smaller sorts: more blocks, fewer stages)
 __global__ void __launch_bounds__(256) logit_histogram_kernel(const __half* logits, uint32_t n,
                                                               uint32_t* hist) {
   __shared__ __align__(16) uint16_t keys[kHistSeg + 2048];  // keys, then 1024 block counts
