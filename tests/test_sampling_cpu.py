@@ -126,3 +126,40 @@ def test_oracle_generate_sampled_is_seeded():
     e = m.generate_sampled(prompt, 6, 1.0, 1.0, 0, seed=0x9E3779B97F4A7C15)
     assert np.array_equal(d, e)
     assert VOCAB == 151936
+
+
+@pytest.mark.parametrize("case", ["normal", "ties", "zeros", "peaked"])
+@pytest.mark.parametrize("opt", [(1.0, 1.0, 0), (0.6, 0.9, 0), (2.5, 0.5, 0), (0.05, 1.0, 0)])
+def test_parallel_pass_algorithm_matches_sequential(case, opt):
+    """The GPU sampler's scan + event algorithm (restated in sampler_model)
+    picks the same candidate as the sequential oracle, with chunks of 8
+    groups so that chunk boundaries, binade crossings, ties and jumps occur."""
+    from sampler_model import sample_model
+    temperature, top_p, _ = opt
+    bits = logits_case(case, seed=4)
+    finite = (bits & 0x7C00) != 0x7C00
+    keys = [int(k) for k in order_key(bits)[finite]]
+    vals = {}
+    inv = np.float32(1.0) / np.float32(temperature)
+
+    def value(key):
+        b = (key & 0x7FFF) if key & 0x8000 else ((~key) & 0xFFFF)
+        return np.array([b], np.uint16).view(np.float16).astype(np.float32)[0]
+    kmax = max(keys)
+
+    def weight(key):
+        if key not in vals:
+            z = np.float32(np.float32(value(key) - value(kmax)) * inv)
+            vals[key] = float(O.exp(np.array([z], np.float32))[0])
+        return vals[key]
+    state = O.xorshift_seed(21)
+    for _ in range(5):
+        tok, nxt = O.sample(bits, temperature, top_p, 0, state)
+        _, u = xorshift_next(state)
+        state = nxt
+        gkeys, stop = sample_model(keys, weight, float(np.float32(top_p)), u)
+        assert stop is not None
+        key = gkeys[stop[0]]
+        b = (key & 0x7FFF) if key & 0x8000 else ((~key) & 0xFFFF)
+        idx = int(np.nonzero(bits == b)[0][stop[1]])
+        assert idx == tok
