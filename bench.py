@@ -417,17 +417,26 @@ def run_reference(args, rank):
     print(json.dumps(line), flush=True)
 
 
-# ---- tensor-parallel workload (Qwen3-8B) ----------------------------
+# ---- tensor-parallel workloads (BASELINE configs 3 and 4) ----------------------------
 CONFIG_8B = dict(hidden_size=4096, intermediate_size=12288, num_hidden_layers=36,
                  num_attention_heads=32, num_key_value_heads=8, head_dim=128, rms_norm_eps=1e-6,
                  rope_theta=1e6, vocab_size=151936, tie_word_embeddings=0)
+CONFIG_32B = dict(hidden_size=5120, intermediate_size=25600, num_hidden_layers=64,
+                  num_attention_heads=64, num_key_value_heads=8, head_dim=128, rms_norm_eps=1e-6,
+                  rope_theta=1e6, vocab_size=151936, tie_word_embeddings=0)
+# workload: (name, config, seed, prompt tokens, decode steps, BASELINE config)
+TP_WORKLOADS = {
+    "8b-tp": ("Qwen3-8B", CONFIG_8B, 3, 2048, 512, 3),
+    "32b-tp": ("Qwen3-32B", CONFIG_32B, 4, 32768, 256, 4),
+}
 
 
 def run_tp(args, rank, world, local_rank):
-    """Qwen3-8B (config 3 shapes) sharded over the torchrun ranks: a
-    2048-token prompt, then `--decode-steps` greedy steps (capacity 4096).
-    value = decode tokens/s of the one sequence (all ranks serve it; max over
-    ranks of the device time)."""
+    """A Qwen3-8B (config 3) or Qwen3-32B (config 4) shape sharded over the
+    torchrun ranks: the config's prompt (`--prompt-tokens` overrides it), then
+    `--decode-steps` greedy steps (default: the config's), capacity prompt +
+    decode. value = decode tokens/s of the one sequence (all ranks serve it;
+    max over ranks of the device time)."""
     import numpy as np
     import torch
     import torch.distributed as dist
@@ -435,6 +444,12 @@ def run_tp(args, rank, world, local_rank):
     import metal_infer as mi
     import oracle as O
 
+    name, cfg, seed, prompt_len, decode, cfg_id = TP_WORKLOADS[args.workload]
+    if args.prompt_tokens:
+        prompt_len = args.prompt_tokens
+    if args.decode_steps is not None:
+        decode = args.decode_steps
+    capacity = prompt_len + decode if cfg_id == 4 else 4096
     torch.cuda.set_device(local_rank)
     if world > 1:
         dist.init_process_group("gloo", timeout=timedelta(seconds=300))
@@ -442,13 +457,12 @@ def run_tp(args, rank, world, local_rank):
     else:
         ident = bytes(128)  # one GPU: no communicator (tp = 1 is the plain model)
     ctx = mi.MetalContext(local_rank)
-    model = mi.Qwen3Model.random_tp(ctx, CONFIG_8B, seed=3, tp=world, rank=rank, nccl_id=ident)
-    prompt = O.gen_tokens(3, INPUT_STREAM, 2048, CONFIG_8B["vocab_size"])
+    model = mi.Qwen3Model.random_tp(ctx, cfg, seed=seed, tp=world, rank=rank, nccl_id=ident)
+    prompt = O.gen_tokens(seed, INPUT_STREAM, prompt_len, cfg["vocab_size"])
     stream = torch.cuda.ExternalStream(ctx.stream())
-    decode = args.decode_steps if args.decode_steps != DECODE else 512
     times = []
     for i in range(args.warmup + args.steps):
-        cache = model.kv_cache(4096)
+        cache = model.kv_cache(capacity)
         slot = ctx.empty([1], mi.DType.U32)
         e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
         e0.record(stream)
@@ -474,10 +488,10 @@ def run_tp(args, rank, world, local_rank):
             "ms_per_step": round((prefill_ms + decode_ms) / args.steps, 3),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f16",
             "data": "synthetic (random-init FP16 N(0,0.02) weights, uniform prompt ids)",
-            "config": {"workload": f"Qwen3-8B tensor-parallel TP{world}: 2048-token prompt + "
-                                   f"{decode} decode steps (BASELINE config 3)",
-                       "parallelism": f"tp{world}", "kv_capacity": 4096},
-            "prefill_tokens_per_s": round(2048 * args.steps / (prefill_ms / 1e3), 1),
+            "config": {"workload": f"{name} tensor-parallel TP{world}: {prompt_len}-token prompt + "
+                                   f"{decode} decode steps (BASELINE config {cfg_id} shapes)",
+                       "parallelism": f"tp{world}", "kv_capacity": capacity},
+            "prefill_tokens_per_s": round(prompt_len * args.steps / (prefill_ms / 1e3), 1),
             "decode_path": "persistent kernel" if model.decode_persistent()
                            else "per-kernel chain + NCCL all-gathers"}), flush=True)
     del model
@@ -488,9 +502,11 @@ def run_tp(args, rank, world, local_rank):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--workload", choices=["0.6b", "8b-tp"], default="0.6b",
-                    help="0.6b: the headline config (replicas over GPUs); 8b-tp: Qwen3-8B "
-                         "sharded over the GPUs")
+    ap.add_argument("--workload", choices=["0.6b", "8b-tp", "32b-tp"], default="0.6b",
+                    help="0.6b: the headline config (replicas over GPUs); 8b-tp / 32b-tp: "
+                         "Qwen3-8B / Qwen3-32B shapes sharded over the GPUs")
+    ap.add_argument("--prompt-tokens", type=int, default=0,
+                    help="tensor-parallel workloads: prompt length instead of the config's")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
@@ -500,10 +516,10 @@ def main():
                     help="skip the untimed sampled-decode report (short profiling runs)")
     ap.add_argument("--cpu-sample-steps", type=int, default=48)
     ap.add_argument("--cpu-sample-steps-ref", type=int, default=8)
-    ap.add_argument("--decode-steps", type=int, default=DECODE,
+    ap.add_argument("--decode-steps", type=int, default=None,
                     help="decode steps per request (smaller only for profiler launch lists)")
     args = ap.parse_args()
-    if args.decode_steps != DECODE:
+    if args.decode_steps is not None and args.workload == "0.6b":
         globals()["DECODE"] = args.decode_steps
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -513,7 +529,7 @@ def main():
         return
     if args.warmup < 3:
         args.warmup = 3
-    if args.workload == "8b-tp":
+    if args.workload in TP_WORKLOADS:
         run_tp(args, rank, world, local_rank)
         return
     run_ours(args, rank, world, local_rank)

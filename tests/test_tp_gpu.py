@@ -1,7 +1,7 @@
-"""Tensor parallelism on 2 GPUs against the oracle's TP arithmetic
+"""Tensor parallelism on 2, 4 and 8 GPUs against the oracle's TP arithmetic
 (bit-exact logits and greedy ids through the persistent kernel, which
 exchanges partials through peer memory, and through the NCCL kernel chain).
-Skipped on hosts with fewer than 2 GPUs.
+Each size is skipped on hosts with fewer GPUs.
 
 Each rank is its own process (spawned), owns one GPU and one context, and
 joins the NCCL communicator whose id rank 0 shares over a gloo group.
@@ -19,7 +19,6 @@ from conftest import INPUT_STREAM
 
 pytestmark = pytest.mark.gpu
 
-TP = 2
 SAMPLED = dict(temperature=0.9, top_p=0.95, top_k=64, seed=13)
 
 
@@ -35,14 +34,14 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _rank_main(rank, port, cfg, prompt, steps, out, ckpt=None):
+def _rank_main(rank, tp, port, cfg, prompt, steps, out, ckpt=None):
     import torch.distributed as dist
     dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
-                            world_size=TP)
+                            world_size=tp)
     try:
         ident = mi.share_nccl_id()
         ctx = mi.MetalContext(rank)
-        model = mi.Qwen3Model.random_tp(ctx, cfg, seed=11, tp=TP, rank=rank, nccl_id=ident)
+        model = mi.Qwen3Model.random_tp(ctx, cfg, seed=11, tp=tp, rank=rank, nccl_id=ident)
         res = {}
         cache = model.kv_cache(128)
         res["prefill"] = model.prefill(prompt, cache).f16_bits().ravel()
@@ -58,7 +57,7 @@ def _rank_main(rank, port, cfg, prompt, steps, out, ckpt=None):
         res["config"] = model.config()
         if ckpt:
             # the same shard read from a checkpoint of the full model
-            loaded = mi.Qwen3Model.load_tp(ckpt, ctx, TP, rank, mi.share_nccl_id())
+            loaded = mi.Qwen3Model.load_tp(ckpt, ctx, tp, rank, mi.share_nccl_id())
             res["loaded_prefill"] = loaded.prefill(prompt, loaded.kv_cache(128)).f16_bits().ravel()
             del loaded
         res["status"] = ctx.kernel_status()
@@ -71,8 +70,10 @@ def _rank_main(rank, port, cfg, prompt, steps, out, ckpt=None):
         dist.destroy_process_group()
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < TP, reason="needs 2 GPUs")
-def test_tp2_matches_oracle_tp_arithmetic(tmp_path):
+@pytest.mark.parametrize("tp", [2, 4, 8])
+def test_tp_matches_oracle_tp_arithmetic(tmp_path, tp):
+    if torch.cuda.device_count() < tp:
+        pytest.skip(f"needs {tp} GPUs")
     cfg = small_cfg()
     prompt = O.gen_tokens(11, INPUT_STREAM, 20, cfg["vocab_size"])
     steps = 16
@@ -85,28 +86,28 @@ def test_tp2_matches_oracle_tp_arithmetic(tmp_path):
     ctx = tmp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank_main, args=(r, port, cfg, prompt, steps, q, str(tmp_path)))
-             for r in range(TP)]
+    procs = [ctx.Process(target=_rank_main, args=(r, tp, port, cfg, prompt, steps, q, str(tmp_path)))
+             for r in range(tp)]
     for p in procs:
         p.start()
     res = {}
-    for _ in range(TP):
+    for _ in range(tp):
         rank, r = q.get(timeout=300)
         res[rank] = r
     for p in procs:
         p.join(timeout=120)
-    for r in range(TP):
+    for r in range(tp):
         assert "error" not in res[r], res[r]["error"]
     ref = O.Qwen3(cfg, seed=11, capacity=128)
-    ref.set_tp(TP)
+    ref.set_tp(tp)
     want_prefill = ref.forward(prompt)
     want_decode = [ref.forward(np.array([t], np.uint32)) for t in (7, 900)]
     ref_ids = O.Qwen3(cfg, seed=11, capacity=128)
-    ref_ids.set_tp(TP)
+    ref_ids.set_tp(tp)
     want_ids = ref_ids.generate_greedy(prompt, steps)
     want_sampled = ref_ids.generate_sampled(prompt, steps, SAMPLED["temperature"],
                                             SAMPLED["top_p"], SAMPLED["top_k"], SAMPLED["seed"])
-    for r in range(TP):
+    for r in range(tp):
         got = res[r]
         assert got["config"]["num_attention_heads"] == cfg["num_attention_heads"]
         np.testing.assert_array_equal(got["prefill"], want_prefill)
