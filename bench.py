@@ -55,6 +55,15 @@ def peaks():
         return 6650.0, "fallback"
 
 
+def synthetic_tokens(ctx, seed: int, n: int, vocab: int):
+    """Uniform prompt ids from the library's seeded SplitMix64 stream (the
+    generator the weights use), made on the device and read back once."""
+    import metal_infer as mi
+    t = ctx.empty([n], mi.DType.U32)
+    ctx.fill_tokens_u32(t, seed, INPUT_STREAM, vocab)
+    return t.to_u32_vec()
+
+
 # ---- algorithmic bytes ------------------------------------------------------------
 def weight_bytes_per_layer(c):
     h, I = c["hidden_size"], c["intermediate_size"]
@@ -154,7 +163,6 @@ def run_ours(args, rank, world, local_rank):
     import numpy as np
     import torch
     import metal_infer as mi
-    import oracle as O
 
     torch.cuda.set_device(local_rank)
     dist = None
@@ -167,7 +175,7 @@ def run_ours(args, rank, world, local_rank):
     ctx = mi.MetalContext(local_rank)
     model = mi.Qwen3Model.random(ctx, CONFIG, seed=SEED)
     cache = model.kv_cache(CAPACITY)
-    prompt = O.gen_tokens(SEED, INPUT_STREAM, PROMPT, CONFIG["vocab_size"])
+    prompt = synthetic_tokens(ctx, SEED, PROMPT, CONFIG["vocab_size"])
     pinned = torch.from_numpy(prompt.astype(np.int64)).to(torch.int32).pin_memory()
     prompt_ptr = pinned.numpy().view(np.uint32)
     stream = torch.cuda.ExternalStream(ctx.stream())
@@ -442,7 +450,6 @@ def run_tp(args, rank, world, local_rank):
     import torch.distributed as dist
     from datetime import timedelta
     import metal_infer as mi
-    import oracle as O
 
     name, cfg, seed, prompt_len, decode, cfg_id = TP_WORKLOADS[args.workload]
     if args.prompt_tokens:
@@ -458,7 +465,7 @@ def run_tp(args, rank, world, local_rank):
         ident = bytes(128)  # one GPU: no communicator (tp = 1 is the plain model)
     ctx = mi.MetalContext(local_rank)
     model = mi.Qwen3Model.random_tp(ctx, cfg, seed=seed, tp=world, rank=rank, nccl_id=ident)
-    prompt = O.gen_tokens(seed, INPUT_STREAM, prompt_len, cfg["vocab_size"])
+    prompt = synthetic_tokens(ctx, seed, prompt_len, cfg["vocab_size"])
     stream = torch.cuda.ExternalStream(ctx.stream())
     times = []
     for i in range(args.warmup + args.steps):
@@ -500,11 +507,128 @@ def run_tp(args, rank, world, local_rank):
         dist.destroy_process_group()
 
 
+# ---- op sweep -------------------------------------------------------
+# GEMV shapes (out x in, weights per launch) and decode attention lengths.
+SWEEP_GEMV = [("q_proj", 2048, 1024, 1), ("k_proj", 1024, 1024, 1), ("v_proj", 1024, 1024, 1),
+              ("o_proj", 1024, 2048, 1), ("gate_up", 3072, 1024, 2), ("down", 1024, 3072, 1),
+              ("lm_head", 151936, 1024, 1)]
+SWEEP_ATTN = [512, 2048, 8192]
+ROTATE_BYTES = 256 << 20   # working set of distinct operands per batch, above the 126 MB L2
+SLEEP_CYCLES = 40_000_000  # ~20 ms spin queued first, so the launches run back to back
+
+
+def run_op_sweep(args):
+    """each decode GEMV shape and flash-decode attention at
+    L = 512 / 2048 / 8192 (16 query / 8 KV heads, head_dim 128) through the
+    C-ABI batch, with the rotated working-set protocol of the reference's
+    `bench kernel --rotate` (bench.rs:849-912): one batch launches the op once
+    per distinct copy of its operands (together > 256 MB, so every launch
+    reads HBM), and the batch's device time is divided by the copies. A
+    bounded ~20 ms spin is queued on the stream before each batch so that the
+    host has enqueued every launch before the first one runs (the time is then
+    the kernels', not the host's launch rate). Bytes per launch are the
+    algorithmic ones: weights + input + output (GEMV), K/V rows + q + out
+    (attention)."""
+    import math
+    import torch
+    import metal_infer as mi
+
+    torch.cuda.set_device(0)
+    ctx = mi.MetalContext(0)
+    stream = torch.cuda.ExternalStream(ctx.stream())
+    peak, peak_kind = peaks()
+
+    def timed(encode, copies):
+        """Median device seconds per launch, and the slowest host enqueue of a
+        batch (it must stay well under the spin for the timing to hold)."""
+        samples, enqueue = [], 0.0
+        for i in range(args.warmup + args.steps):
+            with torch.cuda.stream(stream):
+                torch.cuda._sleep(SLEEP_CYCLES)
+            t0 = time.perf_counter()
+            b = ctx.begin_batch()
+            outs = encode(b)
+            t1 = time.perf_counter()
+            st = b.finish()
+            del outs
+            if i >= args.warmup:
+                samples.append(st.gpu_time / copies)
+                enqueue = max(enqueue, t1 - t0)
+        return statistics.median(samples), enqueue
+
+    rows = []
+    x_cache = {}
+    for name, n, k, segs in SWEEP_GEMV:
+        bytes_ = segs * n * k * 2 + k * 2 + segs * n * 2
+        copies = max(1, math.ceil(ROTATE_BYTES / (segs * n * k * 2)))
+        if k not in x_cache:
+            x_cache[k] = ctx.empty([1, k], mi.DType.F16)
+            ctx.fill_normal_f16(x_cache[k], 1, 1000 + k, 1.0)
+        x = x_cache[k]
+        ws = []
+        for c in range(copies):
+            group = []
+            for s_ in range(segs):
+                w = ctx.empty([n, k], mi.DType.F16)
+                ctx.fill_normal_f16(w, 1, 16 * c + s_, 0.02)
+                group.append(w)
+            ws.append(group)
+        if segs == 1:
+            enc = lambda b: [b.matmul(x, g[0]) for g in ws]
+        else:
+            enc = lambda b: [b.matmul2(x, g[0], g[1]) for g in ws]
+        t, enq = timed(enc, copies)
+        rows.append({"op": name, "kernel": "gemv", "shape": f"{segs}x{n}x{k}" if segs > 1
+                     else f"{n}x{k}", "bytes": bytes_, "copies": copies,
+                     "us_per_launch": round(t * 1e6, 3), "gb_s": round(bytes_ / t / 1e9, 1),
+                     "frac": round(bytes_ / t / 1e9 / peak, 3),
+                     "host_enqueue_ms": round(enq * 1e3, 2)})
+        del ws
+        ctx.synchronize()
+    qh, kvh, hd = 16, 8, 128
+    q = ctx.empty([1, qh, hd], mi.DType.F16)
+    ctx.fill_normal_f16(q, 1, 2000, 1.0)
+    for L in SWEEP_ATTN:
+        kv_bytes = L * kvh * hd * 2 * 2
+        bytes_ = kv_bytes + qh * hd * 2 * 2
+        copies = max(1, math.ceil(ROTATE_BYTES / kv_bytes))
+        kvs = []
+        for c in range(copies):
+            kk = ctx.empty([L, kvh, hd], mi.DType.F16)
+            vv = ctx.empty([L, kvh, hd], mi.DType.F16)
+            ctx.fill_normal_f16(kk, 1, 3000 + 2 * c, 1.0)
+            ctx.fill_normal_f16(vv, 1, 3001 + 2 * c, 1.0)
+            kvs.append((kk, vv))
+        cfg = mi.AttentionConfig(qh, kvh, hd, 1, L - 1)
+        enc = lambda b: [b.attention(q, kk, vv, cfg, mi.AttentionKind.FLASH_DECODE)
+                         for kk, vv in kvs]
+        t, enq = timed(enc, copies)
+        rows.append({"op": f"attention_L{L}", "kernel": "flash_decode",
+                     "shape": f"q[1,{qh},{hd}] kv[{L},{kvh},{hd}]", "bytes": bytes_,
+                     "copies": copies, "us_per_launch": round(t * 1e6, 3),
+                     "gb_s": round(bytes_ / t / 1e9, 1), "frac": round(bytes_ / t / 1e9 / peak, 3),
+                     "host_enqueue_ms": round(enq * 1e3, 2)})
+        del kvs
+        ctx.synchronize()
+    total_bytes = sum(r["bytes"] for r in rows)
+    total_s = sum(r["us_per_launch"] for r in rows) / 1e6
+    print(json.dumps({
+        "metric": "GEMV / attention HBM GB/s (op sweep)", "impl": "ours",
+        "value": round(total_bytes / total_s / 1e9, 1), "unit": "GB/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+        "dtype": "f16", "data": "synthetic (seeded N(0,0.02) weights, N(0,1) activations)",
+        "config": {"workload": "BASELINE config 1 decode-op sweep, rotated working sets "
+                               f"> {ROTATE_BYTES >> 20} MB (inputs larger than L2)"},
+        "peak": {"hbm_gbs": peak, "kind": peak_kind}, "ops": rows}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--workload", choices=["0.6b", "8b-tp", "32b-tp"], default="0.6b",
+    ap.add_argument("--workload", choices=["0.6b", "8b-tp", "32b-tp", "op-sweep"],
+                    default="0.6b",
                     help="0.6b: the headline config (replicas over GPUs); 8b-tp / 32b-tp: "
-                         "Qwen3-8B / Qwen3-32B shapes sharded over the GPUs")
+                         "Qwen3-8B / Qwen3-32B shapes sharded over the GPUs; op-sweep: the "
+                         "decode GEMV and attention kernels alone (one GPU)")
     ap.add_argument("--prompt-tokens", type=int, default=0,
                     help="tensor-parallel workloads: prompt length instead of the config's")
     ap.add_argument("--gpus", type=int, default=1)
@@ -531,6 +655,10 @@ def main():
         args.warmup = 3
     if args.workload in TP_WORKLOADS:
         run_tp(args, rank, world, local_rank)
+        return
+    if args.workload == "op-sweep":
+        if rank == 0:
+            run_op_sweep(args)
         return
     run_ours(args, rank, world, local_rank)
 

@@ -305,21 +305,91 @@ __global__ void __launch_bounds__(kDecodeThreads) attention_decode_kernel(Decode
   __syncthreads();
   if (!sm.last) return;
   __threadfence();
+  // Block merge in index order, staged through shared memory: the K/V tile
+  // buffers (free now) take the records of up to `chunk` blocks at a time,
+  // copied by every thread with 16-byte cp.async (one L2 round trip per
+  // chunk). The arithmetic is the sequential merge: M = the max of the block
+  // maxima (exact in any order), then per block f = exp(m - M) and
+  // den / num = fma(l / acc, f, den / num) in block order.
   const float* base = a.scratch + (size_t)g_kv * gridDim.x * G * stride;
-  for (int idx = threadIdx.x; idx < G * HD; idx += kDecodeThreads) {
-    int g = idx / HD, d = idx - g * HD;
-    float M = -INFINITY;
-    for (int s = 0; s < nb; ++s) M = fmaxf(M, __ldcg(base + (size_t)(s * G + g) * stride));
-    float num = 0.f, den = 0.f;
-    for (int s = 0; s < nb; ++s) {
-      const float* ps = base + (size_t)(s * G + g) * stride;
-      float mm = __ldcg(ps);
-      float f = mm == -INFINITY ? 0.f : mi_exp(__fsub_rn(mm, M));
-      den = __fmaf_rn(__ldcg(ps + 1), f, den);
-      num = __fmaf_rn(__ldcg(ps + 2 + d), f, num);
+  float* buf = reinterpret_cast<float*>(&sm.k[0][0][0]);  // k and v tiles: 64 KB
+  constexpr int kBufFloats = (int)(2 * sizeof(DecodeSmem<G>::k) / sizeof(float));
+  constexpr int kRec = G * (HD + 2);                        // floats of one block record
+  constexpr int kChunk = (kBufFloats - 3) / kRec;           // blocks per staged chunk
+  float* fs = &sm.acc[0][0][0];                             // [kChunk][G] merge factors
+  static_assert(kChunk * G <= kStreams * G * HD, "factor buffer");
+  // M per head of the group (sm.m[0][g]).
+  {
+    float mloc[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) mloc[g] = -INFINITY;
+    for (int s0 = threadIdx.x * 8; s0 < nb; s0 += kDecodeThreads * 8) {
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        if (s0 + u < nb) {
+#pragma unroll
+          for (int g = 0; g < G; ++g)
+            mloc[g] = fmaxf(mloc[g], __ldcg(base + (size_t)((s0 + u) * G + g) * stride));
+        }
+      }
     }
-    a.out[(size_t)(g_kv * G + g) * HD + d] = __float2half_rn(__fdiv_rn(num, den));
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      float v = mloc[g];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+      if (lane == 0) sm.l[warp][g] = v;
+    }
+    __syncthreads();
+    if (threadIdx.x < G) {
+      float v = sm.l[0][threadIdx.x];
+#pragma unroll
+      for (int w = 1; w < kDecodeThreads / 32; ++w) v = fmaxf(v, sm.l[w][threadIdx.x]);
+      sm.m[0][threadIdx.x] = v;
+    }
+    __syncthreads();
   }
+  float num[G], den = 0.f;  // thread t: element t of each head g (t < 128 = HD)
+#pragma unroll
+  for (int g = 0; g < G; ++g) num[g] = 0.f;
+  static_assert(kDecodeThreads == HD, "one thread per head dimension");
+  const int d = threadIdx.x;
+  for (int s0 = 0; s0 < nb; s0 += kChunk) {
+    const int cnt = min(kChunk, nb - s0);
+    const float* src = base + (size_t)s0 * kRec;
+    const int n = cnt * kRec;
+    const int head = (int)((4 - ((reinterpret_cast<uintptr_t>(src) >> 2) & 3)) & 3);
+    const int h = min(n, head);
+    float* stage = buf + ((4 - h) & 3);  // stage + h is 16-byte aligned
+    const int n4 = (n - h) >> 2;
+    for (int i = threadIdx.x; i < n4; i += kDecodeThreads)
+      pipe::cp_async16(stage + h + 4 * i, src + h + 4 * i);
+    pipe::cp_async_commit();
+    if (threadIdx.x < h) stage[threadIdx.x] = __ldcg(src + threadIdx.x);
+    const int t0 = h + 4 * n4;
+    if (threadIdx.x < n - t0) stage[t0 + threadIdx.x] = __ldcg(src + t0 + threadIdx.x);
+    pipe::cp_async_wait_all();
+    __syncthreads();
+    for (int i = threadIdx.x; i < cnt * G; i += kDecodeThreads) {
+      const int g = i % G;
+      const float mm = stage[i * (HD + 2)];
+      fs[i] = mm == -INFINITY ? 0.f : mi_exp(__fsub_rn(mm, sm.m[0][g]));
+    }
+    __syncthreads();
+    if (threadIdx.x < G)
+      for (int u = 0; u < cnt; ++u)
+        den = __fmaf_rn(stage[(u * G + threadIdx.x) * (HD + 2) + 1], fs[u * G + threadIdx.x], den);
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+      for (int u = 0; u < cnt; ++u)
+        num[g] = __fmaf_rn(stage[(u * G + g) * (HD + 2) + 2 + d], fs[u * G + g], num[g]);
+    __syncthreads();
+  }
+  if (threadIdx.x < G) sm.l[0][threadIdx.x] = den;
+  __syncthreads();
+#pragma unroll
+  for (int g = 0; g < G; ++g)
+    a.out[(size_t)(g_kv * G + g) * HD + d] = __float2half_rn(__fdiv_rn(num[g], sm.l[0][g]));
   if (threadIdx.x == 0) a.counters[g_kv] = 0u;
 }
 

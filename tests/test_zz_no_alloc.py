@@ -59,6 +59,25 @@ def test_noalloc_flash_decode_matches_allocating_entry_point(ctx, qh, kvh, lengt
     assert not np.array_equal(results[0], results[1])
 
 
+# Other GQA ratios against the oracle's block-ordered merge, with enough
+# blocks that the final merge runs over several shared-memory chunks (125 / 31
+# / 15 blocks for ratios 1 / 4 / 8) and, with 3 KV heads of 141 blocks, block
+# records that start off a 16-byte boundary.
+@pytest.mark.parametrize("qh,kvh,length,block",
+                         [(3, 3, 9000, 64), (8, 2, 2500, 32), (8, 1, 2000, 64)])
+def test_noalloc_flash_decode_other_ratios_match_oracle(ctx, qh, kvh, length, block):
+    q = O.gen_normal_f16(3, INPUT_STREAM + 230, qh * 128)
+    k = O.gen_normal_f16(3, INPUT_STREAM + 231, length * kvh * 128)
+    v = O.gen_normal_f16(3, INPUT_STREAM + 232, length * kvh * 128)
+    tq = ctx.tensor_f16_bits(q, [1, qh, 128])
+    tk = ctx.tensor_f16_bits(k, [length, kvh, 128])
+    tv = ctx.tensor_f16_bits(v, [length, kvh, 128])
+    out = ctx.empty([1, qh, 128], mi.DType.F16)
+    _call_noalloc(ctx, tq, tk, tv, out, qh, kvh, length, block)
+    np.testing.assert_array_equal(out.f16_bits().ravel(),
+                                  O.attention_decode(q, k, v, qh, kvh, 128, block=block).ravel())
+
+
 def test_noalloc_flash_decode_rejects_oversized_problems(ctx):
     q = ctx.empty([1, 64, 128], mi.DType.F16)
     kv = ctx.empty([8, 8, 128], mi.DType.F16)
