@@ -94,10 +94,15 @@ struct DecodeArgs {
   const float2* rope;     // RoPE table (null: evaluate the terms)
 };
 
+struct alignas(16) DecodeTile {
+  __half k[kTile][HD];
+  __half v[kTile][HD];
+};
+
+// The K/V tiles come last: a launch whose blocks fit one tile (block <=
+// kTile) reserves only the first, which doubles the CTAs an SM holds.
 template <int G>
 struct DecodeSmem {
-  __half k[2][kTile][HD];
-  __half v[2][kTile][HD];
   __half new_k[HD];
   __half new_v[HD];
   float q[G][HD];
@@ -105,7 +110,13 @@ struct DecodeSmem {
   float l[kStreams][G];
   float acc[kStreams][G][HD];
   bool last;
+  DecodeTile tile[2];
 };
+
+template <int G>
+constexpr size_t decode_smem_bytes(bool two_tiles) {
+  return sizeof(DecodeSmem<G>) - (two_tiles ? 0 : sizeof(DecodeTile));
+}
 
 // Stages keys [j0, j1) of head g into buffer `buf` (cp.async, 16 bytes per
 // copy), skipping `skip`.
@@ -145,7 +156,8 @@ __global__ void __launch_bounds__(kDecodeThreads) attention_decode_kernel(Decode
   const int begin = b * a.block;
   const int end = min(L, begin + a.block);
   const int ntiles = b < nb ? (end - begin + kTile - 1) / kTile : 0;
-  if (ntiles > 0) stage_tile(a, g_kv, begin, min(end, begin + kTile), pos, sm.k[0], sm.v[0]);
+  if (ntiles > 0)
+    stage_tile(a, g_kv, begin, min(end, begin + kTile), pos, sm.tile[0].k, sm.tile[0].v);
   pdl_trigger();
   pdl_wait();
   if (b >= nb) return;
@@ -209,7 +221,7 @@ __global__ void __launch_bounds__(kDecodeThreads) attention_decode_kernel(Decode
     const int j0 = begin + t * kTile;
     const int j1 = min(end, j0 + kTile);
     if (t + 1 < ntiles)
-      stage_tile(a, g_kv, j1, min(end, j1 + kTile), pos, sm.k[buf ^ 1], sm.v[buf ^ 1]);
+      stage_tile(a, g_kv, j1, min(end, j1 + kTile), pos, sm.tile[buf ^ 1].k, sm.tile[buf ^ 1].v);
     if (t + 1 < ntiles)
       asm volatile("cp.async.wait_group 1;" ::: "memory");
     else
@@ -229,8 +241,8 @@ __global__ void __launch_bounds__(kDecodeThreads) attention_decode_kernel(Decode
         kk = reinterpret_cast<const uint4*>(sm.new_k)[li];
         vv = reinterpret_cast<const uint4*>(sm.new_v)[li];
       } else if (valid) {
-        kk = reinterpret_cast<const uint4*>(sm.k[buf][r])[li];
-        vv = reinterpret_cast<const uint4*>(sm.v[buf][r])[li];
+        kk = reinterpret_cast<const uint4*>(sm.tile[buf].k[r])[li];
+        vv = reinterpret_cast<const uint4*>(sm.tile[buf].v[r])[li];
       }
       float kf[8], vf[8];
       const __half2* hk = reinterpret_cast<const __half2*>(&kk);
@@ -299,9 +311,13 @@ __global__ void __launch_bounds__(kDecodeThreads) attention_decode_kernel(Decode
     }
   }
   if (nb == 1) return;
-  __threadfence();
+  // Release: the barrier orders every thread's partial stores before thread
+  // 0's fence, which orders them before its arrival.
   __syncthreads();
-  if (threadIdx.x == 0) sm.last = atomicAdd(a.counters + g_kv, 1u) == (uint32_t)nb - 1;
+  if (threadIdx.x == 0) {
+    __threadfence();
+    sm.last = atomicAdd(a.counters + g_kv, 1u) == (uint32_t)nb - 1;
+  }
   __syncthreads();
   if (!sm.last) return;
   __threadfence();
@@ -312,12 +328,14 @@ __global__ void __launch_bounds__(kDecodeThreads) attention_decode_kernel(Decode
   // maxima (exact in any order), then per block f = exp(m - M) and
   // den / num = fma(l / acc, f, den / num) in block order.
   const float* base = a.scratch + (size_t)g_kv * gridDim.x * G * stride;
-  float* buf = reinterpret_cast<float*>(&sm.k[0][0][0]);  // k and v tiles: 64 KB
-  constexpr int kBufFloats = (int)(2 * sizeof(DecodeSmem<G>::k) / sizeof(float));
+  float* buf = reinterpret_cast<float*>(&sm.tile[0]);      // the reserved K/V tiles
+  const int buf_floats =
+      (int)((a.block > kTile ? 2 : 1) * sizeof(DecodeTile) / sizeof(float));
   constexpr int kRec = G * (HD + 2);                        // floats of one block record
-  constexpr int kChunk = (kBufFloats - 3) / kRec;           // blocks per staged chunk
+  const int kChunk = (buf_floats - 3) / kRec;               // blocks per staged chunk
   float* fs = &sm.acc[0][0][0];                             // [kChunk][G] merge factors
-  static_assert(kChunk * G <= kStreams * G * HD, "factor buffer");
+  static_assert((2 * sizeof(DecodeTile) / sizeof(float) - 3) / kRec * G <= kStreams * G * HD,
+                "factor buffer");
   // M per head of the group (sm.m[0][g]).
   {
     float mloc[G];
@@ -396,10 +414,11 @@ __global__ void __launch_bounds__(kDecodeThreads) attention_decode_kernel(Decode
 template <int G>
 void launch_decode_g(const Launch& l, const DecodeArgs& a, int blocks) {
   auto kernel = attention_decode_kernel<G>;
-  size_t smem = sizeof(DecodeSmem<G>);
+  const size_t smem = decode_smem_bytes<G>(a.block > kTile);
   static bool configured = false;
-  if (!configured) {
-    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (!configured) {  // the largest layout, so that every launch fits
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         (int)decode_smem_bytes<G>(true));
     configured = true;
   }
   launch_kernel(l, dim3(blocks, a.kvh), dim3(kDecodeThreads), smem, kernel, a);
