@@ -228,48 +228,71 @@ __global__ void __launch_bounds__(kDecodeThreads) attention_decode_kernel(Decode
       pipe::cp_async_wait_all();
     __syncthreads();
     // Stream hw takes block-relative keys hw, hw + 8, ... (tiles are
-    // multiples of 8 keys, so the order is the block's). Both half-warps of
-    // a warp run the same trip count (the shuffles span the whole warp); a
-    // half-warp past the end computes on zeros and keeps its state.
+    // multiples of 8 keys, so the order is the block's), two at a time: the
+    // scores of keys r and r + 8 first, then their updates in key order. Both
+    // half-warps of a warp run the same trip count (the shuffles span the
+    // whole warp); a half-warp past the end computes on zeros and keeps its
+    // state.
     const int count = j1 - j0;
-    for (int base = warp * 2; base < count; base += kStreams) {
-      const int r = base + (lane >> 4);
-      const bool valid = r < count;
-      const int j = j0 + r;
-      uint4 kk = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
-      if (valid && j == pos) {
-        kk = reinterpret_cast<const uint4*>(sm.new_k)[li];
-        vv = reinterpret_cast<const uint4*>(sm.new_v)[li];
-      } else if (valid) {
-        kk = reinterpret_cast<const uint4*>(sm.tile[buf].k[r])[li];
-        vv = reinterpret_cast<const uint4*>(sm.tile[buf].v[r])[li];
+    for (int base = warp * 2; base < count; base += 2 * kStreams) {
+      uint4 kk[2], vv[2];
+      bool valid[2];
+#pragma unroll
+      for (int t2 = 0; t2 < 2; ++t2) {
+        const int r = base + t2 * kStreams + (lane >> 4);
+        const int j = j0 + r;
+        valid[t2] = r < count;
+        kk[t2] = make_uint4(0, 0, 0, 0);
+        vv[t2] = make_uint4(0, 0, 0, 0);
+        if (valid[t2] && j == pos) {
+          kk[t2] = reinterpret_cast<const uint4*>(sm.new_k)[li];
+          vv[t2] = reinterpret_cast<const uint4*>(sm.new_v)[li];
+        } else if (valid[t2]) {
+          kk[t2] = reinterpret_cast<const uint4*>(sm.tile[buf].k[r])[li];
+          vv[t2] = reinterpret_cast<const uint4*>(sm.tile[buf].v[r])[li];
+        }
       }
-      float kf[8], vf[8];
-      const __half2* hk = reinterpret_cast<const __half2*>(&kk);
-      const __half2* hv = reinterpret_cast<const __half2*>(&vv);
+      float sc[2][G];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        float2 fk = __half22float2(hk[i]);
-        float2 fv = __half22float2(hv[i]);
-        kf[2 * i] = fk.x;
-        kf[2 * i + 1] = fk.y;
-        vf[2 * i] = fv.x;
-        vf[2 * i + 1] = fv.y;
+      for (int t2 = 0; t2 < 2; ++t2) {
+        float kf[8];
+        const __half2* hk = reinterpret_cast<const __half2*>(&kk[t2]);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          float2 fk = __half22float2(hk[i]);
+          kf[2 * i] = fk.x;
+          kf[2 * i + 1] = fk.y;
+        }
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          float d = 0.f;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) d = __fmaf_rn(qreg[g][e], kf[e], d);
+          sc[t2][g] = __fmul_rn(canon_butterfly(d, 16), scale);
+        }
       }
 #pragma unroll
-      for (int g = 0; g < G; ++g) {
-        float d = 0.f;
+      for (int t2 = 0; t2 < 2; ++t2) {
+        if (!valid[t2]) continue;
+        float vf[8];
+        const __half2* hv = reinterpret_cast<const __half2*>(&vv[t2]);
 #pragma unroll
-        for (int e = 0; e < 8; ++e) d = __fmaf_rn(qreg[g][e], kf[e], d);
-        float s = __fmul_rn(canon_butterfly(d, 16), scale);
-        if (!valid) continue;
-        float nm = fmaxf(m[g], s);
-        float pa = mi_exp(__fsub_rn(m[g], nm));
-        float pc = mi_exp(__fsub_rn(s, nm));
+        for (int i = 0; i < 4; ++i) {
+          float2 fv = __half22float2(hv[i]);
+          vf[2 * i] = fv.x;
+          vf[2 * i + 1] = fv.y;
+        }
 #pragma unroll
-        for (int e = 0; e < 8; ++e) acc[g][e] = __fmaf_rn(acc[g][e], pa, __fmul_rn(pc, vf[e]));
-        l[g] = __fmaf_rn(l[g], pa, pc);
-        m[g] = nm;
+        for (int g = 0; g < G; ++g) {
+          const float s = sc[t2][g];
+          float nm = fmaxf(m[g], s);
+          float pa = mi_exp(__fsub_rn(m[g], nm));
+          float pc = mi_exp(__fsub_rn(s, nm));
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[g][e] = __fmaf_rn(acc[g][e], pa, __fmul_rn(pc, vf[e]));
+          l[g] = __fmaf_rn(l[g], pa, pc);
+          m[g] = nm;
+        }
       }
     }
     __syncthreads();
@@ -394,13 +417,39 @@ __global__ void __launch_bounds__(kDecodeThreads) attention_decode_kernel(Decode
       fs[i] = mm == -INFINITY ? 0.f : mi_exp(__fsub_rn(mm, sm.m[0][g]));
     }
     __syncthreads();
-    if (threadIdx.x < G)
-      for (int u = 0; u < cnt; ++u)
-        den = __fmaf_rn(stage[(u * G + threadIdx.x) * (HD + 2) + 1], fs[u * G + threadIdx.x], den);
+    // The chains read their operands kMB blocks at a time, loads first.
+    constexpr int kMB = G >= 4 ? 4 : 8;
+    if (threadIdx.x < G) {
+      const int g = threadIdx.x;
+      for (int u0 = 0; u0 < cnt; u0 += kMB) {
+        float lv[kMB], fv[kMB];
 #pragma unroll
-    for (int g = 0; g < G; ++g)
-      for (int u = 0; u < cnt; ++u)
-        num[g] = __fmaf_rn(stage[(u * G + g) * (HD + 2) + 2 + d], fs[u * G + g], num[g]);
+        for (int e = 0; e < kMB; ++e) {
+          const int u = min(u0 + e, cnt - 1);
+          lv[e] = stage[(u * G + g) * (HD + 2) + 1];
+          fv[e] = fs[u * G + g];
+        }
+#pragma unroll
+        for (int e = 0; e < kMB; ++e)
+          if (u0 + e < cnt) den = __fmaf_rn(lv[e], fv[e], den);
+      }
+    }
+    for (int u0 = 0; u0 < cnt; u0 += kMB) {
+      float sv[G][kMB], fv[G][kMB];
+#pragma unroll
+      for (int g = 0; g < G; ++g)
+#pragma unroll
+        for (int e = 0; e < kMB; ++e) {
+          const int u = min(u0 + e, cnt - 1);
+          sv[g][e] = stage[(u * G + g) * (HD + 2) + 2 + d];
+          fv[g][e] = fs[u * G + g];
+        }
+#pragma unroll
+      for (int g = 0; g < G; ++g)
+#pragma unroll
+        for (int e = 0; e < kMB; ++e)
+          if (u0 + e < cnt) num[g] = __fmaf_rn(sv[g][e], fv[g][e], num[g]);
+    }
     __syncthreads();
   }
   if (threadIdx.x < G) sm.l[0][threadIdx.x] = den;
