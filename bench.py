@@ -556,9 +556,12 @@ def run_op_sweep(args):
                 enqueue = max(enqueue, t1 - t0)
         return statistics.median(samples), enqueue
 
+    only = set(args.ops.split(",")) if args.ops else None
     rows = []
     x_cache = {}
     for name, n, k, segs in SWEEP_GEMV:
+        if only is not None and name not in only:
+            continue
         bytes_ = segs * n * k * 2 + k * 2 + segs * n * 2
         copies = max(1, math.ceil(ROTATE_BYTES / (segs * n * k * 2)))
         if k not in x_cache:
@@ -589,6 +592,8 @@ def run_op_sweep(args):
     q = ctx.empty([1, qh, hd], mi.DType.F16)
     ctx.fill_normal_f16(q, 1, 2000, 1.0)
     for L in SWEEP_ATTN:
+        if only is not None and f"attention_L{L}" not in only:
+            continue
         kv_bytes = L * kvh * hd * 2 * 2
         bytes_ = kv_bytes + qh * hd * 2 * 2
         copies = max(1, math.ceil(ROTATE_BYTES / kv_bytes))
@@ -629,6 +634,9 @@ def main():
                     help="0.6b: the headline config (replicas over GPUs); 8b-tp / 32b-tp: "
                          "Qwen3-8B / Qwen3-32B shapes sharded over the GPUs; op-sweep: the "
                          "decode GEMV and attention kernels alone (one GPU)")
+    ap.add_argument("--ops", default="",
+                    help="op-sweep: comma-separated subset (q_proj, ..., lm_head, "
+                         "attention_L512, attention_L2048, attention_L8192)")
     ap.add_argument("--prompt-tokens", type=int, default=0,
                     help="tensor-parallel workloads: prompt length instead of the config's")
     ap.add_argument("--gpus", type=int, default=1)
