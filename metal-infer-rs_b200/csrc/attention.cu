@@ -464,12 +464,7 @@ template <int G>
 void launch_decode_g(const Launch& l, const DecodeArgs& a, int blocks) {
   auto kernel = attention_decode_kernel<G>;
   const size_t smem = decode_smem_bytes<G>(a.block > kTile);
-  static bool configured = false;
-  if (!configured) {  // the largest layout, so that every launch fits
-    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         (int)decode_smem_bytes<G>(true));
-    configured = true;
-  }
+  allow_dynamic_smem(kernel, decode_smem_bytes<G>(true));  // the largest layout
   launch_kernel(l, dim3(blocks, a.kvh), dim3(kDecodeThreads), smem, kernel, a);
 }
 

@@ -5,6 +5,9 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <mutex>
+#include <set>
+#include <tuple>
 
 #include "kernels.h"
 #include "mi_internal.h"
@@ -167,6 +170,27 @@ inline void launch_kernel(const k::Launch& l, dim3 grid, dim3 block, size_t smem
   cudaError_t err = cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
   if (err != cudaSuccess)
     fail(MI_ERR_COMMAND, "kernel launch failed: %s", cudaGetErrorString(err));
+}
+
+// Host: raises `kernel`'s dynamic shared-memory limit to `bytes` on the
+// current device, once per (kernel, device, bytes). The attribute belongs to
+// the device's context, so a process that launches on several devices
+// (tensor-parallel ranks as threads, say) sets it on each of them.
+template <typename... KArgs>
+inline void allow_dynamic_smem(void (*kernel)(KArgs...), size_t bytes) {
+  static std::mutex mu;
+  static std::set<std::tuple<const void*, int, size_t>> done;
+  int device = 0;
+  cudaError_t err = cudaGetDevice(&device);
+  if (err != cudaSuccess) fail(MI_ERR_COMMAND, "no current device: %s", cudaGetErrorString(err));
+  const auto key = std::make_tuple(reinterpret_cast<const void*>(kernel), device, bytes);
+  std::lock_guard<std::mutex> lock(mu);
+  if (done.count(key)) return;
+  err = cudaFuncSetAttribute(reinterpret_cast<const void*>(kernel),
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+  if (err != cudaSuccess)
+    fail(MI_ERR_COMMAND, "kernel configuration failed: %s", cudaGetErrorString(err));
+  done.insert(key);
 }
 
 }  // namespace mi

@@ -296,10 +296,7 @@ template <int BN>
 void launch_tc(const Launch& l, const CUtensorMap& mx, const CUtensorMap& mw, __half* out, int m,
                int n, int k, int ldo) {
   auto kernel = gemm_tc_kernel<BN>;
-  static std::once_flag once;
-  std::call_once(once, [&] {
-    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Smem<BN>::kBytes);
-  });
+  allow_dynamic_smem(kernel, Smem<BN>::kBytes);
   dim3 grid((n + BN - 1) / BN, (m + BM - 1) / BM);
   launch_kernel(l, grid, dim3(kThreads), Smem<BN>::kBytes, kernel, mx, mw, out, m, n, k, ldo);
 }

@@ -408,11 +408,7 @@ void launch_staged(const Launch& l, const GemvProblem& p) {
   grid = (items + plan.rpc - 1) / plan.rpc;
   size_t smem = (size_t)plan.x_bytes + (size_t)plan.stages * plan.stage_bytes;
   auto kernel = gemv_staged_kernel<IN, OUT>;
-  static bool configured = false;
-  if (!configured) {
-    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBudget + 1024);
-    configured = true;
-  }
+  allow_dynamic_smem(kernel, kSmemBudget + 1024);
   launch_kernel(l, dim3(grid), dim3(kThreads), smem, kernel, p, plan);
 }
 
