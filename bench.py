@@ -81,6 +81,18 @@ def decode_bytes_per_token(c, kv_len):
     return c["num_hidden_layers"] * weight_bytes_per_layer(c) + 2 * V * h + 2 * h + kv
 
 
+def gemv_bytes(n, k, segs=1):
+    """One decode GEMV launch: `segs` weight matrices [n, k], the input row
+    read once and `segs` output rows (FP16)."""
+    return segs * n * k * 2 + k * 2 + segs * n * 2
+
+
+def flash_decode_bytes(L, qh, kvh, hd):
+    """One flash-decode launch: L cached K and V rows of every KV head, the
+    queries and the output (FP16)."""
+    return L * kvh * hd * 2 * 2 + qh * hd * 2 * 2
+
+
 def kernel_bytes(c, name, mean_len, steps=1):
     """Algorithmic bytes of one launch of `name` (`steps` decode steps for the
     persistent decode kernel, which runs a whole call in one launch)."""
@@ -562,7 +574,7 @@ def run_op_sweep(args):
     for name, n, k, segs in SWEEP_GEMV:
         if only is not None and name not in only:
             continue
-        bytes_ = segs * n * k * 2 + k * 2 + segs * n * 2
+        bytes_ = gemv_bytes(n, k, segs)
         copies = max(1, math.ceil(ROTATE_BYTES / (segs * n * k * 2)))
         if k not in x_cache:
             x_cache[k] = ctx.empty([1, k], mi.DType.F16)
@@ -595,7 +607,7 @@ def run_op_sweep(args):
         if only is not None and f"attention_L{L}" not in only:
             continue
         kv_bytes = L * kvh * hd * 2 * 2
-        bytes_ = kv_bytes + qh * hd * 2 * 2
+        bytes_ = flash_decode_bytes(L, qh, kvh, hd)
         copies = max(1, math.ceil(ROTATE_BYTES / kv_bytes))
         kvs = []
         for c in range(copies):
