@@ -1,5 +1,6 @@
-"""Tensor parallelism, host side (no GPU): the shard plan, the NCCL id
-exchange over a world-2 gloo group, and the oracle's TP arithmetic."""
+"""Tensor parallelism, host side (no GPU): the shard plan (8B and 32B shapes
+at 1, 2, 4 and 8 ranks), the NCCL id exchange over gloo groups of 2 and 4
+ranks, and the oracle's TP arithmetic."""
 import os
 import socket
 
@@ -20,9 +21,10 @@ def small_cfg(**kw):
     return cfg
 
 
+@pytest.mark.parametrize("model", ["8b", "32b"])
 @pytest.mark.parametrize("tp", [1, 2, 4, 8])
-def test_shards_cover_every_head_column_and_row_once(tp):
-    cfg = dict(mi.QWEN3_8B)
+def test_shards_cover_every_head_column_and_row_once(model, tp):
+    cfg = dict(mi.QWEN3_8B if model == "8b" else mi.QWEN3_32B)
     shards = [mi.tp_shard(cfg, tp, r) for r in range(tp)]
     for key, start, total in (("q_heads", "q_head0", cfg["num_attention_heads"]),
                               ("kv_heads", "kv_head0", cfg["num_key_value_heads"]),
@@ -76,21 +78,25 @@ def _rank_main(rank, world, port, cfg, out):
         dist.destroy_process_group()
 
 
-def test_world2_gloo_shares_one_nccl_id_and_disjoint_shards():
+@pytest.mark.parametrize("world", [2, 4])
+def test_gloo_ranks_share_one_nccl_id_and_disjoint_shards(world):
     cfg = small_cfg()
     ctx = tmp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, cfg, q)) for r in range(2)]
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, cfg, q))
+             for r in range(world)]
     for p in procs:
         p.start()
     got = dict()
-    for _ in range(2):
+    for _ in range(world):
         rank, ident, shard = q.get(timeout=120)
         got[rank] = (ident, shard)
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
-    assert got[0][0] == got[1][0] and len(got[0][0]) == 128
-    assert got[0][1]["q_head0"] == 0 and got[1][1]["q_head0"] == cfg["num_attention_heads"] // 2
-    assert got[0][1]["vocab"] + got[1][1]["vocab"] == cfg["vocab_size"]
+    assert len(got[0][0]) == 128
+    assert all(got[r][0] == got[0][0] for r in range(world))
+    per = cfg["num_attention_heads"] // world
+    assert [got[r][1]["q_head0"] for r in range(world)] == [r * per for r in range(world)]
+    assert sum(got[r][1]["vocab"] for r in range(world)) == cfg["vocab_size"]
