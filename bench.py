@@ -81,6 +81,20 @@ def decode_bytes_per_token(c, kv_len):
     return c["num_hidden_layers"] * weight_bytes_per_layer(c) + 2 * V * h + 2 * h + kv
 
 
+def tp_decode_bytes_per_token(c, tp, kv_len):
+    """Bytes one rank reads per decode step under tensor parallelism: its
+    1/tp of every sharded matrix (heads, MLP columns, LM-head rows) and of
+    the KV cache (KV heads), plus the replicated norms."""
+    h, I, V = c["hidden_size"], c["intermediate_size"], c["vocab_size"]
+    qw = c["num_attention_heads"] * c["head_dim"]
+    kw = c["num_key_value_heads"] * c["head_dim"]
+    mats = (qw + 2 * kw) * h + h * qw + 2 * I * h + h * I
+    norms = 2 * h + 2 * c["head_dim"]
+    layers = c["num_hidden_layers"]
+    kv = kv_len * kw * 2 * 2 * layers
+    return layers * (2 * mats / tp + 2 * norms) + 2 * V * h / tp + 2 * h + kv / tp
+
+
 def gemv_bytes(n, k, segs=1):
     """One decode GEMV launch: `segs` weight matrices [n, k], the input row
     read once and `segs` output rows (FP16)."""
@@ -181,7 +195,9 @@ def run_ours(args, rank, world, local_rank):
     if world > 1:
         import torch.distributed as dist
         from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
+        # gloo for host tensors (the NCCL id of the tensor-parallel block),
+        # NCCL for the device-side max over ranks
+        dist.init_process_group("cpu:gloo,cuda:nccl", timeout=timedelta(seconds=300),
                                 device_id=torch.device("cuda", local_rank))
 
     ctx = mi.MetalContext(local_rank)
@@ -206,8 +222,6 @@ def run_ours(args, rank, world, local_rank):
     for _ in range(args.warmup):
         ev = one_step()
         ev[2].synchronize()
-    # The generated ids must match the oracle's greedy ids (checked once).
-    ids = cache.tokens(PROMPT, DECODE + 1)
 
     if dist:
         dist.barrier()
@@ -219,6 +233,14 @@ def run_ours(args, rank, world, local_rank):
             events.append(one_step())
         torch.cuda.synchronize()
         wall = time.perf_counter() - t0
+    # Validation of the timed run: no bounded device wait expired (a launch
+    # that gave up would leave early and be timed as fast: kernel_status
+    # raises MI_ERR_TIMEOUT), and the last request's ids (read through the
+    # cache's token ring) are the CPU oracle's greedy ids for this config,
+    # committed as tests/golden/qwen3_0_6b_greedy.json.
+    ctx.kernel_status()
+    ids = cache.tokens(PROMPT, DECODE + 1)
+    golden = golden_ids()
     prefill_ms = sum(e0.elapsed_time(e1) for e0, e1, _ in events)
     decode_ms = sum(e1.elapsed_time(e2) for _, e1, e2 in events)
     total_ms = sum(e0.elapsed_time(e2) for e0, _, e2 in events)
@@ -240,6 +262,7 @@ def run_ours(args, rank, world, local_rank):
         dt = time.perf_counter() - t
         if i >= args.warmup:
             e2e_times.append(dt)
+    ctx.kernel_status()
     e2e_s = sum(e2e_times)
     if dist:
         t = torch.tensor([e2e_s], device="cuda", dtype=torch.float64)
@@ -311,7 +334,16 @@ def run_ours(args, rank, world, local_rank):
     per_gpu_tps = decode_tps / world
 
     ok = bool(np.array_equal(ids, out_ids)) if out_ids is not None else False
+    n_cmp = min(len(golden), DECODE + 1)
+    match_golden = bool(np.array_equal(ids[:n_cmp], golden[:n_cmp]))
+    match_golden_e2e = bool(out_ids is not None and np.array_equal(out_ids[:n_cmp], golden[:n_cmp]))
+
     persistent = model.decode_persistent()
+    # Tensor parallelism: Qwen3-8B sharded over the same
+    # ranks (TP1 on one GPU), after the replica model is freed.
+    del model, cache
+    ctx.synchronize()
+    tp_block = None if args.no_tp_report else tp_report(args, ctx, rank, world, dist)
     layer_launches = 5 * CONFIG["num_hidden_layers"] + 1
     prefill_launches = 1 + 14 * CONFIG["num_hidden_layers"] + 2
     decode_launches = 1 if persistent else DECODE * layer_launches
@@ -324,24 +356,29 @@ def run_ours(args, rank, world, local_rank):
             "ms_per_step": round(total_ms / args.steps, 3), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f16",
             "data": "synthetic (random-init FP16 N(0,0.02) weights, uniform prompt ids)",
-            "config": {"workload": "Qwen3-0.6B batch-1 greedy: 128-token prompt + 256 decode "
-                                   "steps (BASELINE config 2)",
-                       "layers": 28, "hidden": 1024, "vocab": 151936, "prompt": PROMPT,
-                       "decode_steps": DECODE, "kv_capacity": CAPACITY,
-                       "parallelism": f"replicas x{world}",
-                       "l2": "weights 1.2 GB > 126 MB L2 (no flush needed)"},
+            "config": workload_config(world),
             "prefill_tokens_per_s": round(prefill_tps, 1),
             "decode_hbm": {"bytes_per_token": int(bytes_tok),
                            "achieved_gbs": round(bytes_tok * per_gpu_tps / 1e9, 1),
                            "peak_gbs": hbm, "frac": round(bytes_tok * per_gpu_tps / 1e9 / hbm, 4),
                            "note": f"weights + KV bytes per token / time, {peak_kind} peak"},
             "greedy_ids_consistent": ok,
+            "ids_match_golden": match_golden and match_golden_e2e,
+            "validation": {"kernel_status": "ok (no bounded device wait expired)",
+                           "ids_vs_golden": f"{n_cmp} ids of the timed run and of the e2e "
+                                            "generate call vs the CPU oracle's greedy ids "
+                                            "(tests/golden/qwen3_0_6b_greedy.json)",
+                           "timed_ids_match": match_golden, "e2e_ids_match": match_golden_e2e,
+                           "decode_paths_agree": ok},
             "e2e": {"value": round(e2e_tps, 2), "unit": "tokens/s",
                     "h2d_bytes_per_step": PROMPT * 4, "d2h_bytes_per_step": (DECODE + 1) * 4,
                     "note": "mi_qwen3_generate per request (prefill included), host clock"},
             "roofline": {"bound": "hbm", "kernel": dominant, "achieved": round(achieved, 1),
                          "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4),
                          "traffic": traffic, "bytes_per_launch": dom_bytes,
+                         "traffic_source": "not measured in this run: ncu DRAM bytes of the "
+                                           "committed summary profiles/ncu_traffic.md, scaled "
+                                           "to this launch's steps",
                          "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)"},
             "decode_path": "persistent kernel" if persistent else "kernel chain (CUDA graph)",
             "sampled_decode": sampled,
@@ -350,13 +387,105 @@ def run_ours(args, rank, world, local_rank):
             "clocks": clocks.summary(),
             "wall_s": round(wall, 3),
         }
+        if tp_block is not None:
+            line["tp"] = tp_block
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(args.cpu_sample_steps)
         print(json.dumps(line), flush=True)
-    del model, cache
     if dist:
         dist.barrier()
         dist.destroy_process_group()
+    if not (match_golden and match_golden_e2e and ok):
+        sys.exit("bench: the generated ids differ from the oracle's greedy ids")
+
+
+def golden_ids():
+    import numpy as np
+    with open(os.path.join(ROOT, "tests", "golden", "qwen3_0_6b_greedy.json")) as f:
+        g = json.load(f)
+    assert g["seed"] == SEED and g["prompt_len"] == PROMPT and g["prompt_stream"] == INPUT_STREAM
+    return np.array(g["ids"], dtype=np.uint32)
+
+
+TP_REPORT_STEPS = 2  # timed requests of the tensor-parallel block (after one warm-up)
+
+
+def tp_report(args, ctx, rank, world, dist):
+    """BASELINE config 3 at TP = the bench's GPU count: Qwen3-8B shapes
+    (seed 3), a 2048-token prompt then 512 greedy decode steps, capacity
+    4096, one warm-up request and TP_REPORT_STEPS timed ones. Heads, MLP
+    columns and LM-head rows are split over the ranks; the persistent decode
+    kernel exchanges the row-parallel O / down partials and the argmax
+    records through the ranks' mailboxes over NVLink. Device times are the
+    max over ranks."""
+    import numpy as np
+    import torch
+    import metal_infer as mi
+
+    name, cfg, seed, prompt_len, decode, cfg_id = TP_WORKLOADS["8b-tp"]
+    capacity = 4096
+    ident = mi.share_nccl_id() if world > 1 else bytes(128)
+    model = mi.Qwen3Model.random_tp(ctx, cfg, seed=seed, tp=world, rank=rank, nccl_id=ident)
+    prompt = synthetic_tokens(ctx, seed, prompt_len, cfg["vocab_size"])
+    stream = torch.cuda.ExternalStream(ctx.stream())
+    times, waits, ids = [], [], None
+    for i in range(1 + TP_REPORT_STEPS):
+        cache = model.kv_cache(capacity)
+        slot = ctx.empty([1], mi.DType.U32)
+        e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+        e0.record(stream)
+        model.prefill_argmax(prompt, cache, slot)
+        e1.record(stream)
+        model.decode_steps(cache, decode)
+        e2.record(stream)
+        e2.synchronize()
+        ctx.kernel_status()
+        if i >= 1:
+            times.append((e0.elapsed_time(e1), e1.elapsed_time(e2)))
+            waits.append(model.exchange_wait()["mean_s"])
+        ids = cache.tokens(prompt_len, decode + 1)
+        del cache
+    prefill_ms = sum(t[0] for t in times)
+    decode_ms = sum(t[1] for t in times)
+    wait_s = sum(waits)
+    agree = True
+    if world > 1:
+        t = torch.tensor([prefill_ms, decode_ms, wait_s], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        prefill_ms, decode_ms, wait_s = (float(x) for x in t.tolist())
+        mine = torch.tensor(ids.astype(np.int64), device="cuda")
+        ref = mine.clone()
+        dist.broadcast(ref, src=0)
+        same = torch.tensor([int(bool(torch.equal(mine, ref)))], device="cuda")
+        dist.all_reduce(same, op=dist.ReduceOp.MIN)
+        agree = bool(same.item())
+    persistent = model.decode_persistent()
+    del model
+    ctx.synchronize()
+    tokens = decode * len(times)
+    tps = tokens / (decode_ms / 1e3)
+    kv_mean = prompt_len + (decode + 1) / 2.0
+    per_rank = tp_decode_bytes_per_token(cfg, world, kv_mean)
+    hbm, peak_kind = peaks()
+    gbs = per_rank * tps / 1e9
+    return {
+        "workload": f"{name} TP{world} (BASELINE config {cfg_id}): {prompt_len}-token prompt + "
+                    f"{decode} greedy decode steps, capacity {capacity}, seed {seed}",
+        "tp": world, "nccl_ranks": world if world > 1 else 0,
+        "decode_tokens_per_s": round(tps, 2),
+        "ms_per_token": round(decode_ms / tokens, 4),
+        "prefill_tokens_per_s": round(prompt_len * len(times) / (prefill_ms / 1e3), 1),
+        "hbm_per_gpu": {"bytes_per_token_per_rank": int(per_rank), "achieved_gbs": round(gbs, 1),
+                        "peak_gbs": hbm, "frac": round(gbs / hbm, 4),
+                        "note": f"this rank's weight + KV bytes per token / time, {peak_kind} peak"},
+        "exchange_wait_us_per_token": round(wait_s / tokens * 1e6, 3) if world > 1 else 0.0,
+        "exchange_note": "mean over CTAs of the time spent waiting on the O / down / LM-head "
+                         "mailbox counters (partials of the other ranks over NVLink), max over "
+                         "ranks" if world > 1 else "one GPU: no exchange",
+        "decode_path": "persistent kernel" if persistent else "per-kernel chain + NCCL all-gathers",
+        "ids_ranks_agree": agree,
+        "timed_requests": len(times),
+    }
 
 
 def read_traffic(kernel):
@@ -370,6 +499,16 @@ def read_traffic(kernel):
     except OSError:
         pass
     return None
+
+
+def workload_config(world):
+    """The `config` of both arms' lines (the same workload)."""
+    return {"workload": f"Qwen3-0.6B batch-1 greedy: {PROMPT}-token prompt + {DECODE} decode "
+                        "steps (BASELINE config 2)",
+            "layers": 28, "hidden": 1024, "vocab": 151936, "prompt": PROMPT,
+            "decode_steps": DECODE, "kv_capacity": CAPACITY,
+            "parallelism": f"replicas x{world}",
+            "l2": "weights 1.2 GB > 126 MB L2 (no flush needed)"}
 
 
 # ---- CPU legs ---------------------------------------------------------------------------
@@ -402,38 +541,54 @@ def cpu_baseline(decode_steps: int):
 
 
 def run_reference(args, rank):
+    """The reference arm: the reference's kernels restated in C++ (oracle/) on
+    the host cores, on the same workload as our arm. After the 128-token
+    prompt (untimed) the timed steps together decode the request's 256 greedy
+    tokens in order, each step a consecutive slice of them (so the mean KV
+    length, 256.5, is our arm's); warm-up steps decode a slice and roll the
+    cache back to the prompt. The ids are checked against the committed
+    golden ids of the same config."""
     if rank != 0:
         return
     import numpy as np
     import oracle as O
-    m, tok, prefill_s = oracle_decode_rate(0)
-    per_step = args.cpu_sample_steps_ref
-    times = []
-    for i in range(args.warmup + args.steps):
-        t = time.perf_counter()
-        for _ in range(per_step):
+    m, first, prefill_s = oracle_decode_rate(0)
+    base = len(m)
+    slices = [DECODE // args.steps + (1 if i < DECODE % args.steps else 0)
+              for i in range(args.steps)]
+    for _ in range(args.warmup):
+        tok = first
+        for _ in range(max(slices)):
             tok = O.argmax(m.forward(np.array([tok], np.uint32)))
-        if i >= args.warmup:
-            times.append(time.perf_counter() - t)
-        if len(m) + per_step > CAPACITY:
-            m.reset()
-            tok = O.argmax(m.forward(O.gen_tokens(SEED, INPUT_STREAM, PROMPT, CONFIG["vocab_size"])))
+        m.truncate(base)
+    tok, ids, times = first, [first], []
+    for n in slices:
+        t = time.perf_counter()
+        for _ in range(n):
+            tok = O.argmax(m.forward(np.array([tok], np.uint32)))
+            ids.append(tok)
+        times.append(time.perf_counter() - t)
     threads = O.lib().or_num_threads()
-    value = args.steps * per_step / sum(times)
+    m.close()
+    golden = golden_ids()
+    n_cmp = min(len(golden), len(ids))
+    match = bool(np.array_equal(np.array(ids[:n_cmp], np.uint32), golden[:n_cmp]))
+    value = sum(slices) / sum(times)
     sample = (f"reference path restated in C++ (oracle/, OpenMP {threads} threads; the Rust/Metal "
-              f"reference cannot run here): {per_step} greedy decode steps per step after a "
-              "128-token prefill, Qwen3-0.6B seed 2")
+              f"reference cannot run here): after the {PROMPT}-token prompt ({prefill_s:.1f} s, "
+              f"untimed) the {args.steps} timed steps decode the {sum(slices)} greedy tokens in "
+              f"order ({min(slices)}-{max(slices)} per step), Qwen3-0.6B seed 2")
     line = {"impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "tokens/s",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(1e3 * sum(times) / args.steps, 3), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
-            "config": {"workload": "Qwen3-0.6B batch-1 greedy decode (BASELINE config 2)",
-                       "prompt": PROMPT},
+            "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+            "data": "synthetic (random-init FP16 N(0,0.02) weights, uniform prompt ids)",
+            "config": workload_config(args.gpus),
+            "ids_match_golden": match,
             "cpu_baseline": {"value": round(value, 3), "unit": "tokens/s", "cores": threads,
                              "kind": "port", "sample": sample},
             "e2e": {"value": round(value, 3), "unit": "tokens/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
-    m.close()
     print(json.dumps(line), flush=True)
 
 
@@ -658,8 +813,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-sampled-report", action="store_true",
                     help="skip the untimed sampled-decode report (short profiling runs)")
+    ap.add_argument("--no-tp-report", action="store_true",
+                    help="skip the Qwen3-8B tensor-parallel block (short profiling runs)")
     ap.add_argument("--cpu-sample-steps", type=int, default=48)
-    ap.add_argument("--cpu-sample-steps-ref", type=int, default=8)
     ap.add_argument("--decode-steps", type=int, default=None,
                     help="decode steps per request (smaller only for profiler launch lists)")
     args = ap.parse_args()

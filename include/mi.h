@@ -199,7 +199,9 @@ mi_status mi_batch_commit(mi_batch* b, mi_pending** out);
 mi_status mi_batch_finish(mi_batch* b, mi_dispatch_stats* stats);
 /* Dropping an uncommitted batch. */
 void mi_batch_abandon(mi_batch* b);
-/* PendingBatch::wait: consumes the pending handle; stats may be NULL. */
+/* PendingBatch::wait: consumes the pending handle; stats may be NULL.
+ * Returns MI_ERR_TIMEOUT when a kernel's bounded device wait expired (its
+ * outputs are not valid), as mi_context_kernel_status reports it. */
 mi_status mi_pending_wait(mi_pending* p, mi_dispatch_stats* stats);
 /* Non-consuming completion query: 1 done, 0 running. */
 int mi_pending_is_complete(const mi_pending* p);
@@ -281,9 +283,11 @@ mi_status mi_batch_copy_into_cache(mi_batch* b, const mi_tensor* source, mi_tens
  * partials plus 64 merge counters), held by every GPU that loads the library
  * until exit. Limits: head_dim 128, GQA ratio 1/2/4/8, block_keys 32/64/
  * 128/256, kv_heads <= 64, kv_heads * ceil(length / block_keys) * ratio *
- * 130 * 4 <= 1 MiB; larger sizes return MI_ERR_SHAPE. The first call on a
- * device looks up the array's device address (make it before any stream
- * capture). Calls share the array: calls that overlap on the GPU race. */
+ * 130 * 4 <= 1 MiB; larger sizes return MI_ERR_SHAPE. The first call in a
+ * CUDA context looks up the array's device address in that context (make it
+ * before any stream capture); `stream` must belong to the current context
+ * (else MI_ERR_INVALID_ARGUMENT). Calls share the array: calls that overlap
+ * on the GPU race. */
 mi_status mi_attention_flash_decode_noalloc(const void* query, const void* key,
                                             const void* value, void* out, size_t query_heads,
                                             size_t kv_heads, size_t head_dim, size_t length,
@@ -397,6 +401,14 @@ mi_status mi_qwen3_set_fusion_options(mi_qwen3* m, mi_fusion_options options);
 mi_fusion_options mi_qwen3_fusion_options(const mi_qwen3* m);
 /* Decode steps run as one CUDA graph (default on); 0 launches eagerly. */
 mi_status mi_qwen3_set_decode_graphs(mi_qwen3* m, int enabled);
+/* Tensor-parallel diagnostics (no reference counterpart: the reference is
+ * single-device). Synchronizes, then reports how long the CTAs of the most
+ * recent persistent decode launch waited on their mailbox counters (the O,
+ * DOWN and LM-head partials of the other ranks arriving over NVLink):
+ * the mean and the maximum over CTAs in seconds, and that launch's decode
+ * steps. Zeros when tp = 1 or no persistent launch ran. */
+mi_status mi_qwen3_exchange_wait(mi_qwen3* m, double* mean_seconds, double* max_seconds,
+                                 size_t* steps);
 /* No counterpart in the reference (its decode encodes one command buffer per
  * step). Greedy decode steps run in one persistent cooperative kernel per
  * call (default on, also off with the environment variable
@@ -436,13 +448,18 @@ mi_status mi_qwen3_decode_argmax(mi_qwen3* m, const mi_tensor* token, mi_kv_cach
  * and bench.rs run_pipelined_decode (bench.rs:1850-1895): enqueues `steps`
  * decode steps, each feeding the previous step's argmax (kept on the
  * device), without waiting. The cache must hold a prefilled prompt. Ids are
- * read back with mi_kv_cache_tokens. */
+ * read back with mi_kv_cache_tokens. A launch whose bounded device wait
+ * expired (it then leaves early and its ids are not valid) is reported as
+ * MI_ERR_TIMEOUT by the next synchronizing call: mi_kv_cache_tokens,
+ * mi_qwen3_generate*, mi_pending_wait or mi_context_kernel_status. */
 mi_status mi_qwen3_decode_steps(mi_qwen3* m, mi_kv_cache* cache, size_t steps);
 /* Copies cache positions [start, start + count) of the token ring (prompt
  * ids, then the greedy ids fed back; position len holds the next id) to the
- * host; synchronizes the context stream. */
+ * host; synchronizes the context stream, then returns MI_ERR_TIMEOUT if a
+ * bounded device wait expired in the work before it. */
 mi_status mi_kv_cache_tokens(mi_kv_cache* cache, size_t start, size_t count, uint32_t* out);
-/* Qwen3Model::generate (qwen3.rs:424-439): greedy, max_tokens ids. */
+/* Qwen3Model::generate (qwen3.rs:424-439): greedy, max_tokens ids;
+ * MI_ERR_TIMEOUT if a bounded device wait of its launches expired. */
 mi_status mi_qwen3_generate(mi_qwen3* m, const uint32_t* prompt, size_t prompt_len,
                             size_t max_tokens, mi_kv_cache* cache, uint32_t* out_ids,
                             size_t* out_count);

@@ -18,7 +18,11 @@
 //                        probabilities to FP16 (transformer.metal:1614-1822)
 // All reductions follow numerics.cuh.
 
+#include <cuda.h>
+
 #include <mutex>
+#include <utility>
+#include <vector>
 
 #include "device.cuh"
 #include "pipeline.cuh"
@@ -730,26 +734,59 @@ namespace {
 constexpr size_t kNoAllocPartialBytes = size_t(1) << 20;  // FP32 block partials
 constexpr size_t kNoAllocMaxKvHeads = 64;                  // one u32 counter each
 constexpr size_t kNoAllocBytes = kNoAllocPartialBytes + kNoAllocMaxKvHeads * sizeof(uint32_t);
-constexpr int kNoAllocMaxDevices = 64;
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocBytes];
 
 std::mutex g_noalloc_mutex;
-void* g_noalloc_ptr[kNoAllocMaxDevices] = {};
+std::vector<std::pair<CUcontext, void*>> g_noalloc_ptr;  // per CUDA context
 
-// Device address of the scratch array on the current device, looked up once
-// per device (the array's host-side name is not a device address).
-void* noalloc_scratch(int device) {
+// Driver entry points through the runtime (the library does not link
+// libcuda directly, so that it loads on hosts without a driver).
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+using StreamGetCtxFn = CUresult (*)(CUstream, CUcontext*);
+template <typename F>
+F driver_fn(const char* name) {
+  void* f = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  if (cudaGetDriverEntryPoint(name, &f, cudaEnableDefault, &q) != cudaSuccess ||
+      q != cudaDriverEntryPointSuccess || !f)
+    fail(MI_ERR_RESOURCE, "driver entry point %s is unavailable", name);
+  return reinterpret_cast<F>(f);
+}
+CUresult ctx_get_current(CUcontext* c) {
+  static const CtxGetCurrentFn fn = driver_fn<CtxGetCurrentFn>("cuCtxGetCurrent");
+  return fn(c);
+}
+CUresult stream_get_ctx(CUstream s, CUcontext* c) {
+  static const StreamGetCtxFn fn = driver_fn<StreamGetCtxFn>("cuStreamGetCtx");
+  return fn(s, c);
+}
+
+// Device address of the scratch array in the current CUDA context, looked up
+// once per context (the array's host-side name is not a device address; the
+// module, and so the address, belongs to a context, not to a device ordinal).
+// Returns the context too, so that the caller can check its stream against it.
+void* noalloc_scratch(CUcontext* ctx_out) {
   std::lock_guard<std::mutex> lock(g_noalloc_mutex);
-  if (!g_noalloc_ptr[device]) {
+  CUcontext cur = nullptr;
+  if (ctx_get_current(&cur) != CUDA_SUCCESS || !cur) {
+    // no context current yet: the runtime call below makes the device's
+    // primary context current
     void* ptr = nullptr;
     cudaError_t err = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
-    if (err != cudaSuccess || !ptr)
+    if (err != cudaSuccess || !ptr || ctx_get_current(&cur) != CUDA_SUCCESS || !cur)
       fail(MI_ERR_RESOURCE, "cannot resolve the decode scratch array: %s",
            cudaGetErrorString(err));
-    g_noalloc_ptr[device] = ptr;
   }
-  return g_noalloc_ptr[device];
+  *ctx_out = cur;
+  for (const auto& e : g_noalloc_ptr)
+    if (e.first == cur) return e.second;
+  void* ptr = nullptr;
+  cudaError_t err = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+  if (err != cudaSuccess || !ptr)
+    fail(MI_ERR_RESOURCE, "cannot resolve the decode scratch array: %s", cudaGetErrorString(err));
+  g_noalloc_ptr.emplace_back(cur, ptr);
+  return ptr;
 }
 
 }  // namespace
@@ -788,12 +825,18 @@ extern "C" mi_status mi_attention_flash_decode_noalloc(const void* query, const 
                "kv_heads x blocks x group x 130 x 4 = %zu bytes exceeds the %zu-byte scratch "
                "(lengthen block_keys or split the call)",
                partial_bytes, kNoAllocPartialBytes);
-    int device = 0;
-    MI_CUDA(cudaGetDevice(&device));
-    MI_REQUIRE(device >= 0 && device < kNoAllocMaxDevices, MI_ERR_NO_DEVICE, "device %d", device);
-    uint8_t* scratch = static_cast<uint8_t*>(noalloc_scratch(device));
+    CUcontext cur = nullptr;
+    uint8_t* scratch = static_cast<uint8_t*>(noalloc_scratch(&cur));
     uint32_t* counters = reinterpret_cast<uint32_t*>(scratch + kNoAllocPartialBytes);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
+    // The scratch belongs to the current context: a stream of another
+    // context (another device) would have the kernel and the counter reset
+    // reach this context's array across devices.
+    CUcontext stream_ctx = nullptr;
+    MI_REQUIRE(stream_get_ctx(reinterpret_cast<CUstream>(s), &stream_ctx) == CUDA_SUCCESS &&
+                   stream_ctx == cur,
+               MI_ERR_INVALID_ARGUMENT,
+               "the stream must belong to the current device's CUDA context");
     // The merge counters must start at zero (the kernel leaves them at zero,
     // but an interrupted earlier call may not have).
     MI_CUDA(cudaMemsetAsync(counters, 0, kv_heads * sizeof(uint32_t), s));

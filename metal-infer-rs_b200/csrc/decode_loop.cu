@@ -57,7 +57,8 @@ constexpr int kMaxSlots = 16;
 constexpr int kUnitsDone = 2;
 constexpr int kStageDone = 8;
 constexpr int kPart = HD + 4;  // partial record: max, denominator, 2 pad, 128 numerators
-constexpr int kSyncWords = 256;
+constexpr int kSyncWords = 512;
+constexpr int kWaitWord0 = 256;  // per-CTA mailbox wait time (64 ns units)
 constexpr int kMaxKvHeads = 64;
 constexpr int kMaxDownRows = 64;
 constexpr int kMaxGrid = 256;
@@ -199,6 +200,7 @@ struct Shared {
   uint32_t best_key[kConsumerWarps];
   uint32_t best_idx[kConsumerWarps];
   uint32_t token;
+  unsigned long long mbox_ns;  // thread 0: time spent in mailbox waits this launch
   volatile int abort;  // raised by any warp (or the producer) that gives up
   int stop;            // the consumers' uniform decision, written by one thread between barriers
   int astop;           // the same for the attention warps
@@ -382,13 +384,20 @@ __device__ __forceinline__ void push_count(const DecodeLoop& p, int k) {
   for (int r = 0; r < p.tp; ++r) red_sys_add_u64(p.peers[r] + mb.ctr + 16 * k, 1ull);
 }
 
-// Single thread: wait until this rank's mailbox counter k reaches target.
+// Single thread (thread 0): wait until this rank's mailbox counter k
+// reaches target; the time it takes is added to sh.mbox_ns.
 __device__ bool wait_mbox(const DecodeLoop& p, int k, unsigned long long target, Shared& sh) {
   const MailboxLayout mb = mailbox_layout(p.tp, p.hidden, gridDim.x);
+  const uint64_t t0 = pipe::global_ns();
   PollClock clock;
+  bool ok = true;
   while (ld_sys_u64(p.mbox + mb.ctr + 16 * k) < target)
-    if (!clock.keep_going(p, sh)) return false;
-  return true;
+    if (!clock.keep_going(p, sh)) {
+      ok = false;
+      break;
+    }
+  sh.mbox_ns += pipe::global_ns() - t0;
+  return ok;
 }
 
 // Chunk c (8 values) of the ranks' partials in region `region`, summed in
@@ -717,6 +726,7 @@ __device__ bool build_input(const DecodeLoop& p, const StageIn& in, int wait_st,
     MI_TRACE_ARRIVE(1);
   }
   consumers_sync();
+  if (tid == 0) MI_TRACE_CUR(9);
   uint4 g_first = make_uint4(0, 0, 0, 0);
   if (norm && tid < kc) g_first = __ldg(g4 + tid);
   for (int c = tid; c < kc; c += kConsumers) {
@@ -742,12 +752,14 @@ __device__ bool build_input(const DecodeLoop& p, const StageIn& in, int wait_st,
     if (in.wb && blockIdx.x == 0) put8(in.wb, c, v, in.wbtag);
   }
   consumers_sync();
+  if (tid == 0) MI_TRACE_CUR(10);
   if (norm) {
     if (tid < 32) {
       const float total = canon_reduce(staged_sumsq(in.mode, xs, xs2, kc, lane), canon_lanes(in.k));
       if (lane == 0) sh.scale = rms_scale(total, in.k, p.eps);
     }
     consumers_sync();
+    if (tid == 0) MI_TRACE_CUR(15);
     const float scale = sh.scale;
     for (int c = tid; c < kc; c += kConsumers) {
       const uint4 v = two ? add_chunk(in.mode, xs[c], xs2[c]) : xs[c];
@@ -906,8 +918,10 @@ __device__ void reduce_rows_p(const DecodeLoop& p, const StageW& s, const Tiles&
       }
     }
     __syncwarp();
+    if (threadIdx.x == 0 && tile == 0) MI_TRACE_CUR(6);
     if (lane == 0) mbar_arrive(&sh.empty[slot]);
   }
+  if (threadIdx.x == 0) MI_TRACE_CUR(7);
 }
 
 template <int ST>
@@ -1235,6 +1249,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_loop_kernel(DecodeLoop par
     for (int st = 0; st < 5; ++st) sh.tiles[st] = tiles_of(p, stage_weights(p, lay, 0, st));
     sh.stop = 0;
     sh.astop = 0;
+    sh.mbox_ns = 0;
     for (int s = 0; s < p.slots; ++s) {
       pipe::mbar_init(&sh.full[s], 1);
       pipe::mbar_init(&sh.empty[s], kConsumerWarps);
@@ -1489,6 +1504,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_loop_kernel(DecodeLoop par
     }
   }
   if (blockIdx.x == 0 && tid == 0) *p.dev_len = len0 + (uint32_t)p.steps;
+  if (tid == 0 && p.tp > 1)
+    p.sync[kWaitWord0 + blockIdx.x] = (uint32_t)min(sh.mbox_ns >> 6, 0xFFFFFFFFull);
 }
 
 template <int G>
@@ -1566,6 +1583,8 @@ void decode_loop(cudaStream_t stream, const DecodeLoop& p) {
              "decode loop plan missing");
   MI_CUDA(cudaMemsetAsync(p.sync, 0, kSyncWords * sizeof(uint32_t), stream));
   static_assert(kSyncWords == decode_loop_sync_words(), "sync buffer size");
+  static_assert(kWaitWord0 == decode_loop_wait_word0() && kWaitWord0 + kMaxGrid <= kSyncWords,
+                "sync buffer layout");
   const size_t smem = decode_loop_smem(p);
   cudaError_t err = cudaErrorInvalidValue;
   switch (p.qh / p.kvh) {

@@ -294,8 +294,11 @@ void decode_loop(cudaStream_t stream, const DecodeLoop& p);
 inline size_t decode_loop_part_floats(int kvh, int blocks, int group) {
   return (size_t)kvh * blocks * group * (128 + 4);
 }
-// u32 words of DecodeLoop::sync.
-constexpr size_t decode_loop_sync_words() { return 256; }
+// u32 words of DecodeLoop::sync: 256 control words, then one word per CTA
+// (at most 256 CTAs) with the time its mailbox waits took in the launch
+// (tensor parallelism only), in units of 64 ns.
+constexpr size_t decode_loop_sync_words() { return 512; }
+constexpr size_t decode_loop_wait_word0() { return 256; }
 // Expired-wait code of the persistent kernel (0 = none), optionally cleared.
 unsigned decode_loop_status(bool reset);
 

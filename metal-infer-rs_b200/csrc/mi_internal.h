@@ -145,6 +145,13 @@ void context_retain(mi_context* ctx);
 void context_release(mi_context* ctx);
 void* context_scratch(mi_context* ctx, size_t bytes);
 void sync_context(mi_context* ctx);
+// First code recorded by any kernel's bounded device wait since the last
+// read (0: none), cleared when read. Call after a synchronization.
+unsigned take_device_wait_status();
+// Fails with MI_ERR_TIMEOUT when a bounded device wait expired (after a
+// synchronization): a launch that gave up returns early, so its outputs are
+// not valid and must not be reported as a result.
+void check_device_waits(const char* what);
 
 // Per-launch profiling hooks (CUDA events around a launch when enabled).
 struct ProfileScope {

@@ -137,6 +137,7 @@ struct mi_qwen3 {
   bool persistent = true;  // decode through the persistent kernel when it fits
   bool sampling = false;   // LM heads draw tokens (generate_with, temperature > 0)
   int loop_state = 0;      // 0 unplanned, 1 planned, -1 not admitted
+  int last_loop_steps = 0; // decode steps of the most recent persistent launch
   k::DecodeLoop loop;
   Workspace ws;
   uint64_t plan_version = 1;  // bumps invalidate captured graphs
@@ -625,6 +626,7 @@ void run_decode_loop(mi_qwen3* m, mi_kv_cache* c, size_t steps) {
     for (int i = 0; i < 3; ++i) p.ctr_base[i] = m->mbox.ctr_base[i];
     ProfileScope ps(ctx, "decode_loop");
     k::decode_loop(ctx->stream, p);
+    m->last_loop_steps = p.steps;
     w.loop_epoch += (uint64_t)p.steps * (uint64_t)p.layers;
     const unsigned long long per_step = (unsigned long long)m->tp * p.grid;
     m->mbox.ctr_base[0] += per_step * p.steps * p.layers;
@@ -1231,6 +1233,32 @@ mi_status mi_qwen3_set_decode_persistent(mi_qwen3* m, int enabled) {
   });
 }
 
+mi_status mi_qwen3_exchange_wait(mi_qwen3* m, double* mean_seconds, double* max_seconds,
+                                 size_t* steps) {
+  return guard([&] {
+    require(m, "model");
+    require(mean_seconds, "mean_seconds");
+    require(max_seconds, "max_seconds");
+    require(steps, "steps");
+    *mean_seconds = *max_seconds = 0.0;
+    *steps = (size_t)m->last_loop_steps;
+    if (m->tp == 1 || !m->ws.loop_sync.t || m->last_loop_steps == 0) return;
+    const int grid = m->loop.grid;
+    std::vector<uint32_t> words((size_t)grid);
+    MI_CUDA(cudaMemcpyAsync(words.data(), m->ws.loop_sync.t->u32() + k::decode_loop_wait_word0(),
+                            words.size() * 4, cudaMemcpyDeviceToHost, m->ctx->stream));
+    MI_CUDA(cudaStreamSynchronize(m->ctx->stream));
+    double sum = 0.0, mx = 0.0;
+    for (uint32_t v : words) {
+      const double sec = (double)v * 64e-9;
+      sum += sec;
+      mx = std::max(mx, sec);
+    }
+    *mean_seconds = sum / grid;
+    *max_seconds = mx;
+  });
+}
+
 mi_status mi_qwen3_decode_persistent(mi_qwen3* m, int* active) {
   return guard([&] {
     require(m, "model");
@@ -1454,6 +1482,8 @@ size_t generate_greedy(mi_qwen3* m, mi_kv_cache* c, const uint32_t* prompt, size
     MI_CUDA(cudaMemcpyAsync(ids.data() + have, c->toks.t->u32() + prompt_len + have,
                             (avail - have) * 4, cudaMemcpyDeviceToHost, m->ctx->stream));
     MI_CUDA(cudaStreamSynchronize(m->ctx->stream));
+    // a launch whose bounded wait expired left early: its ids are not valid
+    check_device_waits("generate");
     have = avail;
     for (; seen < have && stop_index == max_tokens; ++seen) {
       uint32_t tok = ids[seen];
@@ -1508,6 +1538,9 @@ mi_status mi_kv_cache_tokens(mi_kv_cache* cache, size_t start, size_t count, uin
     MI_CUDA(cudaMemcpyAsync(out, cache->toks.t->u32() + start, count * 4, cudaMemcpyDeviceToHost,
                             ctx->stream));
     MI_CUDA(cudaStreamSynchronize(ctx->stream));
+    // decode_steps is asynchronous: a timed-out launch is reported here,
+    // at the first call that reads its ids
+    check_device_waits("kv_cache_tokens");
   });
 }
 

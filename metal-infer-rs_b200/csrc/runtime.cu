@@ -124,6 +124,20 @@ void* context_scratch(mi_context* ctx, size_t bytes) {
 
 void sync_context(mi_context* ctx) { MI_CUDA(cudaStreamSynchronize(ctx->stream)); }
 
+unsigned take_device_wait_status() {
+  unsigned code = k::gemm_tc_status(true);
+  if (unsigned g = k::gemv_status(true)) code = code ? code : g;
+  if (unsigned a = k::attention_status(true)) code = code ? code : a;
+  if (unsigned d = k::decode_loop_status(true)) code = code ? code : d;
+  return code;
+}
+
+void check_device_waits(const char* what) {
+  if (unsigned code = take_device_wait_status())
+    fail(MI_ERR_TIMEOUT, "%s: a bounded device wait expired (code 0x%x); the results are not valid",
+         what, code);
+}
+
 ProfileScope::ProfileScope(mi_context* c, const char* n) : ctx(c), name(n) {
   if (!ctx || !ctx->profiling) return;
   cudaStreamCaptureStatus cs;
@@ -309,10 +323,7 @@ mi_status mi_context_kernel_status(mi_context* ctx, uint32_t* code) {
     require_ctx(ctx, "ctx");
     require_ctx(code, "code");
     sync_context(ctx);
-    *code = k::gemm_tc_status(true);
-    if (unsigned g = k::gemv_status(true)) *code = *code ? *code : g;
-    if (unsigned a = k::attention_status(true)) *code = *code ? *code : a;
-    if (unsigned d = k::decode_loop_status(true)) *code = *code ? *code : d;
+    *code = take_device_wait_status();
   });
   if (st == MI_OK && *code != 0) {
     set_error("a bounded device wait expired (code %u)", *code);
@@ -623,6 +634,7 @@ mi_status mi_pending_wait(mi_pending* p, mi_dispatch_stats* stats) {
     context_release(p->ctx);
     delete p;
     if (err != cudaSuccess) fail(MI_ERR_COMMAND, "command failed: %s", cudaGetErrorString(err));
+    check_device_waits("batch");
     if (stats) {
       stats->gpu_time = ms * 1e-3;
       stats->wall_time = std::chrono::duration<double>(wall).count();

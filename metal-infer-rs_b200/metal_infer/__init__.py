@@ -201,7 +201,7 @@ EXPORTS = [
     "mi_qwen3_config_validate", "mi_qwen3_create_random", "mi_qwen3_load", "mi_qwen3_destroy",
     "mi_qwen3_get_config", "mi_qwen3_set_attention_kind", "mi_qwen3_set_fusion_options",
     "mi_qwen3_fusion_options", "mi_qwen3_set_decode_graphs",
-    "mi_qwen3_set_decode_persistent", "mi_qwen3_decode_persistent",
+    "mi_qwen3_set_decode_persistent", "mi_qwen3_decode_persistent", "mi_qwen3_exchange_wait",
     "mi_tp_shard", "mi_nccl_unique_id", "mi_qwen3_create_random_tp", "mi_qwen3_load_tp", "mi_kv_cache_create",
     "mi_kv_cache_destroy", "mi_kv_cache_len", "mi_kv_cache_capacity", "mi_kv_cache_reset",
     "mi_kv_cache_layer", "mi_qwen3_prefill", "mi_qwen3_decode", "mi_qwen3_prefill_argmax",
@@ -750,6 +750,14 @@ class Qwen3Model:
     def set_decode_persistent(self, enabled: bool) -> None:
         """Decode through the persistent kernel (default) or the kernel chain."""
         _check(lib().mi_qwen3_set_decode_persistent(self._h, ctypes.c_int(int(enabled))))
+
+    def exchange_wait(self) -> dict:
+        """Mailbox waits of the most recent persistent decode launch (tensor
+        parallelism): mean / max over CTAs in seconds, and its decode steps."""
+        mean, mx, steps = ctypes.c_double(0), ctypes.c_double(0), _sz(0)
+        _check(lib().mi_qwen3_exchange_wait(self._h, ctypes.byref(mean), ctypes.byref(mx),
+                                            ctypes.byref(steps)))
+        return {"mean_s": mean.value, "max_s": mx.value, "steps": steps.value}
 
     def decode_persistent(self) -> bool:
         active = ctypes.c_int(0)

@@ -976,6 +976,14 @@ void or_qwen3_set_tp(or_qwen3* m, size_t tp) { m->tp = tp ? tp : 1; }
 
 void or_qwen3_reset(or_qwen3* m) { m->filled = 0; }
 
+// KvCache rollback of generate_greedy (qwen3.rs:475-555): keep the first
+// `len` positions (the cached rows past them are overwritten later).
+int or_qwen3_truncate(or_qwen3* m, size_t len) {
+  if (len > m->filled) return -1;
+  m->filled = len;
+  return 0;
+}
+
 size_t or_qwen3_len(const or_qwen3* m) { return m->filled; }
 
 int or_qwen3_forward_hidden(or_qwen3* m, const uint16_t* hidden, size_t count,

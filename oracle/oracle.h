@@ -157,6 +157,9 @@ void or_qwen3_set_fusion(or_qwen3* m, int qk_rope_cache, int add_rms_norm);
  * input columns, rounded once to FP16. Everything else is unchanged. */
 void or_qwen3_set_tp(or_qwen3* m, size_t tp);
 void or_qwen3_reset(or_qwen3* m);
+/* Keeps the first len cached positions (len <= the current length), as the
+ * reference's generate_greedy rolls its cache back; -1 otherwise. */
+int or_qwen3_truncate(or_qwen3* m, size_t len);
 size_t or_qwen3_len(const or_qwen3* m);
 /* Embeds tokens and runs the model; logits of the last row (half[vocab]).
  * Returns 0 on success, -1 on cache overflow. */

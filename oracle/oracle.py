@@ -61,6 +61,7 @@ def lib():
         L.or_qwen3_set_fusion.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int]
         L.or_qwen3_set_tp.argtypes = [ctypes.c_void_p, ctypes.c_size_t]
         L.or_qwen3_reset.argtypes = [ctypes.c_void_p]
+        L.or_qwen3_truncate.argtypes = [ctypes.c_void_p, _sz]
         L.or_qwen3_len.argtypes = [ctypes.c_void_p]
         L.or_qwen3_len.restype = _sz
         L.or_qwen3_forward.argtypes = [ctypes.c_void_p, _u32p, _sz, _u16p]
@@ -357,6 +358,11 @@ class Qwen3:
 
     def reset(self):
         lib().or_qwen3_reset(self.h)
+
+    def truncate(self, length: int) -> None:
+        """Keeps the first `length` cached positions (a cache rollback)."""
+        if lib().or_qwen3_truncate(self.h, _sz(length)) != 0:
+            raise ValueError(f"cannot truncate a cache of {len(self)} positions to {length}")
 
     def __len__(self):
         return int(lib().or_qwen3_len(self.h))

@@ -58,3 +58,19 @@ def test_tp_workloads_are_configs_3_and_4():
     assert (cfg["hidden_size"], cfg["intermediate_size"], cfg["num_hidden_layers"],
             cfg["num_attention_heads"], seed, prompt, decode, cfg_id) == \
         (5120, 25600, 64, 64, 4, 32768, 256, 4)
+
+
+def test_tp_bytes_per_rank():
+    """A rank reads 1/tp of every sharded matrix and of the KV cache plus the
+    replicated norms: tp = 1 is the one-GPU figure, and tp ranks together
+    read the one-GPU bytes plus (tp - 1) extra copies of the norms."""
+    c = bench.CONFIG_8B
+    L = 2048 + 513 / 2
+    one = bench.decode_bytes_per_token(c, L)
+    assert bench.tp_decode_bytes_per_token(c, 1, L) == pytest.approx(one, rel=1e-12)
+    assert bench.decode_bytes_per_token(c, 0) == 15_136_811_008
+    norms = c["num_hidden_layers"] * 2 * (2 * c["hidden_size"] + 2 * c["head_dim"]) + \
+        2 * c["hidden_size"]
+    for tp in (2, 4, 8):
+        per_rank = bench.tp_decode_bytes_per_token(c, tp, L)
+        assert tp * per_rank == pytest.approx(one + (tp - 1) * norms, rel=1e-12)
