@@ -19,6 +19,7 @@
 // All reductions follow numerics.cuh.
 
 #include <cuda.h>
+#include <cudaTypedefs.h>
 
 #include <mutex>
 #include <utility>
@@ -741,24 +742,27 @@ std::mutex g_noalloc_mutex;
 std::vector<std::pair<CUcontext, void*>> g_noalloc_ptr;  // per CUDA context
 
 // Driver entry points through the runtime (the library does not link
-// libcuda directly, so that it loads on hosts without a driver).
-using CtxGetCurrentFn = CUresult (*)(CUcontext*);
-using StreamGetCtxFn = CUresult (*)(CUstream, CUcontext*);
+// libcuda directly, so that it loads on hosts without a driver). Each is
+// requested at the ABI version whose signature is used here: the
+// unversioned lookup follows the runtime's version, and from CUDA 12.5 on
+// that gives cuStreamGetCtx the three-argument form of cuStreamGetCtx_v2.
 template <typename F>
-F driver_fn(const char* name) {
+F driver_fn(const char* name, unsigned version) {
   void* f = nullptr;
   cudaDriverEntryPointQueryResult q;
-  if (cudaGetDriverEntryPoint(name, &f, cudaEnableDefault, &q) != cudaSuccess ||
+  if (cudaGetDriverEntryPointByVersion(name, &f, version, cudaEnableDefault, &q) != cudaSuccess ||
       q != cudaDriverEntryPointSuccess || !f)
-    fail(MI_ERR_RESOURCE, "driver entry point %s is unavailable", name);
+    fail(MI_ERR_RESOURCE, "driver entry point %s (ABI %u) is unavailable", name, version);
   return reinterpret_cast<F>(f);
 }
 CUresult ctx_get_current(CUcontext* c) {
-  static const CtxGetCurrentFn fn = driver_fn<CtxGetCurrentFn>("cuCtxGetCurrent");
+  static const PFN_cuCtxGetCurrent_v4000 fn =
+      driver_fn<PFN_cuCtxGetCurrent_v4000>("cuCtxGetCurrent", 4000);
   return fn(c);
 }
 CUresult stream_get_ctx(CUstream s, CUcontext* c) {
-  static const StreamGetCtxFn fn = driver_fn<StreamGetCtxFn>("cuStreamGetCtx");
+  static const PFN_cuStreamGetCtx_v9020 fn =
+      driver_fn<PFN_cuStreamGetCtx_v9020>("cuStreamGetCtx", 9020);
   return fn(s, c);
 }
 
