@@ -75,6 +75,7 @@ constexpr int kTraceStages = 5 * 64 + 1;
 constexpr int kTraceEvents = 16;
 static __device__ unsigned long long g_trace[2][2][kTraceStages][kTraceEvents];
 __shared__ int g_trace_cur[2];  // step, stage of the running stage (traced CTAs)
+__shared__ int g_trace_alt;     // events 9 / 10 / 15 of build_input recorded as 11 / 12 / 13
 __device__ __forceinline__ void trace(int step, int stage, int ev) {
   const int c = blockIdx.x == 0 ? 0 : (blockIdx.x == gridDim.x - 1 ? 1 : -1);
   if (c < 0 || step >= 2 || stage >= kTraceStages) return;
@@ -89,10 +90,13 @@ __device__ __forceinline__ void trace_arrive(int step, int stage, int ev) {
 #define MI_TRACE(step, stage, ev) trace(step, stage, ev)
 #define MI_TRACE_ARRIVE(ev) trace_arrive(g_trace_cur[0], g_trace_cur[1], ev)
 #define MI_TRACE_CUR(ev) trace(g_trace_cur[0], g_trace_cur[1], ev)
+#define MI_TRACE_IN(ev) \
+  trace(g_trace_cur[0], g_trace_cur[1], g_trace_alt ? ((ev) == 9 ? 11 : (ev) == 10 ? 12 : 13) : (ev))
 #define MI_TRACE_SET(step, stage) (g_trace_cur[0] = (step), g_trace_cur[1] = (stage))
 #else
 #define MI_TRACE(step, stage, ev) ((void)0)
 #define MI_TRACE_CUR(ev) ((void)0)
+#define MI_TRACE_IN(ev) ((void)0)
 #define MI_TRACE_ARRIVE(ev) ((void)0)
 #define MI_TRACE_SET(step, stage) ((void)0)
 #endif
@@ -105,6 +109,7 @@ constexpr unsigned kCodeEmpty = 0x0200;
 constexpr unsigned kCodeDrain = 0x0400;
 constexpr unsigned kCodeHead = 0x0500;
 constexpr unsigned kCodeTag = 0x0600;
+constexpr unsigned kCodeKv = 0x0700;
 
 struct StageW {
   const __half* w[3];
@@ -173,27 +178,37 @@ __device__ __forceinline__ Tiles tiles_of(const DecodeLoop& p, const StageW& s) 
   return t;
 }
 
+// Shared state of the attention units. K and V tiles arrive by TMA as two
+// 64-column halves of kTile rows each, 128-byte swizzled (16-byte chunk c of
+// row j sits at chunk position c ^ (j & 7) of the row's 128 bytes), so one
+// thread per key reads its row without bank conflicts. After a unit's last
+// tile the tile region holds the stream accumulators of the stream merge.
 template <int G>
 struct AttnSmem {
-  __half k[kTile][HD];
-  __half v[kTile][HD];
-  __half new_k[HD];
+  __half k[2][kTile][64];  // 1024-byte aligned (the swizzle atom)
+  __half v[2][kTile][64];
+  __half new_k[HD];        // this step's K / V row (the tile's copy is stale)
   __half new_v[HD];
-  __half qn_w[HD];        // QK-norm weights of the layer (prefetched)
+  __half qn_w[HD];         // QK-norm weights of the layer (prefetched)
   __half kn_w[HD];
-  float2 rope[HD / 2];    // (cos, sin) at the step's position (prefetched)
-  float q[G][HD];
-  float m[kStreams][G];
+  float2 rope[HD / 2];     // (cos, sin) at the step's position (prefetched)
+  __half q[G][HD];         // normed, rotated, FP16-rounded queries
+  float sc[G][kTile];      // scaled scores of the tile
+  float pa[G][kTile];      // exp(m_prev - m), exp(s - m) per key
+  float pc[G][kTile];
+  float m[2][kStreams][G]; // running max per stream, by tile parity
   float l[kStreams][G];
-  float f[kStreams][G];   // stream merge factors
+  float f[kStreams][G];    // stream merge factors
   float M[G];
-  float acc[kStreams][G][HD];
-  int last;
 };
+static_assert(sizeof(float) * kStreams * 8 * HD <= 2 * 2 * kTile * 64 * sizeof(__half),
+              "stream accumulators must fit in the tile region");
 
 struct Shared {
   uint64_t full[kMaxSlots];
   uint64_t empty[kMaxSlots];
+  uint64_t kv_full;  // the attention prefetch (first key tile, norms, RoPE row)
+  uint64_t kv_tile;  // the attention units' other key tiles
   Tiles tiles[5];  // this CTA's tiling of each stage (the same in every layer)
   float scale;
   __half res[kMaxDownRows];         // DOWN: residual values of this CTA's rows
@@ -209,6 +224,18 @@ struct Shared {
 __device__ __forceinline__ void consumers_sync() {
   asm volatile("bar.sync 1, %0;" ::"n"(kConsumers) : "memory");
 }
+// The consumers' barrier with an OR of `pred` over its threads: every thread
+// gets the same answer, so a decision taken on it stays uniform.
+__device__ __forceinline__ bool consumers_any(bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.or.pred q, 1, %2, p;\n"
+      " selp.u32 %0, 1, 0, q;\n}"
+      : "=r"(r)
+      : "r"((uint32_t)pred), "n"(kConsumers)
+      : "memory");
+  return r != 0;
+}
 __device__ __forceinline__ void attn_sync() {
   asm volatile("bar.sync 2, %0;" ::"n"(kAttnThreads) : "memory");
 }
@@ -218,10 +245,11 @@ __device__ __forceinline__ uint32_t ld_relaxed(const uint32_t* p) {
   asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
+
+
 __device__ __forceinline__ void red_release_add(uint32_t* p, uint32_t v) {
   asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
-
 
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(pipe::smem_u32(bar)) : "memory");
@@ -242,6 +270,28 @@ __device__ bool ring_wait(uint64_t* bar, uint32_t parity, Shared& sh, unsigned c
     }
   }
   return true;
+}
+
+// 2-D TMA tile load (no multicast) from a tensor map in global memory.
+__device__ __forceinline__ void tma_load_2d(void* dst, const void* map, uint64_t* bar, int c0,
+                                            int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, "
+      "{%3, %4}], [%2];" ::"r"(pipe::smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(pipe::smem_u32(bar)), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+// Wait for bulk copies this CTA issued (bounded in time, but not cut short
+// by an abort: the copies must land before the CTA may leave).
+__device__ void copies_wait(uint64_t* bar, uint32_t parity, unsigned code) {
+  if (pipe::mbar_try_wait(bar, parity)) return;
+  const uint64_t start = pipe::global_ns();
+  while (!pipe::mbar_try_wait(bar, parity))
+    if (pipe::global_ns() - start > pipe::kWaitNs) {
+      record(code);
+      return;
+    }
 }
 
 // ---- epoch-tagged activations ----------------------------------------------------
@@ -273,6 +323,14 @@ __device__ __forceinline__ void st_relaxed_v4(uint32_t* p, uint4 v) {
   asm volatile("st.relaxed.gpu.global.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y),
                "r"(v.z), "r"(v.w)
                : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_relaxed_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.release.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 __device__ __forceinline__ void st_relaxed_u64(unsigned long long* p, unsigned long long v) {
   asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
@@ -431,8 +489,8 @@ __device__ uint4 take_partials8(const DecodeLoop& p, size_t region, int c, uint3
   return out;
 }
 
-// Single-thread bounded wait until *ctr >= target (cumulative counters of
-// the per-head dataflow); false when the kernel is aborting.
+// Single-thread bounded wait until *ctr >= target (a cumulative counter);
+// false when the kernel is aborting.
 __device__ bool wait_counter(const DecodeLoop& p, const uint32_t* ctr, uint32_t target,
                              Shared& sh) {
   volatile uint32_t* abort_flag = p.sync + 1;
@@ -456,10 +514,12 @@ __device__ bool wait_counter(const DecodeLoop& p, const uint32_t* ctr, uint32_t 
   return true;
 }
 
-
 // Start of the O stage: wait until `units` attention units (cumulative over
-// the launch) have published their block partials.
-__device__ bool wait_units(const DecodeLoop& p, uint32_t units, Shared& sh) {
+// the launch) have published their block partials. While this CTA's own
+// attention warps work, the other warps wait at a barrier rather than have
+// one of them spin on the counter beside them.
+__device__ bool wait_units(const DecodeLoop& p, uint32_t units, bool ran_units, Shared& sh) {
+  if (ran_units) consumers_sync();
   if (threadIdx.x == 0) {
     const bool ok = !sh.abort && wait_counter(p, p.sync + kUnitsDone, units, sh);
     sh.stop = ok ? 0 : 1;
@@ -660,32 +720,51 @@ __device__ __forceinline__ uint4 input_chunk(const DecodeLoop& p, const StageIn&
   return take8(p, in.x, c, in.xtag, sh);
 }
 
-// Canonical sum of squares of the staged input (warp 0, from shared memory):
-// xs holds x (or the embedding row), xs2 holds x2 for the residual adds;
-// kAddNormIn squares the unrounded float sums (matvec2_add_rms_impl).
-__device__ __forceinline__ float staged_sumsq(int mode, const uint4* xs, const uint4* xs2, int kc,
-                                              int lane) {
-  float acc = 0.f;
-  for (int c = lane; c < kc; c += 32) {
-    if (mode == kAddNormIn) {
-      const uint4 a = xs[c], b = xs2[c];
-      const __half2* ha = reinterpret_cast<const __half2*>(&a);
-      const __half2* hb = reinterpret_cast<const __half2*>(&b);
+// One staged chunk's contribution to the canonical sum of squares
+// (gemv.cu build_input): kAddNormIn squares the unrounded float sums
+// (matvec2_add_rms_impl), kAddThenNormIn the rounded FP16 sums.
+__device__ __forceinline__ float sq_chunk(int mode, const uint4& a, const uint4& b, float acc) {
+  if (mode == kAddNormIn) {
+    const __half2* ha = reinterpret_cast<const __half2*>(&a);
+    const __half2* hb = reinterpret_cast<const __half2*>(&b);
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        float2 fa = __half22float2(ha[i]);
-        float2 fb = __half22float2(hb[i]);
-        float s0 = __fadd_rn(fa.x, fb.x), s1 = __fadd_rn(fa.y, fb.y);
-        acc = __fmaf_rn(s0, s0, acc);
-        acc = __fmaf_rn(s1, s1, acc);
-      }
-    } else if (mode == kAddThenNormIn) {
-      acc = chunk_sq(add_chunk(mode, xs[c], xs2[c]), acc);
-    } else {
-      acc = chunk_sq(xs[c], acc);
+    for (int i = 0; i < 4; ++i) {
+      float2 fa = __half22float2(ha[i]);
+      float2 fb = __half22float2(hb[i]);
+      float s0 = __fadd_rn(fa.x, fb.x), s1 = __fadd_rn(fa.y, fb.y);
+      acc = __fmaf_rn(s0, s0, acc);
+      acc = __fmaf_rn(s1, s1, acc);
     }
+    return acc;
   }
-  return acc;
+  if (mode == kAddThenNormIn) return chunk_sq(add_chunk(mode, a, b), acc);
+  return chunk_sq(a, acc);
+}
+
+// Every warp, from the staged input in shared memory: the canonical sum of
+// squares (lane l accumulates chunks l, l + 32, ... in order, loaded four at
+// a time), reduced over the canonical lanes, and the RMSNorm scale, returned
+// to every lane. Each warp computes the same value, so no barrier is needed
+// to share it.
+__device__ float warp_scale(const DecodeLoop& p, int mode, const uint4* xs, const uint4* xs2,
+                            int k) {
+  const int lane = threadIdx.x & 31;
+  const int kc = k >> 3;
+  const bool two = mode == kAddNormIn || mode == kAddThenNormIn;
+  float acc = 0.f;
+  int c = lane;
+  for (; c + 96 < kc; c += 128) {
+    uint4 a[4], b[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      a[j] = xs[c + 32 * j];
+      b[j] = two ? xs2[c + 32 * j] : a[j];
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc = sq_chunk(mode, a[j], b[j], acc);
+  }
+  for (; c < kc; c += 32) acc = sq_chunk(mode, xs[c], two ? xs2[c] : xs[c], acc);
+  return rms_scale(canon_reduce(acc, canon_lanes(k)), k, p.eps);
 }
 
 __device__ __forceinline__ uint4 normalize_chunk(const uint4& v, const uint4& g, float scale) {
@@ -702,73 +781,85 @@ __device__ __forceinline__ uint4 normalize_chunk(const uint4& v, const uint4& g,
   return o;
 }
 
-// Builds the stage input (k halves) in xs with the prologue of the GEMV
-// family (gemv.cu build_input): the same roundings and the canonical sum of
-// squares. One poller per CTA waits on the producing stage's counter; then
-// every thread stages its chunks in shared memory (one L2 round trip, the
-// tags validate each word), warp 0 reduces the squares from shared memory
-// and the chunks are normalized in place. The first barrier also orders
-// this stage's writes of xs after the previous stage's reads. Returns the
-// CTA's uniform decision to continue (false when the kernel is aborting).
+// Builds the stage input (k halves) with the prologue of the GEMV family
+// (gemv.cu build_input): the same roundings and the canonical sum of
+// squares. Every thread stages its chunks of the tagged vector(s) into xs
+// (xs2) in shared memory (one L2 round trip; the tags validate each word);
+// one barrier, which also takes the CTA's uniform decision to continue
+// (false when the kernel is aborting); then, for the norm modes, every warp
+// computes the scale itself and the chunks are normalized into xn, followed
+// by a second barrier. Stages without a norm read xs directly.
 __device__ bool build_input(const DecodeLoop& p, const StageIn& in, int wait_st, uint4* xs,
-                            uint4* xs2, Shared& sh) {
+                            uint4* xs2, uint4* xn, Shared& sh) {
   const int tid = threadIdx.x;
-  const int lane = tid & 31;
   const int kc = in.k >> 3;
   const bool two = in.mode == kAddNormIn || in.mode == kAddThenNormIn;
   const bool norm = in.mode != kPlainIn;
   const uint4* g4 = reinterpret_cast<const uint4*>(in.norm_w);
-  if (tid == 0) {
-    if (in.mb_wait >= 0)
-      wait_mbox(p, in.mb_wait, in.mb_target, sh);
-    else if (wait_st >= 0)
-      stage_ready(p, wait_st, sh);
-    MI_TRACE_ARRIVE(1);
+  if (in.mb_wait >= 0) {
+    // tensor parallelism: one thread waits for the mailbox counter
+    if (tid == 0) wait_mbox(p, in.mb_wait, in.mb_target, sh);
+    consumers_sync();
+  } else if (wait_st >= 0 && tid < kc) {
+    stage_ready(p, wait_st, sh);  // one L2 round trip of delay before the polls
   }
-  consumers_sync();
-  if (tid == 0) MI_TRACE_CUR(9);
+  if (tid == 0) MI_TRACE_IN(9);
   uint4 g_first = make_uint4(0, 0, 0, 0);
   if (norm && tid < kc) g_first = __ldg(g4 + tid);
-  for (int c = tid; c < kc; c += kConsumers) {
-    uint4 v;
-    if (two && in.x2_part >= 0) {
+  const bool wb = in.wb && blockIdx.x == 0;
+  if (two && in.x2_part >= 0) {
+    for (int c = tid; c < kc; c += kConsumers) {
       const Raw8 ra = raw8(in.x, c);
       const uint4 b = take_partials8(p, (size_t)in.x2_part, c, in.x2tag, sh);
       const uint4 a = take8_from(p, ra, in.x, c, in.xtag, sh);
       xs[c] = a;
       xs2[c] = b;
-      v = add_chunk(in.mode, a, b);
-    } else if (two) {
+      if (wb) put8(in.wb, c, add_chunk(in.mode, a, b), in.wbtag);
+    }
+  } else if (two) {
+    for (int c = tid; c < kc; c += kConsumers) {
       const Raw8 ra = raw8(in.x, c), rb = raw8(in.x2, c);
       const uint4 a = take8_from(p, ra, in.x, c, in.xtag, sh);
       const uint4 b = take8_from(p, rb, in.x2, c, in.x2tag, sh);
       xs[c] = a;
       xs2[c] = b;
-      v = add_chunk(in.mode, a, b);
-    } else {
-      v = input_chunk(p, in, c, sh);
+      if (wb) put8(in.wb, c, add_chunk(in.mode, a, b), in.wbtag);
+    }
+  } else if (in.mode == kEmbedNormIn) {
+    for (int c = tid; c < kc; c += kConsumers) {
+      const uint4 v = input_chunk(p, in, c, sh);
       xs[c] = v;
+      if (wb) put8(in.wb, c, v, in.wbtag);
     }
-    if (in.wb && blockIdx.x == 0) put8(in.wb, c, v, in.wbtag);
+  } else {
+    for (int c = tid; c < kc; c += kConsumers) {
+      const uint4 v = take8(p, in.x, c, in.xtag, sh);
+      xs[c] = v;
+      if (wb) put8(in.wb, c, v, in.wbtag);
+    }
   }
-  consumers_sync();
-  if (tid == 0) MI_TRACE_CUR(10);
+  if (consumers_any(sh.abort)) return false;
+  if (tid == 0) MI_TRACE_IN(10);
   if (norm) {
-    if (tid < 32) {
-      const float total = canon_reduce(staged_sumsq(in.mode, xs, xs2, kc, lane), canon_lanes(in.k));
-      if (lane == 0) sh.scale = rms_scale(total, in.k, p.eps);
+    // every warp computes the scale when a lane's chain is short; for wide
+    // inputs one warp does and shares it (the redundant shared-memory reads
+    // of 15 warps would cost more than the extra barrier)
+    const bool every_warp = kc <= 4 * 32;
+    float scale = 0.f;
+    if (every_warp || tid < 32) scale = warp_scale(p, in.mode, xs, xs2, in.k);
+    if (!every_warp) {
+      if (tid == 0) sh.scale = scale;
+      consumers_sync();
+      scale = sh.scale;
     }
-    consumers_sync();
-    if (tid == 0) MI_TRACE_CUR(15);
-    const float scale = sh.scale;
+    if (tid == 0) MI_TRACE_IN(15);
     for (int c = tid; c < kc; c += kConsumers) {
       const uint4 v = two ? add_chunk(in.mode, xs[c], xs2[c]) : xs[c];
-      xs[c] = normalize_chunk(v, c == tid ? g_first : __ldg(g4 + c), scale);
+      xn[c] = normalize_chunk(v, c == tid ? g_first : __ldg(g4 + c), scale);
     }
+    consumers_sync();
   }
-  if (tid == 0) sh.stop = sh.abort ? 1 : 0;
-  consumers_sync();
-  return !sh.stop;
+  return true;
 }
 
 // ---- consumers: rows from the ring --------------------------------------------------
@@ -942,45 +1033,46 @@ __device__ void reduce_rows(const DecodeLoop& p, const StageW& s, const uint4* x
 // Thread index within the attention warps.
 __device__ __forceinline__ int atid() { return (int)threadIdx.x - kAttnBase; }
 
-// Stages keys [j0, j1) of KV head g (cp.async, 16 bytes per copy), skipping
-// position `skip` (the new token, taken from shared memory).
+// One thread: TMA loads of the K and V tile of KV head g_kv at positions
+// [j0, j0 + kTile) (four 64-column halves), completing on `bar`, whose
+// expected bytes the caller has registered. The proxy fence orders the
+// generic-proxy writes before it (K/V rows written in earlier steps, and the
+// stream accumulators this CTA kept in the tile region) before the copies.
 template <int G>
-__device__ void stage_keys(const LoopLayer& L, int kvh, int g, int j0, int j1, int skip,
-                           AttnSmem<G>& sm) {
-  const int per_row = HD * 2 / 16;
-  const int total = (j1 - j0) * per_row;
-  const size_t stride = (size_t)kvh * HD;
-  for (int i = atid(); i < total; i += kAttnThreads) {
-    int r = i / per_row, c = i - r * per_row;
-    int j = j0 + r;
-    if (j == skip) continue;
-    pipe::cp_async16(&sm.k[r][8 * c], L.k_cache + (size_t)j * stride + (size_t)g * HD + 8 * c);
-    pipe::cp_async16(&sm.v[r][8 * c], L.v_cache + (size_t)j * stride + (size_t)g * HD + 8 * c);
-  }
-  pipe::cp_async_commit();
+__device__ __forceinline__ void issue_kv_tile(const DecodeLoop& p, int layer, int g_kv, int j0,
+                                              AttnSmem<G>& sm, uint64_t* bar) {
+  asm volatile("fence.proxy.async;" ::: "memory");
+  const uint8_t* maps = static_cast<const uint8_t*>(p.kv_maps) + (size_t)layer * 256;
+  tma_load_2d(&sm.k[0][0][0], maps, bar, g_kv * HD, j0);
+  tma_load_2d(&sm.k[1][0][0], maps, bar, g_kv * HD + 64, j0);
+  tma_load_2d(&sm.v[0][0][0], maps + 128, bar, g_kv * HD, j0);
+  tma_load_2d(&sm.v[1][0][0], maps + 128, bar, g_kv * HD + 64, j0);
 }
+constexpr uint32_t kKvTileBytes = 2u * kTile * HD * 2u;
 
-// During the QKV stage (whose outputs the attention needs) a CTA that owns
-// attention unit blockIdx.x stages that unit's first key tile, which is
-// already final, and loads the layer's QK-norm weights and the RoPE terms of
-// the position into shared memory. Warps 4..11.
+// After its QKV input, a CTA that owns attention unit blockIdx.x prefetches
+// that unit's first key tile (final: written in earlier steps; the row of
+// the new position is stale and is taken from this step's K/V instead), the
+// layer's QK-norm weights and the RoPE terms of the position into shared
+// memory, so the attention stage finds them there: one thread issues the
+// TMA tile loads and 1-D bulk copies of the rest, all completing on
+// sh.kv_full. Returns whether this CTA issued them (uniform over the CTA).
 template <int G>
-__device__ void attention_prefetch(const DecodeLoop& p, const LoopLayer& L, int pos,
-                                   AttnSmem<G>& sm) {
+__device__ bool attention_prefetch(const DecodeLoop& p, int layer, const LoopLayer& L, int pos,
+                                   AttnSmem<G>& sm, Shared& sh) {
   const int nb = (pos + p.block) / p.block;
-  if ((int)blockIdx.x >= p.kvh * nb) return;
+  if ((int)blockIdx.x >= p.kvh * nb) return false;
+  if (threadIdx.x != kAttnBase) return true;
   const int g_kv = blockIdx.x / nb, b = blockIdx.x % nb;
-  const int begin = b * p.block;
-  const int end = min(pos + 1, begin + p.block);
-  stage_keys<G>(L, p.kvh, g_kv, begin, min(end, begin + kTile), pos, sm);
-  // the norms and the RoPE row are copied asynchronously too: these warps
-  // join the QKV stage's input barrier next, which must not wait on them
-  const int tid = atid();
-  if (tid < 16) pipe::cp_async16(&sm.qn_w[8 * tid], L.q_norm + 8 * tid);
-  else if (tid < 32) pipe::cp_async16(&sm.kn_w[8 * (tid - 16)], L.k_norm + 8 * (tid - 16));
-  else if (tid < 32 + HD / 4 && p.rope)
-    pipe::cp_async16(&sm.rope[2 * (tid - 32)], p.rope + (size_t)pos * (HD / 2) + 2 * (tid - 32));
-  pipe::cp_async_commit();
+  pipe::mbar_expect_tx(&sh.kv_full, kKvTileBytes + 2u * (HD * 2u) +
+                                        (p.rope ? (uint32_t)sizeof(sm.rope) : 0u));
+  issue_kv_tile<G>(p, layer, g_kv, b * p.block, sm, &sh.kv_full);
+  pipe::bulk_g2s(sm.qn_w, L.q_norm, HD * 2, &sh.kv_full);
+  pipe::bulk_g2s(sm.kn_w, L.k_norm, HD * 2, &sh.kv_full);
+  if (p.rope)
+    pipe::bulk_g2s(sm.rope, p.rope + (size_t)pos * (HD / 2), (uint32_t)sizeof(sm.rope),
+                   &sh.kv_full);
+  return true;
 }
 
 // QK-norm + RoPE of one head half-warp from the prefetched shared copies
@@ -995,37 +1087,58 @@ __device__ __forceinline__ void head_rope(const DecodeLoop& p, const AttnSmem<G>
     norm_rope_half(raw, w, (uint32_t)pos, p.theta, p.eps, p.round_norm != 0, mask, nullptr, out);
 }
 
-constexpr int kKeyBatch = 2;  // keys of a stream scored together (2 measured fastest of 2, 4, 8)
+// Row j of a swizzled tile half-pair as 16-byte chunks: chunk c (0..15).
+__device__ __forceinline__ uint4 tile_chunk(const __half (*t)[kTile][64], int j, int c) {
+  return reinterpret_cast<const uint4*>(&t[c >> 3][j][0])[(c & 7) ^ (j & 7)];
+}
 
-// One flash-decode unit: KV head g_kv, key block b of nb. The arithmetic is
-// attention.cu's attention_decode_kernel with the fused front end; the
-// independent parts of consecutive keys of a stream (scores, exponentials)
-// are computed together, the dependent online-softmax updates stay in key
-// order. Run by warps 4..11: for G >= 2 the two warpgroups each take half of
-// the query heads of the group over the same 8 key streams.
+// Canonical score of FP16 query q (16 chunks) with the K row of tile key j
+// (or the new row): one partial per chunk (8 sequential mixed-precision
+// FMAs; both operands are FP16 values, so this is the FP32 FMA of the
+// widened operands), then the 16-lane butterfly tree in registers.
 template <int G>
-__device__ void attention_unit(const DecodeLoop& p, const LoopLayer& L, int g_kv, int b, int nb,
-                               int pos, bool prefetched, uint32_t qkv_tag,
-                               AttnSmem<G>& sm, Shared& sh) {
-  constexpr int NG = G >= 2 ? 2 : 1;  // warpgroups sharing the heads
-  constexpr int GS = G / NG;          // heads per warpgroup
+__device__ __forceinline__ float key_score(const AttnSmem<G>& sm, int g, int j, bool fresh) {
+  const uint4* q = reinterpret_cast<const uint4*>(sm.q[g]);
+  const uint4* nk = reinterpret_cast<const uint4*>(sm.new_k);
+  float d[8];
+#pragma unroll
+  for (int c = 0; c < 8; ++c) d[c] = chunk_dot(q[c], fresh ? nk[c] : tile_chunk(sm.k, j, c), 0.f);
+#pragma unroll
+  for (int c = 0; c < 8; ++c)  // the tree's first level as the upper partials arrive
+    d[c] = __fadd_rn(d[c], chunk_dot(q[c + 8], fresh ? nk[c + 8] : tile_chunk(sm.k, j, c + 8), 0.f));
+#pragma unroll
+  for (int step = 4; step >= 1; step >>= 1)
+#pragma unroll
+    for (int c = 0; c < step; ++c) d[c] = __fadd_rn(d[c], d[c + step]);
+  return d[0];
+}
+
+// One flash-decode unit: KV head g_kv, key block b of nb, run by the 256
+// attention threads (warps 4..11). The arithmetic is attention.cu's
+// attention_decode_kernel with the fused front end: kStreams interleaved
+// online-softmax streams per block (stream s takes the block's keys s,
+// s + 8, ... in order), merged in stream order into the block partial. The
+// work is laid out for latency: one thread per (key, head) score; a key's
+// running maximum is its stream's prefix maximum (exact in any order), so
+// every key's pair of exponentials is computed independently; only the
+// accumulations stay sequential in key order, one thread per (stream, head,
+// 8 dims). Tiles past the prefetched one arrive by TMA on sh.kv_tile.
+template <int G>
+__device__ void attention_unit(const DecodeLoop& p, int layer, const LoopLayer& L, int g_kv,
+                               int b, int nb, int pos, bool prefetched, uint32_t kv_parity,
+                               uint32_t& tile_uses, uint32_t qkv_tag, AttnSmem<G>& sm,
+                               Shared& sh) {
+  constexpr int R = (kStreams * G * 16 + kAttnThreads - 1) / kAttnThreads;  // accumulators per thread
   const int t = atid();
-  const int wg = t >> 7;
-  const bool active = wg < NG;
-  const int g0 = wg * GS;
-  const int lane = threadIdx.x & 31;
-  const int warp = (t & 127) >> 5;
-  const int li = lane & 15;
-  const int hw = warp * 2 + (lane >> 4);
-  const int Lk = pos + 1;
+  const int li = t & 15;
   const int begin = b * p.block;
-  const int end = min(Lk, begin + p.block);
+  const int end = min(pos + 1, begin + p.block);
   const int ntiles = (end - begin + kTile - 1) / kTile;
 
-  // every CTA's QKV rows are out (the tags then validate each word); this
-  // thread's prefetched copies (norms, RoPE row, first key tile) have landed
+  // every CTA's QKV rows are out (the tags then validate each word); the
+  // prefetched copies (norms, RoPE row, first key tile) have landed
   if (t == 0) stage_ready(p, kQKV, sh);
-  pipe::cp_async_wait_all();
+  if (prefetched) copies_wait(&sh.kv_full, kv_parity, kCodeKv);
   attn_sync();
   {
     const int hq = t >> 4;  // one query head per half-warp
@@ -1034,8 +1147,11 @@ __device__ void attention_unit(const DecodeLoop& p, const LoopLayer& L, int g_kv
       const uint4 raw = take8(p, p.t_qkv, (g_kv * G + hq) * (HD / 8) + li, qkv_tag, sh);
       float qv[8];
       head_rope<G>(p, sm, raw, sm.qn_w, pos, mask, qv);
+      uint4 qq;
+      __half2* hq2 = reinterpret_cast<__half2*>(&qq);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) sm.q[hq][8 * li + e] = qv[e];
+      for (int i = 0; i < 4; ++i) hq2[i] = __floats2half2_rn(qv[2 * i], qv[2 * i + 1]);
+      reinterpret_cast<uint4*>(sm.q[hq])[li] = qq;
     }
   }
   if (pos >= begin && pos < end && t >= kAttnThreads - 16) {
@@ -1054,142 +1170,113 @@ __device__ void attention_unit(const DecodeLoop& p, const LoopLayer& L, int g_kv
     reinterpret_cast<uint4*>(sm.new_k)[li] = kk;
     reinterpret_cast<uint4*>(sm.new_v)[li] = vv;
   }
+  if (t < kStreams * G) sm.m[0][t / G][t % G] = -INFINITY;
   if (t == 0) MI_TRACE_CUR(5);
 
-  float qreg[GS][8];
-  float m[GS], l[GS], acc[GS][8];
-  attn_sync();
+  float acc[R][8], l[R];
 #pragma unroll
-  for (int g = 0; g < GS; ++g) {
+  for (int r = 0; r < R; ++r) {
+    l[r] = 0.f;
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      qreg[g][e] = active ? sm.q[g0 + g][8 * li + e] : 0.f;
-      acc[g][e] = 0.f;
-    }
-    m[g] = -INFINITY;
-    l[g] = 0.f;
+    for (int e = 0; e < 8; ++e) acc[r][e] = 0.f;
   }
   const float scale = __frcp_rn(__fsqrt_rn((float)HD));
 
   for (int tl = 0; tl < ntiles; ++tl) {
     const int j0 = begin + tl * kTile;
-    const int j1 = min(end, j0 + kTile);
-    if (tl > 0 || !prefetched) stage_keys<G>(L, p.kvh, g_kv, j0, j1, pos, sm);
-    pipe::cp_async_wait_all();
-    attn_sync();
+    const int cnt = min(end, j0 + kTile) - j0;
+    const int cur = tl & 1;
+    attn_sync();  // the front (tl = 0) or the previous tile's reads are done
+    if (tl > 0 || !prefetched) {
+      if (t == 0) {
+        pipe::mbar_expect_tx(&sh.kv_tile, kKvTileBytes);
+        issue_kv_tile<G>(p, layer, g_kv, j0, sm, &sh.kv_tile);
+      }
+      copies_wait(&sh.kv_tile, tile_uses & 1u, kCodeKv | 1u);
+      ++tile_uses;
+    }
     if (t == 0 && tl == 0) MI_TRACE_CUR(6);
-    // Stream hw takes tile keys hw, hw + 8, ... in order; both half-warps of
-    // a warp run the same trip count (the score butterflies span the warp).
-    const int count = active ? j1 - j0 : 0;
-    for (int base = warp * 2; base < count; base += kStreams * kKeyBatch) {
-      uint4 kk[kKeyBatch];
-      bool valid[kKeyBatch];
-#pragma unroll
-      for (int q = 0; q < kKeyBatch; ++q) {
-        const int r = base + q * kStreams + (lane >> 4);
-        valid[q] = r < count;
-        const int rr = valid[q] ? r : 0;
-        kk[q] = (j0 + rr == pos) ? reinterpret_cast<const uint4*>(sm.new_k)[li]
-                                 : reinterpret_cast<const uint4*>(sm.k[rr])[li];
-      }
-      float sc[GS][kKeyBatch];
-#pragma unroll
-      for (int q = 0; q < kKeyBatch; ++q) {
-        float kf[8];
-        const __half2* hk = reinterpret_cast<const __half2*>(&kk[q]);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          float2 f = __half22float2(hk[i]);
-          kf[2 * i] = f.x;
-          kf[2 * i + 1] = f.y;
-        }
-#pragma unroll
-        for (int g = 0; g < GS; ++g) {
-          float d = 0.f;
-#pragma unroll
-          for (int e = 0; e < 8; ++e) d = __fmaf_rn(qreg[g][e], kf[e], d);
-          sc[g][q] = d;
-        }
-      }
-#pragma unroll
-      for (int o = 8; o >= 1; o >>= 1)
-#pragma unroll
-        for (int q = 0; q < kKeyBatch; ++q)
-#pragma unroll
-          for (int g = 0; g < GS; ++g)
-            sc[g][q] = __fadd_rn(sc[g][q], __shfl_xor_sync(0xffffffffu, sc[g][q], o));
-      if (t == 0 && tl == 0 && base == 0) MI_TRACE_CUR(11);
-      // running maxima in key order, then every exponential at once
-      float mp[GS][kKeyBatch], mn[GS][kKeyBatch];
-#pragma unroll
-      for (int g = 0; g < GS; ++g) {
-        float mm = m[g];
-#pragma unroll
-        for (int q = 0; q < kKeyBatch; ++q) {
-          sc[g][q] = __fmul_rn(sc[g][q], scale);
-          mp[g][q] = mm;
-          if (valid[q]) mm = fmaxf(mm, sc[g][q]);
-          mn[g][q] = mm;
-        }
-        m[g] = mm;
-      }
-      float pa[GS][kKeyBatch], pc[GS][kKeyBatch];
-#pragma unroll
-      for (int g = 0; g < GS; ++g)
-#pragma unroll
-        for (int q = 0; q < kKeyBatch; ++q) {
-          pa[g][q] = mi_exp(__fsub_rn(mp[g][q], mn[g][q]));
-          pc[g][q] = mi_exp(__fsub_rn(sc[g][q], mn[g][q]));
-        }
-      if (t == 0 && tl == 0 && base == 0) MI_TRACE_CUR(12);
-#pragma unroll
-      for (int q = 0; q < kKeyBatch; ++q) {
-        if (!valid[q]) continue;
-        const int r = base + q * kStreams + (lane >> 4);
-        const uint4 vv = (j0 + r == pos) ? reinterpret_cast<const uint4*>(sm.new_v)[li]
-                                         : reinterpret_cast<const uint4*>(sm.v[r])[li];
-        const __half2* hv = reinterpret_cast<const __half2*>(&vv);
-        float vf[8];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          float2 f = __half22float2(hv[i]);
-          vf[2 * i] = f.x;
-          vf[2 * i + 1] = f.y;
-        }
-#pragma unroll
-        for (int g = 0; g < GS; ++g) {
-#pragma unroll
-          for (int e = 0; e < 8; ++e)
-            acc[g][e] = __fmaf_rn(acc[g][e], pa[g][q], __fmul_rn(pc[g][q], vf[e]));
-          l[g] = __fmaf_rn(l[g], pa[g][q], pc[g][q]);
-        }
-      }
-      if (t == 0 && tl == 0 && base == 0) MI_TRACE_CUR(13);
+    // scores, one thread per (key, head)
+    for (int idx = t; idx < kTile * G; idx += kAttnThreads) {
+      const int j = idx & (kTile - 1), g = idx / kTile;
+      if (j < cnt) sm.sc[g][j] = __fmul_rn(key_score<G>(sm, g, j, j0 + j == pos), scale);
     }
     attn_sync();
+    if (t == 0 && tl == 0) MI_TRACE_CUR(11);
+    // prefix maxima and the two exponentials of every key
+    for (int idx = t; idx < kTile * G; idx += kAttnThreads) {
+      const int j = idx & (kTile - 1), g = idx / kTile, st = j & (kStreams - 1);
+      if (j < cnt) {
+        // the stream's earlier keys of the tile, loaded together
+        float prev[kTile / kStreams];
+#pragma unroll
+        for (int i = 0; i < kTile / kStreams; ++i) prev[i] = sm.sc[g][st + kStreams * i];
+        float mp = sm.m[cur][st][g];
+#pragma unroll
+        for (int i = 0; i < kTile / kStreams; ++i)
+          if (st + kStreams * i < j) mp = fmaxf(mp, prev[i]);
+        const float sc = sm.sc[g][j];
+        const float mn = fmaxf(mp, sc);
+        sm.pa[g][j] = mi_exp(__fsub_rn(mp, mn));
+        sm.pc[g][j] = mi_exp(__fsub_rn(sc, mn));
+        if (j + kStreams >= cnt) sm.m[cur ^ 1][st][g] = mn;  // the stream's last key here
+      } else if (j < kStreams) {
+        sm.m[cur ^ 1][j][g] = sm.m[cur][j][g];  // a stream with no key in this tile
+      }
+    }
+    attn_sync();
+    if (t == 0 && tl == 0) MI_TRACE_CUR(12);
+    // accumulations in key order, one thread per (stream, head, 8 dims)
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const int idx = t + r * kAttnThreads;
+      const int st = (idx >> 4) & (kStreams - 1), g = idx >> 7;
+      if (g < G) {
+#pragma unroll
+        for (int i = 0; i < kTile / kStreams; ++i) {
+          const int j = st + kStreams * i;
+          if (j >= cnt) break;
+          const float a = sm.pa[g][j], c = sm.pc[g][j];
+          const uint4 vv = j0 + j == pos ? reinterpret_cast<const uint4*>(sm.new_v)[li]
+                                         : tile_chunk(sm.v, j, li);
+          const __half2* hv = reinterpret_cast<const __half2*>(&vv);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float2 f = __half22float2(hv[i]);
+            acc[r][2 * i] = __fmaf_rn(acc[r][2 * i], a, __fmul_rn(c, f.x));
+            acc[r][2 * i + 1] = __fmaf_rn(acc[r][2 * i + 1], a, __fmul_rn(c, f.y));
+          }
+          l[r] = __fmaf_rn(l[r], a, c);
+        }
+      }
+    }
+    if (t == 0 && tl == 0) MI_TRACE_CUR(13);
   }
+  attn_sync();  // every tile read is done: the tile region takes the accumulators
   if (t == 0) MI_TRACE_CUR(7);
 
-  // Stream merge (index order) -> block partial; the factors once per (stream, head).
-  if (active) {
+  // Stream merge (stream order) -> block partial; the factors once per (stream, head).
+  float* accs = reinterpret_cast<float*>(&sm.k[0][0][0]);  // [kStreams][G][HD]
+  const int fin = ntiles & 1;
 #pragma unroll
-    for (int g = 0; g < GS; ++g) {
-      if (li == 0) {
-        sm.m[hw][g0 + g] = m[g];
-        sm.l[hw][g0 + g] = l[g];
-      }
+  for (int r = 0; r < R; ++r) {
+    const int idx = t + r * kAttnThreads;
+    const int st = (idx >> 4) & (kStreams - 1), g = idx >> 7;
+    if (g < G) {
 #pragma unroll
-      for (int e = 0; e < 8; ++e) sm.acc[hw][g0 + g][8 * li + e] = acc[g][e];
+      for (int e = 0; e < 8; ++e) accs[(st * G + g) * HD + 8 * li + e] = acc[r][e];
+      if (li == 0) sm.l[st][g] = l[r];
     }
   }
   attn_sync();
   if (t < kStreams * G) {
-    const int s = t / G, g = t % G;
+    const int st = t / G, g = t % G;
     float M = -INFINITY;
 #pragma unroll
-    for (int u = 0; u < kStreams; ++u) M = fmaxf(M, sm.m[u][g]);
-    sm.f[s][g] = sm.m[s][g] == -INFINITY ? 0.f : mi_exp(__fsub_rn(sm.m[s][g], M));
-    if (s == 0) sm.M[g] = M;
+    for (int u = 0; u < kStreams; ++u) M = fmaxf(M, sm.m[fin][u][g]);
+    const float ms = sm.m[fin][st][g];
+    sm.f[st][g] = ms == -INFINITY ? 0.f : mi_exp(__fsub_rn(ms, M));
+    if (st == 0) sm.M[g] = M;
   }
   attn_sync();
   // Block partial (max, denominator, numerators) of every head; the O stage
@@ -1199,9 +1286,9 @@ __device__ void attention_unit(const DecodeLoop& p, const LoopLayer& L, int g_kv
     const int g = idx / HD, d = idx - g * HD;
     float num = 0.f, den = 0.f;
 #pragma unroll
-    for (int s = 0; s < kStreams; ++s) {
-      num = __fmaf_rn(sm.acc[s][g][d], sm.f[s][g], num);
-      den = __fmaf_rn(sm.l[s][g], sm.f[s][g], den);
+    for (int st = 0; st < kStreams; ++st) {
+      num = __fmaf_rn(accs[(st * G + g) * HD + d], sm.f[st][g], num);
+      den = __fmaf_rn(sm.l[st][g], sm.f[st][g], den);
     }
     part[g * kPart + 4 + d] = num;
     if (d == 0) {
@@ -1214,6 +1301,9 @@ __device__ void attention_unit(const DecodeLoop& p, const LoopLayer& L, int g_kv
   if (t == 0) red_release_add(p.sync + kUnitsDone, 1u);
 }
 
+// Bytes of one hidden-size FP16 vector in shared memory.
+__host__ __device__ size_t x2_bytes(int hidden) { return ((size_t)hidden * 2 + 127) / 128 * 128; }
+
 // Bytes of the shared-memory copy of the layer table.
 __host__ __device__ size_t layer_table_bytes(int layers) {
   return ((size_t)layers * sizeof(LoopLayer) + 127) / 128 * 128;
@@ -1221,13 +1311,16 @@ __host__ __device__ size_t layer_table_bytes(int layers) {
 
 template <int G>
 __global__ void __launch_bounds__(kThreads, 1) decode_loop_kernel(DecodeLoop params) {
-  extern __shared__ __align__(128) uint8_t smem[];
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
   __shared__ Shared sh;
   // Parameters live in shared memory: a persistent kernel would otherwise
   // miss the constant cache on them at every stage.
   __shared__ DecodeLoop p;
   if (threadIdx.x == 0) p = params;
   __syncthreads();
+  // 1024-byte aligned base (the swizzled attention tiles need it; the plan
+  // reserves the slack)
+  uint8_t* smem = smem_raw + ((1024u - (pipe::smem_u32(smem_raw) & 1023u)) & 1023u);
   uint8_t* ring = smem;
   uint4* xs = reinterpret_cast<uint4*>(smem + (size_t)p.slots * p.slot_bytes);
   AttnSmem<G>& asm_ = *reinterpret_cast<AttnSmem<G>*>(smem + (size_t)p.slots * p.slot_bytes +
@@ -1237,6 +1330,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_loop_kernel(DecodeLoop par
   // second operand of the residual-add inputs (hidden halves)
   uint4* xs2 = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(lay) +
                                         layer_table_bytes(p.layers));
+  // normalized stage input of the norm stages (hidden halves)
+  uint4* xn = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(xs2) + x2_bytes(p.hidden));
   const int tid = threadIdx.x;
   {
     // per-layer pointer table -> shared memory (read at every stage)
@@ -1246,6 +1341,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_loop_kernel(DecodeLoop par
     for (int i = tid; i < words; i += kThreads) dst[i] = src[i];
   }
   if (tid == 0) {
+#ifdef MI_TRACE_TWICE
+    g_trace_alt = 0;
+#endif
     for (int st = 0; st < 5; ++st) sh.tiles[st] = tiles_of(p, stage_weights(p, lay, 0, st));
     sh.stop = 0;
     sh.astop = 0;
@@ -1254,6 +1352,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_loop_kernel(DecodeLoop par
       pipe::mbar_init(&sh.full[s], 1);
       pipe::mbar_init(&sh.empty[s], kConsumerWarps);
     }
+    pipe::mbar_init(&sh.kv_full, 1);
+    pipe::mbar_init(&sh.kv_tile, 1);
     sh.abort = 0;
     pipe::fence_mbar_init();
   }
@@ -1268,6 +1368,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_loop_kernel(DecodeLoop par
   uint32_t token = __ldcg(p.toks + len0);
   uint32_t g = 0;
   uint32_t units_total = 0;  // attention units published so far (all CTAs agree)
+  uint32_t kv_uses = 0;      // attention prefetches completed on sh.kv_full
+  uint32_t tile_uses = 0;    // key tiles completed on sh.kv_tile (attention warps)
   const uint32_t grid = gridDim.x;
   const int warp = tid >> 5, lane = tid & 31;
   for (int step = 0; step < p.steps; ++step) {
@@ -1282,11 +1384,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_loop_kernel(DecodeLoop par
       const uint32_t hidden_in = (layer == 0 || p.tp > 1) ? tagv(e, 0) : tagv(e - 1u, 1);
       const unsigned long long per_ls = (unsigned long long)p.tp * grid;  // mailbox counts
       uint32_t bk = 0, bi = 0xFFFFFFFFu;
+      bool kv_issued = false;  // this CTA's attention prefetch of the layer
       // QKV (layer 0: the embedding row, written back as the hidden stream)
       {
         if (tid == 0) { MI_TRACE(step, layer * 5 + 0, 0); MI_TRACE_SET(step, layer * 5 + 0); }
-        if (tid >= kAttnBase && tid < kAttnBase + kAttnThreads)
-          attention_prefetch<G>(p, L, pos, asm_);
         const StageW s = stage_weights(p, lay, layer, kQKV);
         StageIn in = {};
         in.x2_part = -1;
@@ -1315,9 +1416,15 @@ __global__ void __launch_bounds__(kThreads, 1) decode_loop_kernel(DecodeLoop par
           in.x = p.t_hidden;
           in.xtag = hidden_in;
         }
-        if (!build_input(p, in, layer == 0 ? -1 : kDown, xs, xs2, sh)) return;
+        if (!build_input(p, in, layer == 0 ? -1 : kDown, xs, xs2, xn, sh)) return;
+#ifdef MI_TRACE_TWICE
+        if (tid == 0) g_trace_alt = 1;
+        if (!build_input(p, in, layer == 0 ? -1 : kDown, xs, xs2, xn, sh)) return;
+        if (tid == 0) g_trace_alt = 0;
+#endif
         if (tid == 0) MI_TRACE(step, layer * 5 + 0, 1);
-        reduce_rows<kQKV>(p, s, xs, ring, sh, g, tagv(e, 0), bk, bi);
+        kv_issued = attention_prefetch<G>(p, layer, L, pos, asm_, sh);
+        reduce_rows<kQKV>(p, s, xn, ring, sh, g, tagv(e, 0), bk, bi);
         stage_done(p, kQKV);
         if (tid == 0) MI_TRACE(step, layer * 5 + 0, 2);
       }
@@ -1327,14 +1434,15 @@ __global__ void __launch_bounds__(kThreads, 1) decode_loop_kernel(DecodeLoop par
         const int units = p.kvh * nb;
         if (tid >= kAttnBase && tid < kAttnBase + kAttnThreads)
           for (int u = blockIdx.x; u < units; u += gridDim.x)
-            attention_unit<G>(p, L, u / nb, u % nb, nb, pos, u == (int)blockIdx.x, tagv(e, 0),
-                              asm_, sh);
+            attention_unit<G>(p, layer, L, u / nb, u % nb, nb, pos, u == (int)blockIdx.x,
+                              kv_uses & 1u, tile_uses, tagv(e, 0), asm_, sh);
+        kv_uses += kv_issued ? 1u : 0u;
         if (tid == 0) MI_TRACE(step, layer * 5 + 1, 2);
       }
       // O (waits for every attention unit's partial, merges them as its input)
       {
         units_total += (uint32_t)(p.kvh * nb);
-        if (!wait_units(p, units_total, sh)) return;
+        if (!wait_units(p, units_total, (int)blockIdx.x < p.kvh * nb, sh)) return;
         if (tid == 0) { MI_TRACE(step, layer * 5 + 2, 0); MI_TRACE_SET(step, layer * 5 + 2); }
         if (tid == 0) MI_TRACE_ARRIVE(1);
         const StageW s = stage_weights(p, lay, layer, kO);
@@ -1367,9 +1475,14 @@ __global__ void __launch_bounds__(kThreads, 1) decode_loop_kernel(DecodeLoop par
         in.norm_w = L.post_norm;
         in.wb = p.t_res;
         in.wbtag = tagv(e, 0);
-        if (!build_input(p, in, kO, xs, xs2, sh)) return;
+        if (!build_input(p, in, kO, xs, xs2, xn, sh)) return;
+#ifdef MI_TRACE_TWICE
+        if (tid == 0) g_trace_alt = 1;
+        if (!build_input(p, in, kO, xs, xs2, xn, sh)) return;
+        if (tid == 0) g_trace_alt = 0;
+#endif
         if (tid == 0) MI_TRACE(step, layer * 5 + 3, 1);
-        reduce_rows<kGU>(p, s, xs, ring, sh, g, tagv(e, 0), bk, bi);
+        reduce_rows<kGU>(p, s, xn, ring, sh, g, tagv(e, 0), bk, bi);
         stage_done(p, kGU);
         if (tid == 0) MI_TRACE(step, layer * 5 + 3, 2);
       }
@@ -1384,7 +1497,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_loop_kernel(DecodeLoop par
         in.k = p.inter;
         in.x = p.t_act;
         in.xtag = tagv(e, 0);
-        if (!build_input(p, in, kGU, xs, xs2, sh)) return;
+        if (!build_input(p, in, kGU, xs, xs2, xn, sh)) return;
         if (p.tp == 1) {
           // residuals of this CTA's rows (written back by CTA 0 in GU); under
           // tensor parallelism the next QKV stage adds them
@@ -1422,9 +1535,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_loop_kernel(DecodeLoop par
         in.mb_wait = 1;
         in.mb_target = p.ctr_base[1] + (unsigned long long)(ls_last + 1u) * p.tp * grid;
       }
-      if (!build_input(p, in, kDown, xs, xs2, sh)) return;
+      if (!build_input(p, in, kDown, xs, xs2, xn, sh)) return;
       if (tid == 0) MI_TRACE(step, p.layers * 5, 1);
-      reduce_rows<kLM>(p, s, xs, ring, sh, g, 0u, bk, bi);
+      reduce_rows<kLM>(p, s, xn, ring, sh, g, 0u, bk, bi);
       if (tid == 0) MI_TRACE(step, p.layers * 5, 2);
       // per-lane bests -> warp best -> CTA best -> tagged record per CTA
 #pragma unroll
@@ -1523,7 +1636,6 @@ size_t attn_smem_for(int group) {
   }
 }
 
-size_t x2_bytes(int hidden) { return ((size_t)hidden * 2 + 127) / 128 * 128; }
 
 template <int G>
 cudaError_t launch_g(cudaStream_t stream, const DecodeLoop& p, int grid, size_t smem) {
@@ -1555,13 +1667,13 @@ bool decode_loop_plan(DecodeLoop& p, int device) {
   const int max_k = std::max(std::max(p.hidden, p.inter), p.qh * HD);
   int max_item = std::max(std::max(p.hidden * 4, p.inter * 2), p.qh * HD * 2);
   p.slot_bytes = std::max(kMinSlotBytes, (max_item + 127) / 128 * 128);
-  p.x_bytes = (max_k * 2 + 127) / 128 * 128;
+  p.x_bytes = (max_k * 2 + 1023) / 1024 * 1024;  // keeps the attention tiles 1024-aligned
   int optin = 0;
   if (cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, device) !=
       cudaSuccess)
     return false;
   const size_t fixed = (size_t)p.x_bytes + attn_smem_for(group) + layer_table_bytes(p.layers) +
-                       x2_bytes(p.hidden) + sizeof(Shared) + 1024;
+                       2 * x2_bytes(p.hidden) + sizeof(Shared) + 2048;
   if (fixed >= (size_t)optin) return false;
   p.slots = (int)std::min<size_t>(kMaxSlots, ((size_t)optin - fixed) / p.slot_bytes);
   if (p.slots < 2) return false;
@@ -1575,7 +1687,7 @@ bool decode_loop_plan(DecodeLoop& p, int device) {
 
 size_t decode_loop_smem(const DecodeLoop& p) {
   return (size_t)p.slots * p.slot_bytes + p.x_bytes + attn_smem_for(p.qh / p.kvh) +
-         layer_table_bytes(p.layers) + x2_bytes(p.hidden);
+         layer_table_bytes(p.layers) + 2 * x2_bytes(p.hidden) + 1024;  // + alignment slack
 }
 
 void decode_loop(cudaStream_t stream, const DecodeLoop& p) {

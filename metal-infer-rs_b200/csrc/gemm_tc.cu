@@ -315,6 +315,19 @@ bool enabled() {
 
 bool gemm_tc_available() { return enabled() && encoder() != nullptr; }
 
+bool make_kv_tile_map(void* map, const __half* cache, int capacity, int kv_heads, int box_rows) {
+  EncodeTiled enc = encoder();
+  if (!enc) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)kv_heads * 128, (cuuint64_t)capacity};
+  cuuint64_t strides[1] = {(cuuint64_t)kv_heads * 128 * 2};
+  cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+  cuuint32_t elem[2] = {1, 1};
+  return enc(static_cast<CUtensorMap*>(map), CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+             const_cast<__half*>(cache), dims, strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 bool gemm_tc(const Launch& l, const __half* x, const __half* w, __half* out, int m, int n, int k,
              int ldo) {
   if (!gemm_tc_available()) return false;

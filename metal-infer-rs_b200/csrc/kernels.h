@@ -117,6 +117,12 @@ void gemm_partial_f32(const Launch& l, const __half* x, const __half* w, float* 
 // Expired-wait code of the tensor-core GEMM (0 = none); optionally cleared.
 unsigned gemm_tc_status(bool reset);
 bool gemm_tc_available();
+// A 2-D TMA tensor map (128 bytes, written to `map`) over one layer's K or V
+// cache [capacity, kv_heads, 128] FP16 whose box is 64 consecutive values
+// (half of one KV head's row) of `box_rows` consecutive positions, 128-byte
+// swizzled (rows past the capacity read as zeros). False when the driver's
+// encoder is unavailable.
+bool make_kv_tile_map(void* map, const __half* cache, int capacity, int kv_heads, int box_rows);
 
 // ---- row / elementwise kernels ---------------------------------------------
 void add(const Launch& l, const __half* a, const __half* b, __half* out, size_t n);
@@ -238,6 +244,9 @@ struct DecodeLoop {
   int attn_blocks = 0; // blocks per head the partial buffer holds
   int steps = 0;
   const LoopLayer* layer = nullptr;
+  // [layers][2] CUtensorMap (K, V) of the cache, 64-byte aligned: boxes of
+  // 64 values x 64 positions (128-byte swizzle) for the attention tiles
+  const void* kv_maps = nullptr;
   const __half* embedding = nullptr;
   const __half* final_norm = nullptr;
   const __half* lm_head = nullptr;

@@ -158,6 +158,8 @@ struct mi_kv_cache {
   uint64_t graph_sampled_version = 0;
   std::vector<k::LoopLayer> loop_host;  // layer table of the persistent decode
   TensorRef loop_layers;                // its device copy
+  std::vector<uint8_t> kv_maps_host;    // [layers][K, V] CUtensorMap bytes
+  TensorRef kv_maps;                    // their device copy (256-byte aligned)
   ~mi_kv_cache() {
     if (graph) cudaGraphExecDestroy(graph);
     if (graph_sampled) cudaGraphExecDestroy(graph_sampled);
@@ -579,6 +581,18 @@ void run_decode_loop(mi_qwen3* m, mi_kv_cache* c, size_t steps) {
     c->loop_layers = TensorRef(new_tensor(ctx, {(bytes + 3) / 4}, MI_U32, false));
     MI_CUDA(cudaMemcpyAsync(c->loop_layers.t->base(), c->loop_host.data(), bytes,
                             cudaMemcpyHostToDevice, ctx->stream));
+    // K / V tile maps of every layer for the attention prefetch (TMA 2-D)
+    const int kvh = (int)m->cfg.num_key_value_heads;
+    c->kv_maps_host.assign(m->layers.size() * 2 * 128, 0);
+    for (size_t li = 0; li < m->layers.size(); ++li)
+      for (int v = 0; v < 2; ++v)
+        if (!k::make_kv_tile_map(c->kv_maps_host.data() + (li * 2 + v) * 128,
+                                 v ? c->value[li].h() : c->key[li].h(), (int)c->capacity, kvh,
+                                 64))
+          fail(MI_ERR_KERNEL, "cannot encode the KV cache tile map of layer %zu", li);
+    c->kv_maps = TensorRef(new_tensor(ctx, {c->kv_maps_host.size() / 4}, MI_U32, false));
+    MI_CUDA(cudaMemcpyAsync(c->kv_maps.t->base(), c->kv_maps_host.data(), c->kv_maps_host.size(),
+                            cudaMemcpyHostToDevice, ctx->stream));
   }
   k::DecodeLoop p = m->loop;
   p.round_norm = m->fusion.qk_rope_cache ? 0 : 1;
@@ -586,6 +600,7 @@ void run_decode_loop(mi_qwen3* m, mi_kv_cache* c, size_t steps) {
   p.block = k::decode_block_for((int)c->capacity);
   p.attn_blocks = w.attn_splits;
   p.layer = reinterpret_cast<const k::LoopLayer*>(c->loop_layers.t->base());
+  p.kv_maps = c->kv_maps.t->base();
   p.embedding = m->embedding.h();
   p.final_norm = m->final_norm.h();
   p.lm_head = m->lm_head->f16();
@@ -610,7 +625,9 @@ void run_decode_loop(mi_qwen3* m, mi_kv_cache* c, size_t steps) {
   p.logits = w.logits.h();
   const size_t part = k::decode_loop_part_floats(p.kvh, w.attn_splits, p.qh / p.kvh);
   if (!w.loop_part.t || w.loop_part.t->len() < part)
-    w.loop_part = TensorRef(new_tensor(ctx, {part}, MI_F32, false));
+    // zeroed: block records are validated by their epoch tags, so the
+    // buffer must not start with tags a previous user left there
+    w.loop_part = TensorRef(new_tensor(ctx, {part}, MI_F32, true));
   p.attn_part = w.loop_part.t->f32();
   p.sync = w.loop_sync.t->u32();
   p.tp = m->tp;

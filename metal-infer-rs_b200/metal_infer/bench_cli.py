@@ -113,19 +113,31 @@ def run_kernel(ctx, a) -> dict:
                   (flops / 1e12) / (sum(wall) / len(wall)), "TFLOP/s")
 
 
+ATTENTION_KINDS = {"reference": mi.AttentionKind.REFERENCE, "tiled": mi.AttentionKind.TILED,
+                   "flash-prefill": mi.AttentionKind.FLASH_PREFILL,
+                   "decode-split-kv": mi.AttentionKind.DECODE_SPLIT_KV,
+                   "flash-decode": mi.AttentionKind.FLASH_DECODE}
+
+
+def attention_inputs(T: int, L: int, qh: int, kvh: int, hd: int):
+    """The attention subcommand's seeded Q [T, qh, hd], K and V [L, kvh, hd]
+    (N(0, 1) rounded to FP16), as float32 arrays."""
+    rng = np.random.default_rng(0)
+    return (rng.normal(0, 1, T * qh * hd).astype(np.float32),
+            rng.normal(0, 1, L * kvh * hd).astype(np.float32),
+            rng.normal(0, 1, L * kvh * hd).astype(np.float32))
+
+
 def run_attention(ctx, a) -> dict:
     """Command::Attention (bench.rs:560-581, 927-1108): each attention kind
     on random Q/K/V, with its max abs error against the reference kind."""
     T, L, qh, kvh, hd = a.tokens, a.length, a.query_heads, a.kv_heads, a.head_dim
-    rng = np.random.default_rng(0)
-    q = ctx.tensor_f16(rng.normal(0, 1, T * qh * hd).astype(np.float32), [T, qh, hd])
-    k = ctx.tensor_f16(rng.normal(0, 1, L * kvh * hd).astype(np.float32), [L, kvh, hd])
-    v = ctx.tensor_f16(rng.normal(0, 1, L * kvh * hd).astype(np.float32), [L, kvh, hd])
+    qf, kf, vf = attention_inputs(T, L, qh, kvh, hd)
+    q = ctx.tensor_f16(qf, [T, qh, hd])
+    k = ctx.tensor_f16(kf, [L, kvh, hd])
+    v = ctx.tensor_f16(vf, [L, kvh, hd])
     cfg = mi.AttentionConfig(qh, kvh, hd, 1, L - T)
-    kinds = {"reference": mi.AttentionKind.REFERENCE, "tiled": mi.AttentionKind.TILED,
-             "flash-prefill": mi.AttentionKind.FLASH_PREFILL,
-             "decode-split-kv": mi.AttentionKind.DECODE_SPLIT_KV,
-             "flash-decode": mi.AttentionKind.FLASH_DECODE}
+    kinds = ATTENTION_KINDS
     names = list(kinds) if a.kind == "compare" else [a.kind]
     if T != 1:
         names = [n for n in names if n not in ("decode-split-kv", "flash-decode")]

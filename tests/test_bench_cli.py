@@ -87,3 +87,42 @@ def test_bench_cli_json_schemas(tmp_path):
             assert s["fed_token_ids"] == [5, 6, 7]
         else:
             assert s["fed_token_ids"] == s["sampled_token_ids"][:3]
+
+
+@pytest.mark.gpu
+def test_attention_compare_against_oracle():
+    """`attention --kind compare` reports each kind's error against the
+    engine's reference kind; here every kind's output on the subcommand's own
+    seeded inputs is pinned to the CPU oracle (the reference semantics of
+    transformer.metal:1579-1612 for the prefill kinds, the oracle's flash
+    decode for the decode kinds), and the CLI's error column to those outputs."""
+    import metal_infer as mi
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    T, L, qh, kvh, hd = 1, 640, 16, 8, 128
+    qf, kf, vf = B.attention_inputs(T, L, qh, kvh, hd)
+    qb, kb, vb = O.f16_bits(qf), O.f16_bits(kf), O.f16_bits(vf)
+    ctx = mi.MetalContext(0)
+    q = ctx.tensor_f16_bits(qb, [T, qh, hd])
+    k = ctx.tensor_f16_bits(kb, [L, kvh, hd])
+    v = ctx.tensor_f16_bits(vb, [L, kvh, hd])
+    cfg = mi.AttentionConfig(qh, kvh, hd, 1, L - T)
+    want = O.f32(O.attention(qb, kb, vb, qh, kvh, hd, True, L - T)).ravel()
+    outs = {}
+    for name, kind in B.ATTENTION_KINDS.items():
+        outs[name] = ctx.attention(q, k, v, cfg, kind).to_f32_vec()
+        # per-op tolerance of the north star: max relative error 2e-3
+        err = np.max(np.abs(outs[name] - want)) / np.max(np.abs(want))
+        assert err <= 2e-3, (name, err)
+    np.testing.assert_array_equal(
+        outs["flash-decode"], O.f32(O.attention_decode(qb, kb, vb, qh, kvh, hd)).ravel())
+    out = subprocess.run([sys.executable, "-m", "metal_infer.bench_cli", "--format", "json",
+                          "attention", "--kind", "compare", "--tokens", "1", "--length", str(L),
+                          "--iterations", "2", "--warmup", "1"],
+                         capture_output=True, text=True, env=ENV, timeout=600)
+    assert out.returncode == 0, out.stderr
+    cmp_ = json.loads(out.stdout)["attention_comparison"]
+    for name in B.ATTENTION_KINDS:
+        got = cmp_[name.replace("-", "_")]["max_abs_error"]
+        assert got == pytest.approx(float(np.max(np.abs(outs[name] - outs["reference"]))), abs=1e-6)
+

@@ -1,7 +1,9 @@
 """The serving layer on the engine (crates/metal-infer-cli): a random Qwen3
 checkpoint exported to safetensors with a synthetic tokenizer, served over
 HTTP and run through the generate CLI; the tokens must be those of
-generate_with on the same prompt and options."""
+generate_with on the same prompt and options, and those in turn the CPU
+oracle's greedy and sampled ids for the same seeded model (cut at the first
+end-of-sequence id, where the engine stops)."""
 import json
 import os
 import subprocess
@@ -16,6 +18,7 @@ import metal_infer as mi
 from metal_infer import serving as S
 from test_loader_gpu import export, small_cfg
 from tokenizer_fixture import write_tokenizer
+import oracle as O
 
 pytestmark = pytest.mark.gpu
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
@@ -29,6 +32,21 @@ def checkpoint(tmp_path_factory):
     export(mi.Qwen3Model.random(ctx, cfg, seed=31), cfg, d)
     write_tokenizer(d, cfg["vocab_size"])
     return d, cfg
+
+
+def oracle_ids(cfg, prompt, max_tokens, stops, **sampling):
+    """The oracle's ids for the seed-31 model of the checkpoint: greedy, or
+    sampled with the engine's options, cut before the first stop id."""
+    ref = O.Qwen3(cfg, seed=31, capacity=256)
+    if sampling.get("temperature", 0.0) > 0.0:
+        ids = ref.generate_sampled(prompt, max_tokens, sampling["temperature"],
+                                   sampling.get("top_p", 1.0), sampling.get("top_k", 0),
+                                   sampling.get("seed", 0))
+    else:
+        ids = ref.generate_greedy(prompt, max_tokens)
+    ref.close()
+    cut = [i for i, t in enumerate(ids.tolist()) if t in set(stops)]
+    return ids[:cut[0]] if cut else ids
 
 
 def _post(url, body):
@@ -54,6 +72,10 @@ def test_server_matches_generate_with(checkpoint):
                                                                top_k=0, seed=0), **opts,
                                                           stop_token_ids=engine.tokenizer.eos_token_ids),
                                               engine.model.kv_cache(256))
+            np.testing.assert_array_equal(
+                np.asarray(want, np.uint32),
+                oracle_ids(cfg, np.asarray(prompt, np.uint32), 12, engine.tokenizer.eos_token_ids,
+                           **opts))
             r = json.loads(_post(base + "/v1/chat/completions",
                                  dict(messages=messages, max_tokens=12, **opts)))
             assert r["usage"]["prompt_tokens"] == len(prompt)
@@ -85,6 +107,9 @@ def test_generate_cli(checkpoint):
     ids = model.generate_with(tk.encode("hello world"), dict(max_tokens=10, stop_token_ids=tk.eos_token_ids),
                               model.kv_cache(2048))
     assert out.stdout == tk.decode(ids)
+    prompt = np.asarray(tk.encode("hello world"), np.uint32)
+    np.testing.assert_array_equal(np.asarray(ids, np.uint32),
+                                  oracle_ids(cfg, prompt, 10, tk.eos_token_ids))
     bad = subprocess.run([sys.executable, "-m", "metal_infer", "generate", "--model", d, "--prompt",
                           "hello", "--max-tokens", "5000", "--context", "64"], capture_output=True,
                          text=True, env=env, timeout=300)
