@@ -705,6 +705,7 @@ void attention_decode_fused(const Launch& l, const DecodeFused& p, int splits, f
 void attention_prefill(const Launch& l, const AttnProblem& p) {
   MI_REQUIRE(p.hd <= 256, MI_ERR_SHAPE, "prefill attention needs head_dim <= 256");
   if (p.tokens * p.qh <= 0) return;
+  if (attention_prefill_mma(l, p)) return;  // long prompts: tensor cores
   dim3 grid((p.tokens + kPrefillWarps - 1) / kPrefillWarps, p.qh);
   dim3 block(kPrefillWarps * 32);
   const bool aligned =

@@ -17,6 +17,7 @@
 
 #include <cuda.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "device.cuh"
@@ -242,8 +243,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             reinterpret_cast<uint4*>(dst)[q] = v;
           }
         } else {
-          for (int i = 0; i < 32 && col + i < n; ++i)
-            dst[i] = __float2half_rn(__uint_as_float(r[i]));
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (col + i < n) dst[i] = __float2half_rn(__uint_as_float(r[i]));
         }
       }
     }
@@ -254,6 +256,184 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BN)
+                 : "memory");
+  }
+}
+
+// ---- persistent kernel with two TMEM accumulators ---------------------------------
+// One CTA per SM walks the output tiles blockIdx.x, blockIdx.x + gridDim.x, ...
+// (M fastest, so CTAs running at the same time share the weight tile in L2).
+// The producer and the MMA issuer run ahead across tile boundaries; the MMA
+// warp alternates between two BN-column TMEM accumulators, so the epilogue
+// warps drain tile i while tile i + 1 is being multiplied.
+constexpr int kPBN = 256;
+
+struct PSmem {
+  static constexpr int kStages = 4;
+  static constexpr int kABytes = BM * BK * 2;    // 16 KB
+  static constexpr int kBBytes = kPBN * BK * 2;  // 32 KB
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kBytes = 1024 /*align*/ + kStages * kStageBytes + 256;
+};
+
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tc_persistent_kernel(const __grid_constant__ CUtensorMap map_x,
+                              const __grid_constant__ CUtensorMap map_w, __half* out, int m, int n,
+                              int k, int ldo) {
+  using S = PSmem;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::kStages * S::kStageBytes);
+  uint64_t* empty = full + S::kStages;
+  uint64_t* acc_full = empty + S::kStages;  // [2] MMA -> epilogue
+  uint64_t* acc_empty = acc_full + 2;       // [2] epilogue -> MMA
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int tiles_m = (m + BM - 1) / BM;
+  const int tiles = tiles_m * ((n + kPBN - 1) / kPBN);
+  const int ktiles = (k + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S::kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 4);  // one arrival per epilogue warp
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_x)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&map_w)) : "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(2 * kPBN)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = *tmem_slot;
+
+  pdl_trigger();
+  pdl_wait();
+
+  if (warp == 0 && lane == 0) {
+    // TMA producer over all of this CTA's tiles.
+    bool ok = true;
+    uint32_t g = 0;
+    for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
+      const int m0 = (tile % tiles_m) * BM, n0 = (tile / tiles_m) * kPBN;
+      for (int kt = 0; kt < ktiles; ++kt, ++g) {
+        const int s = g % S::kStages;
+        const uint32_t phase = (g / S::kStages) & 1;
+        if (!mbar_wait(&empty[s], phase ^ 1, 1)) {
+          ok = false;
+          break;
+        }
+        uint8_t* a = smem + s * S::kStageBytes;
+        mbar_expect_tx(&full[s], S::kStageBytes);
+        tma_load_2d(a, &map_x, &full[s], kt * BK, m0);
+        tma_load_2d(a + S::kABytes, &map_w, &full[s], kt * BK, n0);
+      }
+    }
+    // Drain: the copies into the last stages must land before the CTA exits.
+    const uint32_t first = g > (uint32_t)S::kStages ? g - S::kStages : 0u;
+    for (uint32_t q = first; q < g; ++q) mbar_wait(&full[q % S::kStages], (q / S::kStages) & 1, 4);
+  } else if (warp == 1 && lane == 0) {
+    // MMA issuer: accumulator i & 1 for this CTA's i-th tile.
+    constexpr uint32_t idesc = idesc_f16<kPBN>();
+    bool ok = true;
+    uint32_t g = 0;
+    int i = 0;
+    for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x, ++i) {
+      const int a = i & 1;
+      if (!mbar_wait(&acc_empty[a], ((i >> 1) & 1) ^ 1, 5)) break;
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const uint32_t d = tmem + (uint32_t)(a * kPBN);
+      for (int kt = 0; kt < ktiles; ++kt, ++g) {
+        const int s = g % S::kStages;
+        if (!mbar_wait(&full[s], (g / S::kStages) & 1, 2)) {
+          ok = false;
+          break;
+        }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t a_addr = smem_u32(smem + s * S::kStageBytes);
+        const uint64_t adesc = sw128_desc(a_addr), bdesc = sw128_desc(a_addr + S::kABytes);
+#pragma unroll
+        for (int kk = 0; kk < BK / 16; ++kk)
+          mma_f16(d, adesc + 2 * kk, bdesc + 2 * kk, idesc, (kt | kk) != 0);
+        mma_commit(&empty[s]);
+      }
+      mma_commit(&acc_full[a]);
+    }
+  } else if (warp >= 2) {
+    // Epilogue: warp w reads TMEM lanes [32 * (w % 4), +32) of the tile's accumulator.
+    const int quad = warp & 3;
+    int i = 0;
+    for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++i) {
+      const int a = i & 1;
+      const int m0 = (tile % tiles_m) * BM, n0 = (tile / tiles_m) * kPBN;
+      const int row = m0 + quad * 32 + lane;
+      if (!mbar_wait(&acc_full[a], (i >> 1) & 1, 3)) break;
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+#pragma unroll 1
+      for (int c = 0; c < kPBN; c += 32) {
+        uint32_t r[32];
+        const uint32_t taddr = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(a * kPBN + c);
+        asm volatile(
+            "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,"
+            "%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+            : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+              "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+              "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),
+              "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+              "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
+              "=r"(r[31])
+            : "r"(taddr));
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        if (row < m) {
+          const int col = n0 + c;
+          __half* dst = out + (size_t)row * ldo + col;
+          if (col + 32 <= n && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              uint4 v;
+              __half2* hv = reinterpret_cast<__half2*>(&v);
+#pragma unroll
+              for (int e = 0; e < 4; ++e)
+                hv[e] = __floats2half2_rn(__uint_as_float(r[q * 8 + 2 * e]),
+                                          __uint_as_float(r[q * 8 + 2 * e + 1]));
+              reinterpret_cast<uint4*>(dst)[q] = v;
+            }
+          } else {
+#pragma unroll
+            for (int e = 0; e < 32; ++e)
+              if (col + e < n) dst[e] = __float2half_rn(__uint_as_float(r[e]));
+          }
+        }
+      }
+      // this warp's reads of the accumulator are done: the MMA may reuse it
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(
+                                      smem_u32(&acc_empty[a]))
+                                  : "memory");
+    }
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(2 * kPBN)
                  : "memory");
   }
 }
@@ -311,6 +491,16 @@ bool enabled() {
   return on == 1;
 }
 
+// MI_GEMM_PERSISTENT=0 keeps every shape on the one-tile-per-CTA kernel.
+bool persistent_enabled() {
+  static int on = -1;
+  if (on < 0) {
+    const char* e = getenv("MI_GEMM_PERSISTENT");
+    on = (e && *e == '0') ? 0 : 1;
+  }
+  return on == 1;
+}
+
 }  // namespace
 
 bool gemm_tc_available() { return enabled() && encoder() != nullptr; }
@@ -333,10 +523,20 @@ bool gemm_tc(const Launch& l, const __half* x, const __half* w, __half* out, int
   if (!gemm_tc_available()) return false;
   if (m < 2 || k < 8 || (k & 7) || ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w)) & 15))
     return false;
-  // Narrow tiles when the grid would not fill the GPU.
   int tiles_m = (m + BM - 1) / BM;
-  int bn = (tiles_m * ((n + 127) / 128) >= l.sm_count) ? 128 : 64;
   CUtensorMap mx, mw;
+  if (persistent_enabled() && tiles_m * ((n + kPBN - 1) / kPBN) >= l.sm_count) {
+    // enough 128 x 256 tiles for every SM: the persistent kernel
+    if (!make_map(&mx, x, m, k, BM) || !make_map(&mw, w, n, k, kPBN)) return false;
+    auto kernel = gemm_tc_persistent_kernel;
+    allow_dynamic_smem(kernel, PSmem::kBytes);
+    const int tiles = tiles_m * ((n + kPBN - 1) / kPBN);
+    launch_kernel(l, dim3(std::min(tiles, l.sm_count)), dim3(kThreads), PSmem::kBytes, kernel, mx,
+                  mw, out, m, n, k, ldo);
+    return true;
+  }
+  // Narrow tiles when the grid would not fill the GPU.
+  int bn = (tiles_m * ((n + 127) / 128) >= l.sm_count) ? 128 : 64;
   if (!make_map(&mx, x, m, k, BM) || !make_map(&mw, w, n, k, bn)) return false;
   if (bn == 128)
     launch_tc<128>(l, mx, mw, out, m, n, k, ldo);

@@ -203,11 +203,21 @@ unsigned attention_status(bool reset);
 // round_p the flash-prefill semantics (FP16 probabilities), without it the
 // FP32 online softmax of the tiled kernel.
 void attention_prefill(const Launch& l, const AttnProblem& p);
+// Prompts of at least this many tokens (head_dim 128, FP16 probabilities)
+// take the tensor-core prefill attention (attention_mma.cu): per-op
+// tolerance instead of the canonical kernel's bit-exact arithmetic.
+constexpr int kMmaPrefillMinTokens = 512;
+// The tensor-core prefill attention; false when the problem does not fit it.
+bool attention_prefill_mma(const Launch& l, const AttnProblem& p);
 
 // ---- tensor parallelism -----------------------------------------------------------
 // out[i] = half(parts[0][i] + parts[1][i] + ... + parts[tp-1][i]), summed in
 // rank order in FP32 (parts: [tp, n] as gathered from the ranks).
 void rank_sum_round(cudaStream_t s, const float* parts, int tp, size_t n, __half* out);
+// Slice `rank` ([n]) of that sum from the other ranks' slices (`pieces`,
+// [tp, n], row q from rank q) and this rank's own slice `mine`.
+void rank_sum_round_slice(cudaStream_t s, const float* pieces, const float* mine, int rank, int tp,
+                          size_t n, __half* out);
 // Greedy id over the ranks' {key, index} pairs ([tp, 2]): writes it to
 // token_out[*token_pos + 1] (or token_out[0] without token_pos) and adds one
 // to *step_counter when given.

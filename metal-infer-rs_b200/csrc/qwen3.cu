@@ -242,12 +242,48 @@ void tp_allgather(mi_qwen3* m, const void* send, void* recv, size_t count, int d
 #endif
 }
 
-// Row-parallel projection result: this rank's FP32 partials `part` ([n])
-// are gathered from every rank into `gather` ([tp, n]) and summed in rank
-// order into `out` (FP16).
+// Row-parallel projection result: the sum of the ranks' FP32 partials
+// `part` ([n] each) in rank order, rounded once to FP16 into `out` ([n]).
+// Large results (prefill) are reduced slice by slice: rank r receives only
+// slice r (n / tp elements) of every other rank's partials (grouped NCCL
+// send / receive into `gather`, [tp, n / tp]), sums its slice in rank order
+// and the FP16 slices are all-gathered in place, so a rank receives
+// (tp - 1) * n / tp * 6 bytes instead of (tp - 1) * n * 4. Small results
+// (the per-kernel decode chain) gather the full partials ([tp, n]) and sum
+// them; both give the same bits.
+constexpr size_t kSliceReduceMin = 1 << 16;
+
 void tp_reduce(mi_qwen3* m, const float* part, size_t n, float* gather, __half* out) {
-  tp_allgather(m, part, gather, n, 4);
-  k::rank_sum_round(m->ctx->stream, gather, m->tp, n, out);
+  const int tp = m->tp, rank = m->rank;
+  if (n < kSliceReduceMin || n % (size_t)tp != 0) {
+    tp_allgather(m, part, gather, n, 4);
+    k::rank_sum_round(m->ctx->stream, gather, tp, n, out);
+    return;
+  }
+#ifdef MI_HAVE_NCCL
+  const size_t chunk = n / (size_t)tp;
+  cudaStream_t s = m->ctx->stream;
+  ncclResult_t r = ncclGroupStart();
+  for (int q = 0; q < tp && r == ncclSuccess; ++q) {
+    if (q == rank) continue;
+    r = ncclSend(part + (size_t)q * chunk, chunk, ncclFloat32, q, m->comm, s);
+    if (r == ncclSuccess)
+      r = ncclRecv(gather + (size_t)q * chunk, chunk, ncclFloat32, q, m->comm, s);
+  }
+  const ncclResult_t e = ncclGroupEnd();
+  if (r == ncclSuccess) r = e;
+  if (r != ncclSuccess)
+    fail(MI_ERR_COLLECTIVE, "NCCL partial-slice exchange failed: %s", ncclGetErrorString(r));
+  k::rank_sum_round_slice(s, gather, part + (size_t)rank * chunk, rank, tp, chunk,
+                          out + (size_t)rank * chunk);
+  r = ncclAllGather(out + (size_t)rank * chunk, out, chunk, ncclFloat16, m->comm, s);
+  if (r != ncclSuccess)
+    fail(MI_ERR_COLLECTIVE, "NCCL all-gather of the reduced slices failed: %s",
+         ncclGetErrorString(r));
+#else
+  (void)rank, (void)gather, (void)out, (void)part;
+  fail(MI_ERR_UNSUPPORTED, "built without NCCL: tensor parallelism is unavailable");
+#endif
 }
 
 // Vocab-parallel greedy id: the ranks' {key, index} candidates in

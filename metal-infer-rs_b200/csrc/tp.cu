@@ -22,6 +22,20 @@ __global__ void rank_sum_round_kernel(const float* parts, int tp, size_t n, __ha
   }
 }
 
+// Slice `rank` of the rank-ordered sum: rank q's piece is `mine` for q ==
+// rank, else row q of `pieces` ([tp, n]).
+__global__ void rank_sum_round_slice_kernel(const float* pieces, const float* mine, int rank,
+                                            int tp, size_t n, __half* out) {
+  pdl_wait();
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (size_t)gridDim.x * blockDim.x) {
+    float acc = rank == 0 ? mine[i] : pieces[i];
+    for (int t = 1; t < tp; ++t)
+      acc = __fadd_rn(acc, t == rank ? mine[i] : pieces[(size_t)t * n + i]);
+    out[i] = __float2half_rn(acc);
+  }
+}
+
 __global__ void argmax_combine_kernel(const uint32_t* pairs, int tp, uint32_t* token_out,
                                       const uint32_t* token_pos, uint32_t* step_counter) {
   pdl_wait();
@@ -41,6 +55,14 @@ void rank_sum_round(cudaStream_t s, const float* parts, int tp, size_t n, __half
   if (n == 0) return;
   const int grid = (int)std::min<size_t>((n + 255) / 256, 1024);
   rank_sum_round_kernel<<<grid, 256, 0, s>>>(parts, tp, n, out);
+  MI_CUDA(cudaGetLastError());
+}
+
+void rank_sum_round_slice(cudaStream_t s, const float* pieces, const float* mine, int rank, int tp,
+                          size_t n, __half* out) {
+  if (n == 0) return;
+  const int grid = (int)std::min<size_t>((n + 255) / 256, 1024);
+  rank_sum_round_slice_kernel<<<grid, 256, 0, s>>>(pieces, mine, rank, tp, n, out);
   MI_CUDA(cudaGetLastError());
 }
 

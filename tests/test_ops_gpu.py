@@ -376,6 +376,26 @@ def test_flash_prefill_matches_oracle_at_tile_edges(ctx, head_dim):
         assert_close(out, ref)
 
 
+# Prompts of kMmaPrefillMinTokens (512) tokens and more take the tensor-core
+# flash prefill (attention_mma.cu): FP16 MMAs with FP32 accumulation whose
+# order is the hardware's, so it is held to the per-op tolerance of the
+# reference semantics (max relative error 2e-3), as the tcgen05 GEMM is.
+@pytest.mark.parametrize("tokens,length,qh,kvh", [(512, 512, 8, 4), (700, 1100, 8, 2),
+                                                  (1024, 1024, 4, 4), (513, 2100, 8, 1)])
+def test_flash_prefill_tensor_cores_within_tolerance(ctx, tokens, length, qh, kvh):
+    q = rand16(6, INPUT_STREAM + 400, (tokens, qh, 128))
+    k = rand16(6, INPUT_STREAM + 401, (length, kvh, 128))
+    v = rand16(6, INPUT_STREAM + 402, (length, kvh, 128))
+    cfg = _cfg(qh, kvh, 128, length - tokens)
+    out = ctx.attention(T(ctx, q, [tokens, qh, 128]), T(ctx, k, [length, kvh, 128]),
+                        T(ctx, v, [length, kvh, 128]), cfg,
+                        mi.AttentionKind.FLASH_PREFILL).f16_bits()
+    ref = O.attention(q, k, v, qh, kvh, 128, True, length - tokens)
+    a, e = O.f32(out.ravel()), O.f32(ref.ravel())
+    assert np.all(np.isfinite(a))
+    assert float(np.max(np.abs(a - e)) / np.max(np.abs(e))) <= 2e-3
+
+
 @pytest.mark.parametrize("length", [1, 63, 64, 65, 256, 640, 8192])
 def test_flash_decode_matches_reference_across_block_boundaries(ctx, length):
     q = f16(np.where(np.arange(2 * 128) % 3 == 0, 2.0, -2.0))

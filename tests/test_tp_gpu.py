@@ -34,7 +34,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _rank_main(rank, tp, port, cfg, prompt, steps, out, ckpt=None):
+def _rank_main(rank, tp, port, cfg, prompt, long_prompt, steps, out, ckpt=None):
     import torch.distributed as dist
     dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
                             world_size=tp)
@@ -45,6 +45,9 @@ def _rank_main(rank, tp, port, cfg, prompt, steps, out, ckpt=None):
         res = {}
         cache = model.kv_cache(128)
         res["prefill"] = model.prefill(prompt, cache).f16_bits().ravel()
+        # a prompt whose row-parallel results (tokens x hidden >= 65,536) are
+        # reduced slice by slice (NCCL send / receive, then an FP16 all-gather)
+        res["prefill_long"] = model.prefill(long_prompt, model.kv_cache(160)).f16_bits().ravel()
         res["decode"] = [model.decode(int(t), cache).f16_bits().ravel() for t in (7, 900)]
         res["persistent"] = model.decode_persistent()
         for path in ("persistent", "graph", "eager"):
@@ -76,6 +79,7 @@ def test_tp_matches_oracle_tp_arithmetic(tmp_path, tp):
         pytest.skip(f"needs {tp} GPUs")
     cfg = small_cfg()
     prompt = O.gen_tokens(11, INPUT_STREAM, 20, cfg["vocab_size"])
+    long_prompt = O.gen_tokens(11, INPUT_STREAM + 1, 136, cfg["vocab_size"])
     steps = 16
     # a checkpoint of the full (one-GPU) model for the shard-on-load check
     import safetensors_io as st
@@ -86,7 +90,8 @@ def test_tp_matches_oracle_tp_arithmetic(tmp_path, tp):
     ctx = tmp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank_main, args=(r, tp, port, cfg, prompt, steps, q, str(tmp_path)))
+    procs = [ctx.Process(target=_rank_main,
+                         args=(r, tp, port, cfg, prompt, long_prompt, steps, q, str(tmp_path)))
              for r in range(tp)]
     for p in procs:
         p.start()
@@ -102,6 +107,9 @@ def test_tp_matches_oracle_tp_arithmetic(tmp_path, tp):
     ref.set_tp(tp)
     want_prefill = ref.forward(prompt)
     want_decode = [ref.forward(np.array([t], np.uint32)) for t in (7, 900)]
+    ref_long = O.Qwen3(cfg, seed=11, capacity=160)
+    ref_long.set_tp(tp)
+    want_long = ref_long.forward(long_prompt)
     ref_ids = O.Qwen3(cfg, seed=11, capacity=128)
     ref_ids.set_tp(tp)
     want_ids = ref_ids.generate_greedy(prompt, steps)
@@ -111,6 +119,7 @@ def test_tp_matches_oracle_tp_arithmetic(tmp_path, tp):
         got = res[r]
         assert got["config"]["num_attention_heads"] == cfg["num_attention_heads"]
         np.testing.assert_array_equal(got["prefill"], want_prefill)
+        np.testing.assert_array_equal(got["prefill_long"], want_long)
         np.testing.assert_array_equal(got["loaded_prefill"], want_prefill)
         for a, b in zip(got["decode"], want_decode):
             np.testing.assert_array_equal(a, b)
