@@ -343,6 +343,12 @@ def run_ours(args, rank, world, local_rank):
     # ranks (TP1 on one GPU), after the replica model is freed.
     del model, cache
     ctx.synchronize()
+    # BASELINE config 1 (the decode ops alone, rotated working sets), one GPU
+    sweep = None
+    if world == 1 and not args.no_op_sweep:
+        sweep = {r["op"]: {"kernel": r["kernel"], "us_per_launch": r["us_per_launch"],
+                           "gb_s": r["gb_s"], "frac": r["frac"], "bytes": r["bytes"]}
+                 for r in op_sweep_rows(ctx, 3, 1)}
     tp_block = None if args.no_tp_report else tp_report(args, ctx, rank, world, dist)
     layer_launches = 5 * CONFIG["num_hidden_layers"] + 1
     prefill_launches = 1 + 14 * CONFIG["num_hidden_layers"] + 2
@@ -389,6 +395,12 @@ def run_ours(args, rank, world, local_rank):
         }
         if tp_block is not None:
             line["tp"] = tp_block
+        if sweep is not None:
+            line["kernels_sweep"] = {
+                "workload": "BASELINE config 1: each decode GEMV shape and flash-decode attention "
+                            "(16 q / 8 KV heads) at L = 512 / 2048 / 8192 through the op API, "
+                            f"rotated working sets > {ROTATE_BYTES >> 20} MB, median of 3",
+                "peak_gbs": hbm, "ops": sweep}
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(args.cpu_sample_steps)
         print(json.dumps(line), flush=True)
@@ -696,20 +708,41 @@ def run_op_sweep(args):
     the kernels', not the host's launch rate). Bytes per launch are the
     algorithmic ones: weights + input + output (GEMV), K/V rows + q + out
     (attention)."""
-    import math
     import torch
     import metal_infer as mi
 
     torch.cuda.set_device(0)
     ctx = mi.MetalContext(0)
-    stream = torch.cuda.ExternalStream(ctx.stream())
     peak, peak_kind = peaks()
+    only = set(args.ops.split(",")) if args.ops else None
+    rows = op_sweep_rows(ctx, args.steps, args.warmup, only)
+    total_bytes = sum(r["bytes"] for r in rows)
+    total_s = sum(r["us_per_launch"] for r in rows) / 1e6
+    print(json.dumps({
+        "metric": "GEMV / attention HBM GB/s (op sweep)", "impl": "ours",
+        "value": round(total_bytes / total_s / 1e9, 1), "unit": "GB/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+        "dtype": "f16", "data": "synthetic (seeded N(0,0.02) weights, N(0,1) activations)",
+        "config": {"workload": "BASELINE config 1 decode-op sweep, rotated working sets "
+                               f"> {ROTATE_BYTES >> 20} MB (inputs larger than L2)"},
+        "peak": {"hbm_gbs": peak, "kind": peak_kind}, "ops": rows}), flush=True)
+
+
+def op_sweep_rows(ctx, steps, warmup, only=None):
+    """The op sweep's rows on context `ctx` (see run_op_sweep): per op the
+    median device time per launch, its algorithmic bytes and GB/s."""
+    import math
+    import torch
+    import metal_infer as mi
+
+    stream = torch.cuda.ExternalStream(ctx.stream())
+    peak, _ = peaks()
 
     def timed(encode, copies):
         """Median device seconds per launch, and the slowest host enqueue of a
         batch (it must stay well under the spin for the timing to hold)."""
         samples, enqueue = [], 0.0
-        for i in range(args.warmup + args.steps):
+        for i in range(warmup + steps):
             with torch.cuda.stream(stream):
                 torch.cuda._sleep(SLEEP_CYCLES)
             t0 = time.perf_counter()
@@ -718,12 +751,11 @@ def run_op_sweep(args):
             t1 = time.perf_counter()
             st = b.finish()
             del outs
-            if i >= args.warmup:
+            if i >= warmup:
                 samples.append(st.gpu_time / copies)
                 enqueue = max(enqueue, t1 - t0)
         return statistics.median(samples), enqueue
 
-    only = set(args.ops.split(",")) if args.ops else None
     rows = []
     x_cache = {}
     for name, n, k, segs in SWEEP_GEMV:
@@ -782,16 +814,7 @@ def run_op_sweep(args):
                      "host_enqueue_ms": round(enq * 1e3, 2)})
         del kvs
         ctx.synchronize()
-    total_bytes = sum(r["bytes"] for r in rows)
-    total_s = sum(r["us_per_launch"] for r in rows) / 1e6
-    print(json.dumps({
-        "metric": "GEMV / attention HBM GB/s (op sweep)", "impl": "ours",
-        "value": round(total_bytes / total_s / 1e9, 1), "unit": "GB/s", "n_gpus": 1,
-        "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
-        "dtype": "f16", "data": "synthetic (seeded N(0,0.02) weights, N(0,1) activations)",
-        "config": {"workload": "BASELINE config 1 decode-op sweep, rotated working sets "
-                               f"> {ROTATE_BYTES >> 20} MB (inputs larger than L2)"},
-        "peak": {"hbm_gbs": peak, "kind": peak_kind}, "ops": rows}), flush=True)
+    return rows
 
 
 def main():
@@ -815,6 +838,8 @@ def main():
                     help="skip the untimed sampled-decode report (short profiling runs)")
     ap.add_argument("--no-tp-report", action="store_true",
                     help="skip the Qwen3-8B tensor-parallel block (short profiling runs)")
+    ap.add_argument("--no-op-sweep", action="store_true",
+                    help="skip the decode-op sweep block (short profiling runs)")
     ap.add_argument("--cpu-sample-steps", type=int, default=48)
     ap.add_argument("--decode-steps", type=int, default=None,
                     help="decode steps per request (smaller only for profiler launch lists)")

@@ -99,9 +99,13 @@ struct DecodeArgs {
   const float2* rope;     // RoPE table (null: evaluate the terms)
 };
 
+// K / V rows padded to 272 bytes: one thread per key reads its row
+// without bank conflicts.
+constexpr int kRowP = HD + 8;
+
 struct alignas(16) DecodeTile {
-  __half k[kTile][HD];
-  __half v[kTile][HD];
+  __half k[kTile][kRowP];
+  __half v[kTile][kRowP];
 };
 
 // The K/V tiles come last: a launch whose blocks fit one tile (block <=
@@ -110,7 +114,11 @@ template <int G>
 struct DecodeSmem {
   __half new_k[HD];
   __half new_v[HD];
-  float q[G][HD];
+  __half q[G][HD];              // FP16-rounded queries (after QK-norm + RoPE when fused)
+  float sc[G][kTile];           // scaled scores of the tile
+  float pa[G][kTile];           // exp(m_prev - m), exp(s - m) per key
+  float pc[G][kTile];
+  float mrun[2][kStreams][G];   // running max per stream, by tile parity
   float m[kStreams][G];
   float l[kStreams][G];
   float acc[kStreams][G][HD];
@@ -126,7 +134,7 @@ constexpr size_t decode_smem_bytes(bool two_tiles) {
 // Stages keys [j0, j1) of head g into buffer `buf` (cp.async, 16 bytes per
 // copy), skipping `skip`.
 __device__ __forceinline__ void stage_tile(const DecodeArgs& a, int g, int j0, int j1, int skip,
-                                           __half (*kt)[HD], __half (*vt)[HD]) {
+                                           __half (*kt)[kRowP], __half (*vt)[kRowP]) {
   const int per_row = kRowBytes / 16;
   const int total = (j1 - j0) * per_row;
   const size_t stride = (size_t)a.kvh * HD;
@@ -186,8 +194,12 @@ __global__ void __launch_bounds__(kDecodeThreads) attention_decode_kernel(Decode
         qv[2 * i + 1] = f.y;
       }
     }
+    // FP16-rounded values (the fused RoPE rounds; raw queries are FP16)
+    uint4 qq;
+    __half2* hq2 = reinterpret_cast<__half2*>(&qq);
 #pragma unroll
-    for (int e = 0; e < 8; ++e) sm.q[hw][8 * li + e] = qv[e];
+    for (int i = 0; i < 4; ++i) hq2[i] = __floats2half2_rn(qv[2 * i], qv[2 * i + 1]);
+    reinterpret_cast<uint4*>(sm.q[hw])[li] = qq;
   }
   if (a.fused && pos >= begin && pos < end && warp == 3 && lane >= 16) {
     uint4 raw = reinterpret_cast<const uint4*>(a.k_raw + (size_t)g_kv * HD)[li];
@@ -206,25 +218,31 @@ __global__ void __launch_bounds__(kDecodeThreads) attention_decode_kernel(Decode
     reinterpret_cast<uint4*>(sm.new_v)[li] = vv;
   }
 
-  float qreg[G][8];
-  float m[G], l[G], acc[G][8];
-  __syncthreads();
+  // Lane per key: one thread per (key, head) score with the canonical tree
+  // in registers; a key's running maximum is its stream's prefix maximum
+  // (exact in any order), so each key's two exponentials are independent;
+  // the accumulations stay sequential in key order, one thread per (stream,
+  // head, 8 dims). Stream s takes block-relative keys s, s + 8, ... (tiles
+  // are multiples of 8 keys, so the order is the block's).
+  constexpr int R = G;  // accumulators per thread: kStreams * G * 16 / 128
+  if (threadIdx.x < kStreams * G) sm.mrun[0][threadIdx.x / G][threadIdx.x % G] = -INFINITY;
+  float acc[R][8], l[R];
 #pragma unroll
-  for (int g = 0; g < G; ++g) {
+  for (int r = 0; r < R; ++r) {
+    l[r] = 0.f;
 #pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      qreg[g][e] = sm.q[g][8 * li + e];
-      acc[g][e] = 0.f;
-    }
-    m[g] = -INFINITY;
-    l[g] = 0.f;
+    for (int e = 0; e < 8; ++e) acc[r][e] = 0.f;
   }
   const float scale = __frcp_rn(__fsqrt_rn((float)HD));
+  const uint4* nk = reinterpret_cast<const uint4*>(sm.new_k);
+  const uint4* nv = reinterpret_cast<const uint4*>(sm.new_v);
 
   for (int t = 0; t < ntiles; ++t) {
     const int buf = t & 1;
     const int j0 = begin + t * kTile;
     const int j1 = min(end, j0 + kTile);
+    const int cnt = j1 - j0;
+    const int cur = t & 1;
     if (t + 1 < ntiles)
       stage_tile(a, g_kv, j1, min(end, j1 + kTile), pos, sm.tile[buf ^ 1].k, sm.tile[buf ^ 1].v);
     if (t + 1 < ntiles)
@@ -232,87 +250,84 @@ __global__ void __launch_bounds__(kDecodeThreads) attention_decode_kernel(Decode
     else
       pipe::cp_async_wait_all();
     __syncthreads();
-    // Stream hw takes block-relative keys hw, hw + 8, ... (tiles are
-    // multiples of 8 keys, so the order is the block's), two at a time: the
-    // scores of keys r and r + 8 first, then their updates in key order. Both
-    // half-warps of a warp run the same trip count (the shuffles span the
-    // whole warp); a half-warp past the end computes on zeros and keeps its
-    // state.
-    const int count = j1 - j0;
-    for (int base = warp * 2; base < count; base += 2 * kStreams) {
-      uint4 kk[2], vv[2];
-      bool valid[2];
+    // scores
+    for (int idx = threadIdx.x; idx < kTile * G; idx += kDecodeThreads) {
+      const int jj = idx & (kTile - 1), g = idx / kTile;
+      if (jj < cnt) {
+        const bool fresh = j0 + jj == pos;
+        const uint4* q = reinterpret_cast<const uint4*>(sm.q[g]);
+        const uint4* kr = reinterpret_cast<const uint4*>(sm.tile[buf].k[jj]);
+        float d[8];
 #pragma unroll
-      for (int t2 = 0; t2 < 2; ++t2) {
-        const int r = base + t2 * kStreams + (lane >> 4);
-        const int j = j0 + r;
-        valid[t2] = r < count;
-        kk[t2] = make_uint4(0, 0, 0, 0);
-        vv[t2] = make_uint4(0, 0, 0, 0);
-        if (valid[t2] && j == pos) {
-          kk[t2] = reinterpret_cast<const uint4*>(sm.new_k)[li];
-          vv[t2] = reinterpret_cast<const uint4*>(sm.new_v)[li];
-        } else if (valid[t2]) {
-          kk[t2] = reinterpret_cast<const uint4*>(sm.tile[buf].k[r])[li];
-          vv[t2] = reinterpret_cast<const uint4*>(sm.tile[buf].v[r])[li];
-        }
+        for (int c = 0; c < 8; ++c) d[c] = chunk_dot(q[c], fresh ? nk[c] : kr[c], 0.f);
+#pragma unroll
+        for (int c = 0; c < 8; ++c)
+          d[c] = __fadd_rn(d[c], chunk_dot(q[c + 8], fresh ? nk[c + 8] : kr[c + 8], 0.f));
+#pragma unroll
+        for (int step = 4; step >= 1; step >>= 1)
+#pragma unroll
+          for (int c = 0; c < step; ++c) d[c] = __fadd_rn(d[c], d[c + step]);
+        sm.sc[g][jj] = __fmul_rn(d[0], scale);
       }
-      float sc[2][G];
+    }
+    __syncthreads();
+    // prefix maxima and the two exponentials of every key
+    for (int idx = threadIdx.x; idx < kTile * G; idx += kDecodeThreads) {
+      const int jj = idx & (kTile - 1), g = idx / kTile, st = jj & (kStreams - 1);
+      if (jj < cnt) {
+        float prev[kTile / kStreams];
 #pragma unroll
-      for (int t2 = 0; t2 < 2; ++t2) {
-        float kf[8];
-        const __half2* hk = reinterpret_cast<const __half2*>(&kk[t2]);
+        for (int i = 0; i < kTile / kStreams; ++i) prev[i] = sm.sc[g][st + kStreams * i];
+        float mp = sm.mrun[cur][st][g];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          float2 fk = __half22float2(hk[i]);
-          kf[2 * i] = fk.x;
-          kf[2 * i + 1] = fk.y;
-        }
-#pragma unroll
-        for (int g = 0; g < G; ++g) {
-          float d = 0.f;
-#pragma unroll
-          for (int e = 0; e < 8; ++e) d = __fmaf_rn(qreg[g][e], kf[e], d);
-          sc[t2][g] = __fmul_rn(canon_butterfly(d, 16), scale);
-        }
+        for (int i = 0; i < kTile / kStreams; ++i)
+          if (st + kStreams * i < jj) mp = fmaxf(mp, prev[i]);
+        const float sc = sm.sc[g][jj];
+        const float mn = fmaxf(mp, sc);
+        sm.pa[g][jj] = mi_exp(__fsub_rn(mp, mn));
+        sm.pc[g][jj] = mi_exp(__fsub_rn(sc, mn));
+        if (jj + kStreams >= cnt) sm.mrun[cur ^ 1][st][g] = mn;  // the stream's last key here
+      } else if (jj < kStreams) {
+        sm.mrun[cur ^ 1][jj][g] = sm.mrun[cur][jj][g];  // a stream with no key in this tile
       }
+    }
+    __syncthreads();
+    // accumulations in key order
 #pragma unroll
-      for (int t2 = 0; t2 < 2; ++t2) {
-        if (!valid[t2]) continue;
-        float vf[8];
-        const __half2* hv = reinterpret_cast<const __half2*>(&vv[t2]);
+    for (int r = 0; r < R; ++r) {
+      const int idx = threadIdx.x + r * kDecodeThreads;
+      const int st = (idx >> 4) & (kStreams - 1), g = idx >> 7;
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          float2 fv = __half22float2(hv[i]);
-          vf[2 * i] = fv.x;
-          vf[2 * i + 1] = fv.y;
+      for (int i = 0; i < kTile / kStreams; ++i) {
+        const int jj = st + kStreams * i;
+        if (jj >= cnt) break;
+        const float pa = sm.pa[g][jj], pc = sm.pc[g][jj];
+        const uint4 vv = j0 + jj == pos ? nv[li]
+                                        : reinterpret_cast<const uint4*>(sm.tile[buf].v[jj])[li];
+        const __half2* hv = reinterpret_cast<const __half2*>(&vv);
+#pragma unroll
+        for (int e2 = 0; e2 < 4; ++e2) {
+          const float2 f = __half22float2(hv[e2]);
+          acc[r][2 * e2] = __fmaf_rn(acc[r][2 * e2], pa, __fmul_rn(pc, f.x));
+          acc[r][2 * e2 + 1] = __fmaf_rn(acc[r][2 * e2 + 1], pa, __fmul_rn(pc, f.y));
         }
-#pragma unroll
-        for (int g = 0; g < G; ++g) {
-          const float s = sc[t2][g];
-          float nm = fmaxf(m[g], s);
-          float pa = mi_exp(__fsub_rn(m[g], nm));
-          float pc = mi_exp(__fsub_rn(s, nm));
-#pragma unroll
-          for (int e = 0; e < 8; ++e) acc[g][e] = __fmaf_rn(acc[g][e], pa, __fmul_rn(pc, vf[e]));
-          l[g] = __fmaf_rn(l[g], pa, pc);
-          m[g] = nm;
-        }
+        l[r] = __fmaf_rn(l[r], pa, pc);
       }
     }
     __syncthreads();
   }
 
-  // Stream merge (index order) -> block partial.
+  // Stream states -> shared memory for the stream merge (index order).
 #pragma unroll
-  for (int g = 0; g < G; ++g) {
-    if (li == 0) {
-      sm.m[hw][g] = m[g];
-      sm.l[hw][g] = l[g];
-    }
+  for (int r = 0; r < R; ++r) {
+    const int idx = threadIdx.x + r * kDecodeThreads;
+    const int st = (idx >> 4) & (kStreams - 1), g = idx >> 7;
 #pragma unroll
-    for (int e = 0; e < 8; ++e) sm.acc[hw][g][8 * li + e] = acc[g][e];
+    for (int e = 0; e < 8; ++e) sm.acc[st][g][8 * li + e] = acc[r][e];
+    if (li == 0) sm.l[st][g] = l[r];
   }
+  if (threadIdx.x < kStreams * G)
+    sm.m[threadIdx.x / G][threadIdx.x % G] = sm.mrun[ntiles & 1][threadIdx.x / G][threadIdx.x % G];
   __syncthreads();
   const int stride = HD + 2;
   float* part = a.scratch + ((size_t)g_kv * gridDim.x + b) * G * stride;

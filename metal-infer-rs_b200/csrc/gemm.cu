@@ -73,6 +73,103 @@ __global__ void __launch_bounds__(256) gemm_canon_kernel(const __half* x, const 
   }
 }
 
+// Staged canonical kernel (K >= 256, so every dot spans all 32 lanes): the
+// CTA's 16 x rows and 32 w rows are staged 256 elements (one chunk per lane)
+// at a time in shared memory by double-buffered 16-byte cp.async; the warp
+// tiles and each lane's FMA chains are those of gemm_canon_kernel. The final
+// butterflies of the 64 dots run as a transpose-reduce: at each level a lane
+// keeps half of its dots and adds its partner's copies (the same operand
+// pairs as the butterfly), so each lane ends with two finished dots and the
+// warp issues 62 shuffles instead of 320.
+constexpr int kSM = 16, kSN = 32, kSK = 256;
+
+struct CanonSmem {
+  __half x[2][kSM][kSK];
+  __half w[2][kSN][kSK];
+};
+
+__device__ __forceinline__ void canon_stage(const __half* x, const __half* w, int m, int n, int k,
+                                            int m0, int n0, int k0, CanonSmem& sm, int buf) {
+  for (int i = threadIdx.x; i < (kSM + kSN) * (kSK / 8); i += 256) {
+    const int r = i / (kSK / 8), c = i % (kSK / 8);
+    const int kk = k0 + 8 * c;
+    const bool is_x = r < kSM;
+    const int row = is_x ? m0 + r : n0 + (r - kSM);
+    __half* dst = is_x ? &sm.x[buf][r][8 * c] : &sm.w[buf][r - kSM][8 * c];
+    if ((is_x ? row < m : row < n) && kk < k) {
+      const __half* src = (is_x ? x : w) + (size_t)row * k + kk;
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
+                       static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
+                   "l"(src)
+                   : "memory");
+    } else {
+      *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);  // adds exact zeros
+    }
+  }
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+
+__global__ void __launch_bounds__(256) gemm_canon_staged_kernel(const __half* x, const __half* w,
+                                                                __half* out, int m, int n, int k,
+                                                                int ldo, float* outf) {
+  extern __shared__ __align__(16) uint8_t canon_smem[];
+  CanonSmem& sm = *reinterpret_cast<CanonSmem*>(canon_smem);
+  pdl_wait();
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int m0 = blockIdx.y * kSM, n0 = blockIdx.x * kSN;
+  const int wm = (warp & 1) * 8, wn = (warp >> 1) * 8;
+  const int steps = (k + kSK - 1) / kSK;
+  float acc[64];
+#pragma unroll
+  for (int a = 0; a < 64; ++a) acc[a] = 0.f;
+  canon_stage(x, w, m, n, k, m0, n0, 0, sm, 0);
+  for (int st = 0; st < steps; ++st) {
+    const int buf = st & 1;
+    if (st + 1 < steps) {
+      canon_stage(x, w, m, n, k, m0, n0, (st + 1) * kSK, sm, buf ^ 1);
+      asm volatile("cp.async.wait_group 1;" ::: "memory");
+    } else {
+      asm volatile("cp.async.wait_group 0;" ::: "memory");
+    }
+    __syncthreads();
+    uint4 xv[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) xv[i] = reinterpret_cast<const uint4*>(sm.x[buf][wm + i])[lane];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const uint4 wv = reinterpret_cast<const uint4*>(sm.w[buf][wn + j])[lane];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i * 8 + j] = chunk_dot(xv[i], wv, acc[i * 8 + j]);
+    }
+    __syncthreads();  // the buffer is staged again two steps on
+  }
+  // Transpose-reduce: dot d = i * 8 + j; at the level of lane bit b (16, 8,
+  // 4, 2, 1) a lane keeps the half of its dots whose matching index bit
+  // equals its lane bit and adds the partner's value of the same dot.
+#pragma unroll
+  for (int half = 32, o = 16; o >= 1; half >>= 1, o >>= 1) {
+    const bool up = (lane & o) != 0;
+#pragma unroll
+    for (int a = 0; a < half; ++a) {
+      const float keep = up ? acc[a + half] : acc[a];
+      const float send = up ? acc[a] : acc[a + half];
+      acc[a] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, o));
+    }
+  }
+  // lane l holds dots 2l and 2l + 1 (index bits 5..1 = lane bits 4..0)
+#pragma unroll
+  for (int s2 = 0; s2 < 2; ++s2) {
+    const int d = 2 * lane + s2;
+    const int i = d >> 3, j = d & 7;
+    if (m0 + wm + i < m && n0 + wn + j < n) {
+      const size_t o2 = (size_t)(m0 + wm + i) * ldo + n0 + wn + j;
+      if (outf) outf[o2] = acc[s2];
+      else out[o2] = __float2half_rn(acc[s2]);
+    }
+  }
+}
+
 constexpr int BM = 64, BN = 64, BK = 16;
 
 // 256 threads; each computes a 4x4 block of the 64x64 tile.
@@ -124,6 +221,20 @@ __global__ void __launch_bounds__(256) gemm_simt_kernel(const __half* x, const _
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
+// The canonical GEMM: the staged kernel when every dot spans 32 lanes
+// (K >= 256), else the direct one; FP16 `out` or FP32 `outf`.
+void launch_canon(const Launch& l, const __half* x, const __half* w, __half* out, int m, int n,
+                  int k, int ldo, float* outf) {
+  dim3 grid((n + 31) / 32, (m + 15) / 16);
+  if (k >= kSK) {
+    auto kernel = gemm_canon_staged_kernel;
+    allow_dynamic_smem(kernel, sizeof(CanonSmem));
+    launch_kernel(l, grid, dim3(256), sizeof(CanonSmem), kernel, x, w, out, m, n, k, ldo, outf);
+  } else {
+    launch_kernel(l, grid, dim3(256), 0, gemm_canon_kernel, x, w, out, m, n, k, ldo, outf);
+  }
+}
+
 }  // namespace
 
 bool gemm_tc(const Launch& l, const __half* x, const __half* w, __half* out, int m, int n, int k,
@@ -134,9 +245,7 @@ void gemm(const Launch& l, const __half* x, const __half* w, __half* out, int m,
   if (m <= 0 || n <= 0) return;
   const bool vec = k % 8 == 0 && aligned16(x) && aligned16(w);
   if (vec && m <= kCanonRows) {
-    dim3 grid((n + 31) / 32, (m + 15) / 16);
-    launch_kernel(l, grid, dim3(256), 0, gemm_canon_kernel, x, w, out, m, n, k, ldo,
-                  static_cast<float*>(nullptr));
+    launch_canon(l, x, w, out, m, n, k, ldo, nullptr);
     return;
   }
   if (gemm_tc(l, x, w, out, m, n, k, ldo)) return;
@@ -149,9 +258,7 @@ void gemm_partial_f32(const Launch& l, const __half* x, const __half* w, float* 
   if (m <= 0 || n <= 0) return;
   MI_REQUIRE(k % 8 == 0 && aligned16(x) && aligned16(w), MI_ERR_SHAPE,
              "tensor-parallel partial products need K %% 8 == 0 and 16-byte aligned operands");
-  dim3 grid((n + 31) / 32, (m + 15) / 16);
-  launch_kernel(l, grid, dim3(256), 0, gemm_canon_kernel, x, w, static_cast<__half*>(nullptr), m,
-                n, k, n, out);
+  launch_canon(l, x, w, nullptr, m, n, k, n, out);
 }
 
 }  // namespace k
