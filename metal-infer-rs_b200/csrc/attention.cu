@@ -375,10 +375,34 @@ __global__ void __launch_bounds__(kDecodeThreads) attention_decode_kernel(Decode
   const int buf_floats =
       (int)((a.block > kTile ? 2 : 1) * sizeof(DecodeTile) / sizeof(float));
   constexpr int kRec = G * (HD + 2);                        // floats of one block record
-  const int kChunk = (buf_floats - 3) / kRec;               // blocks per staged chunk
+  // two halves: chunk c + 1 streams into one while chunk c is merged from the other
+  const int half = buf_floats / 2 / 4 * 4;
+  const int kChunk = (half - 3) / kRec;                     // blocks per staged chunk
   float* fs = &sm.acc[0][0][0];                             // [kChunk][G] merge factors
   static_assert((2 * sizeof(DecodeTile) / sizeof(float) - 3) / kRec * G <= kStreams * G * HD,
                 "factor buffer");
+  // Chunk `ci` (blocks [ci * kChunk, +cnt)) into half `hb`: 16-byte cp.async
+  // for the aligned middle, plain loads for a misaligned head and the tail.
+  auto issue = [&](int ci, int hb) -> float* {
+    const int s0 = ci * kChunk;
+    const int cnt = min(kChunk, nb - s0);
+    const float* src = base + (size_t)s0 * kRec;
+    const int n = cnt * kRec;
+    const int head = (int)((4 - ((reinterpret_cast<uintptr_t>(src) >> 2) & 3)) & 3);
+    const int h = min(n, head);
+    float* stage = buf + hb * half + ((4 - h) & 3);  // stage + h is 16-byte aligned
+    const int n4 = (n - h) >> 2;
+    for (int i2 = threadIdx.x; i2 < n4; i2 += kDecodeThreads)
+      pipe::cp_async16(stage + h + 4 * i2, src + h + 4 * i2);
+    pipe::cp_async_commit();
+    if (threadIdx.x < h) stage[threadIdx.x] = __ldcg(src + threadIdx.x);
+    const int t0 = h + 4 * n4;
+    if (threadIdx.x < n - t0) stage[t0 + threadIdx.x] = __ldcg(src + t0 + threadIdx.x);
+    return stage;
+  };
+  const int nchunks = (nb + kChunk - 1) / kChunk;
+  float* stage_a = issue(0, 0);  // the chunk staged in half 0 / half 1
+  float* stage_b = nullptr;
   // M per head of the group (sm.m[0][g]).
   {
     float mloc[G];
@@ -415,26 +439,23 @@ __global__ void __launch_bounds__(kDecodeThreads) attention_decode_kernel(Decode
   for (int g = 0; g < G; ++g) num[g] = 0.f;
   static_assert(kDecodeThreads == HD, "one thread per head dimension");
   const int d = threadIdx.x;
-  for (int s0 = 0; s0 < nb; s0 += kChunk) {
-    const int cnt = min(kChunk, nb - s0);
-    const float* src = base + (size_t)s0 * kRec;
-    const int n = cnt * kRec;
-    const int head = (int)((4 - ((reinterpret_cast<uintptr_t>(src) >> 2) & 3)) & 3);
-    const int h = min(n, head);
-    float* stage = buf + ((4 - h) & 3);  // stage + h is 16-byte aligned
-    const int n4 = (n - h) >> 2;
-    for (int i = threadIdx.x; i < n4; i += kDecodeThreads)
-      pipe::cp_async16(stage + h + 4 * i, src + h + 4 * i);
-    pipe::cp_async_commit();
-    if (threadIdx.x < h) stage[threadIdx.x] = __ldcg(src + threadIdx.x);
-    const int t0 = h + 4 * n4;
-    if (threadIdx.x < n - t0) stage[t0 + threadIdx.x] = __ldcg(src + t0 + threadIdx.x);
-    pipe::cp_async_wait_all();
+  for (int ci = 0; ci < nchunks; ++ci) {
+    const int cnt = min(kChunk, nb - ci * kChunk);
+    if (ci + 1 < nchunks) {
+      if ((ci + 1) & 1)
+        stage_b = issue(ci + 1, 1);
+      else
+        stage_a = issue(ci + 1, 0);
+      asm volatile("cp.async.wait_group 1;" ::: "memory");
+    } else {
+      pipe::cp_async_wait_all();
+    }
     __syncthreads();
-    for (int i = threadIdx.x; i < cnt * G; i += kDecodeThreads) {
-      const int g = i % G;
-      const float mm = stage[i * (HD + 2)];
-      fs[i] = mm == -INFINITY ? 0.f : mi_exp(__fsub_rn(mm, sm.m[0][g]));
+    const float* stage = (ci & 1) ? stage_b : stage_a;
+    for (int i2 = threadIdx.x; i2 < cnt * G; i2 += kDecodeThreads) {
+      const int g = i2 % G;
+      const float mm = stage[i2 * (HD + 2)];
+      fs[i2] = mm == -INFINITY ? 0.f : mi_exp(__fsub_rn(mm, sm.m[0][g]));
     }
     __syncthreads();
     // The chains read their operands kMB blocks at a time, loads first.
