@@ -10,7 +10,7 @@
 //   DOWN  down rows + residual add
 // then final RMSNorm + LM head + greedy argmax, whose id feeds the next step.
 //
-// One CTA per SM: 15 consumer warps and one producer warp. The producer
+// One CTA per SM: 11 consumer warps and one producer warp. The producer
 // walks the static schedule of weight tiles this CTA will reduce (every
 // stage of every layer of every step, then the LM head) and streams them
 // into a ring of shared-memory slots with 1-D bulk copies that complete on
@@ -23,8 +23,9 @@
 // There are no grid barriers. Activations that cross CTAs are stored as
 // epoch-tagged words (tag << 16 | FP16 bits) that validate themselves: after
 // one L2 round trip of delay a CTA reads the words of the stage it consumes
-// and re-polls those whose tag is not there yet (no completion counters on one
-// GPU; under tensor parallelism the ranks count into each other's mailboxes).
+// and re-polls those whose tag is not there yet (no completion counters; under
+// tensor parallelism every rank polls the tagged partials the others store
+// into its mailbox the same way).
 // Attention units publish their block partials with a release reduction,
 // and the O stage merges the partials of every head while building its input.
 //
@@ -38,19 +39,22 @@
 #include "device.cuh"
 #include "pipeline.cuh"
 
+
 namespace mi {
 namespace k {
 
 namespace {
 
 constexpr int HD = 128;
-constexpr int kConsumerWarps = 15;  // + 1 producer: 512 threads, 128 registers
+// 11 consumer warps + 1 producer: 384 threads, 168 registers (15 consumer
+// warps at 128 registers measured 1.5% slower on Qwen3-0.6B)
+constexpr int kConsumerWarps = 11;
 constexpr int kConsumers = kConsumerWarps * 32;
 constexpr int kThreads = kConsumers + 32;  // + producer warp
 constexpr int kStreams = 8;
 constexpr int kTile = 64;                  // keys staged per attention tile
-constexpr int kAttnThreads = 256;          // warps 4..11 run the attention units
-constexpr int kAttnBase = 128;             // (warp 0 keeps the stage-input norms)
+constexpr int kAttnThreads = 256;          // the last 8 consumer warps run the attention units
+constexpr int kAttnBase = kConsumerWarps * 32 - kAttnThreads;  // warps 3..10
 constexpr int kMaxSlots = 16;
 // sync[]: [1] abort flag, [2] attention units finished (cumulative over the
 // launch), [kStageDone + st] a word the stage hand-off loads (its delay).
@@ -215,7 +219,7 @@ struct Shared {
   uint32_t best_key[kConsumerWarps];
   uint32_t best_idx[kConsumerWarps];
   uint32_t token;
-  unsigned long long mbox_ns;  // thread 0: time spent in mailbox waits this launch
+  unsigned long long mbox_ns;  // thread 0: time spent on inputs fed by the other ranks
   volatile int abort;  // raised by any warp (or the producer) that gives up
   int stop;            // the consumers' uniform decision, written by one thread between barriers
   int astop;           // the same for the attention warps
@@ -408,7 +412,9 @@ __device__ __forceinline__ void put8(uint32_t* dst, int c, const uint4& v, uint3
 // ---- tensor-parallel exchange through peer memory ------------------------------------
 // Partials are pushed with plain stores into every rank's mailbox (NVLink
 // peer mappings); readers poll their own mailbox. System-scope relaxed
-// accesses: the tags validate every word, the counters only say when to look.
+// accesses: the tags validate every word. (Counting every CTA of every rank
+// into one counter per rank, 1,184 remote reductions per exchange at TP8,
+// cost more than the exchange itself.)
 __device__ __forceinline__ void st_sys_u64(unsigned long long* p, unsigned long long v) {
   asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
@@ -426,28 +432,6 @@ __device__ __forceinline__ void push_partial(const DecodeLoop& p, size_t region,
                                              float v, uint32_t tag) {
   const unsigned long long w = ((unsigned long long)tag << 32) | __float_as_uint(v);
   for (int r = 0; r < p.tp; ++r) st_sys_u64(p.peers[r] + region + (size_t)p.rank * p.hidden + item, w);
-}
-
-// Count this CTA into mailbox counter k (0 O, 1 DOWN, 2 LM) of every rank.
-__device__ __forceinline__ void push_count(const DecodeLoop& p, int k) {
-  const MailboxLayout mb = mailbox_layout(p.tp, p.hidden, gridDim.x);
-  for (int r = 0; r < p.tp; ++r) red_sys_add_u64(p.peers[r] + mb.ctr + 16 * k, 1ull);
-}
-
-// Single thread (thread 0): wait until this rank's mailbox counter k
-// reaches target; the time it takes is added to sh.mbox_ns.
-__device__ bool wait_mbox(const DecodeLoop& p, int k, unsigned long long target, Shared& sh) {
-  const MailboxLayout mb = mailbox_layout(p.tp, p.hidden, gridDim.x);
-  const uint64_t t0 = pipe::global_ns();
-  PollClock clock;
-  bool ok = true;
-  while (ld_sys_u64(p.mbox + mb.ctr + 16 * k) < target)
-    if (!clock.keep_going(p, sh)) {
-      ok = false;
-      break;
-    }
-  sh.mbox_ns += pipe::global_ns() - t0;
-  return ok;
 }
 
 // Chunk c (8 values) of the ranks' partials in region `region`, summed in
@@ -520,15 +504,13 @@ __device__ bool wait_units(const DecodeLoop& p, uint32_t units, bool ran_units, 
   return !sh.stop;
 }
 
-// End of a stage: after every warp has issued its tagged stores, count the
-// CTA in (a relaxed reduction: the tags, not the counter, carry
-// correctness; the counter only tells readers when to look).
+// End of a stage: every warp has issued its tagged stores (the readers
+// validate each word by its tag, here and in the other ranks' mailboxes).
 __device__ __forceinline__ void stage_done(const DecodeLoop& p, int st) {
+  (void)p;
+  (void)st;
   consumers_sync();
-  if (threadIdx.x == 0) {
-    MI_TRACE_ARRIVE(0);
-    if (p.tp > 1 && (st == kO || st == kDown)) push_count(p, st == kO ? 0 : 1);
-  }
+  if (threadIdx.x == 0) MI_TRACE_ARRIVE(0);
 }
 
 // Thread 0, before a stage reads another stage's tagged outputs: one L2 round
@@ -538,7 +520,8 @@ __device__ __forceinline__ void stage_done(const DecodeLoop& p, int st) {
 // on Qwen3-0.6B (tokens/s): waiting for a counter of all CTAs 1,387; polling
 // at once 1,387 (the early polls slow the writers); one load's delay 1,466;
 // two loads 1,446; a 300 / 700 ns sleep 1,454 / 1,345; backoff between polls
-// slower still. Under tensor parallelism the mailbox counts remain.
+// slower still. Under tensor parallelism the readers of the other ranks'
+// partials do the same on their own mailbox.
 __device__ __forceinline__ bool stage_ready(const DecodeLoop& p, int st, Shared& sh) {
   const uint32_t v = ld_relaxed(p.sync + kStageDone + st);
   if (v == 0x9E3779B9u) sh.stop = sh.stop;  // a use of the value: the load completes
@@ -548,6 +531,49 @@ __device__ __forceinline__ bool stage_ready(const DecodeLoop& p, int st, Shared&
 // O-stage input: the attention output of every query head, the log-sum-exp
 // merge of its nb block partials in block order (the arithmetic of
 // attention.cu's final merge), written to xs as FP16.
+// Blocks of a batch whose records (max, denominator, 8 numerators) one
+// thread loads together.
+constexpr int kMergeBatch = 4;
+
+struct MergeRec {
+  float m[kMergeBatch], l[kMergeBatch];
+  float4 n0[kMergeBatch], n1[kMergeBatch];
+};
+
+// Records of blocks [b0, b0 + kMergeBatch) that exist (< nb), loads issued together.
+__device__ __forceinline__ void merge_load(const float* hb, size_t block_stride, int d0, int b0,
+                                           int nb, MergeRec& r) {
+#pragma unroll
+  for (int i = 0; i < kMergeBatch; ++i)
+    if (b0 + i < nb) {
+      const float* rec = hb + (size_t)(b0 + i) * block_stride;
+      r.m[i] = __ldcg(rec);
+      r.l[i] = __ldcg(rec + 1);
+      r.n0[i] = __ldcg(reinterpret_cast<const float4*>(rec + 4 + d0));
+      r.n1[i] = __ldcg(reinterpret_cast<const float4*>(rec + 8 + d0));
+    }
+}
+
+// The block-order accumulation of loaded records (the arithmetic of the
+// generic loop below).
+__device__ __forceinline__ void merge_apply(const MergeRec& r, int b0, int nb, float M,
+                                            float (&num)[8], float& den) {
+#pragma unroll
+  for (int i = 0; i < kMergeBatch; ++i)
+    if (b0 + i < nb) {
+      const float f = r.m[i] == -INFINITY ? 0.f : mi_exp(__fsub_rn(r.m[i], M));
+      den = __fmaf_rn(r.l[i], f, den);
+      num[0] = __fmaf_rn(r.n0[i].x, f, num[0]);
+      num[1] = __fmaf_rn(r.n0[i].y, f, num[1]);
+      num[2] = __fmaf_rn(r.n0[i].z, f, num[2]);
+      num[3] = __fmaf_rn(r.n0[i].w, f, num[3]);
+      num[4] = __fmaf_rn(r.n1[i].x, f, num[4]);
+      num[5] = __fmaf_rn(r.n1[i].y, f, num[5]);
+      num[6] = __fmaf_rn(r.n1[i].z, f, num[6]);
+      num[7] = __fmaf_rn(r.n1[i].w, f, num[7]);
+    }
+}
+
 __device__ void build_attn_input(const DecodeLoop& p, int nb, uint4* xs) {
   const int G = p.qh / p.kvh;
   const int kc = p.qh * HD / 8;
@@ -557,11 +583,40 @@ __device__ void build_attn_input(const DecodeLoop& p, int nb, uint4* xs) {
     const int d0 = (c % (HD / 8)) * 8;
     const float* hb = p.attn_part + ((size_t)(qi / G) * p.attn_blocks * G + qi % G) * kPart;
     float M = -INFINITY;
-#pragma unroll 4
-    for (int b = 0; b < nb; ++b) M = fmaxf(M, __ldcg(hb + b * block_stride));
     float num[8], den = 0.f;
 #pragma unroll
     for (int e = 0; e < 8; ++e) num[e] = 0.f;
+    if (nb <= 2 * kMergeBatch) {
+      // Short caches: the maxima of every block and the first batch's
+      // records are loaded together (one L2 round trip up to 4 blocks, two
+      // up to 8; the loop below takes two to four).
+      MergeRec r;
+      float m2[kMergeBatch];
+      merge_load(hb, block_stride, d0, 0, nb, r);
+#pragma unroll
+      for (int i = 0; i < kMergeBatch; ++i)
+        if (kMergeBatch + i < nb) m2[i] = __ldcg(hb + (size_t)(kMergeBatch + i) * block_stride);
+#pragma unroll
+      for (int i = 0; i < kMergeBatch; ++i) {
+        if (i < nb) M = fmaxf(M, r.m[i]);
+        if (kMergeBatch + i < nb) M = fmaxf(M, m2[i]);
+      }
+      merge_apply(r, 0, nb, M, num, den);
+      if (nb > kMergeBatch) {
+        merge_load(hb, block_stride, d0, kMergeBatch, nb, r);
+        merge_apply(r, kMergeBatch, nb, M, num, den);
+      }
+      uint4 v;
+      __half2* hv = reinterpret_cast<__half2*>(&v);
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        hv[i] = __halves2half2(__float2half_rn(__fdiv_rn(num[2 * i], den)),
+                               __float2half_rn(__fdiv_rn(num[2 * i + 1], den)));
+      xs[c] = v;
+      continue;
+    }
+#pragma unroll 4
+    for (int b = 0; b < nb; ++b) M = fmaxf(M, __ldcg(hb + b * block_stride));
 #pragma unroll 4
     for (int b = 0; b < nb; ++b) {
       const float* rec = hb + b * block_stride;
@@ -673,12 +728,16 @@ struct StageIn {
   const uint32_t* x2;
   uint32_t x2tag;
   long long x2_part;  // >= 0: x2 is the ranks' summed partials in this mailbox region
-  int mb_wait;        // >= 0: first wait until mailbox counter mb_wait reaches mb_target
-  unsigned long long mb_target;
+  int exchange;       // tensor parallelism: x2 comes from the other ranks (timed)
   const __half* embed;  // kEmbedNormIn: table row, null for an out-of-range token
   const __half* norm_w;
   uint32_t* wb;
   uint32_t wbtag;
+  // DOWN on one GPU: the residual values of this CTA's rows, polled into
+  // sh.res by the last res_n consumer threads beside the stage input
+  const uint32_t* res;
+  int res_first, res_n;
+  uint32_t res_tag;
 };
 
 __device__ __forceinline__ uint4 add_chunk(int mode, const uint4& a, const uint4& b) {
@@ -788,14 +847,15 @@ __device__ bool build_input(const DecodeLoop& p, const StageIn& in, int wait_st,
   const bool two = in.mode == kAddNormIn || in.mode == kAddThenNormIn;
   const bool norm = in.mode != kPlainIn;
   const uint4* g4 = reinterpret_cast<const uint4*>(in.norm_w);
-  if (in.mb_wait >= 0) {
-    // tensor parallelism: one thread waits for the mailbox counter
-    if (tid == 0) wait_mbox(p, in.mb_wait, in.mb_target, sh);
-    consumers_sync();
-  } else if (wait_st >= 0 && tid < kc) {
-    stage_ready(p, wait_st, sh);  // one L2 round trip of delay before the polls
-  }
+  // thread 0 times the input of a stage fed by the other ranks' partials
+  // (this rank's wait on the exchange, read back by mi_qwen3_exchange_wait)
+  const uint64_t t_in = (in.exchange && tid == 0) ? pipe::global_ns() : 0;
+  if (wait_st >= 0 && tid < kc) stage_ready(p, wait_st, sh);  // one L2 round trip of delay before the polls
   if (tid == 0) MI_TRACE_IN(9);
+  if (in.res && tid >= kConsumers - in.res_n) {
+    const int i = tid - (kConsumers - in.res_n);
+    sh.res[i] = take1(p, in.res, in.res_first + i, in.res_tag, sh);
+  }
   uint4 g_first = make_uint4(0, 0, 0, 0);
   if (norm && tid < kc) g_first = __ldg(g4 + tid);
   const bool wb = in.wb && blockIdx.x == 0;
@@ -831,11 +891,12 @@ __device__ bool build_input(const DecodeLoop& p, const StageIn& in, int wait_st,
     }
   }
   if (consumers_any(sh.abort)) return false;
+  if (in.exchange && tid == 0) sh.mbox_ns += pipe::global_ns() - t_in;
   if (tid == 0) MI_TRACE_IN(10);
   if (norm) {
     // every warp computes the scale when a lane's chain is short; for wide
     // inputs one warp does and shares it (the redundant shared-memory reads
-    // of 15 warps would cost more than the extra barrier)
+    // of every consumer warp would cost more than the extra barrier)
     const bool every_warp = kc <= 4 * 32;
     float scale = 0.f;
     if (every_warp || tid < 32) scale = warp_scale(p, in.mode, xs, xs2, in.k);
@@ -967,7 +1028,7 @@ __device__ __forceinline__ void rows_group(const DecodeLoop& p, const StageW& s,
 }
 
 // Reduces this CTA's rows of stage ST from the ring: groups of P local rows
-// (never straddling a tile) go round-robin to the 15 consumer warps; every
+// (never straddling a tile) go round-robin to the consumer warps; every
 // warp waits for every tile in order and releases it when done. `g` is the
 // running tile counter.
 template <int ST, int P>
@@ -1021,7 +1082,7 @@ __device__ void reduce_rows(const DecodeLoop& p, const StageW& s, const uint4* x
     reduce_rows_p<ST, 1>(p, s, t, xs, ring, sh, g, tag, best_key, best_idx);
 }
 
-// ---- consumers: attention units (warps 4..11) -------------------------------------------
+// ---- consumers: attention units (warps 3..10) -------------------------------------------
 // Thread index within the attention warps.
 __device__ __forceinline__ int atid() { return (int)threadIdx.x - kAttnBase; }
 
@@ -1106,7 +1167,7 @@ __device__ __forceinline__ float key_score(const AttnSmem<G>& sm, int g, int j, 
 }
 
 // One flash-decode unit: KV head g_kv, key block b of nb, run by the 256
-// attention threads (warps 4..11). The arithmetic is attention.cu's
+// attention threads (warps 3..10). The arithmetic is attention.cu's
 // attention_decode_kernel with the fused front end: kStreams interleaved
 // online-softmax streams per block (stream s takes the block's keys s,
 // s + 8, ... in order), merged in stream order into the block partial. The
@@ -1374,7 +1435,6 @@ __global__ void __launch_bounds__(kThreads, 1) decode_loop_kernel(DecodeLoop par
       // hidden stream read by GU: under tensor parallelism every QKV stage
       // writes it back (it is assembled from the ranks' down partials there)
       const uint32_t hidden_in = (layer == 0 || p.tp > 1) ? tagv(e, 0) : tagv(e - 1u, 1);
-      const unsigned long long per_ls = (unsigned long long)p.tp * grid;  // mailbox counts
       uint32_t bk = 0, bi = 0xFFFFFFFFu;
       bool kv_issued = false;  // this CTA's attention prefetch of the layer
       // QKV (layer 0: the embedding row, written back as the hidden stream)
@@ -1383,7 +1443,6 @@ __global__ void __launch_bounds__(kThreads, 1) decode_loop_kernel(DecodeLoop par
         const StageW s = stage_weights(p, lay, layer, kQKV);
         StageIn in = {};
         in.x2_part = -1;
-        in.mb_wait = -1;
         in.k = p.hidden;
         in.norm_w = L.in_norm;
         if (layer == 0) {
@@ -1399,8 +1458,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_loop_kernel(DecodeLoop par
           in.xtag = tagv(e - 1u, 0);
           in.x2_part = (long long)mailbox_layout(p.tp, p.hidden, grid).d;
           in.x2tag = tagv(e - 1u, 1);  // as the DOWN stage tagged its partials
-          in.mb_wait = 1;
-          in.mb_target = p.ctr_base[1] + (unsigned long long)ls * per_ls;
+          in.exchange = 1;
           in.wb = p.t_hidden;
           in.wbtag = tagv(e, 0);
         } else {
@@ -1450,7 +1508,6 @@ __global__ void __launch_bounds__(kThreads, 1) decode_loop_kernel(DecodeLoop par
         const StageW s = stage_weights(p, lay, layer, kGU);
         StageIn in = {};
         in.x2_part = -1;
-        in.mb_wait = -1;
         in.mode = p.add_norm ? kAddNormIn : kAddThenNormIn;
         in.k = p.hidden;
         in.x = p.t_hidden;
@@ -1461,8 +1518,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_loop_kernel(DecodeLoop par
           // attention output = half(sum of the ranks' O partials)
           in.x2_part = (long long)mailbox_layout(p.tp, p.hidden, grid).o;
           in.x2tag = tagv(e, 0);  // as the O stage tagged its partials
-          in.mb_wait = 0;
-          in.mb_target = p.ctr_base[0] + (unsigned long long)(ls + 1u) * per_ls;
+          in.exchange = 1;
         }
         in.norm_w = L.post_norm;
         in.wb = p.t_res;
@@ -1484,19 +1540,20 @@ __global__ void __launch_bounds__(kThreads, 1) decode_loop_kernel(DecodeLoop par
         const StageW s = stage_weights(p, lay, layer, kDown);
         StageIn in = {};
         in.x2_part = -1;
-        in.mb_wait = -1;
         in.mode = kPlainIn;
         in.k = p.inter;
         in.x = p.t_act;
         in.xtag = tagv(e, 0);
-        if (!build_input(p, in, kGU, xs, xs2, xn, sh)) return;
         if (p.tp == 1) {
           // residuals of this CTA's rows (written back by CTA 0 in GU); under
           // tensor parallelism the next QKV stage adds them
           const Tiles& td = sh.tiles[kDown];
-          if (tid < td.last - td.first) sh.res[tid] = take1(p, p.t_res, td.first + tid, tagv(e, 0), sh);
-          consumers_sync();
+          in.res = p.t_res;
+          in.res_first = td.first;
+          in.res_n = td.last - td.first;
+          in.res_tag = tagv(e, 0);
         }
+        if (!build_input(p, in, kGU, xs, xs2, xn, sh)) return;
         if (tid == 0) MI_TRACE(step, layer * 5 + 4, 1);
         reduce_rows<kDown>(p, s, xs, ring, sh, g, tagv(e, 1), bk, bi);
         stage_done(p, kDown);
@@ -1511,7 +1568,6 @@ __global__ void __launch_bounds__(kThreads, 1) decode_loop_kernel(DecodeLoop par
       const StageW s = stage_weights(p, lay, p.layers, kLM);
       StageIn in = {};
       in.x2_part = -1;
-      in.mb_wait = -1;
       in.mode = kNormIn;
       in.k = p.hidden;
       in.x = p.t_hidden;
@@ -1524,8 +1580,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_loop_kernel(DecodeLoop par
         in.xtag = tagv(e, 0);
         in.x2_part = (long long)mailbox_layout(p.tp, p.hidden, grid).d;
         in.x2tag = tagv(e, 1);
-        in.mb_wait = 1;
-        in.mb_target = p.ctr_base[1] + (unsigned long long)(ls_last + 1u) * p.tp * grid;
+        in.exchange = 1;
       }
       if (!build_input(p, in, kDown, xs, xs2, xn, sh)) return;
       if (tid == 0) MI_TRACE(step, p.layers * 5, 1);
@@ -1547,45 +1602,55 @@ __global__ void __launch_bounds__(kThreads, 1) decode_loop_kernel(DecodeLoop par
       }
       consumers_sync();
       const unsigned long long rtag = e & 0x3FFFu;
-      if (warp == 0) {
-        if (lane == 0) {
-          uint32_t ck = 0, ci = 0xFFFFFFFFu;
-          for (int w = 0; w < kConsumerWarps; ++w)
-            if (argmax_better(sh.best_key[w], sh.best_idx[w], ck, ci)) {
-              ck = sh.best_key[w];
-              ci = sh.best_idx[w];
-            }
-          const unsigned long long idx =
-              ci == 0xFFFFFFFFu ? 0x3FFFFull : (unsigned long long)(ci + p.vocab0);
-          const unsigned long long rec = ((unsigned long long)ck << 32) | (idx << 14) | rtag;
-          if (p.tp > 1) {
-            // vocab-parallel: the record goes to every rank's mailbox
-            const MailboxLayout mb = mailbox_layout(p.tp, p.hidden, grid);
-            for (int r = 0; r < p.tp; ++r)
-              st_sys_u64(p.peers[r] + mb.rec + (size_t)p.rank * grid + blockIdx.x, rec);
-            push_count(p, 2);
-            wait_mbox(p, 2, p.ctr_base[2] + (unsigned long long)(step + 1) * p.tp * grid, sh);
-          } else {
-            st_relaxed_u64(p.t_argmax + blockIdx.x, rec);
-            stage_ready(p, kLM, sh);
+      if (tid == 0) {
+        uint32_t ck = 0, ci = 0xFFFFFFFFu;
+        for (int w = 0; w < kConsumerWarps; ++w)
+          if (argmax_better(sh.best_key[w], sh.best_idx[w], ck, ci)) {
+            ck = sh.best_key[w];
+            ci = sh.best_idx[w];
           }
+        const unsigned long long idx =
+            ci == 0xFFFFFFFFu ? 0x3FFFFull : (unsigned long long)(ci + p.vocab0);
+        const unsigned long long rec = ((unsigned long long)ck << 32) | (idx << 14) | rtag;
+        if (p.tp > 1) {
+          // vocab-parallel: the record goes to every rank's mailbox
+          const MailboxLayout mb = mailbox_layout(p.tp, p.hidden, grid);
+          for (int r = 0; r < p.tp; ++r)
+            st_sys_u64(p.peers[r] + mb.rec + (size_t)p.rank * grid + blockIdx.x, rec);
+        } else {
+          st_relaxed_u64(p.t_argmax + blockIdx.x, rec);
         }
-        __syncwarp();
-        // every CTA reduces all records (argmax order is total: any order)
+        stage_ready(p, kLM, sh);  // one L2 round trip of delay before the polls
+      }
+      consumers_sync();
+      // Every CTA reduces all records (argmax order is total: any order).
+      // Each consumer thread loads its records together (one poll round
+      // trip when they are there), the CTA then reduces in shared memory.
+      {
+        const uint64_t t_rec = (p.tp > 1 && tid == 0) ? pipe::global_ns() : 0;
         const unsigned long long* recs =
             p.tp > 1 ? p.mbox + mailbox_layout(p.tp, p.hidden, grid).rec : p.t_argmax;
         const int nrec = p.tp * (int)gridDim.x;
         uint32_t ck = 0, ci = 0xFFFFFFFFu;
-        for (int b = lane; b < nrec; b += 32) {
-          unsigned long long r = ld_sys_u64(recs + b);
-          PollClock clock;
-          while ((r & 0x3FFFull) != rtag && clock.keep_going(p, sh)) r = ld_sys_u64(recs + b);
-          const uint32_t k2 = (uint32_t)(r >> 32);
-          uint32_t i2 = (uint32_t)((r >> 14) & 0x3FFFFull);
-          if (i2 == 0x3FFFFu) i2 = 0xFFFFFFFFu;
-          if (argmax_better(k2, i2, ck, ci)) {
-            ck = k2;
-            ci = i2;
+        constexpr int kRecBatch = 4;
+        for (int b0 = tid; b0 < nrec; b0 += kRecBatch * kConsumers) {
+          unsigned long long r[kRecBatch];
+#pragma unroll
+          for (int i = 0; i < kRecBatch; ++i)
+            if (b0 + i * kConsumers < nrec) r[i] = ld_sys_u64(recs + b0 + i * kConsumers);
+#pragma unroll
+          for (int i = 0; i < kRecBatch; ++i) {
+            const int b = b0 + i * kConsumers;
+            if (b >= nrec) break;
+            PollClock clock;
+            while ((r[i] & 0x3FFFull) != rtag && clock.keep_going(p, sh)) r[i] = ld_sys_u64(recs + b);
+            const uint32_t k2 = (uint32_t)(r[i] >> 32);
+            uint32_t i2 = (uint32_t)((r[i] >> 14) & 0x3FFFFull);
+            if (i2 == 0x3FFFFu) i2 = 0xFFFFFFFFu;
+            if (argmax_better(k2, i2, ck, ci)) {
+              ck = k2;
+              ci = i2;
+            }
           }
         }
 #pragma unroll
@@ -1597,10 +1662,23 @@ __global__ void __launch_bounds__(kThreads, 1) decode_loop_kernel(DecodeLoop par
             ci = oi;
           }
         }
+        consumers_sync();  // the CTA-best slots are free again
         if (lane == 0) {
-          sh.token = ci;
-          if (blockIdx.x == 0) p.toks[pos + 1] = ci;
+          sh.best_key[warp] = ck;
+          sh.best_idx[warp] = ci;
+        }
+        consumers_sync();
+        if (tid == 0) {
+          uint32_t gk = 0, gi = 0xFFFFFFFFu;
+          for (int w = 0; w < kConsumerWarps; ++w)
+            if (argmax_better(sh.best_key[w], sh.best_idx[w], gk, gi)) {
+              gk = sh.best_key[w];
+              gi = sh.best_idx[w];
+            }
+          sh.token = gi;
+          if (blockIdx.x == 0) p.toks[pos + 1] = gi;
           sh.stop = sh.abort ? 1 : 0;
+          if (p.tp > 1) sh.mbox_ns += pipe::global_ns() - t_rec;
         }
       }
       consumers_sync();

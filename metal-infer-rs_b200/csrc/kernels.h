@@ -278,30 +278,27 @@ struct DecodeLoop {
   // Tensor parallelism (tp > 1): the shapes above are this rank's shard.
   // The row-parallel O and down products leave the kernel as FP32 partials
   // stored straight into every rank's mailbox over NVLink (u64 words: 32-bit
-  // epoch tag << 32 | float bits), and every CTA counts itself into each
-  // rank's stage counter; readers sum the ranks' partials in rank order.
+  // epoch tag << 32 | float bits); readers poll their own mailbox until every
+  // word carries the tag it wants and sum the ranks' partials in rank order.
   int tp = 1, rank = 0;
   uint32_t vocab0 = 0;                        // global id of this rank's first LM-head row
   uint32_t vocab_full = 0;                    // rows of the (replicated) embedding
   unsigned long long* const* peers = nullptr; // [tp] device pointers to each rank's mailbox
   unsigned long long* mbox = nullptr;         // this rank's mailbox (peers[rank])
-  unsigned long long ctr_base[3] = {0, 0, 0}; // mailbox counts (O, DOWN, LM) before this launch
   // plan (decode_loop_plan)
   int slot_bytes = 0, slots = 0, x_bytes = 0, grid = 0;
 };
 // Mailbox layout in u64 words for `tp` ranks, hidden size h and grid CTAs:
-// [tp][h] O partials, [tp][h] down partials, [tp][grid] argmax records,
-// then three counters on their own 128-byte lines.
+// [tp][h] O partials, [tp][h] down partials, [tp][grid] argmax records.
 struct MailboxLayout {
-  size_t o, d, rec, ctr, words;
+  size_t o, d, rec, words;
 };
 __host__ __device__ inline MailboxLayout mailbox_layout(int tp, int h, int grid) {
   MailboxLayout m;
   m.o = 0;
   m.d = (size_t)tp * h;
   m.rec = m.d + (size_t)tp * h;
-  m.ctr = (m.rec + (size_t)tp * grid + 15) / 16 * 16;
-  m.words = m.ctr + 3 * 16;
+  m.words = m.rec + (size_t)tp * grid;
   return m;
 }
 // Fills the plan fields for `device`; false when the model shape or the

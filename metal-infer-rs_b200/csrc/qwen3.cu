@@ -132,7 +132,6 @@ struct mi_qwen3 {
     std::vector<void*> peer;
     TensorRef table;  // device array of the tp mailbox pointers
     int grid = 0;
-    unsigned long long ctr_base[3] = {0, 0, 0};
   } mbox;
   bool persistent = true;  // decode through the persistent kernel when it fits
   bool sampling = false;   // LM heads draw tokens (generate_with, temperature > 0)
@@ -676,15 +675,10 @@ void run_decode_loop(mi_qwen3* m, mi_kv_cache* c, size_t steps) {
   for (size_t done = 0; done < steps;) {
     p.steps = (int)std::min<size_t>(steps - done, 2048);
     p.epoch0 = (uint32_t)w.loop_epoch;
-    for (int i = 0; i < 3; ++i) p.ctr_base[i] = m->mbox.ctr_base[i];
     ProfileScope ps(ctx, "decode_loop");
     k::decode_loop(ctx->stream, p);
     m->last_loop_steps = p.steps;
     w.loop_epoch += (uint64_t)p.steps * (uint64_t)p.layers;
-    const unsigned long long per_step = (unsigned long long)m->tp * p.grid;
-    m->mbox.ctr_base[0] += per_step * p.steps * p.layers;
-    m->mbox.ctr_base[1] += per_step * p.steps * p.layers;
-    m->mbox.ctr_base[2] += per_step * p.steps;
     done += (size_t)p.steps;
   }
 }
