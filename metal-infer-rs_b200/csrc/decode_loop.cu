@@ -423,9 +423,6 @@ __device__ __forceinline__ unsigned long long ld_sys_u64(const unsigned long lon
   asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
-__device__ __forceinline__ void red_sys_add_u64(unsigned long long* p, unsigned long long v) {
-  asm volatile("red.relaxed.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
 
 // This rank's FP32 partial of row `item` into region `region` of every rank.
 __device__ __forceinline__ void push_partial(const DecodeLoop& p, size_t region, int item,
@@ -1573,7 +1570,6 @@ __global__ void __launch_bounds__(kThreads, 1) decode_loop_kernel(DecodeLoop par
       in.x = p.t_hidden;
       in.xtag = tagv(e, 1);
       in.norm_w = p.final_norm;
-      const uint32_t ls_last = (uint32_t)(step * p.layers + p.layers - 1);
       if (p.tp > 1) {
         in.mode = kAddThenNormIn;
         in.x = p.t_res;
