@@ -86,6 +86,7 @@ struct DecodeArgs {
   __half* out;            // [qh, 128]
   float* scratch;         // [kvh, gridDim.x, G, 130]
   uint32_t* counters;     // [kvh], zero on entry and exit
+  int early;              // the first K/V tile is staged before the dependency wait
   // fused front end
   int fused;
   const __half* k_raw;
@@ -169,10 +170,14 @@ __global__ void __launch_bounds__(kDecodeThreads) attention_decode_kernel(Decode
   const int begin = b * a.block;
   const int end = min(L, begin + a.block);
   const int ntiles = b < nb ? (end - begin + kTile - 1) / kTile : 0;
-  if (ntiles > 0)
+  // The cached rows (all but the new one, which this kernel appends) are
+  // staged before the dependency wait when no predecessor writes them.
+  if (ntiles > 0 && a.early)
     stage_tile(a, g_kv, begin, min(end, begin + kTile), pos, sm.tile[0].k, sm.tile[0].v);
   pdl_trigger();
   pdl_wait();
+  if (ntiles > 0 && !a.early)
+    stage_tile(a, g_kv, begin, min(end, begin + kTile), pos, sm.tile[0].k, sm.tile[0].v);
   if (b >= nb) return;
 
   // Queries of this group (and, fused, the new key / value).
@@ -509,7 +514,9 @@ void launch_decode_g(const Launch& l, const DecodeArgs& a, int blocks) {
   launch_kernel(l, dim3(blocks, a.kvh), dim3(kDecodeThreads), smem, kernel, a);
 }
 
-void launch_decode(const Launch& l, const DecodeArgs& a, int blocks) {
+void launch_decode(const Launch& l, const DecodeArgs& args, int blocks) {
+  DecodeArgs a = args;
+  a.early = l.early ? 1 : 0;
   switch (a.qh / a.kvh) {
     case 1: launch_decode_g<1>(l, a, blocks); break;
     case 2: launch_decode_g<2>(l, a, blocks); break;

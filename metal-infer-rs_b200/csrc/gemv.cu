@@ -40,6 +40,7 @@ struct Plan {
   int stages;   // ring depth (1 .. kMaxStages)
   int x_bytes;  // shared bytes of the input row
   int stage_bytes;
+  int early;    // the weight stream starts before the dependency wait
 };
 
 __device__ __forceinline__ int items_of(const GemvProblem& p, int out_mode) {
@@ -192,15 +193,20 @@ __global__ void __launch_bounds__(kThreads) gemv_staged_kernel(GemvProblem p, Pl
   const int nchunks = first < last ? (last - first + plan.rps - 1) / plan.rps : 0;
   const uint32_t row_bytes = (uint32_t)p.k * 2u;
 
-  // Predecessor-independent: start the weight stream.
+  // The weight stream starts before the dependency wait when no predecessor
+  // can write the weights (the model's launches), else right after it.
   if (tid == 0) {
     for (int s = 0; s < plan.stages; ++s) pipe::mbar_init(&full[s], 1);
     pipe::fence_mbar_init();
-    for (int c = 0; c < plan.stages && c < nchunks; ++c)
-      issue_stage<OUT>(p, plan, stages, full, first, last, c);
+    if (plan.early)
+      for (int c = 0; c < plan.stages && c < nchunks; ++c)
+        issue_stage<OUT>(p, plan, stages, full, first, last, c);
   }
   pdl_trigger();
   pdl_wait();
+  if (!plan.early && tid == 0)
+    for (int c = 0; c < plan.stages && c < nchunks; ++c)
+      issue_stage<OUT>(p, plan, stages, full, first, last, c);
   build_input<IN>(p, xs, &s_scale);
 
   uint32_t best_key = 0, best_idx = 0xFFFFFFFFu;
@@ -377,6 +383,7 @@ __global__ void matmul_reference_kernel(const __half* x, const __half* w, __half
 
 Plan make_plan(const GemvProblem& p, int items, int grid, bool pair) {
   Plan pl;
+  pl.early = 1;
   pl.rpc = (items + grid - 1) / grid;
   pl.x_bytes = ((p.k * 2) + 127) / 128 * 128;
   int item_bytes = p.k * 2 * (pair ? 2 : 1);
@@ -405,6 +412,7 @@ void launch_staged(const Launch& l, const GemvProblem& p) {
   int grid = items < l.sm_count ? items : l.sm_count;
   if (items >= 64 * l.sm_count) grid = kLargeCtasPerSm * l.sm_count;
   Plan plan = make_plan(p, items, grid, OUT == kOutSwiglu);
+  plan.early = l.early ? 1 : 0;
   grid = (items + plan.rpc - 1) / plan.rpc;
   size_t smem = (size_t)plan.x_bytes + (size_t)plan.stages * plan.stage_bytes;
   auto kernel = gemv_staged_kernel<IN, OUT>;

@@ -17,6 +17,10 @@ namespace k {
 struct Launch {
   cudaStream_t stream;
   bool pdl = false;
+  // Kernels may read operands no predecessor writes (weights, cached K/V
+  // rows) before their dependency wait. True inside the model's launches;
+  // the op API, whose operands may be any earlier op's outputs, clears it.
+  bool early = true;
   int sm_count = 148;
 };
 

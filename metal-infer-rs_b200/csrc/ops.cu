@@ -12,10 +12,14 @@ using namespace mi;
 
 namespace {
 
+// Op launches use programmatic dependent launch (each kernel waits for its
+// predecessor before it reads any operand, so back-to-back ops overlap only
+// their launch latency), unless per-kernel profiling puts events between them.
 k::Launch launch_of(mi_context* ctx) {
   k::Launch l;
   l.stream = ctx->stream;
-  l.pdl = false;
+  l.pdl = !ctx->profiling;
+  l.early = false;
   l.sm_count = ctx->sm_count;
   return l;
 }
