@@ -75,17 +75,31 @@ __global__ void __launch_bounds__(256) gemm_canon_kernel(const __half* x, const 
 
 // Staged canonical kernel (K >= 256, so every dot spans all 32 lanes): the
 // CTA's 16 x rows and 32 w rows are staged 256 elements (one chunk per lane)
-// at a time in shared memory by double-buffered 16-byte cp.async; the warp
-// tiles and each lane's FMA chains are those of gemm_canon_kernel. The final
-// butterflies of the 64 dots run as a transpose-reduce: at each level a lane
-// keeps half of its dots and adds its partner's copies (the same operand
+// at a time in shared memory by a three-stage 16-byte cp.async pipeline; the
+// warp tiles and each lane's FMA chains are those of gemm_canon_kernel. The
+// final butterflies of the 64 dots run as a transpose-reduce: at each level a
+// lane keeps half of its dots and adds its partner's copies (the same operand
 // pairs as the butterfly), so each lane ends with two finished dots and the
-// warp issues 62 shuffles instead of 320.
-constexpr int kSM = 16, kSN = 32, kSK = 256;
+// warp issues 62 shuffles instead of 320. Up to three weight matrices that
+// share the input (Q / K / V, gate / up) run as one launch: the grid's
+// columns walk their rows back to back, each 32-row tile inside one of them.
+constexpr int kSM = 16, kSN = 32, kSK = 256, kStages = 3;
 
 struct CanonSmem {
-  __half x[2][kSM][kSK];
-  __half w[2][kSN][kSK];
+  __half x[kStages][kSM][kSK];
+  __half w[kStages][kSN][kSK];
+};
+
+struct CanonSeg {
+  const __half* w = nullptr;
+  __half* out = nullptr;
+  float* outf = nullptr;  // FP32 output instead of FP16 (tensor-parallel partials)
+  int n = 0;              // rows of w (a multiple of kSN unless it is the only one)
+  int ldo = 0;
+};
+struct CanonSegs {
+  CanonSeg s[3];
+  int count = 0;
 };
 
 __device__ __forceinline__ void canon_stage(const __half* x, const __half* w, int m, int n, int k,
@@ -109,25 +123,40 @@ __device__ __forceinline__ void canon_stage(const __half* x, const __half* w, in
   asm volatile("cp.async.commit_group;" ::: "memory");
 }
 
-__global__ void __launch_bounds__(256) gemm_canon_staged_kernel(const __half* x, const __half* w,
-                                                                __half* out, int m, int n, int k,
-                                                                int ldo, float* outf) {
+__global__ void __launch_bounds__(256) gemm_canon_staged_kernel(const __half* x, int m, int k,
+                                                                CanonSegs segs) {
   extern __shared__ __align__(16) uint8_t canon_smem[];
   CanonSmem& sm = *reinterpret_cast<CanonSmem*>(canon_smem);
   pdl_wait();
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
-  const int m0 = blockIdx.y * kSM, n0 = blockIdx.x * kSN;
+  // this CTA's weight matrix and its 32-row tile there
+  int n0 = blockIdx.x * kSN;
+  CanonSeg seg = segs.s[0];
+  if (segs.count > 1 && n0 >= segs.s[0].n) {
+    n0 -= segs.s[0].n;
+    seg = segs.s[1];
+    if (segs.count > 2 && n0 >= segs.s[1].n) {
+      n0 -= segs.s[1].n;
+      seg = segs.s[2];
+    }
+  }
+  const __half* w = seg.w;
+  const int n = seg.n;
+  const int m0 = blockIdx.y * kSM;
   const int wm = (warp & 1) * 8, wn = (warp >> 1) * 8;
   const int steps = (k + kSK - 1) / kSK;
   float acc[64];
 #pragma unroll
   for (int a = 0; a < 64; ++a) acc[a] = 0.f;
   canon_stage(x, w, m, n, k, m0, n0, 0, sm, 0);
+  if (steps > 1) canon_stage(x, w, m, n, k, m0, n0, kSK, sm, 1);
   for (int st = 0; st < steps; ++st) {
-    const int buf = st & 1;
-    if (st + 1 < steps) {
-      canon_stage(x, w, m, n, k, m0, n0, (st + 1) * kSK, sm, buf ^ 1);
+    const int buf = st % kStages;
+    if (st + 2 < steps) {
+      canon_stage(x, w, m, n, k, m0, n0, (st + 2) * kSK, sm, (st + 2) % kStages);
+      asm volatile("cp.async.wait_group 2;" ::: "memory");
+    } else if (st + 1 < steps) {
       asm volatile("cp.async.wait_group 1;" ::: "memory");
     } else {
       asm volatile("cp.async.wait_group 0;" ::: "memory");
@@ -142,7 +171,7 @@ __global__ void __launch_bounds__(256) gemm_canon_staged_kernel(const __half* x,
 #pragma unroll
       for (int i = 0; i < 8; ++i) acc[i * 8 + j] = chunk_dot(xv[i], wv, acc[i * 8 + j]);
     }
-    __syncthreads();  // the buffer is staged again two steps on
+    __syncthreads();  // this buffer is staged again at the next step
   }
   // Transpose-reduce: dot d = i * 8 + j; at the level of lane bit b (16, 8,
   // 4, 2, 1) a lane keeps the half of its dots whose matching index bit
@@ -163,9 +192,9 @@ __global__ void __launch_bounds__(256) gemm_canon_staged_kernel(const __half* x,
     const int d = 2 * lane + s2;
     const int i = d >> 3, j = d & 7;
     if (m0 + wm + i < m && n0 + wn + j < n) {
-      const size_t o2 = (size_t)(m0 + wm + i) * ldo + n0 + wn + j;
-      if (outf) outf[o2] = acc[s2];
-      else out[o2] = __float2half_rn(acc[s2]);
+      const size_t o2 = (size_t)(m0 + wm + i) * seg.ldo + n0 + wn + j;
+      if (seg.outf) seg.outf[o2] = acc[s2];
+      else seg.out[o2] = __float2half_rn(acc[s2]);
     }
   }
 }
@@ -221,18 +250,51 @@ __global__ void __launch_bounds__(256) gemm_simt_kernel(const __half* x, const _
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
-// The canonical GEMM: the staged kernel when every dot spans 32 lanes
-// (K >= 256), else the direct one; FP16 `out` or FP32 `outf`.
-void launch_canon(const Launch& l, const __half* x, const __half* w, __half* out, int m, int n,
-                  int k, int ldo, float* outf) {
-  dim3 grid((n + 31) / 32, (m + 15) / 16);
+// The canonical GEMM over one to three weight matrices sharing x: the staged
+// kernel when every dot spans 32 lanes (K >= 256; matrices whose rows are
+// not a multiple of its 32-row tile run as launches of their own), else the
+// direct one.
+void launch_canon(const Launch& l, const __half* x, int m, int k, const CanonSegs& segs) {
   if (k >= kSK) {
     auto kernel = gemm_canon_staged_kernel;
     allow_dynamic_smem(kernel, sizeof(CanonSmem));
-    launch_kernel(l, grid, dim3(256), sizeof(CanonSmem), kernel, x, w, out, m, n, k, ldo, outf);
-  } else {
-    launch_kernel(l, grid, dim3(256), 0, gemm_canon_kernel, x, w, out, m, n, k, ldo, outf);
+    bool tiled = true;
+    int n_total = 0;
+    for (int i = 0; i < segs.count; ++i) {
+      tiled &= segs.s[i].n % kSN == 0;
+      n_total += segs.s[i].n;
+    }
+    if (segs.count == 1 || tiled) {
+      dim3 grid((n_total + kSN - 1) / kSN, (m + kSM - 1) / kSM);
+      launch_kernel(l, grid, dim3(256), sizeof(CanonSmem), kernel, x, m, k, segs);
+      return;
+    }
+    for (int i = 0; i < segs.count; ++i) {
+      CanonSegs one;
+      one.s[0] = segs.s[i];
+      one.count = 1;
+      dim3 grid((segs.s[i].n + kSN - 1) / kSN, (m + kSM - 1) / kSM);
+      launch_kernel(l, grid, dim3(256), sizeof(CanonSmem), kernel, x, m, k, one);
+    }
+    return;
   }
+  for (int i = 0; i < segs.count; ++i) {
+    const CanonSeg& g = segs.s[i];
+    dim3 grid((g.n + 31) / 32, (m + 15) / 16);
+    launch_kernel(l, grid, dim3(256), 0, gemm_canon_kernel, x, g.w, g.out, m, g.n, k, g.ldo,
+                  g.outf);
+  }
+}
+
+CanonSegs one_seg(const __half* w, __half* out, float* outf, int n, int ldo) {
+  CanonSegs s;
+  s.s[0].w = w;
+  s.s[0].out = out;
+  s.s[0].outf = outf;
+  s.s[0].n = n;
+  s.s[0].ldo = ldo;
+  s.count = 1;
+  return s;
 }
 
 }  // namespace
@@ -245,7 +307,7 @@ void gemm(const Launch& l, const __half* x, const __half* w, __half* out, int m,
   if (m <= 0 || n <= 0) return;
   const bool vec = k % 8 == 0 && aligned16(x) && aligned16(w);
   if (vec && m <= kCanonRows) {
-    launch_canon(l, x, w, out, m, n, k, ldo, nullptr);
+    launch_canon(l, x, m, k, one_seg(w, out, nullptr, n, ldo));
     return;
   }
   if (gemm_tc(l, x, w, out, m, n, k, ldo)) return;
@@ -258,7 +320,27 @@ void gemm_partial_f32(const Launch& l, const __half* x, const __half* w, float* 
   if (m <= 0 || n <= 0) return;
   MI_REQUIRE(k % 8 == 0 && aligned16(x) && aligned16(w), MI_ERR_SHAPE,
              "tensor-parallel partial products need K %% 8 == 0 and 16-byte aligned operands");
-  launch_canon(l, x, w, nullptr, m, n, k, n, out);
+  launch_canon(l, x, m, k, one_seg(w, nullptr, out, n, n));
+}
+
+void gemm_multi(const Launch& l, const __half* x, int m, int k, int count,
+                const __half* const* w, __half* const* out, const int* n) {
+  if (m <= 0 || count <= 0) return;
+  bool vec = k % 8 == 0 && aligned16(x);
+  for (int i = 0; i < count; ++i) vec &= aligned16(w[i]);
+  if (vec && m <= kCanonRows && count <= 3) {
+    CanonSegs segs;
+    for (int i = 0; i < count; ++i) {
+      segs.s[i].w = w[i];
+      segs.s[i].out = out[i];
+      segs.s[i].n = n[i];
+      segs.s[i].ldo = n[i];
+    }
+    segs.count = count;
+    launch_canon(l, x, m, k, segs);
+    return;
+  }
+  for (int i = 0; i < count; ++i) gemm(l, x, w[i], out[i], m, n[i], k, n[i]);
 }
 
 }  // namespace k

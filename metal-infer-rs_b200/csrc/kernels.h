@@ -114,6 +114,10 @@ void matmul_reference(const Launch& l, const __half* x, const __half* w, __half*
 // Prefill GEMM (M > 1): out[m, n] = x[m, :] . w[n, :], FP32 accumulate.
 void gemm(const Launch& l, const __half* x, const __half* w, __half* out, int m, int n, int k,
           int ldo);
+// The same over `count` weight matrices that share x (Q / K / V, gate / up):
+// out[i][m, n] = x[m, :] . w[i][n, :], one launch for the canonical path.
+void gemm_multi(const Launch& l, const __half* x, int m, int k, int count,
+                const __half* const* w, __half* const* out, const int* n);
 // Tensor-parallel partial product: out[m, n] = DOT(x[m], w[n]) in FP32 with
 // the canonical reduction (any m), unrounded.
 void gemm_partial_f32(const Launch& l, const __half* x, const __half* w, float* out, int m, int n,

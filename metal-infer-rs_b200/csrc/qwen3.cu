@@ -222,6 +222,15 @@ k::Launch dlaunch(mi_qwen3* m, bool pdl) {
   return launch(m, pdl && !m->ctx->profiling && pdl_enabled() && m->tp == 1);
 }
 
+// Prefill launches: PDL on one GPU unless profiling (every kernel waits for
+// its predecessor before it reads an operand; nothing is read early, as the
+// prefill's decode-attention path reads K / V rows its predecessor appends).
+k::Launch plaunch(mi_qwen3* m) {
+  k::Launch l = launch(m, !m->ctx->profiling && pdl_enabled() && m->tp == 1);
+  l.early = false;
+  return l;
+}
+
 size_t qwidth(const mi_qwen3_config& c) { return c.num_attention_heads * c.head_dim; }
 size_t kvwidth(const mi_qwen3_config& c) { return c.num_key_value_heads * c.head_dim; }
 
@@ -779,7 +788,7 @@ void layer_prefill(mi_qwen3* m, mi_kv_cache* c, size_t li, __half* hidden, size_
                    Scratch& s) {
   const auto& cfg = m->cfg;
   const Layer& L = m->layers[li];
-  k::Launch l = launch(m, false);
+  k::Launch l = plaunch(m);
   const int h = (int)cfg.hidden_size, I = (int)cfg.intermediate_size;
   const int qw = (int)qwidth(cfg), kw = (int)kvwidth(cfg);
   const int t = (int)T;
@@ -789,9 +798,12 @@ void layer_prefill(mi_qwen3* m, mi_kv_cache* c, size_t li, __half* hidden, size_
   __half* kk = s.f16({T, (size_t)kw});
   __half* v = s.f16({T, (size_t)kw});
   k::rms_norm(l, hidden, L.w[kInputNorm].h(), normalized, t, h, eps);
-  k::gemm(l, normalized, L.w[kQ].h(), q, t, qw, h, qw);
-  k::gemm(l, normalized, L.w[kK].h(), kk, t, kw, h, kw);
-  k::gemm(l, normalized, L.w[kV].h(), v, t, kw, h, kw);
+  {
+    const __half* w3[3] = {L.w[kQ].h(), L.w[kK].h(), L.w[kV].h()};
+    __half* o3[3] = {q, kk, v};
+    const int n3[3] = {qw, kw, kw};
+    k::gemm_multi(l, normalized, t, h, 3, w3, o3, n3);
+  }
   __half* query = s.f16({T, (size_t)qw});
   k::Pos pos;
   pos.base = (uint32_t)off;
@@ -838,8 +850,12 @@ void layer_prefill(mi_qwen3* m, mi_kv_cache* c, size_t li, __half* hidden, size_
   }
   __half* gate = s.f16({T, (size_t)I});
   __half* up = s.f16({T, (size_t)I});
-  k::gemm(l, normalized, L.w[kGate].h(), gate, t, I, h, I);
-  k::gemm(l, normalized, L.w[kUp].h(), up, t, I, h, I);
+  {
+    const __half* w2[2] = {L.w[kGate].h(), L.w[kUp].h()};
+    __half* o2[2] = {gate, up};
+    const int n2[2] = {I, I};
+    k::gemm_multi(l, normalized, t, h, 2, w2, o2, n2);
+  }
   __half* act = s.f16({T, (size_t)I});
   k::swiglu(l, gate, up, act, T * I);
   __half* down = s.f16({T, (size_t)h});
@@ -871,7 +887,7 @@ void forward_tokens(mi_qwen3* m, mi_kv_cache* c, size_t T) {
     return;
   }
   Scratch s(m->ctx);
-  k::Launch l = launch(m, false);
+  k::Launch l = plaunch(m);
   const int h = (int)cfg.hidden_size;
   __half* hidden = s.f16({T, (size_t)h});
   k::embedding(l, c->toks.t->u32() + off, m->embedding.h(), hidden, (int)T, h, vocab_full(m));
