@@ -102,22 +102,46 @@ struct CanonSegs {
   int count = 0;
 };
 
-__device__ __forceinline__ void canon_stage(const __half* x, const __half* w, int m, int n, int k,
-                                            int m0, int n0, int k0, CanonSmem& sm, int buf) {
-  for (int i = threadIdx.x; i < (kSM + kSN) * (kSK / 8); i += 256) {
-    const int r = i / (kSK / 8), c = i % (kSK / 8);
-    const int kk = k0 + 8 * c;
+// One thread's six 16-byte copies of a stage: column chunk c = lane of rows
+// r = warp + 8 j (j < 2: x rows, j >= 2: w rows), addresses computed once;
+// a stage at k0 adds k0 to the sources and the buffer offset to the
+// destinations.
+struct CanonCopies {
+  static constexpr int kPer = (kSM + kSN) * (kSK / 8) / 256;
+  const __half* src[kPer];  // null: outside the matrix (the chunk is zeroed)
+  uint32_t dst[kPer];       // shared address in buffer 0
+};
+static_assert((kSM + kSN) * (kSK / 8) % 256 == 0 && kSK / 8 == 32, "stage copy layout");
+
+__device__ __forceinline__ CanonCopies canon_copies(const __half* x, const __half* w, int m,
+                                                    int n, int k, int m0, int n0,
+                                                    CanonSmem& sm) {
+  CanonCopies cp;
+  const int c = threadIdx.x & 31, r0 = threadIdx.x >> 5;
+#pragma unroll
+  for (int j = 0; j < CanonCopies::kPer; ++j) {
+    const int r = r0 + 8 * j;
     const bool is_x = r < kSM;
     const int row = is_x ? m0 + r : n0 + (r - kSM);
-    __half* dst = is_x ? &sm.x[buf][r][8 * c] : &sm.w[buf][r - kSM][8 * c];
-    if ((is_x ? row < m : row < n) && kk < k) {
-      const __half* src = (is_x ? x : w) + (size_t)row * k + kk;
-      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
-                       static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
-                   "l"(src)
+    __half* dst = is_x ? &sm.x[0][r][8 * c] : &sm.w[0][r - kSM][8 * c];
+    cp.dst[j] = static_cast<uint32_t>(__cvta_generic_to_shared(dst));
+    cp.src[j] = (is_x ? row < m : row < n) ? (is_x ? x : w) + (size_t)row * k + 8 * c : nullptr;
+  }
+  return cp;
+}
+
+__device__ __forceinline__ void canon_stage(const CanonCopies& cp, int k, int k0, int buf) {
+  const bool in_k = k0 + 8 * (int)(threadIdx.x & 31) < k;
+  const uint32_t off = (uint32_t)buf * (uint32_t)(kSM * kSK * 2);
+  const uint32_t offw = (uint32_t)buf * (uint32_t)(kSN * kSK * 2);
+#pragma unroll
+  for (int j = 0; j < CanonCopies::kPer; ++j) {
+    const uint32_t dst = cp.dst[j] + (j < kSM / 8 ? off : offw);
+    if (cp.src[j] && in_k) {
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(cp.src[j] + k0)
                    : "memory");
     } else {
-      *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);  // adds exact zeros
+      asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(dst), "r"(0u) : "memory");
     }
   }
   asm volatile("cp.async.commit_group;" ::: "memory");
@@ -149,12 +173,13 @@ __global__ void __launch_bounds__(256) gemm_canon_staged_kernel(const __half* x,
   float acc[64];
 #pragma unroll
   for (int a = 0; a < 64; ++a) acc[a] = 0.f;
-  canon_stage(x, w, m, n, k, m0, n0, 0, sm, 0);
-  if (steps > 1) canon_stage(x, w, m, n, k, m0, n0, kSK, sm, 1);
+  const CanonCopies cps = canon_copies(x, w, m, n, k, m0, n0, sm);
+  canon_stage(cps, k, 0, 0);
+  if (steps > 1) canon_stage(cps, k, kSK, 1);
   for (int st = 0; st < steps; ++st) {
     const int buf = st % kStages;
     if (st + 2 < steps) {
-      canon_stage(x, w, m, n, k, m0, n0, (st + 2) * kSK, sm, (st + 2) % kStages);
+      canon_stage(cps, k, (st + 2) * kSK, (st + 2) % kStages);
       asm volatile("cp.async.wait_group 2;" ::: "memory");
     } else if (st + 1 < steps) {
       asm volatile("cp.async.wait_group 1;" ::: "memory");
@@ -299,8 +324,9 @@ CanonSegs one_seg(const __half* w, __half* out, float* outf, int n, int ldo) {
 
 }  // namespace
 
+// FP16 `out`, or FP32 `outf` when it is non-null.
 bool gemm_tc(const Launch& l, const __half* x, const __half* w, __half* out, int m, int n, int k,
-             int ldo);
+             int ldo, float* outf = nullptr);
 
 void gemm(const Launch& l, const __half* x, const __half* w, __half* out, int m, int n, int k,
           int ldo) {
@@ -320,6 +346,8 @@ void gemm_partial_f32(const Launch& l, const __half* x, const __half* w, float* 
   if (m <= 0 || n <= 0) return;
   MI_REQUIRE(k % 8 == 0 && aligned16(x) && aligned16(w), MI_ERR_SHAPE,
              "tensor-parallel partial products need K %% 8 == 0 and 16-byte aligned operands");
+  // long prompts: the tensor-core GEMM (the per-op tolerance, as without TP)
+  if (m > kCanonRows && gemm_tc(l, x, w, nullptr, m, n, k, n, out)) return;
   launch_canon(l, x, m, k, one_seg(w, nullptr, out, n, n));
 }
 

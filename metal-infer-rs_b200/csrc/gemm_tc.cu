@@ -126,11 +126,27 @@ struct Smem {
   static constexpr int kBytes = 1024 /*align*/ + kStages * kStageBytes + 256;
 };
 
+// Epilogue of FP32 outputs (tensor-parallel partials): 32 accumulator
+// columns of one row, `left` of them inside the matrix.
+__device__ __forceinline__ void store_f32_row(float* dst, const uint32_t (&r)[32], int left) {
+  if (left >= 32 && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
+#pragma unroll
+    for (int q = 0; q < 8; ++q)
+      reinterpret_cast<float4*>(dst)[q] =
+          make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]),
+                      __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3]));
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      if (i < left) dst[i] = __uint_as_float(r[i]);
+  }
+}
+
 template <int BN>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap map_x,
                    const __grid_constant__ CUtensorMap map_w, __half* out, int m, int n, int k,
-                   int ldo) {
+                   int ldo, float* outf) {
   using S = Smem<BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -228,7 +244,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             "=r"(r[31])
           : "r"(taddr));
       asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-      if (row < m) {
+      if (row < m && outf) {
+        store_f32_row(outf + (size_t)row * ldo + n0 + c, r, n - (n0 + c));
+      } else if (row < m) {
         int col = n0 + c;
         __half* dst = out + (size_t)row * ldo + col;
         if (col + 32 <= n && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
@@ -279,7 +297,7 @@ struct PSmem {
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_persistent_kernel(const __grid_constant__ CUtensorMap map_x,
                               const __grid_constant__ CUtensorMap map_w, __half* out, int m, int n,
-                              int k, int ldo) {
+                              int k, int ldo, float* outf) {
   using S = PSmem;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -398,7 +416,9 @@ __global__ void __launch_bounds__(kThreads, 1)
               "=r"(r[31])
             : "r"(taddr));
         asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-        if (row < m) {
+        if (row < m && outf) {
+          store_f32_row(outf + (size_t)row * ldo + n0 + c, r, n - (n0 + c));
+        } else if (row < m) {
           const int col = n0 + c;
           __half* dst = out + (size_t)row * ldo + col;
           if (col + 32 <= n && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
@@ -475,11 +495,12 @@ bool make_map(CUtensorMap* map, const __half* ptr, int rows, int cols, int box_r
 
 template <int BN>
 void launch_tc(const Launch& l, const CUtensorMap& mx, const CUtensorMap& mw, __half* out, int m,
-               int n, int k, int ldo) {
+               int n, int k, int ldo, float* outf) {
   auto kernel = gemm_tc_kernel<BN>;
   allow_dynamic_smem(kernel, Smem<BN>::kBytes);
   dim3 grid((n + BN - 1) / BN, (m + BM - 1) / BM);
-  launch_kernel(l, grid, dim3(kThreads), Smem<BN>::kBytes, kernel, mx, mw, out, m, n, k, ldo);
+  launch_kernel(l, grid, dim3(kThreads), Smem<BN>::kBytes, kernel, mx, mw, out, m, n, k, ldo,
+                outf);
 }
 
 bool enabled() {
@@ -519,7 +540,7 @@ bool make_kv_tile_map(void* map, const __half* cache, int capacity, int kv_heads
 }
 
 bool gemm_tc(const Launch& l, const __half* x, const __half* w, __half* out, int m, int n, int k,
-             int ldo) {
+             int ldo, float* outf) {
   if (!gemm_tc_available()) return false;
   if (m < 2 || k < 8 || (k & 7) || ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w)) & 15))
     return false;
@@ -532,16 +553,16 @@ bool gemm_tc(const Launch& l, const __half* x, const __half* w, __half* out, int
     allow_dynamic_smem(kernel, PSmem::kBytes);
     const int tiles = tiles_m * ((n + kPBN - 1) / kPBN);
     launch_kernel(l, dim3(std::min(tiles, l.sm_count)), dim3(kThreads), PSmem::kBytes, kernel, mx,
-                  mw, out, m, n, k, ldo);
+                  mw, out, m, n, k, ldo, outf);
     return true;
   }
   // Narrow tiles when the grid would not fill the GPU.
   int bn = (tiles_m * ((n + 127) / 128) >= l.sm_count) ? 128 : 64;
   if (!make_map(&mx, x, m, k, BM) || !make_map(&mw, w, n, k, bn)) return false;
   if (bn == 128)
-    launch_tc<128>(l, mx, mw, out, m, n, k, ldo);
+    launch_tc<128>(l, mx, mw, out, m, n, k, ldo, outf);
   else
-    launch_tc<64>(l, mx, mw, out, m, n, k, ldo);
+    launch_tc<64>(l, mx, mw, out, m, n, k, ldo, outf);
   return true;
 }
 

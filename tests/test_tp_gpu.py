@@ -34,7 +34,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _rank_main(rank, tp, port, cfg, prompt, long_prompt, steps, out, ckpt=None):
+def _rank_main(rank, tp, port, cfg, prompt, long_prompt, steps, out, ckpt=None, tc_prompt=None):
     import torch.distributed as dist
     dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
                             world_size=tp)
@@ -48,6 +48,10 @@ def _rank_main(rank, tp, port, cfg, prompt, long_prompt, steps, out, ckpt=None):
         # a prompt whose row-parallel results (tokens x hidden >= 65,536) are
         # reduced slice by slice (NCCL send / receive, then an FP16 all-gather)
         res["prefill_long"] = model.prefill(long_prompt, model.kv_cache(160)).f16_bits().ravel()
+        if tc_prompt is not None:
+            # more than 512 tokens: tensor-core projections, the row-parallel
+            # partials in FP32 from the tcgen05 GEMM, tensor-core attention
+            res["prefill_tc"] = model.prefill(tc_prompt, model.kv_cache(704)).f16_bits().ravel()
         res["decode"] = [model.decode(int(t), cache).f16_bits().ravel() for t in (7, 900)]
         res["persistent"] = model.decode_persistent()
         for path in ("persistent", "graph", "eager"):
@@ -80,6 +84,7 @@ def test_tp_matches_oracle_tp_arithmetic(tmp_path, tp):
     cfg = small_cfg()
     prompt = O.gen_tokens(11, INPUT_STREAM, 20, cfg["vocab_size"])
     long_prompt = O.gen_tokens(11, INPUT_STREAM + 1, 136, cfg["vocab_size"])
+    tc_prompt = O.gen_tokens(11, INPUT_STREAM + 2, 640, cfg["vocab_size"])
     steps = 16
     # a checkpoint of the full (one-GPU) model for the shard-on-load check
     import safetensors_io as st
@@ -91,7 +96,8 @@ def test_tp_matches_oracle_tp_arithmetic(tmp_path, tp):
     q = ctx.Queue()
     port = _free_port()
     procs = [ctx.Process(target=_rank_main,
-                         args=(r, tp, port, cfg, prompt, long_prompt, steps, q, str(tmp_path)))
+                         args=(r, tp, port, cfg, prompt, long_prompt, steps, q, str(tmp_path),
+                               tc_prompt))
              for r in range(tp)]
     for p in procs:
         p.start()
@@ -110,6 +116,9 @@ def test_tp_matches_oracle_tp_arithmetic(tmp_path, tp):
     ref_long = O.Qwen3(cfg, seed=11, capacity=160)
     ref_long.set_tp(tp)
     want_long = ref_long.forward(long_prompt)
+    ref_tc = O.Qwen3(cfg, seed=11, capacity=704)
+    ref_tc.set_tp(tp)
+    want_tc = O.f32(ref_tc.forward(tc_prompt))
     ref_ids = O.Qwen3(cfg, seed=11, capacity=128)
     ref_ids.set_tp(tp)
     want_ids = ref_ids.generate_greedy(prompt, steps)
@@ -120,6 +129,10 @@ def test_tp_matches_oracle_tp_arithmetic(tmp_path, tp):
         assert got["config"]["num_attention_heads"] == cfg["num_attention_heads"]
         np.testing.assert_array_equal(got["prefill"], want_prefill)
         np.testing.assert_array_equal(got["prefill_long"], want_long)
+        # tensor-core accumulation order: logits within 1e-2 relative
+        tc = O.f32(got["prefill_tc"])
+        tc_err = float(np.max(np.abs(tc - want_tc)) / np.max(np.abs(want_tc)))
+        assert tc_err <= 1e-2, f"rank {r}: >512-token prefill logits rel err {tc_err:.2e}"
         np.testing.assert_array_equal(got["loaded_prefill"], want_prefill)
         for a, b in zip(got["decode"], want_decode):
             np.testing.assert_array_equal(a, b)
