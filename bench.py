@@ -95,6 +95,49 @@ def tp_decode_bytes_per_token(c, tp, kv_len):
     return layers * (2 * mats / tp + 2 * norms) + 2 * V * h / tp + 2 * h + kv / tp
 
 
+def prefill_flops(c, T):
+    """FLOPs of a T-token prefill: every projection (2 per weight per token),
+    causal attention (QK^T and PV over the T(T+1)/2 visible pairs) and the LM
+    head of the last row."""
+    h, I, V = c["hidden_size"], c["intermediate_size"], c["vocab_size"]
+    qw = c["num_attention_heads"] * c["head_dim"]
+    kw = c["num_key_value_heads"] * c["head_dim"]
+    mats = (qw + 2 * kw) * h + h * qw + 2 * I * h + h * I
+    attn = 4 * qw * T * (T + 1) // 2
+    return c["num_hidden_layers"] * (2 * mats * T + attn) + 2 * V * h
+
+
+# The prefill's canonical-order projections run on the CUDA cores (FMAs in
+# the decode GEMVs' order, the token-exact path of prompts up to 512 tokens):
+# 148 SMs x 128 FP32 lanes x 2 FLOPs per FMA at the maximum SM clock.
+def ffma_peak_tflops(sm_mhz=1965.0):
+    return 148 * 128 * 2 * sm_mhz * 1e6 / 1e12
+
+
+def canon_gemm_probe(ctx, m=128, n=4096, k=1024, copies=16, reps=4):
+    """TFLOP/s of the canonical prefill GEMM on the 0.6B fused Q/K/V shape
+    (x[m, k] by w[n, k]) through the op API: `copies` weight copies (134 MB,
+    more than L2) launched back to back, `reps` times, device time."""
+    import metal_infer as mi
+    x = ctx.empty([m, k])
+    ctx.fill_normal_f16(x, 1, 4000, 1.0)
+    ws = []
+    for c in range(copies):
+        w = ctx.empty([n, k])
+        ctx.fill_normal_f16(w, 1, 4001 + c, 0.02)
+        ws.append(w)
+    b = ctx.begin_batch()
+    outs = [b.matmul(x, w) for w in ws]
+    b.finish()
+    del outs
+    b = ctx.begin_batch()
+    outs = [b.matmul(x, w) for _ in range(reps) for w in ws]
+    st = b.finish()
+    del outs, ws, x
+    t = st.gpu_time / (reps * copies)
+    return 2.0 * m * n * k / t / 1e12, t
+
+
 def gemv_bytes(n, k, segs=1):
     """One decode GEMV launch: `segs` weight matrices [n, k], the input row
     read once and `segs` output rows (FP16)."""
@@ -349,9 +392,10 @@ def run_ours(args, rank, world, local_rank):
         sweep = {r["op"]: {"kernel": r["kernel"], "us_per_launch": r["us_per_launch"],
                            "gb_s": r["gb_s"], "frac": r["frac"], "bytes": r["bytes"]}
                  for r in op_sweep_rows(ctx, 3, 1)}
+    gemm_probe = canon_gemm_probe(ctx) if world == 1 and not args.no_op_sweep else None
     tp_block = None if args.no_tp_report else tp_report(args, ctx, rank, world, dist)
     layer_launches = 5 * CONFIG["num_hidden_layers"] + 1
-    prefill_launches = 1 + 14 * CONFIG["num_hidden_layers"] + 2
+    prefill_launches = 1 + 11 * CONFIG["num_hidden_layers"] + 2
     decode_launches = 1 if persistent else DECODE * layer_launches
     launches = args.steps * (prefill_launches + decode_launches)
 
@@ -364,6 +408,8 @@ def run_ours(args, rank, world, local_rank):
             "data": "synthetic (random-init FP16 N(0,0.02) weights, uniform prompt ids)",
             "config": workload_config(world),
             "prefill_tokens_per_s": round(prefill_tps, 1),
+            "prefill_roofline": prefill_roofline(prefill_tps / world, gemm_probe,
+                                                 clocks.summary()),
             "decode_hbm": {"bytes_per_token": int(bytes_tok),
                            "achieved_gbs": round(bytes_tok * per_gpu_tps / 1e9, 1),
                            "peak_gbs": hbm, "frac": round(bytes_tok * per_gpu_tps / 1e9 / hbm, 4),
@@ -726,6 +772,24 @@ def run_op_sweep(args):
         "config": {"workload": "BASELINE config 1 decode-op sweep, rotated working sets "
                                f"> {ROTATE_BYTES >> 20} MB (inputs larger than L2)"},
         "peak": {"hbm_gbs": peak, "kind": peak_kind}, "ops": rows}), flush=True)
+
+
+def prefill_roofline(prefill_tps_per_gpu, gemm_probe, clocks):
+    """The prefill against the CUDA-core FMA peak (its projections are the
+    canonical-order GEMM), and the GEMM alone on the fused Q/K/V shape."""
+    peak = ffma_peak_tflops(clocks.get("sm_max_mhz") or 1965.0)
+    fl = prefill_flops(CONFIG, PROMPT)
+    achieved = fl * prefill_tps_per_gpu / PROMPT / 1e12
+    out = {"bound": "cuda-core fma (canonical-order projections)",
+           "flops_per_prompt": int(fl), "achieved_tflops": round(achieved, 2),
+           "peak_tflops": round(peak, 1), "frac": round(achieved / peak, 4),
+           "peak_source": "148 SMs x 128 lanes x 2 FLOPs x max SM clock",
+           "note": "whole prefill per GPU (norms, attention and launches included)"}
+    if gemm_probe is not None:
+        tf, t = gemm_probe
+        out["gemm_canon_128x4096x1024"] = {"tflops": round(tf, 2), "us": round(t * 1e6, 2),
+                                           "frac": round(tf / peak, 4)}
+    return out
 
 
 def op_sweep_rows(ctx, steps, warmup, only=None):

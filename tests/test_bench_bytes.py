@@ -74,3 +74,18 @@ def test_tp_bytes_per_rank():
     for tp in (2, 4, 8):
         per_rank = bench.tp_decode_bytes_per_token(c, tp, L)
         assert tp * per_rank == pytest.approx(one + (tp - 1) * norms, rel=1e-12)
+
+
+def test_prefill_flops_qwen3_0_6b():
+    # 28 layers x 2 x 15,728,640 weights x 128 tokens, causal attention over
+    # 8,256 visible (query, key) pairs per head, and the last row's LM head:
+    # about 0.115 TFLOP for config 2's prompt
+    c = bench.CONFIG
+    mats = 28 * (4096 * 1024 + 1024 * 2048 + 2 * 3072 * 1024 + 1024 * 3072)
+    want = 2 * mats * 128 + 28 * 4 * 2048 * (128 * 129 // 2) + 2 * 151936 * 1024
+    assert bench.prefill_flops(c, 128) == want
+    assert 0.114e12 < want < 0.116e12
+
+
+def test_ffma_peak():
+    assert abs(bench.ffma_peak_tflops(1965.0) - 74.45) < 0.01
