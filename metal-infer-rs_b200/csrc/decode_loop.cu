@@ -829,6 +829,58 @@ __device__ __forceinline__ uint4 normalize_chunk(const uint4& v, const uint4& g,
   return o;
 }
 
+// Tensor parallelism, the sliced exchange input: see build_input. `part` is
+// shared-memory scratch (the normalized-input buffer, free until the
+// normalization). Kept out of line so that the one-GPU input code keeps its
+// register allocation.
+__device__ __noinline__ void tp_slice_sum(const DecodeLoop& p, const StageIn& in, int kc,
+                                          float* part, Shared& sh) {
+  const int tid = threadIdx.x;
+  // Tensor parallelism, sliced: this CTA sums only its slice of the
+  // ranks' partials (one thread per (chunk, rank), every load in flight
+  // together, then the rank-order sum: the same additions as
+  // take_partials8) and publishes it as tagged FP16 in t_attn_o, which
+  // nothing else writes under tensor parallelism. Every CTA then stages
+  // the summed vector from there like a one-GPU input: a CTA reads its
+  // slice's tp partials and the hidden vector once, instead of tp copies
+  // of the vector.
+  const int c0 = (int)((long long)kc * blockIdx.x / gridDim.x);
+  const int c1 = (int)((long long)kc * (blockIdx.x + 1) / gridDim.x);
+  const int pairs = (c1 - c0) * p.tp;
+  for (int i = tid; i < pairs; i += kConsumers) {
+    const int c = c0 + i / p.tp, r = i - (i / p.tp) * p.tp;
+    const unsigned long long* q = p.mbox + (size_t)in.x2_part + (size_t)r * p.hidden + 8 * c;
+    unsigned long long w[8];
+    PollClock clock;
+    while (true) {
+      bool ok = true;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        w[e] = ld_sys_u64(q + e);
+        ok &= (uint32_t)(w[e] >> 32) == in.x2tag;
+      }
+      if (ok || !clock.keep_going(p, sh)) break;
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) part[8 * i + e] = __uint_as_float((uint32_t)w[e]);
+  }
+  consumers_sync();
+  for (int cc = tid; cc < c1 - c0; cc += kConsumers) {
+    float acc[8];
+    for (int r = 0; r < p.tp; ++r)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float v = part[8 * (cc * p.tp + r) + e];
+        acc[e] = r == 0 ? v : __fadd_rn(acc[e], v);
+      }
+    uint4 v;
+    __half2* hv = reinterpret_cast<__half2*>(&v);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) hv[i] = __floats2half2_rn(acc[2 * i], acc[2 * i + 1]);
+    put8(p.t_attn_o, c0 + cc, v, in.x2tag);
+  }
+}
+
 // Builds the stage input (k halves) with the prologue of the GEMV family
 // (gemv.cu build_input): the same roundings and the canonical sum of
 // squares. Every thread stages its chunks of the tagged vector(s) into xs
@@ -837,6 +889,7 @@ __device__ __forceinline__ uint4 normalize_chunk(const uint4& v, const uint4& g,
 // (false when the kernel is aborting); then, for the norm modes, every warp
 // computes the scale itself and the chunks are normalized into xn, followed
 // by a second barrier. Stages without a norm read xs directly.
+template <bool TP>
 __device__ bool build_input(const DecodeLoop& p, const StageIn& in, int wait_st, uint4* xs,
                             uint4* xs2, uint4* xn, Shared& sh) {
   const int tid = threadIdx.x;
@@ -856,7 +909,12 @@ __device__ bool build_input(const DecodeLoop& p, const StageIn& in, int wait_st,
   uint4 g_first = make_uint4(0, 0, 0, 0);
   if (norm && tid < kc) g_first = __ldg(g4 + tid);
   const bool wb = in.wb && blockIdx.x == 0;
-  if (two && in.x2_part >= 0) {
+  const uint32_t* x2 = in.x2;
+  if (TP && two && in.x2_part >= 0 && p.xslice) {
+    tp_slice_sum(p, in, kc, reinterpret_cast<float*>(xn), sh);
+    x2 = p.t_attn_o;
+  }
+  if (two && in.x2_part >= 0 && !(TP && p.xslice)) {
     for (int c = tid; c < kc; c += kConsumers) {
       const Raw8 ra = raw8(in.x, c);
       const uint4 b = take_partials8(p, (size_t)in.x2_part, c, in.x2tag, sh);
@@ -867,9 +925,9 @@ __device__ bool build_input(const DecodeLoop& p, const StageIn& in, int wait_st,
     }
   } else if (two) {
     for (int c = tid; c < kc; c += kConsumers) {
-      const Raw8 ra = raw8(in.x, c), rb = raw8(in.x2, c);
+      const Raw8 ra = raw8(in.x, c), rb = raw8(x2, c);
       const uint4 a = take8_from(p, ra, in.x, c, in.xtag, sh);
-      const uint4 b = take8_from(p, rb, in.x2, c, in.x2tag, sh);
+      const uint4 b = take8_from(p, rb, x2, c, in.x2tag, sh);
       xs[c] = a;
       xs2[c] = b;
       if (wb) put8(in.wb, c, add_chunk(in.mode, a, b), in.wbtag);
@@ -1359,7 +1417,9 @@ __host__ __device__ size_t layer_table_bytes(int layers) {
   return ((size_t)layers * sizeof(LoopLayer) + 127) / 128 * 128;
 }
 
-template <int G>
+// TP: the tensor-parallel instantiation (mailbox exchanges); the one-GPU one
+// carries none of that code.
+template <int G, bool TP>
 __global__ void __launch_bounds__(kThreads, 1) decode_loop_kernel(DecodeLoop params) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   __shared__ Shared sh;
@@ -1463,10 +1523,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_loop_kernel(DecodeLoop par
           in.x = p.t_hidden;
           in.xtag = hidden_in;
         }
-        if (!build_input(p, in, layer == 0 ? -1 : kDown, xs, xs2, xn, sh)) return;
+        if (!build_input<TP>(p, in, layer == 0 ? -1 : kDown, xs, xs2, xn, sh)) return;
 #ifdef MI_TRACE_TWICE
         if (tid == 0) g_trace_alt = 1;
-        if (!build_input(p, in, layer == 0 ? -1 : kDown, xs, xs2, xn, sh)) return;
+        if (!build_input<TP>(p, in, layer == 0 ? -1 : kDown, xs, xs2, xn, sh)) return;
         if (tid == 0) g_trace_alt = 0;
 #endif
         if (tid == 0) MI_TRACE(step, layer * 5 + 0, 1);
@@ -1520,10 +1580,10 @@ __global__ void __launch_bounds__(kThreads, 1) decode_loop_kernel(DecodeLoop par
         in.norm_w = L.post_norm;
         in.wb = p.t_res;
         in.wbtag = tagv(e, 0);
-        if (!build_input(p, in, kO, xs, xs2, xn, sh)) return;
+        if (!build_input<TP>(p, in, kO, xs, xs2, xn, sh)) return;
 #ifdef MI_TRACE_TWICE
         if (tid == 0) g_trace_alt = 1;
-        if (!build_input(p, in, kO, xs, xs2, xn, sh)) return;
+        if (!build_input<TP>(p, in, kO, xs, xs2, xn, sh)) return;
         if (tid == 0) g_trace_alt = 0;
 #endif
         if (tid == 0) MI_TRACE(step, layer * 5 + 3, 1);
@@ -1550,7 +1610,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_loop_kernel(DecodeLoop par
           in.res_n = td.last - td.first;
           in.res_tag = tagv(e, 0);
         }
-        if (!build_input(p, in, kGU, xs, xs2, xn, sh)) return;
+        if (!build_input<TP>(p, in, kGU, xs, xs2, xn, sh)) return;
         if (tid == 0) MI_TRACE(step, layer * 5 + 4, 1);
         reduce_rows<kDown>(p, s, xs, ring, sh, g, tagv(e, 1), bk, bi);
         stage_done(p, kDown);
@@ -1578,7 +1638,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_loop_kernel(DecodeLoop par
         in.x2tag = tagv(e, 1);
         in.exchange = 1;
       }
-      if (!build_input(p, in, kDown, xs, xs2, xn, sh)) return;
+      if (!build_input<TP>(p, in, kDown, xs, xs2, xn, sh)) return;
       if (tid == 0) MI_TRACE(step, p.layers * 5, 1);
       reduce_rows<kLM>(p, s, xn, ring, sh, g, 0u, bk, bi);
       if (tid == 0) MI_TRACE(step, p.layers * 5, 2);
@@ -1705,7 +1765,7 @@ size_t attn_smem_for(int group) {
 
 template <int G>
 cudaError_t launch_g(cudaStream_t stream, const DecodeLoop& p, int grid, size_t smem) {
-  auto kernel = decode_loop_kernel<G>;
+  auto kernel = p.tp > 1 ? decode_loop_kernel<G, true> : decode_loop_kernel<G, false>;
   cudaError_t err =
       cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (err != cudaSuccess) return err;

@@ -295,6 +295,7 @@ struct DecodeLoop {
   unsigned long long* mbox = nullptr;         // this rank's mailbox (peers[rank])
   // plan (decode_loop_plan)
   int slot_bytes = 0, slots = 0, x_bytes = 0, grid = 0;
+  int xslice = 1;  // tensor parallelism: each CTA sums a slice of the partials (else all)
 };
 // Mailbox layout in u64 words for `tp` ranks, hidden size h and grid CTAs:
 // [tp][h] O partials, [tp][h] down partials, [tp][grid] argmax records.

@@ -675,6 +675,11 @@ void run_decode_loop(mi_qwen3* m, mi_kv_cache* c, size_t steps) {
   p.attn_part = w.loop_part.t->f32();
   p.sync = w.loop_sync.t->u32();
   p.tp = m->tp;
+  {
+    // MI_TP_SLICE=0: every CTA sums all of the ranks' partials itself
+    const char* e = getenv("MI_TP_SLICE");
+    p.xslice = (e && *e == '0') ? 0 : 1;
+  }
   p.rank = m->rank;
   p.vocab0 = (uint32_t)(m->rank * m->cfg.vocab_size);
   if (m->tp > 1) {
