@@ -668,10 +668,69 @@ __device__ void issue_tile(const StageW& s, const Tiles& t, int tile, uint8_t* d
   }
 }
 
+// L2 prefetch of tile `tile` of stage weights s (the byte ranges issue_tile
+// copies): a hint with no completion, so HBM keeps streaming the weights
+// ahead of the ring while the ring is full.
+__device__ void prefetch_tile(const StageW& s, const Tiles& t, int tile) {
+  const int i0 = t.first + tile * t.per_tile;
+  const int cnt = min(t.per_tile, t.last - i0);
+  const uint32_t rb = t.row_bytes;
+  auto pf = [](const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+  };
+  if (s.pair) {
+    pf(s.w[0] + (size_t)i0 * s.k, cnt * rb);
+    pf(s.w[1] + (size_t)i0 * s.k, cnt * rb);
+    return;
+  }
+  int seg_start = 0, done = 0;
+  for (int seg = 0; seg < 3 && done < cnt; ++seg) {
+    const int seg_end = seg_start + s.n[seg];
+    const int a = max(i0 + done, seg_start), b = min(i0 + cnt, seg_end);
+    if (a < b) {
+      pf(s.w[seg] + (size_t)(a - seg_start) * s.k, (uint32_t)(b - a) * rb);
+      done += b - a;
+    }
+    seg_start = seg_end;
+  }
+}
+
+// A position in the producer's static schedule of weight tiles (every stage
+// of every layer of every step, then the LM head).
+struct TileCursor {
+  int step = 0, layer = 0, j = 0, tile = -1;
+  __device__ __forceinline__ static int stage_of(const DecodeLoop& p, int layer, int j) {
+    return layer < p.layers ? (j == 0 ? kQKV : j == 1 ? kO : j == 2 ? kGU : kDown) : kLM;
+  }
+  // Moves to the next tile; false past the end of the schedule.
+  __device__ bool next(const DecodeLoop& p, const Shared& sh) {
+    ++tile;
+    while (step < p.steps) {
+      if (tile < sh.tiles[stage_of(p, layer, j)].count) return true;
+      tile = 0;
+      if (++j >= (layer < p.layers ? 4 : 1)) {
+        j = 0;
+        if (++layer > p.layers) {
+          layer = 0;
+          ++step;
+        }
+      }
+    }
+    return false;
+  }
+};
+
 __device__ void produce(const DecodeLoop& p, const LoopLayer* layers, uint8_t* ring, Shared& sh) {
   const int S = p.slots;
   uint32_t g = 0;
   bool ok = true;
+  // The L2 prefetch cursor runs p.l2_ahead tiles ahead of the copies.
+  TileCursor pf;
+  bool pf_live = true;
+  for (int i = 0; i < p.l2_ahead && pf_live; ++i)
+    if ((pf_live = pf.next(p, sh)))
+      prefetch_tile(stage_weights(p, layers, pf.layer, TileCursor::stage_of(p, pf.layer, pf.j)),
+                    sh.tiles[TileCursor::stage_of(p, pf.layer, pf.j)], pf.tile);
   for (int step = 0; ok && step < p.steps; ++step) {
     for (int layer = 0; ok && layer <= p.layers; ++layer) {
       const int nst = layer < p.layers ? 4 : 1;
@@ -690,6 +749,10 @@ __device__ void produce(const DecodeLoop& p, const LoopLayer* layers, uint8_t* r
             break;
           }
           issue_tile(s, t, tile, ring + (size_t)slot * p.slot_bytes, &sh.full[slot]);
+          if (pf_live && p.l2_ahead > 0 && (pf_live = pf.next(p, sh))) {
+            const int pst = TileCursor::stage_of(p, pf.layer, pf.j);
+            prefetch_tile(stage_weights(p, layers, pf.layer, pst), sh.tiles[pst], pf.tile);
+          }
           if (tile == 0) MI_TRACE(step, trace_stage, 3);
           if (tile == t.count - 1) MI_TRACE(step, trace_stage, 4);
         }

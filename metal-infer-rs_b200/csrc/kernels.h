@@ -296,6 +296,7 @@ struct DecodeLoop {
   // plan (decode_loop_plan)
   int slot_bytes = 0, slots = 0, x_bytes = 0, grid = 0;
   int xslice = 1;  // tensor parallelism: each CTA sums a slice of the partials (else all)
+  int l2_ahead = 0; // the producer's L2 prefetches run this many weight tiles ahead of its copies
 };
 // Mailbox layout in u64 words for `tp` ranks, hidden size h and grid CTAs:
 // [tp][h] O partials, [tp][h] down partials, [tp][grid] argmax records.

@@ -218,6 +218,10 @@ bool pdl_enabled() {
   return on == 1;
 }
 
+// Weight tiles (32 KB each per SM) the persistent decode kernel's producer
+// prefetches into L2 beyond its shared-memory copies.
+constexpr int kL2AheadTiles = 6;
+
 k::Launch dlaunch(mi_qwen3* m, bool pdl) {
   return launch(m, pdl && !m->ctx->profiling && pdl_enabled() && m->tp == 1);
 }
@@ -679,6 +683,13 @@ void run_decode_loop(mi_qwen3* m, mi_kv_cache* c, size_t steps) {
     // MI_TP_SLICE=0: every CTA sums all of the ranks' partials itself
     const char* e = getenv("MI_TP_SLICE");
     p.xslice = (e && *e == '0') ? 0 : 1;
+  }
+  {
+    // weight tiles the producer prefetches into L2 ahead of its copies
+    // (same-box A/B, Qwen3-0.6B / 8B tokens/s: 0 → 1,487 / 208.8, 6 → 1,538 /
+    // 211.6, 16 → 1,347 / 166.1); MI_L2_AHEAD overrides
+    const char* e = getenv("MI_L2_AHEAD");
+    p.l2_ahead = e ? atoi(e) : kL2AheadTiles;
   }
   p.rank = m->rank;
   p.vocab0 = (uint32_t)(m->rank * m->cfg.vocab_size);
