@@ -220,7 +220,7 @@ bool pdl_enabled() {
 
 // Weight tiles (32 KB each per SM) the persistent decode kernel's producer
 // prefetches into L2 beyond its shared-memory copies.
-constexpr int kL2AheadTiles = 6;
+constexpr int kL2AheadTiles = 4;
 
 k::Launch dlaunch(mi_qwen3* m, bool pdl) {
   return launch(m, pdl && !m->ctx->profiling && pdl_enabled() && m->tp == 1);
@@ -686,8 +686,8 @@ void run_decode_loop(mi_qwen3* m, mi_kv_cache* c, size_t steps) {
   }
   {
     // weight tiles the producer prefetches into L2 ahead of its copies
-    // (same-box A/B, Qwen3-0.6B / 8B tokens/s: 0 → 1,487 / 208.8, 6 → 1,538 /
-    // 211.6, 16 → 1,347 / 166.1); MI_L2_AHEAD overrides
+    // (same-box A/B, Qwen3-0.6B / 8B tokens/s: 0 → 1,467 / 208.0, 4 → 1,512 /
+    // 213.9, 6 → 1,500 / 211.9, 16 → 1,347 / 166.1); MI_L2_AHEAD overrides
     const char* e = getenv("MI_L2_AHEAD");
     p.l2_ahead = e ? atoi(e) : kL2AheadTiles;
   }
