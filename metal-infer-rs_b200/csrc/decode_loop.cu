@@ -17,8 +17,12 @@
 // "full" mbarriers. It is throttled only by the ring ("empty" mbarriers the
 // consumer warps arrive on), never by the grid barriers between stages, so
 // HBM keeps streaming weights while the consumers wait on their
-// predecessors. Consumers build each stage's input vector in shared memory,
+// predecessors; a second cursor over the same schedule prefetches the tiles
+// a few slots beyond the ring into L2, so the stream goes on while the ring
+// is full. Consumers build each stage's input vector in shared memory,
 // reduce their rows from the ring and write the outputs to global memory.
+// The kernel is instantiated twice: for one GPU, and for tensor parallelism
+// (the mailbox exchanges), so that neither carries the other's code.
 //
 // There are no grid barriers. Activations that cross CTAs are stored as
 // epoch-tagged words (tag << 16 | FP16 bits) that validate themselves: after
