@@ -403,10 +403,12 @@ mi_fusion_options mi_qwen3_fusion_options(const mi_qwen3* m);
 mi_status mi_qwen3_set_decode_graphs(mi_qwen3* m, int enabled);
 /* Tensor-parallel diagnostics (no reference counterpart: the reference is
  * single-device). Synchronizes, then reports how long the CTAs of the most
- * recent persistent decode launch waited on their mailbox counters (the O,
- * DOWN and LM-head partials of the other ranks arriving over NVLink):
- * the mean and the maximum over CTAs in seconds, and that launch's decode
- * steps. Zeros when tp = 1 or no persistent launch ran. */
+ * recent persistent decode launch spent on inputs fed by the other ranks
+ * (from the start of such a stage input until the O / DOWN partials that
+ * arrived over NVLink, and the LM-head argmax records, had all validated,
+ * staging included): the mean and the maximum over CTAs in seconds, and
+ * that launch's decode steps. Zeros when tp = 1 or no persistent launch
+ * ran. */
 mi_status mi_qwen3_exchange_wait(mi_qwen3* m, double* mean_seconds, double* max_seconds,
                                  size_t* steps);
 /* No counterpart in the reference (its decode encodes one command buffer per
