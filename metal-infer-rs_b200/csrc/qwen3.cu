@@ -219,8 +219,29 @@ bool pdl_enabled() {
 }
 
 // Weight tiles (32 KB each per SM) the persistent decode kernel's producer
-// prefetches into L2 beyond its shared-memory copies.
+// prefetches into L2 beyond its shared-memory copies (same-box A/B,
+// Qwen3-0.6B / 8B tokens/s: 0 → 1,467 / 208.0, 4 → 1,512 / 213.9, 6 → 1,500 /
+// 211.9, 16 → 1,347 / 166.1). MI_L2_AHEAD=n overrides (0..64).
 constexpr int kL2AheadTiles = 4;
+int l2_ahead_tiles() {
+  static int n = -1;
+  if (n < 0) {
+    const char* e = getenv("MI_L2_AHEAD");
+    n = e ? std::min(std::max(atoi(e), 0), 64) : kL2AheadTiles;
+  }
+  return n;
+}
+
+// Tensor parallelism: each CTA sums its slice of the ranks' partials;
+// MI_TP_SLICE=0 has every CTA sum all of them itself.
+bool tp_slice_enabled() {
+  static int on = -1;
+  if (on < 0) {
+    const char* e = getenv("MI_TP_SLICE");
+    on = (e && *e == '0') ? 0 : 1;
+  }
+  return on == 1;
+}
 
 k::Launch dlaunch(mi_qwen3* m, bool pdl) {
   return launch(m, pdl && !m->ctx->profiling && pdl_enabled() && m->tp == 1);
@@ -679,18 +700,8 @@ void run_decode_loop(mi_qwen3* m, mi_kv_cache* c, size_t steps) {
   p.attn_part = w.loop_part.t->f32();
   p.sync = w.loop_sync.t->u32();
   p.tp = m->tp;
-  {
-    // MI_TP_SLICE=0: every CTA sums all of the ranks' partials itself
-    const char* e = getenv("MI_TP_SLICE");
-    p.xslice = (e && *e == '0') ? 0 : 1;
-  }
-  {
-    // weight tiles the producer prefetches into L2 ahead of its copies
-    // (same-box A/B, Qwen3-0.6B / 8B tokens/s: 0 → 1,467 / 208.0, 4 → 1,512 /
-    // 213.9, 6 → 1,500 / 211.9, 16 → 1,347 / 166.1); MI_L2_AHEAD overrides
-    const char* e = getenv("MI_L2_AHEAD");
-    p.l2_ahead = e ? atoi(e) : kL2AheadTiles;
-  }
+  p.xslice = tp_slice_enabled() ? 1 : 0;
+  p.l2_ahead = l2_ahead_tiles();
   p.rank = m->rank;
   p.vocab0 = (uint32_t)(m->rank * m->cfg.vocab_size);
   if (m->tp > 1) {
